@@ -1,0 +1,206 @@
+"""TEST INFRASTRUCTURE ONLY -- ctypes front end of the two CPU checkers.
+
+* ``port``: ``oracle/libs2oracle.so``, our plain-C restatement of the
+  reference hot path (``oracle/s2_oracle.c``; always built by ``build()``).
+* ``ref``: ``oracle/_ref/libs2ref.so``, the reference's own CPU layer code
+  (``src/layers/seedvr2_dit_block.cpp``, ``dynamic_framewise_spatial_attention.cpp``)
+  compiled unmodified against an ncnn-API shim (``oracle/ref_harness.cpp``).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's cpu_baseline /
+``--impl reference`` legs may use this package, and only as the checker or the
+timed CPU baseline. The product library never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "libs2oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libs2ref.so")
+HEAD_DIM = 128
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int)
+_u8p = ctypes.POINTER(ctypes.c_ubyte)
+
+
+def build(ref_root: str = "/root/reference") -> None:
+    """Compile the restatement, and the reference build when its tree exists."""
+    subprocess.run(["make", "-s", "-C", HERE, "port", f"REF={ref_root}"], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
+
+
+def _ptr(a, t=_f32p):
+    if a is None:
+        return None
+    return a.ctypes.data_as(t)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class _Lib:
+    def __init__(self, path: str):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.path = path
+        self.lib = ctypes.CDLL(path)
+
+
+class Port(_Lib):
+    """The C restatement (``oracle/s2_oracle.c``)."""
+
+    def __init__(self, path: str = PORT_SO):
+        super().__init__(path)
+        L = self.lib
+        L.s2o_make_windows.restype = ctypes.c_int
+        L.s2o_make_windows.argtypes = [ctypes.c_int] * 7 + [_i32p, ctypes.c_int]
+        L.s2o_round_bf16.restype = ctypes.c_float
+        L.s2o_round_bf16.argtypes = [ctypes.c_float]
+        L.s2o_window_attention.restype = ctypes.c_int
+        L.s2o_window_attention.argtypes = (
+            [_f32p, ctypes.c_int, _f32p, ctypes.c_int]
+            + [ctypes.c_int] * 8 + [ctypes.c_float]
+            + [_f32p] * 5 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, _u8p, ctypes.c_int]
+            + [_f32p] * 6)
+        L.s2o_vae_attention.restype = ctypes.c_int
+        L.s2o_vae_attention.argtypes = [ctypes.c_int] * 4 + [_f32p] * 11 + [ctypes.c_int] * 3 + [_f32p]
+
+    def make_windows(self, T, H, W, shifted, override=(0, 0, 0)):
+        n = self.lib.s2o_make_windows(T, H, W, int(shifted), *override, None, 0)
+        out = np.zeros((max(n, 1), 6), dtype=np.int32)
+        self.lib.s2o_make_windows(T, H, W, int(shifted), *override, _ptr(out, _i32p), n)
+        return out[:n]
+
+    def window_attention(self, vid_qkv, txt_qkv, shape, heads, gammas, freqs, shifted,
+                         override=(0, 0, 0), eps=1e-5, round_out=True, heads_range=None,
+                         window_mask=None, threads=0, packed=False):
+        """Returns (vid_out [L,dim], txt_out [Lt,dim], packed dict or None)."""
+        T, H, W = shape
+        vid_qkv, txt_qkv = _f32(vid_qkv), _f32(txt_qkv)
+        L, Lt = vid_qkv.shape[0], txt_qkv.shape[0]
+        dim = heads * HEAD_DIM
+        g = [_f32(x) for x in gammas]
+        fr = _f32(freqs)
+        vo = np.zeros((L, dim), np.float32)
+        to = np.zeros((Lt, dim), np.float32)
+        pk = None
+        if packed:
+            wins = self.make_windows(T, H, W, shifted, override)
+            rows = int(sum((w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + Lt for w in wins))
+            pk = {k: np.zeros((rows, dim), np.float32) for k in "qkvo"}
+        hb, he = heads_range if heads_range else (0, heads)
+        mask = None if window_mask is None else np.ascontiguousarray(window_mask, dtype=np.uint8)
+        rc = self.lib.s2o_window_attention(
+            _ptr(vid_qkv), L, _ptr(txt_qkv), Lt, T, H, W, heads, int(shifted), *override,
+            ctypes.c_float(eps), *[_ptr(x) for x in g], _ptr(fr), int(round_out), hb, he,
+            _ptr(mask, _u8p), int(threads or os.cpu_count() or 1), _ptr(vo), _ptr(to),
+            *([_ptr(pk[k]) for k in "qkvo"] if pk else [None] * 4))
+        if rc != 0:
+            raise ValueError(f"s2o_window_attention failed: {rc}")
+        return vo, to, pk
+
+    def vae_attention(self, x, weights, frames=None, threads=0):
+        """x [C,T,H,W]; weights dict with the reference's load_model keys."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        fb, fe = frames if frames else (0, T)
+        y = np.zeros_like(x)
+        order = ["norm_bias", "norm_weight", "k_bias", "k_weight", "out_bias", "out_weight",
+                 "q_bias", "q_weight", "v_bias", "v_weight"]
+        ws = [_f32(weights[k]) for k in order]
+        rc = self.lib.s2o_vae_attention(C, T, H, W, *[_ptr(w) for w in ws], _ptr(x), fb, fe,
+                                        int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"s2o_vae_attention failed: {rc}")
+        return y
+
+
+class Ref(_Lib):
+    """The reference's own CPU code (``oracle/_ref/libs2ref.so``)."""
+
+    def __init__(self, path: str = REF_SO):
+        super().__init__(path)
+        L = self.lib
+        L.ref_make_windows.restype = ctypes.c_int
+        L.ref_make_windows.argtypes = [ctypes.c_int] * 4 + [_i32p, ctypes.c_int]
+        L.ref_attention.restype = ctypes.c_int
+        L.ref_attention.argtypes = (
+            [_f32p, ctypes.c_int, _f32p, ctypes.c_int] + [ctypes.c_int] * 6 + [ctypes.c_float]
+            + [_f32p] * 5 + [ctypes.c_int, ctypes.c_int] + [_f32p] * 6 + [_i32p])
+        L.ref_block_forward.restype = ctypes.c_int
+        L.ref_block_forward.argtypes = (
+            [ctypes.c_int] * 8 + [ctypes.c_float, _f32p, ctypes.c_size_t, _f32p, ctypes.c_int,
+                                  _f32p, ctypes.c_int, _f32p] + [ctypes.c_int] * 4 + [_f32p, _f32p])
+        L.ref_vae_attention.restype = ctypes.c_int
+        L.ref_vae_attention.argtypes = [ctypes.c_int] * 4 + [_f32p, ctypes.c_size_t, _f32p,
+                                                              ctypes.c_int, _f32p]
+
+    def make_windows(self, T, H, W, shifted):
+        n = self.lib.ref_make_windows(T, H, W, int(shifted), None, 0)
+        out = np.zeros((max(n, 1), 6), dtype=np.int32)
+        self.lib.ref_make_windows(T, H, W, int(shifted), _ptr(out, _i32p), n)
+        return out[:n]
+
+    def attention(self, vid_qkv, txt_qkv, shape, heads, gammas, freqs, shifted, eps=1e-5,
+                  head_count=0, threads=0, packed=False):
+        T, H, W = shape
+        vid_qkv, txt_qkv = _f32(vid_qkv), _f32(txt_qkv)
+        L, Lt = vid_qkv.shape[0], txt_qkv.shape[0]
+        dim = heads * HEAD_DIM
+        vo = np.zeros((L, dim), np.float32)
+        to = np.zeros((Lt, dim), np.float32)
+        pk = None
+        rows = ctypes.c_int(0)
+        if packed:
+            wins = self.make_windows(T, H, W, shifted)
+            n = int(sum((w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + Lt for w in wins))
+            pk = {k: np.zeros((n, dim), np.float32) for k in "qkvo"}
+        g = [_f32(x) for x in gammas]
+        rc = self.lib.ref_attention(
+            _ptr(vid_qkv), L, _ptr(txt_qkv), Lt, T, H, W, heads, HEAD_DIM, int(shifted),
+            ctypes.c_float(eps), *[_ptr(x) for x in g], _ptr(_f32(freqs)),
+            int(threads or os.cpu_count() or 1), int(head_count), _ptr(vo), _ptr(to),
+            *([_ptr(pk[k]) for k in "qkvo"] if pk else [None] * 4), ctypes.byref(rows))
+        if rc != 0:
+            raise ValueError(f"ref_attention failed: {rc}")
+        return vo, to, pk
+
+    def block_forward(self, params, weights, vid, txt, emb, shape, threads=0):
+        p = params
+        weights = _f32(weights)
+        vid, txt, emb = _f32(vid), _f32(txt), _f32(emb)
+        vo = np.zeros((vid.shape[0], p["dim"]), np.float32)
+        to = np.zeros((txt.shape[0], p["dim"]), np.float32)
+        rc = self.lib.ref_block_forward(
+            p["block_index"], int(p["shared"]), int(p["last"]), int(p["shifted"]), p["dim"],
+            p["heads"], p["head_dim"], p["mlp_hidden"], ctypes.c_float(p.get("eps", 1e-5)),
+            _ptr(weights), weights.size, _ptr(vid), vid.shape[0], _ptr(txt), txt.shape[0],
+            _ptr(emb), *shape, int(threads or os.cpu_count() or 1), _ptr(vo), _ptr(to))
+        if rc != 0:
+            raise ValueError(f"ref_block_forward failed: {rc}")
+        return vo, to
+
+    def vae_attention(self, x, weights_flat, threads=0):
+        x = _f32(x)
+        C, T, H, W = x.shape
+        w = _f32(weights_flat)
+        y = np.zeros_like(x)
+        rc = self.lib.ref_vae_attention(C, T, H, W, _ptr(w), w.size, _ptr(x),
+                                        int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"ref_vae_attention failed: {rc}")
+        return y
+
+
+def port() -> Port:
+    return Port()
+
+
+def ref() -> Ref | None:
+    return Ref() if os.path.exists(REF_SO) else None
