@@ -1,0 +1,468 @@
+#!/usr/bin/env python
+"""Benchmark of the SeedVR2 windowed MM-attention path on B200.
+
+One step = the attention stage of one DiT Euler step at 720p: 32 window-
+attention layers (16 plain + 16 shifted windows; block parity as in the
+reference's export) over the 6x45x80 = 21,600-token grid, 20 heads x 128,
+58 text tokens. Each layer is the fused prologue (QK-RMSNorm + MM-RoPE, fp16
+packing), the tcgen05 window-attention kernel and the text-mean kernel.
+
+value     = algorithmic attention FLOPs of all ranks / max-over-ranks device
+            time of the timed steps (CUDA events), inputs resident in HBM.
+e2e       = same metric through the layer's host-buffer C-ABI call
+            (s2_attention_layer_forward_host): pinned host QKV in, host
+            outputs back, copies inside the timed region.
+roofline  = the attention kernel alone: FLOPs per launch / mean launch time
+            (events around each launch inside the timed region).
+cpu_baseline / --impl reference: the reference's own CPU attention()
+            (oracle/_ref, built from the reference sources) on a bounded
+            sample of the same workload, on this host's cores.
+
+Multi-GPU (torchrun): each rank processes its own clip's windows (weak
+scaling, no data-path collective). --shard instead splits ONE clip's windows
+across ranks (LPT by S_w^2) and all-reduces the text partial sums over NCCL.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "seedvr2-ncnn-valkan_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "window-attn TFLOP/s (% tcgen05 peak); DiT Euler-step ms at 1/2/4/8 B200 vs CPU ref"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch recorded in a committed ncu summary (profiles/)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- CPU reference
+
+
+def cpu_reference_sample(grid, text_len, heads_total, seed=666):
+    """Times the reference's own attention() (oracle/_ref) on one head per host
+    core (at most all heads) of the plain 720p layer. Returns a dict."""
+    import oracle
+    from s2b200 import synth
+    ref = oracle.ref()
+    kind = "reference"
+    if ref is None:
+        ref, kind = oracle.port(), "port"
+    cores = os.cpu_count() or 1
+    heads = max(1, min(heads_total, cores))
+    vid, txt, gam, fr = synth.layer_inputs(grid, heads=heads_total, text_len=text_len, seed=seed)
+    wins = ref.make_windows(*grid, 0)
+    flops = synth.attention_flops(wins, text_len, heads)
+    t0 = time.perf_counter()
+    if kind == "reference":
+        ref.attention(vid, txt, grid, heads_total, list(gam), fr, 0, head_count=heads, threads=heads)
+    else:
+        ref.window_attention(vid, txt, grid, heads_total, list(gam), fr, 0, heads_range=(0, heads), threads=heads)
+    dt = time.perf_counter() - t0
+    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": heads, "kind": kind, "seconds": dt,
+            "sample": f"plain-window layer of the {grid[0]}x{grid[1]}x{grid[2]} grid, heads 0..{heads - 1} of "
+                      f"{heads_total} (one head per thread, {heads} threads of {cores} host cores), "
+                      f"{flops / 1e9:.1f} GFLOP algorithmic"}
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    from s2b200 import synth
+    grid = synth.GRIDS["cfg2"]
+    vals = []
+    last = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_reference_sample(grid, 58, 20)
+        if i >= args.warmup:
+            vals.append(r["value"])
+        last = r
+    v = float(statistics.mean(vals)) if vals else last["value"]
+    secs = last["seconds"]
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64 (reference CPU)", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": last["cores"], "kind": last["kind"],
+                             "sample": last["sample"]},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU arm
+
+
+def workload_config(args):
+    return {"workload": "720p DiT-step attention stage: 32 MM window-attention layers (16 plain + 16 shifted), "
+                        "token grid 6x45x80 = 21,600, 20 heads x 128, 58 text tokens, reference window rule "
+                        "(2x15x27: 27 plain / 64 shifted windows)" if not args.override else
+                        "720p DiT-step attention stage with BASELINE.json's 6x15x20 window override",
+            "layers_per_step": 32, "grid": [6, 45, 80], "heads": 20, "head_dim": 128, "text_len": 58,
+            "mode": args.mode, "io": "fp16 QKV in, fp16 out" if args.mode == "f16" else "fp16 QKV in, bf16 out",
+            "l2": "no flush: every layer reads a distinct >L2 input (332 MB QKV, 356 MB packed Q/K/V)",
+            "sharding": "window-sharded single clip + NCCL text all-reduce" if args.shard else
+                        "one clip per rank (weak)"}
+
+
+def lpt_assign(costs, n_ranks):
+    order = np.argsort(-np.asarray(costs), kind="stable")
+    load = np.zeros(n_ranks)
+    owner = np.zeros(len(costs), np.int32)
+    for i in order:
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += costs[i]
+    return owner
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    import s2b200
+    from s2b200 import synth
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    rc = s2b200.device_check(local_rank)
+    if rc != 0:
+        raise RuntimeError(s2b200.last_error())
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    grid = synth.GRIDS["cfg2"]
+    T, H, W = grid
+    heads, Lt, dim = 20, 58, 2560
+    mode = s2b200.MODE_F16 if args.mode == "f16" else s2b200.MODE_BF16_REF
+    override = synth.OVERRIDES["cfg2"] if args.override else (0, 0, 0)
+    stream = torch.cuda.current_stream()
+
+    # plans: plain (shifted=0) and shifted layers
+    plans = []
+    for shifted in (0, 1):
+        wins = s2b200.make_windows(T, H, W, shifted, override)
+        sizes = (wins[:, 1] - wins[:, 0]) * (wins[:, 3] - wins[:, 2]) * (wins[:, 5] - wins[:, 4]) + Lt
+        ids = np.arange(len(wins))
+        if args.shard and world > 1:
+            ids = np.nonzero(lpt_assign(sizes.astype(np.float64) ** 2, world) == rank)[0]
+        local = wins[ids]
+        cu, rows = s2b200.build_varlen(T, H, W, local, Lt)
+        work = s2b200.plan_work(cu)
+        max_pos = int(rows[:, 1:].max()) + 1
+        plans.append(dict(
+            shifted=shifted, n_total=len(wins), n_local=len(local), flops=synth.attention_flops(local, Lt, heads),
+            cu=torch.from_numpy(cu).to(dev), rows=torch.from_numpy(rows.copy()).to(dev),
+            work=torch.from_numpy(work).to(dev), n_rows=rows.shape[0], max_pos=max_pos))
+
+    vid_np, txt_np, gam, fr = synth.layer_inputs(grid, heads=heads, text_len=Lt, seed=666 + rank)
+    gam_d = torch.from_numpy(gam).to(dev)
+    fr_d = torch.from_numpy(fr).to(dev)
+    for p in plans:
+        p["tab"] = s2b200.rope_table(fr_d, p["max_pos"])
+    # 4 distinct QKV inputs (2 per layer kind), each 332 MB fp16 > L2
+    base_v = torch.from_numpy(vid_np).to(dev, torch.float16)
+    base_t = torch.from_numpy(txt_np).to(dev, torch.float16)
+    inputs = []
+    for i in range(4):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + i)
+        noise = (torch.randn(base_v.shape, device=dev, generator=g, dtype=torch.float32) * 0.01).to(torch.float16)
+        inputs.append((base_v + noise, base_t.clone()))
+    del base_v
+    out_dtype = s2b200.mode_dtype(mode)
+    n_rows_max = max(p["n_rows"] for p in plans)
+    ws = [torch.empty((heads, n_rows_max, 128), dtype=torch.float16, device=dev) for _ in range(3)]
+    vid_out = torch.zeros((T * H * W, dim), dtype=out_dtype, device=dev)
+    txt_part = torch.empty((max(p["n_local"] for p in plans), Lt, dim), dtype=out_dtype, device=dev)
+    txt_out = torch.empty((Lt, dim), dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = s2b200.lib()
+    sp = s2b200._stream_ptr(stream)
+    vp = lambda t: s2b200._ptr(t)  # noqa: E731
+
+    def layer(i, ev=None):
+        p = plans[i % 2]
+        v_in, t_in = inputs[i % 4]
+        # packed [heads, n_rows, 128] operands: leading slices of the flat workspaces
+        qf, kf, vf = (w.view(-1)[: heads * p["n_rows"] * 128] for w in ws)
+        if ev:
+            ev[0].record(stream)
+        rc = lib.s2_qk_norm_rope(sp, vp(v_in), vp(t_in), s2b200.S2_F16, heads, 1e-5, vp(gam_d), vp(p["tab"]),
+                                 vp(p["rows"]), p["n_rows"], mode, vp(qf), vp(kf), vp(vf))
+        if rc:
+            raise RuntimeError(s2b200.last_error())
+        if ev:
+            ev[1].record(stream)
+        rc = lib.s2_window_attention(sp, mode, vp(qf), vp(kf), vp(vf), heads, p["n_rows"], vp(p["cu"]),
+                                     p["n_local"], Lt, vp(p["rows"]), vp(p["work"]), p["work"].shape[0],
+                                     vp(vid_out), vp(txt_part), vp(err))
+        if rc:
+            raise RuntimeError(s2b200.last_error())
+        if ev:
+            ev[2].record(stream)
+        rc = lib.s2_text_window_sum(sp, mode, vp(txt_part), p["n_local"], Lt, dim, 1.0 / p["n_total"], 0,
+                                    vp(txt_out))
+        if rc:
+            raise RuntimeError(s2b200.last_error())
+        if ev:
+            ev[3].record(stream)
+        if args.shard and world > 1:
+            dist.all_reduce(txt_out)
+
+    layers_per_step = 32
+    for _ in range(args.warmup):
+        for i in range(layers_per_step):
+            layer(i)
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"attention kernel device error {int(err.item())}")
+
+    n_ev = layers_per_step * args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            for i in range(layers_per_step):
+                layer(i, evs[s * layers_per_step + i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"attention kernel device error {int(err.item())}")
+    t_pro = np.array([e[0].elapsed_time(e[1]) for e in evs])
+    t_att = np.array([e[1].elapsed_time(e[2]) for e in evs])
+    t_txt = np.array([e[2].elapsed_time(e[3]) for e in evs])
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+
+    step_flops_local = 16 * (plans[0]["flops"] + plans[1]["flops"])
+    tot = torch.tensor([step_flops_local], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(tot)
+    step_flops_all = float(tot.item())
+    ms_per_step = ms / args.steps
+    value = step_flops_all / (ms_per_step * 1e-3) / 1e12
+
+    # roofline of the attention kernel (per-launch mean, both layer kinds)
+    att_plain = float(np.mean(t_att[0::2]))
+    att_shift = float(np.mean(t_att[1::2]))
+    flops_launch = (plans[0]["flops"] + plans[1]["flops"]) / 2
+    att_ms = (att_plain + att_shift) / 2
+    achieved = flops_launch / (att_ms * 1e-3) / 1e12
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic = profile_traffic("window_attention_cfg2.md")
+    pro_bytes = synth.prologue_bytes(T * H * W, Lt, (plans[0]["n_rows"] + plans[1]["n_rows"]) / 2, heads, 2)
+    pro_gbs = pro_bytes / (float(np.mean(t_pro)) * 1e-3) / 1e9
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+
+    # end-to-end through the host-buffer C-ABI call (layer objects, pinned host memory)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, fr, mode, override,
+                      step_flops_all, dist)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if args.shard and world > 1 else "weak", "vs_baseline": None,
+                "dtype": "f16" if args.mode == "f16" else "f16 (bf16 out)", "data": "synthetic",
+                "config": workload_config(args),
+                "pct_of_peak": 100.0 * value / world / peak,
+                "gpu_launches": 3 * layers_per_step * args.steps,
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "traffic": traffic,
+                             "peak_source": f"{peak_src} bf16 dense (burst)",
+                             "kernel": "window_attention_kernel", "flops_per_launch": flops_launch,
+                             "ms_per_launch": {"plain": att_plain, "shifted": att_shift}},
+                "kernels": {"prologue_ms": float(np.mean(t_pro)), "attention_ms": att_ms,
+                            "text_sum_ms": float(np.mean(t_txt)), "prologue_gbs": pro_gbs,
+                            "prologue_hbm_frac": pro_gbs / hbm_peak},
+                "clocks": clk.summary()}
+        if e2e:
+            line["e2e"] = e2e
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_reference_sample(grid, Lt, heads)
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, fr, mode, override, step_flops_all,
+            dist):
+    T, H, W = grid
+    L, dim = T * H * W, heads * 128
+    stream = torch.cuda.current_stream()
+    layers = []
+    for shifted in (0, 1):
+        lay = s2b200.SeedVR2DiTBlockAttention(device=dev.index, mode=mode, window_override=override)
+        lay.load_param(shifted=shifted, dim=dim, heads=heads)
+        lay.load_model(gam[0], gam[1], fr, gam[2], gam[3])
+        if args.shard and world > 1:
+            wins = s2b200.make_windows(T, H, W, shifted, override)
+            sizes = (wins[:, 1] - wins[:, 0]) * (wins[:, 3] - wins[:, 2]) * (wins[:, 5] - wins[:, 4]) + Lt
+            lay.set_window_subset(np.nonzero(lpt_assign(sizes.astype(np.float64) ** 2, world) == rank)[0])
+        layers.append(lay)
+    vid_np, txt_np, _, _ = synth.layer_inputs(grid, heads=heads, text_len=Lt, seed=666 + rank)
+    hv = torch.from_numpy(vid_np.astype(np.float16)).pin_memory().numpy()
+    ht = torch.from_numpy(txt_np.astype(np.float16)).pin_memory().numpy()
+    out_np = np.float16 if mode == s2b200.MODE_F16 else np.uint16
+    io = s2b200.S2_F16 if mode == s2b200.MODE_F16 else s2b200.S2_F32
+    if io == s2b200.S2_F32:
+        hv = torch.from_numpy(vid_np).pin_memory().numpy()
+        ht = torch.from_numpy(txt_np).pin_memory().numpy()
+        out_np = np.float32
+    ov = torch.empty((L, dim), dtype={np.float16: torch.float16, np.float32: torch.float32}[out_np]).pin_memory().numpy()
+    ot = torch.empty((Lt, dim), dtype=torch.float32).pin_memory().numpy()
+    shape = np.array(grid, np.int32)
+    layers_per_step = 32
+    steps = max(1, min(args.steps, args.e2e_steps))
+    for i in range(2):
+        layers[i % 2].forward_host(hv, ht, shape, io, ov, ot, stream=stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        for i in range(layers_per_step):
+            layers[i % 2].forward_host(hv, ht, shape, io, ov, ot, stream=stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_step = float(ms_t.item()) / steps
+    h2d = layers_per_step * (hv.nbytes + ht.nbytes)
+    d2h = layers_per_step * (ov.nbytes + ot.nbytes)
+    for lay in layers:
+        lay.close()
+    return {"value": step_flops_all / (ms_step * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": ms_step, "steps": steps,
+            "path": "s2_attention_layer_forward_host (pinned host buffers)"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--override", action="store_true", help="BASELINE.json's 6x15x20 windows")
+    ap.add_argument("--shard", action="store_true", help="split one clip's windows across ranks")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,218 @@
+/*
+ * s2_b200.h -- C ABI of the B200 (sm_100a) SeedVR2 windowed MM-attention path.
+ *
+ * This is the drop-in boundary for the hot path of czwdysj/seedvr2-ncnn-valkan:
+ * the body of SeedVR2DiTBlock::attention (src/layers/seedvr2_dit_block.cpp:870-1091),
+ * i.e. window partition, per-head QK-RMSNorm, 3-axis MM-RoPE, bf16 rounding,
+ * joint (video window || shared text) attention, video scatter and the
+ * cross-window text mean. Everything else in the block stays with the caller.
+ *
+ * Conventions
+ *  - Every entry point returns an s2_status (values mirror seedvr2::Status,
+ *    include/seedvr2/engine.h:20-31). On failure s2_last_error() (thread-local)
+ *    holds a one-line diagnostic, like the reference's stderr lines.
+ *  - Device entry points are stream-ordered on the cudaStream_t passed as
+ *    `void* stream` (NULL = legacy default stream) and never synchronise the
+ *    host, except the *_host variants, which copy host buffers in and out.
+ *  - Device pointers are caller-owned. Layer objects own only their weights,
+ *    cached window plans and workspaces.
+ *  - head_dim is 128 (the reference's MM-RoPE covers dims 0..125 and assumes
+ *    128, seedvr2_dit_block.cpp:956-971).
+ */
+#ifndef S2_B200_H
+#define S2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported entry points (the library is built with hidden visibility). */
+#if defined(__GNUC__)
+#define S2_API __attribute__((visibility("default")))
+#else
+#define S2_API
+#endif
+
+#define S2_HEAD_DIM 128
+#define S2_ROPE_PAIRS 21
+
+typedef enum s2_status {
+    S2_OK = 0,                  /* seedvr2::Status::Ok */
+    S2_INVALID_ARGUMENT = -1,   /* bad shape / blob count (reference returns -1) */
+    S2_NOT_LOADED = -2,         /* weights not loaded / runtime shape not set */
+    S2_INFERENCE_FAILED = -5,   /* a CUDA launch or device-side check failed */
+    S2_UNSUPPORTED = -6,        /* no sm_100 device, or unsupported dtype/mode */
+    S2_OUT_OF_MEMORY = -7       /* workspace allocation failed (reference -100) */
+} s2_status;
+
+typedef enum s2_dtype {
+    S2_F32 = 0,
+    S2_F16 = 1,
+    S2_BF16 = 2
+} s2_dtype;
+
+/* Output rounding of the attention core. In both modes the packed Q/K/V hold
+ * the reference's bf16-rounded values (RNE, the .bfloat16() before SDPA),
+ * stored as fp16 -- exact for |x| in fp16's normal range [6.1e-5, 65504),
+ * absolute error < 3e-8 below it -- both GEMMs run f16 x f16 on tcgen05 with
+ * fp32 accumulation in TMEM, and P is fp16.
+ *  S2_MODE_BF16_REF: outputs rounded to bf16 (RNE) and stored as bf16, as the
+ *    reference CPU path rounds each window output (seedvr2_dit_block.cpp:1074).
+ *  S2_MODE_F16: outputs stored as fp16 without the bf16 rounding (the
+ *    reference's Vulkan shader keeps its fp32 result, :416-436). */
+typedef enum s2_mode {
+    S2_MODE_BF16_REF = 0,
+    S2_MODE_F16 = 1
+} s2_mode;
+
+/* One 3-D window box, half-open ranges on the (T, H, W) token grid.
+ * Same fields as SeedVR2DiTBlock::Window (seedvr2_dit_block.h:98-106). */
+typedef struct s2_window {
+    int32_t t0, t1, h0, h1, w0, w1;
+} s2_window;
+
+/* One packed attention row. src >= 0: video token (t*H + y)*W + x;
+ * src < 0: text token -(src+1). (pt, ph, pw) is its MM-RoPE position:
+ * video (Lt + t - t0, y - h0, x - w0), text (l, l, l)
+ * (seedvr2_dit_block.cpp:988, :1011). */
+typedef struct s2_row {
+    int32_t src, pt, ph, pw;
+} s2_row;
+
+/* ---- host-side planning ------------------------------------------------ */
+
+/* Replaces SeedVR2DiTBlock::make_windows (seedvr2_dit_block.cpp:827-868),
+ * bit-identical. wt/wh/ww > 0 override the resolution-adaptive window size
+ * (explicit geometries); pass 0,0,0 for the reference rule. Writes up to
+ * `cap` windows to `out` (may be NULL) and the full count to *count. */
+S2_API s2_status s2_make_windows(int frames, int height, int width, int shifted,
+                          int wt, int wh, int ww,
+                          s2_window *out, int cap, int *count);
+
+/* Packs windows into a varlen sequence list: window w occupies rows
+ * [cu_seqlens[w], cu_seqlens[w+1]) = its L_w video tokens in (t, y, x) order
+ * followed by the Lt text tokens -- the reference's per-window sequence
+ * (seedvr2_dit_block.cpp:976-1028) and debug-capture row order (:899-907).
+ * cu_seqlens has n+1 entries; rows has cu_seqlens[n] entries (either may be
+ * NULL to query *total_rows only). */
+S2_API s2_status s2_build_varlen(int frames, int height, int width,
+                          const s2_window *windows, int n, int text_len,
+                          int32_t *cu_seqlens, s2_row *rows, int *total_rows);
+
+/* ---- device kernels (explicit buffers) ---------------------------------- */
+
+/* Fused prologue: per (packed row, head) RMSNorm over 128 dims (eps) times
+ * gamma, MM-RoPE (3 axes x 21 pairs, angle = pos * freqs[p]), bf16 RNE
+ * rounding; V rounded only. Replaces normalize_and_rotate and the V copy
+ * (seedvr2_dit_block.cpp:942-1028) and the Vulkan qkv_prepare shader (:192-330).
+ *   vid_qkv [L][3*heads*128], txt_qkv [Lt][3*heads*128] in `in_dtype`
+ *   gammas: device fp32 [4][128] = norm_q_vid, norm_k_vid, norm_q_txt, norm_k_txt
+ *   rows: device s2_row [n_rows]
+ *   q, k, v: device fp16 [heads][n_rows][128] (bf16-rounded values).
+ *   rope_table: device table from s2_rope_table for positions [0, max_pos)
+ *   (every rows[].pt/ph/pw must be < max_pos). */
+S2_API size_t s2_rope_table_bytes(int max_pos);
+S2_API s2_status s2_rope_table(void *stream, const float *freqs21, int max_pos, void *rope_table);
+S2_API s2_status s2_qk_norm_rope(void *stream,
+                          const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype,
+                          int heads, float eps, const float *gammas, const void *rope_table,
+                          const s2_row *rows, int n_rows, s2_mode mode, void *q, void *k, void *v);
+
+/* Varlen window attention on sm_100a (tcgen05 MMA into TMEM, TMA-fed
+ * shared-memory ring, warp-specialised online softmax). For window w with
+ * sequence rows [cu[w], cu[w+1]) and text_len trailing text rows:
+ * O = softmax(Q K^T / sqrt(128)) V over the window's own rows, non-causal.
+ * Video rows are scattered to vid_out[rows[r].src][h*128 + d] ([L][heads*128],
+ * bf16 for S2_MODE_BF16_REF, fp16 for S2_MODE_F16); text rows go to
+ * txt_partial[w][l][h*128 + d] ([n_windows][text_len][heads*128], same type). Replaces the attention core
+ * (seedvr2_dit_block.cpp:1045-1079; Vulkan block_attention :339-438 plus
+ * zero_buffer/window_sum scatter :442-457, :541-572).
+ *   cu_seqlens: device int32 [n_windows+1]; rows: device s2_row.
+ *   work: device int32 [n_work] of (window << 16 | q_tile) items, costliest
+ *   first (s2_plan_work); n_work * heads CTAs are launched.
+ *   err: device int32 error word (0 = ok), set on a device-side timeout. */
+S2_API s2_status s2_window_attention(void *stream, s2_mode mode,
+                              const void *q, const void *k, const void *v, int heads, int n_rows,
+                              const int32_t *cu_seqlens, int n_windows, int text_len,
+                              const s2_row *rows, const int32_t *work, int n_work,
+                              void *vid_out, void *txt_partial, int32_t *err);
+
+/* Host helper: the (window, q_tile) work list for s2_window_attention,
+ * sorted by descending cost. Returns the item count in *n_work; `work` may be
+ * NULL to query. cu_seqlens is the host copy. */
+S2_API s2_status s2_plan_work(const int32_t *cu_seqlens, int n_windows, int32_t *work, int cap, int *n_work);
+
+/* Text mean: txt_out[l][c] = (sum over w of txt_partial[w][l][c], in window
+ * order, fp32) * scale (scale = 1/total windows; reference :1081-1088).
+ * accumulate != 0 adds into txt_out instead of overwriting. */
+S2_API s2_status s2_text_window_sum(void *stream, s2_mode mode, const void *txt_partial,
+                             int n_windows, int text_len, int dim, float scale, int accumulate,
+                             float *txt_out);
+
+/* ---- layer object: mirror of SeedVR2DiTBlock's attention stage ---------- */
+
+typedef struct s2_attention_layer s2_attention_layer;
+
+/* load_param subset (seedvr2_dit_block.cpp:643-655): heads, head_dim (must be
+ * 128), eps, shifted; window override wt/wh/ww (0 = reference rule); mode. */
+S2_API s2_status s2_attention_layer_create(int device, int heads, int head_dim, float eps, int shifted,
+                                    int wt, int wh, int ww, s2_mode mode,
+                                    s2_attention_layer **out);
+S2_API s2_status s2_attention_layer_destroy(s2_attention_layer *layer);
+
+/* load_model subset (:657-688): host fp32 norm_q/norm_k of the video branch,
+ * of the text branch (pass the video ones again for shared blocks), and
+ * rope freqs [21]. */
+S2_API s2_status s2_attention_layer_load(s2_attention_layer *layer,
+                                  const float *norm_q_vid, const float *norm_k_vid,
+                                  const float *norm_q_txt, const float *norm_k_txt,
+                                  const float *freqs21);
+
+/* set_runtime_shape (seedvr2_dit_block.h:55). */
+S2_API s2_status s2_attention_layer_set_runtime_shape(s2_attention_layer *layer, int frames, int height, int width);
+
+/* Restrict this layer to a subset of its windows (window sharding across
+ * GPUs). ids NULL / n 0 = all windows. */
+S2_API s2_status s2_attention_layer_set_window_subset(s2_attention_layer *layer, const int32_t *ids, int n);
+
+/* attention() on device buffers: vid_qkv [L][3*dim], txt_qkv [Lt][3*dim] in
+ * in_dtype; vid_out [L][dim] in the mode dtype (rows of windows outside the
+ * subset are left untouched); txt_out [Lt][dim] fp32 = sum over this layer's
+ * windows of the text outputs times 1/(total windows), or, with accumulate,
+ * added into txt_out. Returns -1 on shape mismatch like the reference. */
+S2_API s2_status s2_attention_layer_forward(s2_attention_layer *layer, void *stream,
+                                     const void *vid_qkv, s2_dtype in_dtype, int L,
+                                     const void *txt_qkv, int Lt,
+                                     void *vid_out, float *txt_out);
+
+/* Same on HOST buffers (the ncnn::Mat contract: vid_shape int32[3], inputs
+ * [rows][3*dim], outputs [rows][dim]); copies in, runs, copies out and
+ * synchronises `stream`. io_dtype is the element type of all four host
+ * buffers except txt_out, which is fp32. */
+S2_API s2_status s2_attention_layer_forward_host(s2_attention_layer *layer, void *stream,
+                                          const void *vid_qkv, const void *txt_qkv,
+                                          s2_dtype io_dtype, int L, int Lt, const int32_t *vid_shape,
+                                          void *vid_out, float *txt_out);
+
+/* Number of s2 kernels the last forward launched (for launch accounting). */
+S2_API int s2_attention_layer_last_launches(const s2_attention_layer *layer);
+
+/* Synchronises the layer's last stream and reports the device-side error word
+ * (0 = ok; nonzero = a bounded wait inside the attention kernel timed out).
+ * Returns S2_INFERENCE_FAILED when the word is set or the stream failed. */
+S2_API s2_status s2_attention_layer_device_error(s2_attention_layer *layer, int *code);
+
+/* ---- misc ---------------------------------------------------------------- */
+
+S2_API const char *s2_last_error(void);
+/* 0 if device `device` is an sm_100 part this build can run on. */
+S2_API s2_status s2_device_check(int device);
+S2_API int s2_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* S2_B200_H */

@@ -1,0 +1,370 @@
+// s2_attention_layer: the attention stage of SeedVR2DiTBlock as a CUDA
+// object (load_param / load_model / set_runtime_shape / forward,
+// seedvr2_dit_block.cpp:643-688, 870-1091; seedvr2_dit_block.h:38-58).
+//
+// Per runtime shape it caches a plan -- windows, varlen offsets, packed row
+// table, CTA work list, RoPE cos/sin table -- in device memory, so a forward
+// is three stream-ordered launches (prologue, attention, text mean) with no
+// host synchronisation. Workspaces (packed Q/K/V, per-window text slabs) grow
+// on demand and are reused across calls.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "s2_internal.h"
+
+namespace s2 {
+s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst);
+}
+
+namespace {
+
+struct DeviceBuffer {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    bool ensure(size_t want)
+    {
+        if (want <= bytes) return true;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        if (cudaMalloc(&ptr, want) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        bytes = want;
+        return true;
+    }
+    void release()
+    {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev)
+    {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard()
+    {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+struct s2_attention_layer {
+    int device = 0;
+    int heads = 20;
+    float eps = 1e-5f;
+    int shifted = 0;
+    int wt = 0, wh = 0, ww = 0;
+    s2_mode mode = S2_MODE_BF16_REF;
+    bool loaded = false;
+    int T = 0, H = 0, W = 0;
+    bool shape_valid = false;
+    std::vector<int32_t> subset;
+
+    // plan
+    bool plan_valid = false;
+    int plan_T = 0, plan_H = 0, plan_W = 0, plan_Lt = -1;
+    int n_total_windows = 0, n_local = 0, n_rows = 0, n_work = 0, max_pos = 0;
+    std::vector<int32_t> h_cu;
+    DeviceBuffer d_cu, d_rows, d_work, d_rope;
+
+    DeviceBuffer d_weights;  // gammas [4][128] + freqs [21]
+    DeviceBuffer d_q, d_k, d_v, d_txt_partial, d_err;
+    DeviceBuffer d_in_vid, d_in_txt, d_out_vid, d_out_vid32, d_out_txt;  // host-forward staging
+    cudaStream_t last_stream = nullptr;
+    int last_launches = 0;
+
+    ~s2_attention_layer()
+    {
+        DeviceGuard g(device);
+        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_q, &d_k, &d_v, &d_txt_partial,
+                                &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt})
+            b->release();
+    }
+
+    const float *gammas() const { return static_cast<const float *>(d_weights.ptr); }
+    const float *freqs() const { return static_cast<const float *>(d_weights.ptr) + 4 * S2_HEAD_DIM; }
+
+    s2_status build_plan(int Lt, cudaStream_t st)
+    {
+        if (plan_valid && plan_T == T && plan_H == H && plan_W == W && plan_Lt == Lt) return S2_OK;
+        plan_valid = false;
+        int count = 0;
+        s2_status rc = s2_make_windows(T, H, W, shifted, wt, wh, ww, nullptr, 0, &count);
+        if (rc != S2_OK) return rc;
+        std::vector<s2_window> all(count);
+        s2_make_windows(T, H, W, shifted, wt, wh, ww, all.data(), count, &count);
+        std::vector<s2_window> local;
+        if (subset.empty()) {
+            local = all;
+        } else {
+            for (int32_t id : subset) {
+                if (id < 0 || id >= count)
+                    return s2::set_error(S2_INVALID_ARGUMENT, "window subset id %d out of range [0,%d)", id, count);
+                local.push_back(all[id]);
+            }
+        }
+        n_total_windows = count;
+        n_local = static_cast<int>(local.size());
+        int rows = 0;
+        rc = s2_build_varlen(T, H, W, local.data(), n_local, Lt, nullptr, nullptr, &rows);
+        if (rc != S2_OK) return rc;
+        h_cu.assign(n_local + 1, 0);
+        std::vector<s2_row> h_rows(rows);
+        rc = s2_build_varlen(T, H, W, local.data(), n_local, Lt, h_cu.data(), h_rows.data(), &rows);
+        if (rc != S2_OK) return rc;
+        int nw = 0;
+        rc = s2_plan_work(h_cu.data(), n_local, nullptr, 0, &nw);
+        if (rc != S2_OK) return rc;
+        std::vector<int32_t> h_work(nw);
+        s2_plan_work(h_cu.data(), n_local, h_work.data(), nw, &nw);
+        int mp = 1;
+        for (const s2_row &r : h_rows) mp = std::max(mp, std::max(r.pt, std::max(r.ph, r.pw)) + 1);
+        n_rows = rows;
+        n_work = nw;
+        max_pos = mp;
+        if (!d_cu.ensure(h_cu.size() * sizeof(int32_t)) || !d_rows.ensure(h_rows.size() * sizeof(s2_row)) ||
+            !d_work.ensure(h_work.size() * sizeof(int32_t)) || !d_rope.ensure(s2_rope_table_bytes(max_pos)))
+            return s2::set_error(S2_OUT_OF_MEMORY, "attention plan: device allocation failed");
+        // Stream-ordered uploads from host vectors need the host side to stay
+        // alive until the copy completes: copy synchronously (plans change
+        // rarely -- once per runtime shape).
+        if (cudaMemcpy(d_cu.ptr, h_cu.data(), h_cu.size() * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(d_rows.ptr, h_rows.data(), h_rows.size() * sizeof(s2_row), cudaMemcpyHostToDevice) !=
+                cudaSuccess ||
+            cudaMemcpy(d_work.ptr, h_work.data(), h_work.size() * sizeof(int32_t), cudaMemcpyHostToDevice) !=
+                cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "attention plan: upload failed");
+        rc = s2_rope_table(st, freqs(), max_pos, d_rope.ptr);
+        if (rc != S2_OK) return rc;
+        plan_T = T;
+        plan_H = H;
+        plan_W = W;
+        plan_Lt = Lt;
+        plan_valid = true;
+        return S2_OK;
+    }
+};
+
+extern "C" s2_status s2_device_check(int device)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return s2::set_error(S2_UNSUPPORTED, "no CUDA device available");
+    }
+    if (device < 0 || device >= n) return s2::set_error(S2_INVALID_ARGUMENT, "device %d out of range", device);
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0)
+        return s2::set_error(S2_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a (B200)", device, major,
+                             minor);
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_create(int device, int heads, int head_dim, float eps, int shifted, int wt,
+                                               int wh, int ww, s2_mode mode, s2_attention_layer **out)
+{
+    if (!out) return s2::set_error(S2_INVALID_ARGUMENT, "s2_attention_layer_create: out is NULL");
+    *out = nullptr;
+    if (head_dim != S2_HEAD_DIM)
+        return s2::set_error(S2_INVALID_ARGUMENT, "head_dim must be %d (got %d)", S2_HEAD_DIM, head_dim);
+    if (heads <= 0 || heads > 64) return s2::set_error(S2_INVALID_ARGUMENT, "heads must be in [1, 64]");
+    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16) return s2::set_error(S2_UNSUPPORTED, "unknown mode");
+    if ((wt > 0 || wh > 0 || ww > 0) && !(wt > 0 && wh > 0 && ww > 0))
+        return s2::set_error(S2_INVALID_ARGUMENT, "window override needs wt, wh, ww > 0");
+    const s2_status dc = s2_device_check(device);
+    if (dc != S2_OK) return dc;
+    auto *l = new s2_attention_layer;
+    l->device = device;
+    l->heads = heads;
+    l->eps = eps;
+    l->shifted = shifted ? 1 : 0;
+    l->wt = wt > 0 ? wt : 0;
+    l->wh = wh > 0 ? wh : 0;
+    l->ww = ww > 0 ? ww : 0;
+    l->mode = mode;
+    *out = l;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_destroy(s2_attention_layer *layer)
+{
+    delete layer;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_load(s2_attention_layer *l, const float *nq_vid, const float *nk_vid,
+                                             const float *nq_txt, const float *nk_txt, const float *freqs21)
+{
+    if (!l || !nq_vid || !nk_vid || !nq_txt || !nk_txt || !freqs21)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_attention_layer_load: NULL argument");
+    DeviceGuard g(l->device);
+    std::vector<float> host(4 * S2_HEAD_DIM + S2_ROPE_PAIRS);
+    std::memcpy(host.data() + 0 * S2_HEAD_DIM, nq_vid, S2_HEAD_DIM * sizeof(float));
+    std::memcpy(host.data() + 1 * S2_HEAD_DIM, nk_vid, S2_HEAD_DIM * sizeof(float));
+    std::memcpy(host.data() + 2 * S2_HEAD_DIM, nq_txt, S2_HEAD_DIM * sizeof(float));
+    std::memcpy(host.data() + 3 * S2_HEAD_DIM, nk_txt, S2_HEAD_DIM * sizeof(float));
+    std::memcpy(host.data() + 4 * S2_HEAD_DIM, freqs21, S2_ROPE_PAIRS * sizeof(float));
+    if (!l->d_weights.ensure(host.size() * sizeof(float)))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_attention_layer_load: allocation failed");
+    if (cudaMemcpy(l->d_weights.ptr, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_attention_layer_load: upload failed");
+    l->loaded = true;
+    l->plan_valid = false;  // the RoPE table depends on freqs
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_set_runtime_shape(s2_attention_layer *l, int frames, int height, int width)
+{
+    if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    l->T = frames;
+    l->H = height;
+    l->W = width;
+    l->shape_valid = frames > 0 && height > 0 && width > 0;
+    return l->shape_valid ? S2_OK : s2::set_error(S2_INVALID_ARGUMENT, "invalid runtime shape");
+}
+
+extern "C" s2_status s2_attention_layer_set_window_subset(s2_attention_layer *l, const int32_t *ids, int n)
+{
+    if (!l || n < 0 || (n > 0 && !ids)) return s2::set_error(S2_INVALID_ARGUMENT, "invalid window subset");
+    l->subset.assign(ids, ids + n);
+    l->plan_valid = false;
+    return S2_OK;
+}
+
+extern "C" int s2_attention_layer_last_launches(const s2_attention_layer *l) { return l ? l->last_launches : 0; }
+
+extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *stream, const void *vid_qkv,
+                                                s2_dtype in_dtype, int L, const void *txt_qkv, int Lt,
+                                                void *vid_out, float *txt_out)
+{
+    if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    l->last_launches = 0;
+    if (!l->loaded) return s2::set_error(S2_NOT_LOADED, "attention layer: weights not loaded");
+    if (!l->shape_valid) return s2::set_error(S2_NOT_LOADED, "attention layer: runtime shape not set");
+    if (L != l->T * l->H * l->W)
+        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: vid rows %d != T*H*W = %d", L, l->T * l->H * l->W);
+    if (Lt < 0 || (Lt > 0 && !txt_qkv) || !vid_qkv || !vid_out || (Lt > 0 && !txt_out))
+        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: NULL buffer");
+    DeviceGuard g(l->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    l->last_stream = st;
+    s2_status rc = l->build_plan(Lt, st);
+    if (rc != S2_OK) return rc;
+    const int dim = l->heads * S2_HEAD_DIM;
+    const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;
+    const size_t txt_bytes = static_cast<size_t>(std::max(l->n_local, 1)) * std::max(Lt, 1) * dim * 2;
+    if (!l->d_q.ensure(qkv_bytes) || !l->d_k.ensure(qkv_bytes) || !l->d_v.ensure(qkv_bytes) ||
+        !l->d_txt_partial.ensure(txt_bytes))
+        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: workspace allocation failed");
+    if (!l->d_err.ptr && (!l->d_err.ensure(sizeof(int32_t)) || cudaMemset(l->d_err.ptr, 0, sizeof(int32_t)) != cudaSuccess))
+        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: error word allocation failed");
+    rc = s2_qk_norm_rope(stream, vid_qkv, txt_qkv, in_dtype, l->heads, l->eps, l->gammas(), l->d_rope.ptr,
+                         static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows, l->mode, l->d_q.ptr, l->d_k.ptr,
+                         l->d_v.ptr);
+    if (rc != S2_OK) return rc;
+    rc = s2_window_attention(stream, l->mode, l->d_q.ptr, l->d_k.ptr, l->d_v.ptr, l->heads, l->n_rows,
+                             static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
+                             static_cast<const s2_row *>(l->d_rows.ptr), static_cast<const int32_t *>(l->d_work.ptr),
+                             l->n_work, vid_out, l->d_txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
+    if (rc != S2_OK) return rc;
+    l->last_launches = 2;
+    if (Lt > 0) {
+        rc = s2_text_window_sum(stream, l->mode, l->d_txt_partial.ptr, l->n_local, Lt, dim,
+                                1.f / static_cast<float>(l->n_total_windows), 0, txt_out);
+        if (rc != S2_OK) return rc;
+        l->last_launches = 3;
+    }
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void *stream, const void *vid_qkv,
+                                                     const void *txt_qkv, s2_dtype io_dtype, int L, int Lt,
+                                                     const int32_t *vid_shape, void *vid_out, float *txt_out)
+{
+    if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    if (!vid_shape || !vid_qkv || !vid_out || (Lt > 0 && (!txt_qkv || !txt_out)) || L <= 0 || Lt < 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "forward_host: NULL buffer or bad size");
+    const s2_dtype mode_dtype = l->mode == S2_MODE_F16 ? S2_F16 : S2_BF16;
+    if (io_dtype != S2_F32 && io_dtype != mode_dtype)
+        return s2::set_error(S2_UNSUPPORTED, "forward_host: io dtype must be f32 or the mode's 16-bit type");
+    // The shape blob is authoritative on this path (the CPU forward reads vid_shape).
+    s2_status rc = s2_attention_layer_set_runtime_shape(l, vid_shape[0], vid_shape[1], vid_shape[2]);
+    if (rc != S2_OK) return rc;
+    if (L != l->T * l->H * l->W)
+        return s2::set_error(S2_INVALID_ARGUMENT, "forward_host: vid rows %d != T*H*W", L);
+    DeviceGuard g(l->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int dim = l->heads * S2_HEAD_DIM;
+    const size_t esz = io_dtype == S2_F32 ? 4 : 2;
+    const size_t in_vid = static_cast<size_t>(L) * 3 * dim * esz, in_txt = static_cast<size_t>(Lt) * 3 * dim * esz;
+    const size_t out_vid16 = static_cast<size_t>(L) * dim * 2;
+    if (!l->d_in_vid.ensure(in_vid) || !l->d_in_txt.ensure(std::max<size_t>(in_txt, 16)) ||
+        !l->d_out_vid.ensure(out_vid16) || !l->d_out_txt.ensure(std::max<size_t>(static_cast<size_t>(Lt) * dim * 4, 16)) ||
+        (io_dtype == S2_F32 && !l->d_out_vid32.ensure(static_cast<size_t>(L) * dim * 4)))
+        return s2::set_error(S2_OUT_OF_MEMORY, "forward_host: staging allocation failed");
+    if (cudaMemcpyAsync(l->d_in_vid.ptr, vid_qkv, in_vid, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        (Lt > 0 && cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, in_txt, cudaMemcpyHostToDevice, st) != cudaSuccess))
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: H2D copy failed");
+    // Rows of windows outside a subset are not written by the kernel: keep them zero.
+    if (!l->subset.empty() && cudaMemsetAsync(l->d_out_vid.ptr, 0, out_vid16, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: memset failed");
+    rc = s2_attention_layer_forward(l, stream, l->d_in_vid.ptr, io_dtype, L, l->d_in_txt.ptr, Lt, l->d_out_vid.ptr,
+                                    static_cast<float *>(l->d_out_txt.ptr));
+    if (rc != S2_OK) return rc;
+    const void *vsrc = l->d_out_vid.ptr;
+    size_t vbytes = out_vid16;
+    if (io_dtype == S2_F32) {
+        rc = s2::to_f32(st, l->mode, l->d_out_vid.ptr, static_cast<long long>(L) * dim,
+                        static_cast<float *>(l->d_out_vid32.ptr));
+        if (rc != S2_OK) return rc;
+        l->last_launches++;
+        vsrc = l->d_out_vid32.ptr;
+        vbytes = static_cast<size_t>(L) * dim * 4;
+    }
+    if (cudaMemcpyAsync(vid_out, vsrc, vbytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        (Lt > 0 && cudaMemcpyAsync(txt_out, l->d_out_txt.ptr, static_cast<size_t>(Lt) * dim * 4,
+                                   cudaMemcpyDeviceToHost, st) != cudaSuccess))
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: D2H copy failed");
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream failed: %s", cudaGetErrorString(e));
+    int code = 0;
+    return s2_attention_layer_device_error(l, &code);
+}
+
+extern "C" s2_status s2_attention_layer_device_error(s2_attention_layer *l, int *code)
+{
+    if (!l || !code) return s2::set_error(S2_INVALID_ARGUMENT, "NULL argument");
+    *code = 0;
+    if (!l->d_err.ptr) return S2_OK;
+    DeviceGuard g(l->device);
+    cudaError_t e = cudaStreamSynchronize(l->last_stream);
+    int32_t h = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, l->d_err.ptr, sizeof h, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "device error query failed: %s", cudaGetErrorString(e));
+    *code = h;
+    if (h != 0) {
+        cudaMemset(l->d_err.ptr, 0, sizeof(int32_t));
+        return s2::set_error(S2_INFERENCE_FAILED, "attention kernel reported device error %d (bounded wait timed out)",
+                             h);
+    }
+    return S2_OK;
+}

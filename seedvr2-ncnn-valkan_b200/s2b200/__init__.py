@@ -1,0 +1,315 @@
+"""Python host mirror of the SeedVR2 windowed MM-attention path (B200, sm_100a).
+
+Everything here is a thin ctypes layer over ``lib/libs2b200.so`` (C ABI:
+``include/s2_b200.h``). PyTorch supplies device memory and streams only; all
+compute runs in the library's CUDA kernels. There is no CPU fallback: if the
+library is missing or no sm_100 GPU is present, the device entry points raise.
+
+Mirrors the reference's layer surface (czwdysj/seedvr2-ncnn-valkan):
+  * ``make_windows``            <- SeedVR2DiTBlock::make_windows (src/layers/seedvr2_dit_block.cpp:827-868)
+  * ``SeedVR2DiTBlockAttention`` <- SeedVR2DiTBlock's attention stage: load_param (:643-655),
+    load_model norm/freqs part (:657-688), set_runtime_shape (.h:55), attention() (:870-1091)
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(HERE), "lib", "libs2b200.so")
+HEAD_DIM = 128
+
+S2_OK, S2_INVALID_ARGUMENT, S2_NOT_LOADED, S2_INFERENCE_FAILED, S2_UNSUPPORTED, S2_OUT_OF_MEMORY = 0, -1, -2, -5, -6, -7
+S2_F32, S2_F16, S2_BF16 = 0, 1, 2
+MODE_BF16_REF, MODE_F16 = 0, 1
+
+_STATUS_NAMES = {0: "Ok", -1: "InvalidArgument", -2: "NotLoaded", -5: "InferenceFailed", -6: "UnsupportedBackend",
+                 -7: "OutOfMemory"}
+
+
+class S2Error(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{_STATUS_NAMES.get(status, status)} ({status}): {message}")
+        self.status = status
+
+
+class Window(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
+
+
+class Row(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("src", "pt", "ph", "pw")]
+
+
+_vp = ctypes.c_void_p
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_lib = None
+
+# name -> (restype, argtypes); mirrors include/s2_b200.h
+_SIGS = {
+    "s2_make_windows": (ctypes.c_int, [ctypes.c_int] * 7 + [ctypes.POINTER(Window), ctypes.c_int, _i32p]),
+    "s2_build_varlen": (ctypes.c_int, [ctypes.c_int] * 3 + [ctypes.POINTER(Window), ctypes.c_int, ctypes.c_int,
+                                                           _i32p, ctypes.POINTER(Row), _i32p]),
+    "s2_plan_work": (ctypes.c_int, [_i32p, ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
+    "s2_rope_table_bytes": (ctypes.c_size_t, [ctypes.c_int]),
+    "s2_rope_table": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    "s2_qk_norm_rope": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, _vp,
+                                       ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
+    "s2_window_attention": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp,
+                                           ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp, _vp, _vp]),
+    "s2_text_window_sum": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_float, ctypes.c_int, _vp]),
+    "s2_attention_layer_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                                 ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.POINTER(_vp)]),
+    "s2_attention_layer_destroy": (ctypes.c_int, [_vp]),
+    "s2_attention_layer_load": (ctypes.c_int, [_vp] + [_f32p] * 5),
+    "s2_attention_layer_set_runtime_shape": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "s2_attention_layer_set_window_subset": (ctypes.c_int, [_vp, _i32p, ctypes.c_int]),
+    "s2_attention_layer_forward": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
+                                                  _vp, _vp]),
+    "s2_attention_layer_forward_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int,
+                                                       ctypes.c_int, _i32p, _vp, _vp]),
+    "s2_attention_layer_last_launches": (ctypes.c_int, [_vp]),
+    "s2_attention_layer_device_error": (ctypes.c_int, [_vp, _i32p]),
+    "s2_last_error": (ctypes.c_char_p, []),
+    "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
+    "s2_version": (ctypes.c_int, []),
+}
+
+
+def lib():
+    """Load libs2b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} not built (run __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def last_error() -> str:
+    return lib().s2_last_error().decode()
+
+
+def _check(status: int, what: str = ""):
+    if status != S2_OK:
+        raise S2Error(status, f"{what}: {last_error()}")
+
+
+# ---- host planning (runs without a GPU) --------------------------------------
+
+def make_windows(frames, height, width, shifted, override=(0, 0, 0)) -> np.ndarray:
+    """Window boxes [n, 6] = (t0, t1, h0, h1, w0, w1), in the reference's order."""
+    n = ctypes.c_int32(0)
+    _check(lib().s2_make_windows(frames, height, width, int(shifted), *override, None, 0, ctypes.byref(n)),
+           "s2_make_windows")
+    buf = (Window * max(n.value, 1))()
+    _check(lib().s2_make_windows(frames, height, width, int(shifted), *override, buf, n.value, ctypes.byref(n)),
+           "s2_make_windows")
+    return np.array([[w.t0, w.t1, w.h0, w.h1, w.w0, w.w1] for w in buf[:n.value]], dtype=np.int32).reshape(-1, 6)
+
+
+def build_varlen(frames, height, width, windows: np.ndarray, text_len: int):
+    """(cu_seqlens [n+1] int32, rows [N, 4] int32 = src, pt, ph, pw)."""
+    n = len(windows)
+    wb = (Window * n)(*[Window(*map(int, w)) for w in windows])
+    total = ctypes.c_int32(0)
+    _check(lib().s2_build_varlen(frames, height, width, wb, n, text_len, None, None, ctypes.byref(total)),
+           "s2_build_varlen")
+    cu = np.zeros(n + 1, np.int32)
+    rows = np.zeros((max(total.value, 1), 4), np.int32)
+    _check(lib().s2_build_varlen(frames, height, width, wb, n, text_len, cu.ctypes.data_as(_i32p),
+                                 ctypes.cast(rows.ctypes.data, ctypes.POINTER(Row)), ctypes.byref(total)),
+           "s2_build_varlen")
+    return cu, rows[:total.value]
+
+
+def plan_work(cu_seqlens: np.ndarray) -> np.ndarray:
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    n = ctypes.c_int32(0)
+    _check(lib().s2_plan_work(cu.ctypes.data_as(_i32p), len(cu) - 1, None, 0, ctypes.byref(n)), "s2_plan_work")
+    work = np.zeros(max(n.value, 1), np.int32)
+    _check(lib().s2_plan_work(cu.ctypes.data_as(_i32p), len(cu) - 1, work.ctypes.data_as(_i32p), n.value,
+                              ctypes.byref(n)), "s2_plan_work")
+    return work[:n.value]
+
+
+# ---- device helpers (torch tensors as plumbing) ------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dtype_code(t) -> int:
+    torch = _torch()
+    return {torch.float32: S2_F32, torch.float16: S2_F16, torch.bfloat16: S2_BF16}[t.dtype]
+
+
+def _stream_ptr(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def mode_dtype(mode: int):
+    torch = _torch()
+    return torch.float16 if mode == MODE_F16 else torch.bfloat16
+
+
+class SeedVR2DiTBlockAttention:
+    """The attention stage of SeedVR2DiTBlock on a B200 (drop-in for attention()).
+
+    ``load_param`` takes the reference's ParamDict keys; ``load_model`` the
+    QK-norm gammas of the video and text branches and the RoPE freqs;
+    ``forward`` takes device tensors vid_qkv [L, 3*dim] and txt_qkv [Lt, 3*dim]
+    and returns (vid_out [L, dim] in the mode dtype, txt_out [Lt, dim] fp32).
+    Errors raise S2Error carrying the reference-style status code.
+    """
+
+    def __init__(self, device: int = 0, mode: int = MODE_BF16_REF, window_override=(0, 0, 0)):
+        self.device = device
+        self.mode = mode
+        self.window_override = tuple(int(x) for x in window_override)
+        self.handle = None
+        self.heads = 20
+        self.shifted = False
+        self.shape = None
+
+    # ParamDict keys 0..8 (seedvr2_dit_block.cpp:643-655)
+    def load_param(self, block_index=0, shared=False, last=False, shifted=False, dim=2560, heads=20, head_dim=128,
+                   mlp_hidden=6912, eps=1e-5):
+        if dim != heads * head_dim:
+            return S2_INVALID_ARGUMENT
+        self.heads, self.shifted, self.eps = heads, bool(shifted), float(eps)
+        h = ctypes.c_void_p()
+        _check(lib().s2_attention_layer_create(self.device, heads, head_dim, ctypes.c_float(eps), int(shifted),
+                                               *self.window_override, self.mode, ctypes.byref(h)),
+               "s2_attention_layer_create")
+        self.close()
+        self.handle = h
+        return S2_OK
+
+    def load_model(self, norm_q_vid, norm_k_vid, freqs21, norm_q_txt=None, norm_k_txt=None):
+        """Shared blocks (>= 10) pass no text gammas: the video branch is reused."""
+        g = [np.ascontiguousarray(x, np.float32) for x in
+             (norm_q_vid, norm_k_vid, norm_q_vid if norm_q_txt is None else norm_q_txt,
+              norm_k_vid if norm_k_txt is None else norm_k_txt, freqs21)]
+        _check(lib().s2_attention_layer_load(self.handle, *[x.ctypes.data_as(_f32p) for x in g]),
+               "s2_attention_layer_load")
+        self._keep = g
+        return S2_OK
+
+    def set_runtime_shape(self, frames, height, width):
+        _check(lib().s2_attention_layer_set_runtime_shape(self.handle, frames, height, width), "set_runtime_shape")
+        self.shape = (frames, height, width)
+
+    def set_window_subset(self, ids=None):
+        ids = np.ascontiguousarray([] if ids is None else ids, np.int32)
+        _check(lib().s2_attention_layer_set_window_subset(self.handle, ids.ctypes.data_as(_i32p) if ids.size else None,
+                                                          int(ids.size)), "set_window_subset")
+
+    def forward(self, vid_qkv, txt_qkv, vid_out=None, txt_out=None, stream=None):
+        torch = _torch()
+        dim = self.heads * HEAD_DIM
+        L, Lt = vid_qkv.shape[0], txt_qkv.shape[0]
+        if vid_out is None:
+            vid_out = torch.zeros((L, dim), dtype=mode_dtype(self.mode), device=vid_qkv.device)
+        if txt_out is None:
+            txt_out = torch.empty((Lt, dim), dtype=torch.float32, device=vid_qkv.device)
+        _check(lib().s2_attention_layer_forward(self.handle, _stream_ptr(stream), _ptr(vid_qkv), _dtype_code(vid_qkv),
+                                                L, _ptr(txt_qkv), Lt, _ptr(vid_out), _ptr(txt_out)),
+               "s2_attention_layer_forward")
+        return vid_out, txt_out
+
+    def forward_host(self, vid_qkv: np.ndarray, txt_qkv: np.ndarray, vid_shape, io_dtype=S2_F32,
+                     vid_out: np.ndarray | None = None, txt_out: np.ndarray | None = None, stream=None):
+        """ncnn::Mat-style host buffers in, host buffers out (copies inside)."""
+        dim = self.heads * HEAD_DIM
+        L, Lt = vid_qkv.shape[0], txt_qkv.shape[0]
+        np_out = {S2_F32: np.float32, S2_F16: np.float16, S2_BF16: np.uint16}[io_dtype]
+        if vid_out is None:
+            vid_out = np.zeros((L, dim), np_out)
+        if txt_out is None:
+            txt_out = np.zeros((Lt, dim), np.float32)
+        shape = np.ascontiguousarray(vid_shape, np.int32)
+        _check(lib().s2_attention_layer_forward_host(
+            self.handle, _stream_ptr(stream) if stream is not None else None, ctypes.c_void_p(vid_qkv.ctypes.data),
+            ctypes.c_void_p(txt_qkv.ctypes.data), io_dtype, L, Lt, shape.ctypes.data_as(_i32p),
+            ctypes.c_void_p(vid_out.ctypes.data), ctypes.c_void_p(txt_out.ctypes.data)), "forward_host")
+        return vid_out, txt_out
+
+    def last_launches(self) -> int:
+        return lib().s2_attention_layer_last_launches(self.handle)
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_attention_layer_device_error(self.handle, ctypes.byref(code))
+        return code.value
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            lib().s2_attention_layer_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---- explicit-buffer kernel entry points -------------------------------------
+
+def rope_table(freqs21, max_pos, stream=None):
+    torch = _torch()
+    tab = torch.empty(lib().s2_rope_table_bytes(max_pos) // 4, dtype=torch.float32, device=freqs21.device)
+    _check(lib().s2_rope_table(_stream_ptr(stream), _ptr(freqs21), max_pos, _ptr(tab)), "s2_rope_table")
+    return tab
+
+
+def qk_norm_rope(vid_qkv, txt_qkv, heads, gammas, table, rows, mode=MODE_BF16_REF, eps=1e-5, stream=None):
+    """Returns packed (q, k, v), each [heads, n_rows, 128] in the mode dtype."""
+    torch = _torch()
+    n_rows = rows.shape[0]
+    out = [torch.empty((heads, n_rows, HEAD_DIM), dtype=mode_dtype(mode), device=vid_qkv.device) for _ in range(3)]
+    _check(lib().s2_qk_norm_rope(_stream_ptr(stream), _ptr(vid_qkv), _ptr(txt_qkv), _dtype_code(vid_qkv), heads,
+                                 ctypes.c_float(eps), _ptr(gammas), _ptr(table), _ptr(rows), n_rows, mode,
+                                 *[_ptr(t) for t in out]), "s2_qk_norm_rope")
+    return out
+
+
+def window_attention(q, k, v, cu_seqlens, text_len, rows, work, vid_out, txt_partial, err, mode=MODE_BF16_REF,
+                     stream=None):
+    heads, n_rows = q.shape[0], q.shape[1]
+    _check(lib().s2_window_attention(_stream_ptr(stream), mode, _ptr(q), _ptr(k), _ptr(v), heads, n_rows,
+                                     _ptr(cu_seqlens), cu_seqlens.shape[0] - 1, text_len, _ptr(rows), _ptr(work),
+                                     work.shape[0], _ptr(vid_out), _ptr(txt_partial), _ptr(err)),
+           "s2_window_attention")
+
+
+def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accumulate=False, mode=MODE_BF16_REF,
+                    stream=None):
+    _check(lib().s2_text_window_sum(_stream_ptr(stream), mode, _ptr(txt_partial), n_windows, text_len, dim,
+                                    ctypes.c_float(scale), int(accumulate), _ptr(txt_out)), "s2_text_window_sum")
+
+
+def device_check(device: int = 0) -> int:
+    return lib().s2_device_check(device)

@@ -1,0 +1,56 @@
+"""Seeded synthetic inputs for the windowed MM-attention path.
+
+No public dataset exists for this path; these stand in for real activations
+with the shapes and distributions the reference's benchmarks use: QKV rows
+drawn N(0, 1) and stored as fp16-representable values, 58 text tokens (the
+shipped default positive embedding length), QK-norm gammas ``1 + 0.1 N(0,1)``
+and the model's RoPE frequencies ``1 / 10000^(2p/42)``, p < 21
+(tools/diagnose_seedvr2_rope.py:36-37 of the reference).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+HEAD_DIM = 128
+TEXT_LEN = 58
+
+# Grids (T, H, W) of BASELINE.json's configs after VAE compression + patchify.
+GRIDS = {
+    "cfg0": (2, 16, 30),      # 480x256x5f
+    "cfg2": (6, 45, 80),      # 720p x 21f
+    "cfg3": (12, 67, 120),    # 1080p x 45f
+}
+# BASELINE.json's explicit window geometries (the reference computes its own).
+OVERRIDES = {"cfg0": (2, 8, 10), "cfg2": (6, 15, 20), "cfg3": (4, 17, 20)}
+
+
+def rope_freqs() -> np.ndarray:
+    return (1.0 / 10000.0 ** (np.arange(21, dtype=np.float64) * 2.0 / 42.0)).astype(np.float32)
+
+
+def layer_inputs(grid, heads=20, text_len=TEXT_LEN, seed=666):
+    """(vid_qkv [L, 3*dim] f32, txt_qkv [Lt, 3*dim] f32, gammas [4][128] f32, freqs [21] f32).
+
+    QKV values are exactly representable in fp16, so the fp32 and fp16 copies
+    of the same draw feed identical numbers to the oracle and the GPU."""
+    T, H, W = grid
+    L = T * H * W
+    dim = heads * HEAD_DIM
+    rng = np.random.default_rng(seed)
+    vid = rng.standard_normal((L, 3 * dim), dtype=np.float32).astype(np.float16).astype(np.float32)
+    txt = rng.standard_normal((text_len, 3 * dim), dtype=np.float32).astype(np.float16).astype(np.float32)
+    gam = (1.0 + 0.1 * rng.standard_normal((4, HEAD_DIM))).astype(np.float32)
+    return vid, txt, gam, rope_freqs()
+
+
+def attention_flops(windows: np.ndarray, text_len: int, heads: int) -> float:
+    """Algorithmic FLOPs of one attention layer: sum_w 4 * S_w^2 * 128 * heads."""
+    s = (windows[:, 1] - windows[:, 0]) * (windows[:, 3] - windows[:, 2]) * (windows[:, 5] - windows[:, 4]) + text_len
+    return float(np.sum(4.0 * s.astype(np.float64) ** 2 * HEAD_DIM * heads))
+
+
+def prologue_bytes(L: int, text_len: int, n_rows: int, heads: int, in_bytes: int) -> float:
+    """Algorithmic HBM bytes of the prologue: read each QKV row once (video and
+    text), write the packed q/k/v rows in 16-bit."""
+    dim = heads * HEAD_DIM
+    return float((L + text_len) * 3 * dim * in_bytes + n_rows * 3 * dim * 2)

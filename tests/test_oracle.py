@@ -1,0 +1,94 @@
+"""The C restatement oracle, pinned against the reference's own outputs.
+
+Golden fixtures come from the reference's CPU layer code built unmodified
+(tests/golden/make_golden.py). Same floating-point flags on both sides, so
+the restatement must match bit for bit.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import refcases
+from conftest import from_bf16_bits
+from s2b200 import synth
+
+
+def test_windows_match_reference(port, golden):
+    g = golden("windows.npz")
+    assert len(g.files) >= 30
+    for key in g.files:
+        dims, s = key.split("_s")
+        T, H, W = map(int, dims.split("x"))
+        assert np.array_equal(port.make_windows(T, H, W, int(s)), g[key]), key
+
+
+@pytest.mark.parametrize("shifted", [0, 1])
+def test_attention_cfg0_one_head_bit_exact(port, golden, shifted):
+    g = golden("attn_cfg0_h1.npz")
+    grid = tuple(int(x) for x in g["grid"])
+    vo, to, pk = port.window_attention(g["vid_qkv"].astype(np.float32), g["txt_qkv"].astype(np.float32), grid, 1,
+                                       list(g["gammas"]), g["freqs"], shifted, packed=True)
+    assert np.array_equal(vo, from_bf16_bits(g[f"vid_out_s{shifted}"]))
+    assert np.array_equal(to, g[f"txt_out_s{shifted}"])
+    assert np.array_equal(pk["o"], from_bf16_bits(g[f"packed_o_s{shifted}"]))
+    if shifted == 0:
+        for k in "qkv":
+            assert np.array_equal(pk[k], from_bf16_bits(g[f"packed_{k}_s0"])), k
+
+
+@pytest.mark.parametrize("i", range(len(refcases.BLOCK_CASES)))
+def test_attention_runner_cases_bit_exact(port, golden, i):
+    g = golden("attn_runner_cases.npz")
+    vq, tq, g4, fr, shape, heads, shifted = refcases.attention_case(refcases.BLOCK_CASES[i])
+    vo, to, pk = port.window_attention(vq, tq, shape, heads, list(g4), fr, shifted, packed=True)
+    assert np.array_equal(vo, g[f"c{i}_vid_out"])
+    assert np.array_equal(to, g[f"c{i}_txt_out"])
+    assert np.array_equal(pk["o"], g[f"c{i}_packed_o"])
+
+
+@pytest.mark.parametrize("i", range(len(refcases.VAE_CASES)))
+def test_vae_runner_cases_bit_exact(port, golden, i):
+    g = golden("vae_runner_cases.npz")
+    x, w, _ = refcases.vae_case(refcases.VAE_CASES[i])
+    y = port.vae_attention(x, w)
+    assert np.array_equal(y, g[f"c{i}_y"])
+
+
+def test_unrounded_variant_is_close_and_round_consistent(port):
+    """round_out=0 is the reference Vulkan shader's output (no bf16 rounding)."""
+    vid, txt, gam, freqs = synth.layer_inputs((1, 6, 7), heads=2, text_len=5, seed=3)
+    a, ta, _ = port.window_attention(vid, txt, (1, 6, 7), 2, list(gam), freqs, 0, round_out=True)
+    b, tb, _ = port.window_attention(vid, txt, (1, 6, 7), 2, list(gam), freqs, 0, round_out=False)
+    rounded = np.vectorize(port.lib.s2o_round_bf16, otypes=[np.float32])(b)
+    assert np.array_equal(a, rounded)
+    assert np.allclose(ta, tb, atol=1e-2)
+
+
+def test_heads_and_window_subsets_partition_the_output(port):
+    grid = (2, 9, 11)
+    vid, txt, gam, freqs = synth.layer_inputs(grid, heads=3, text_len=7, seed=5)
+    full, tfull, _ = port.window_attention(vid, txt, grid, 3, list(gam), freqs, 1)
+    n = len(port.make_windows(*grid, 1))
+    acc = np.zeros_like(full)
+    tacc = np.zeros_like(tfull)
+    for hb in range(3):
+        for part in (np.arange(n) % 2 == 0, np.arange(n) % 2 == 1):
+            v, t, _ = port.window_attention(vid, txt, grid, 3, list(gam), freqs, 1, heads_range=(hb, hb + 1),
+                                            window_mask=part)
+            acc += v
+            tacc += t
+    assert np.array_equal(acc, full)
+    assert np.allclose(tacc, tfull, rtol=1e-6, atol=1e-7)
+
+
+def test_restatement_matches_reference_live(port, ref):
+    """Beyond the fixtures: a fresh seeded case, 2 heads, both layer kinds."""
+    grid = (3, 10, 14)
+    vid, txt, gam, freqs = synth.layer_inputs(grid, heads=2, seed=11)
+    for s in (0, 1):
+        a = port.window_attention(vid, txt, grid, 2, list(gam), freqs, s, packed=True)
+        b = ref.attention(vid, txt, grid, 2, list(gam), freqs, s, packed=True)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        for k in "qkvo":
+            assert np.array_equal(a[2][k], b[2][k])
