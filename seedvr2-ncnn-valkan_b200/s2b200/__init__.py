@@ -286,10 +286,10 @@ def rope_table(freqs21, max_pos, stream=None):
 
 
 def qk_norm_rope(vid_qkv, txt_qkv, heads, gammas, table, rows, mode=MODE_BF16_REF, eps=1e-5, stream=None):
-    """Returns packed (q, k, v), each [heads, n_rows, 128] in the mode dtype."""
+    """Returns packed (q, k, v), each fp16 [heads, n_rows, 128] holding the bf16-rounded values."""
     torch = _torch()
     n_rows = rows.shape[0]
-    out = [torch.empty((heads, n_rows, HEAD_DIM), dtype=mode_dtype(mode), device=vid_qkv.device) for _ in range(3)]
+    out = [torch.empty((heads, n_rows, HEAD_DIM), dtype=torch.float16, device=vid_qkv.device) for _ in range(3)]
     _check(lib().s2_qk_norm_rope(_stream_ptr(stream), _ptr(vid_qkv), _ptr(txt_qkv), _dtype_code(vid_qkv), heads,
                                  ctypes.c_float(eps), _ptr(gammas), _ptr(table), _ptr(rows), n_rows, mode,
                                  *[_ptr(t) for t in out]), "s2_qk_norm_rope")
