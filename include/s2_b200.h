@@ -205,6 +205,42 @@ S2_API int s2_attention_layer_last_launches(const s2_attention_layer *layer);
  * Returns S2_INFERENCE_FAILED when the word is set or the stream failed. */
 S2_API s2_status s2_attention_layer_device_error(s2_attention_layer *layer, int *code);
 
+/* ---- allocation-free variant -------------------------------------------- */
+
+/* Limits of the fixed scratch used by s2_dit_window_attention_noalloc
+ * (about 29 MiB of device memory in total). */
+#define S2_NOALLOC_MAX_ROW_HEADS 32768       /* packed rows (sum of L_w + Lt) x heads */
+#define S2_NOALLOC_MAX_TEXT_ELEMS 2097152    /* windows x text_len x heads*128 */
+#define S2_NOALLOC_MAX_WINDOWS 512
+#define S2_NOALLOC_MAX_ROPE_POS 1024         /* largest RoPE position + 1 */
+
+/* No counterpart in the reference. The whole attention stage (what
+ * s2_attention_layer_forward does) for callers that must not allocate device
+ * memory while they run -- e.g. code executing inside another framework's
+ * memory pool or allocator callbacks, or a host that has reserved all HBM up
+ * front -- so it never calls cudaMalloc, cudaFree or an allocating library
+ * routine. Instead of workspaces it uses one fixed device array that belongs
+ * to this library (the S2_NOALLOC_* limits above): every GPU that loads the
+ * library's module holds that array until the process exits. Inputs and
+ * outputs are the caller's: vid_qkv [L][3*heads*128] and txt_qkv
+ * [text_len][3*heads*128] in in_dtype, gammas device fp32 [4][128] (norm_q_vid,
+ * norm_k_vid, norm_q_txt, norm_k_txt), freqs21 device fp32 [21], vid_out
+ * [L][heads*128] (bf16 or fp16 by mode), txt_out fp32 [text_len][heads*128];
+ * err (device int32, may be NULL) receives the kernel's error word (cleared
+ * at the start of every call).
+ * Sizes beyond the limits return S2_INVALID_ARGUMENT with a message naming
+ * the limit. The first call on each device resolves the array's device
+ * address (cudaGetSymbolAddress with that device current), so make the first
+ * call on a device before any stream capture. All calls share the array and
+ * it keeps the last call's contents: calls whose GPU work overlaps (other
+ * streams or threads without ordering) race on it. */
+S2_API s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
+                                                 const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype,
+                                                 int frames, int height, int width, int text_len,
+                                                 int heads, float eps, int shifted, int wt, int wh, int ww,
+                                                 const float *gammas, const float *freqs21,
+                                                 void *vid_out, float *txt_out, int32_t *err);
+
 /* ---- misc ---------------------------------------------------------------- */
 
 S2_API const char *s2_last_error(void);

@@ -75,6 +75,8 @@ _SIGS = {
                                                        ctypes.c_int, _i32p, _vp, _vp]),
     "s2_attention_layer_last_launches": (ctypes.c_int, [_vp]),
     "s2_attention_layer_device_error": (ctypes.c_int, [_vp, _i32p]),
+    "s2_dit_window_attention_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int] + [ctypes.c_int] * 5
+                                        + [ctypes.c_float] + [ctypes.c_int] * 4 + [_vp] * 5),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
