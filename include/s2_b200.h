@@ -131,8 +131,9 @@ S2_API s2_status s2_qk_norm_rope(void *stream,
  * (seedvr2_dit_block.cpp:1045-1079; Vulkan block_attention :339-438 plus
  * zero_buffer/window_sum scatter :442-457, :541-572).
  *   cu_seqlens: device int32 [n_windows+1]; rows: device s2_row.
- *   work: device int32 [n_work] of (window << 16 | q_tile) items, costliest
- *   first (s2_plan_work); n_work * heads CTAs are launched.
+ *   work: device int32 [n_work] of (window << 16 | q_block) items, one per
+ *   256 query rows, costliest first (s2_plan_work); n_work * heads CTAs are
+ *   launched.
  *   err: device int32 error word (0 = ok), set on a device-side timeout. */
 S2_API s2_status s2_window_attention(void *stream, s2_mode mode,
                               const void *q, const void *k, const void *v, int heads, int n_rows,
@@ -140,7 +141,7 @@ S2_API s2_status s2_window_attention(void *stream, s2_mode mode,
                               const s2_row *rows, const int32_t *work, int n_work,
                               void *vid_out, void *txt_partial, int32_t *err);
 
-/* Host helper: the (window, q_tile) work list for s2_window_attention,
+/* Host helper: the (window, q_block) work list for s2_window_attention,
  * sorted by descending cost. Returns the item count in *n_work; `work` may be
  * NULL to query. cu_seqlens is the host copy. */
 S2_API s2_status s2_plan_work(const int32_t *cu_seqlens, int n_windows, int32_t *work, int cap, int *n_work);

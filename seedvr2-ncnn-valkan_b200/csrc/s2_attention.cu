@@ -4,28 +4,32 @@
 // P in fp16 keeps 11 mantissa bits), accumulation is fp32 in TMEM; kF16
 // selects the output type: bf16 RNE (the reference CPU rounding) or fp16.
 //
-// One CTA computes one 128-query tile of one (window, head): the window's
-// packed sequence is its video tokens followed by the shared text tokens, and
-// every query attends to all S_w = L_w + Lt keys of its own window
-// (seedvr2_dit_block.cpp:1045-1079; non-causal).
+// One CTA computes two 128-query tiles (256 query rows) of one (window, head):
+// the window's packed sequence is its video tokens followed by the shared
+// text tokens, and every query attends to all S_w = L_w + Lt keys of its own
+// window (seedvr2_dit_block.cpp:1045-1079; non-causal).
 //
-// Roles (192 threads, one CTA per SM):
-//   warps 0-3  softmax + epilogue. Thread r owns query row r == TMEM lane r.
-//   warp 4     TMA producer: Q once, then K/V tiles of 128 keys into a
-//              2-stage ring (separate K and V stages so a K stage frees as
-//              soon as its QK^T MMA retires).
-//   warp 5     TMEM allocator + single-thread tcgen05.mma issuer.
-// TMEM (512 columns): S double buffer at 0 and 128, O accumulator at 256.
-// Per key tile j: S_j = Q K_j^T (M=N=K=128, 8 MMAs of K=16) -> softmax warps
-// read S_j with tcgen05.ld, update the running max (log2 domain), write
-// P_j = exp2(S_j*c - m) as fp16 into a 128B-swizzled shared tile and
-// rescale O in TMEM only when the max grew by more than 2^8 (the stale max is
-// otherwise kept, which is exact because O and the row sum share it); then
-// O += P_j V_j (V as an MN-major operand). S_{j+2} is issued right after
-// P_j V_j so the tensor core works on the next tile while the softmax warps
-// finish this one. The epilogue divides by the row sum, rounds to the output
-// type and scatters video rows to their global token row and text rows to the
-// window's text-partial slab (no atomics: every output row has one writer).
+// Roles (384 threads, one CTA per SM):
+//   warps 0-3, 4-7  softmax + epilogue of Q tile 0 / Q tile 1; thread r of a
+//                   warpgroup owns query row r == TMEM lane r (224 registers).
+//   warp 8          TMA producer: both Q tiles once, then K and V tiles of 128
+//                   keys into separate 2-stage rings (no multicast).
+//   warp 9          TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 10-11     idle (they complete the control warpgroup's register
+//                   hand-back; 56 registers each).
+// TMEM (512 columns): S_i at 128*i (P_i is written over it, columns 32..95 of
+// S_i, as the A operand of the PV MMA), O_i at 256 + 128*i.
+// The tensor core ping-pongs between the two Q tiles: per key tile j it runs
+// P_0(j-1) V(j-1), S_0(j) = Q_0 K(j)^T, then the same for tile 1, so one
+// warpgroup's softmax overlaps the other tile's GEMMs. Because tcgen05.mma
+// operations of one thread execute in issue order, the commit that announces
+// S_i(j) also guarantees P_i(j-1) V(j-1) has retired: the softmax warps may
+// then overwrite P_i and rescale O_i without a further wait. O is rescaled only
+// when the running max grew by more than 2^8 (log2 domain); the stale max is
+// otherwise kept, which is exact because O and the row sum share it.
+// The epilogue divides by the row sum, rounds to the output type and scatters
+// video rows to their global token row and text rows to the window's
+// text-partial slab (no atomics: every output row has one writer).
 //
 // Every wait is bounded (s2dev::mbar_wait): on timeout the CTA raises an abort
 // flag, records an error code in the caller's error word, drains its own
@@ -46,26 +50,45 @@ using namespace s2dev;
 
 namespace {
 
-constexpr int kBM = s2::kTileM;
-constexpr int kBN = s2::kTileN;
+constexpr int kBM = s2::kTileM;                      // rows per Q tile
+constexpr int kQT = s2::kQTiles;                     // Q tiles per CTA
+constexpr int kBN = s2::kTileN;                      // keys per K/V tile
 constexpr int kHD = S2_HEAD_DIM;
 constexpr int kStages = 2;
-constexpr uint32_t kBoxBytes = 128 * 64 * 2;     // one TMA box: 128 rows x 128 B (64 elements)
-constexpr uint32_t kTileBytes = 2 * kBoxBytes;   // 128 rows x 128 head dims
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kTileBytes;
+constexpr uint32_t kBoxBytes = 128 * 64 * 2;         // one TMA box: 128 rows x 128 B (64 elements)
+constexpr uint32_t kTileBytes = 2 * kBoxBytes;       // 128 rows x 128 head dims
+constexpr uint32_t kOffQ = 0;                        // kQT tiles
+constexpr uint32_t kOffK = kOffQ + kQT * kTileBytes; // kStages tiles
 constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
-constexpr uint32_t kOffP = kOffV + kStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffP + kTileBytes;
+constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + 1 KB alignment slack
 
-enum Bar { B_Q = 0, B_KFULL = 1, B_KEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9, B_PFULL = 11, B_ODONE = 12,
-           B_DRAIN = 13, B_COUNT = 14 };
+enum Bar {
+    B_QFULL = 0,                // [kQT]
+    B_KFULL = B_QFULL + kQT,    // [kStages]
+    B_KEMPTY = B_KFULL + kStages,
+    B_VFULL = B_KEMPTY + kStages,
+    B_VEMPTY = B_VFULL + kStages,
+    B_SFULL = B_VEMPTY + kStages,  // [kQT] S_i(j) ready (and P_i(j-1) V retired)
+    B_PFULL = B_SFULL + kQT,       // [kQT] P_i(j) in TMEM, O_i rescaled (128 arrivals)
+    B_ODONE = B_PFULL + kQT,       // [kQT] final P_i V retired
+    B_DRAIN = B_ODONE + kQT,
+    B_COUNT
+};
+static_assert(8 * B_COUNT + 8 <= 256, "barrier area");
 
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+// Three warpgroups: kQT softmax groups, then one control group (producer warp,
+// MMA warp, two idle warps). The control group gives registers back with
+// setmaxnreg so the softmax groups can hold a full 128-column S row:
+// launch 384 x 168 = 64,512 = 128 x (2 x 224 + 56). The host launcher checks
+// the compiled launch register count against this split before launching.
+constexpr int kThreads = 128 * (kQT + 1);
+constexpr int kProducerWarp = 4 * kQT;
+constexpr int kMmaWarp = kProducerWarp + 1;
+constexpr uint32_t kRegsSoftmax = 224, kRegsControl = 56;
+static_assert(128 * (kQT * kRegsSoftmax + kRegsControl) <= 65536, "register split exceeds the register file");
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColP = 32;                       // P_i offset inside S_i
 constexpr uint32_t kColO = 256;
 
 // device error codes (first failure wins)
@@ -101,11 +124,6 @@ __device__ __forceinline__ uint32_t pack_out(float a, float b)
     }
 }
 
-__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code)
-{
-    return mbar_wait(bar, parity, abort, err, code);
-}
-
 // Wait that ignores the abort flag (used only to drain in-flight async work).
 __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *err)
 {
@@ -122,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (base - raw);
-    const uint32_t sQ = base + kOffQ, sK = base + kOffK, sV = base + kOffV, sP = base + kOffP;
+    const uint32_t sQ = base + kOffQ, sK = base + kOffK, sV = base + kOffV;
     const uint32_t bar0 = base + kOffBar;
     volatile int *abort = reinterpret_cast<volatile int *>(gbase + kOffBar + 8 * B_COUNT);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + kOffBar + 8 * B_COUNT + 4);
@@ -131,15 +149,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int head = blockIdx.x % a.heads;
     const int item = a.work[blockIdx.x / a.heads];
-    const int win = item >> 16, qt = item & 0xFFFF;
+    const int win = item >> 16, qp = item & 0xFFFF;
     const int seq0 = a.cu[win];
     const int S = a.cu[win + 1] - seq0;
     const int Lw = S - a.text_len;
-    const int q0 = qt * kBM;
+    const int q0 = qp * (kQT * kBM);                     // first query row of tile 0 (window-local)
+    const int n_q = min(kQT, (S - q0 + kBM - 1) / kBM);  // active Q tiles (>= 1)
     const int n_kv = (S + kBN - 1) / kBN;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), i == B_PFULL ? 128u : 1u);
+        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), (i >= B_PFULL && i < B_PFULL + kQT) ? 128u : 1u);
         *abort = 0;
         fence_mbar_init();
     }
@@ -152,202 +171,222 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kProducerWarp) {
+    if (warp >= kProducerWarp) {
+      regs_dec<kRegsControl>();
+      if (warp == kProducerWarp) {
         if (lane == 0) {
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
             int issued_k[kStages] = {0, 0}, issued_v[kStages] = {0, 0};
-            const int row_q = seq0 + q0;
-            mbar_arrive_expect_tx(BAR(B_Q), kTileBytes);
-            tma_load_3d(sQ, &tmQ, BAR(B_Q), 0, row_q, head);
-            tma_load_3d(sQ + kBoxBytes, &tmQ, BAR(B_Q), 64, row_q, head);
+            for (int i = 0; i < n_q; ++i) {
+                const int row_q = seq0 + q0 + i * kBM;
+                mbar_arrive_expect_tx(BAR(B_QFULL + i), kTileBytes);
+                tma_load_3d(sQ + i * kTileBytes, &tmQ, BAR(B_QFULL + i), 0, row_q, head);
+                tma_load_3d(sQ + i * kTileBytes + kBoxBytes, &tmQ, BAR(B_QFULL + i), 64, row_q, head);
+            }
             for (int j = 0; j < n_kv; ++j) {
                 const int s = j & 1;
                 const uint32_t u = static_cast<uint32_t>(j >> 1);
                 const int row_kv = seq0 + j * kBN;
-                if (!wait_or_abort(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K)) break;
+                if (!mbar_wait(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K)) break;
                 mbar_arrive_expect_tx(BAR(B_KFULL + s), kTileBytes);
                 tma_load_3d(sK + s * kTileBytes, &tmK, BAR(B_KFULL + s), 0, row_kv, head);
                 tma_load_3d(sK + s * kTileBytes + kBoxBytes, &tmK, BAR(B_KFULL + s), 64, row_kv, head);
                 issued_k[s]++;
-                if (!wait_or_abort(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V)) break;
+                if (!mbar_wait(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V)) break;
                 mbar_arrive_expect_tx(BAR(B_VFULL + s), kTileBytes);
                 tma_load_3d(sV + s * kTileBytes, &tmV, BAR(B_VFULL + s), 0, row_kv, head);
                 tma_load_3d(sV + s * kTileBytes + kBoxBytes, &tmV, BAR(B_VFULL + s), 64, row_kv, head);
                 issued_v[s]++;
             }
             // No load may still be landing in shared memory when the CTA exits.
-            wait_drain(BAR(B_Q), 0, a.err);
+            for (int i = 0; i < n_q; ++i) wait_drain(BAR(B_QFULL + i), 0, a.err);
             for (int s = 0; s < kStages; ++s) {
                 if (issued_k[s]) wait_drain(BAR(B_KFULL + s), static_cast<uint32_t>(issued_k[s] - 1) & 1u, a.err);
                 if (issued_v[s]) wait_drain(BAR(B_VFULL + s), static_cast<uint32_t>(issued_v[s] - 1) & 1u, a.err);
             }
         }
-    } else if (warp == kMmaWarp) {
+      } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            const uint32_t id_qk = idesc_f16(0u, kBN, 0);  // f16 x f16 -> f32
-            const uint32_t id_pv = idesc_f16(0u, kHD, 1);
-            bool ok = wait_or_abort(BAR(B_Q), 0, abort, a.err, E_WAIT_Q);
-            if (ok) tc_fence_after();
-            auto issue_qk = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!wait_or_abort(BAR(B_KFULL + s), static_cast<uint32_t>(j >> 1) & 1u, abort, a.err, E_WAIT_K))
-                    return false;
-                tc_fence_after();
-                const uint32_t kb = sK + s * kTileBytes;
-                const uint32_t d = tmem + static_cast<uint32_t>(s) * kBN;
+            const uint32_t id_qk = idesc_f16(0u, kBN, 0);  // f16 x f16 -> f32, K-major A and B
+            const uint32_t id_pv = idesc_f16(0u, kHD, 1);  // A = P from TMEM, B = V MN-major
+            bool ok = true;
+            // S_i = Q_i K(j)^T into S_i's columns
+            auto qk = [&](int i, int j) {
+                const uint32_t qb = sQ + i * kTileBytes, kb = sK + (j & 1) * kTileBytes;
+                const uint32_t d = tmem + static_cast<uint32_t>(i) * 128u;
 #pragma unroll
                 for (int ks = 0; ks < kHD / 16; ++ks) {
                     const uint32_t off = static_cast<uint32_t>(ks >> 2) * kBoxBytes + static_cast<uint32_t>(ks & 3) * 32u;
-                    mma_f16_ss(d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), id_qk,
+                    mma_f16_ss(d, smem_desc_sw128(qb + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), id_qk,
                                ks > 0 ? 1u : 0u);
                 }
-                mma_commit(BAR(B_SFULL + s));
-                mma_commit(BAR(B_KEMPTY + s));
-                return true;
             };
-            if (ok) ok = issue_qk(0);
-            if (ok && n_kv > 1) ok = issue_qk(1);
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const int s = j & 1;
-                if (!wait_or_abort(BAR(B_PFULL), static_cast<uint32_t>(j) & 1u, abort, a.err, E_WAIT_P)) break;
-                if (!wait_or_abort(BAR(B_VFULL + s), static_cast<uint32_t>(j >> 1) & 1u, abort, a.err, E_WAIT_V))
-                    break;
-                tc_fence_after();
-                const uint32_t vb = sV + s * kTileBytes;
+            // O_i (+)= P_i V(j), P_i read from TMEM
+            auto pv = [&](int i, int j) {
+                const uint32_t vb = sV + (j & 1) * kTileBytes;
+                const uint32_t d = tmem + kColO + static_cast<uint32_t>(i) * 128u;
+                const uint32_t pa = tmem + static_cast<uint32_t>(i) * 128u + kColP;
 #pragma unroll
-                for (int ks = 0; ks < kBN / 16; ++ks) {
-                    const uint32_t a_off = static_cast<uint32_t>(ks >> 2) * kBoxBytes + static_cast<uint32_t>(ks & 3) * 32u;
-                    mma_f16_ss(tmem + kColO, smem_desc_sw128(sP + a_off, 16, 1024),
+                for (int ks = 0; ks < kBN / 16; ++ks)
+                    mma_f16_ts(d, pa + static_cast<uint32_t>(ks) * 8u,
                                smem_desc_sw128(vb + static_cast<uint32_t>(ks) * 2048u, kBoxBytes, 1024), id_pv,
                                (j > 0 || ks > 0) ? 1u : 0u);
+            };
+            // prologue: S_i(0)
+            ok = mbar_wait(BAR(B_KFULL), 0, abort, a.err, E_WAIT_K);
+            for (int i = 0; ok && i < n_q; ++i) {
+                ok = mbar_wait(BAR(B_QFULL + i), 0, abort, a.err, E_WAIT_Q);
+                if (!ok) break;
+                tc_fence_after();
+                qk(i, 0);
+                mma_commit(BAR(B_SFULL + i));
+            }
+            if (ok) mma_commit(BAR(B_KEMPTY + 0));
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const bool more = j + 1 < n_kv;
+                ok = mbar_wait(BAR(B_VFULL + (j & 1)), static_cast<uint32_t>(j >> 1) & 1u, abort, a.err, E_WAIT_V);
+                bool k_next = false;
+                for (int i = 0; ok && i < n_q; ++i) {
+                    ok = mbar_wait(BAR(B_PFULL + i), static_cast<uint32_t>(j) & 1u, abort, a.err, E_WAIT_P);
+                    if (!ok) break;
+                    tc_fence_after();
+                    pv(i, j);
+                    if (more && !k_next) {
+                        ok = mbar_wait(BAR(B_KFULL + ((j + 1) & 1)), static_cast<uint32_t>((j + 1) >> 1) & 1u, abort,
+                                       a.err, E_WAIT_K);
+                        if (!ok) break;
+                        tc_fence_after();
+                        k_next = true;
+                    }
+                    if (more) {
+                        qk(i, j + 1);  // overwrites S_i/P_i after P_i V(j): in-order tcgen05 issue
+                        mma_commit(BAR(B_SFULL + i));
+                    } else {
+                        mma_commit(BAR(B_ODONE + i));
+                    }
                 }
-                mma_commit(BAR(B_ODONE));
-                mma_commit(BAR(B_VEMPTY + s));
-                if (j + 2 < n_kv) ok = issue_qk(j + 2);
+                if (!ok) break;
+                mma_commit(BAR(B_VEMPTY + (j & 1)));
+                if (more) mma_commit(BAR(B_KEMPTY + ((j + 1) & 1)));
             }
             // All issued MMAs must retire before TMEM is released.
             mma_commit(BAR(B_DRAIN));
             wait_drain(BAR(B_DRAIN), 0, a.err);
         }
+      }
     } else {
-        // ---- softmax warps: thread r <-> query row r <-> TMEM lane r ----
-        const int r = threadIdx.x;
-        const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+        regs_inc<kRegsSoftmax>();
+        // ---- softmax warpgroups: thread r of group g <-> query row q0 + g*128 + r <-> TMEM lane r ----
+        const int g = warp >> 2;
+        const int r = threadIdx.x & 127;
+        const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t scol = tmem + lane_off + static_cast<uint32_t>(g) * 128u;
+        const uint32_t pcol = scol + kColP;
+        const uint32_t ocol = tmem + lane_off + kColO + static_cast<uint32_t>(g) * 128u;
         const float c = a.scale_log2;
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < n_kv; ++j) {
-            const int s = j & 1;
-            ok = wait_or_abort(BAR(B_SFULL + s), static_cast<uint32_t>(j >> 1) & 1u, abort, a.err, E_WAIT_S);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t x[4][32];
-            const uint32_t scol = tmem + lane_off + static_cast<uint32_t>(s) * kBN;
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) tmem_ld32(scol + cc * 32, x[cc]);
-            tmem_wait_ld();
-            const int valid = min(S - j * kBN, kBN);
-            float mx = -INFINITY;
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float sv = (cc * 32 + i) < valid ? __uint_as_float(x[cc][i]) : -INFINITY;
-                    x[cc][i] = __float_as_uint(sv);
-                    mx = fmaxf(mx, sv);
-                }
-            const float cand = mx * c;
-            float m_use = m, alpha = 1.f;
-            bool rescale = false;
-            if (j == 0) {
-                m_use = cand;
-            } else if (cand > m + 8.f) {
-                m_use = cand;
-                alpha = ex2_approx(m - cand);
-                rescale = true;
-            }
-            float rs = 0.f;
-            uint32_t pk[4][16];
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i]), c, -m_use));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i + 1]), c, -m_use));
-                    rs += p0 + p1;
-                    pk[cc][i] = pack_p(p0, p1);
-                }
-            if (j > 0) {
-                ok = wait_or_abort(BAR(B_ODONE), static_cast<uint32_t>(j - 1) & 1u, abort, a.err, E_WAIT_O);
+        if (g < n_q) {
+            float m = -INFINITY, l = 0.f;
+            bool ok = true;
+            for (int j = 0; j < n_kv; ++j) {
+                ok = mbar_wait(BAR(B_SFULL + g), static_cast<uint32_t>(j) & 1u, abort, a.err, E_WAIT_S);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc_fence_after();
-            }
-            if (__any_sync(0xffffffffu, rescale)) {
-                const uint32_t ocol = tmem + lane_off + kColO;
+                uint32_t x[4][32];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) tmem_ld32(scol + cc * 32, x[cc]);
+                tmem_wait_ld();
+                const int valid = min(S - j * kBN, kBN);
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (valid < kBN) {
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (cc * 32 + i >= valid) x[cc][i] = __float_as_uint(-INFINITY);
+                }
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(x[cc][i]));
+                const float cand = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * c;
+                float m_use = m, alpha = 1.f;
+                bool rescale = false;
+                if (j == 0) {
+                    m_use = cand;
+                } else if (cand > m + 8.f) {
+                    m_use = cand;
+                    alpha = ex2_approx(m - cand);
+                    rescale = true;
+                }
+                // O_i is stable here: P_i V(j-1) retired before S_i(j) was announced.
+                if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t o[32];
+                        tmem_ld32(ocol + cc * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(ocol + cc * 32, o);
+                    }
+                }
+                float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t o[32];
-                    tmem_ld32(ocol + cc * 32, o);
-                    tmem_wait_ld();
+                    uint32_t pk[16];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(ocol + cc * 32, o);
+                    for (int i = 0; i < 16; ++i) {
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i]), c, -m_use));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i + 1]), c, -m_use));
+                        rs4[(2 * i) & 3] += p0;
+                        rs4[(2 * i + 1) & 3] += p1;
+                        pk[i] = pack_p(p0, p1);
+                    }
+                    tmem_st16(pcol + cc * 16, pk);
                 }
                 tmem_wait_st();
+                l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+                m = m_use;
+                tc_fence_before();
+                mbar_arrive(BAR(B_PFULL + g));
             }
-            l = l * alpha + rs;
-            m = m_use;
-            // P row r -> 128B-swizzled K-major tile (two 64-key blocks).
-#pragma unroll
-            for (int c16 = 0; c16 < 16; ++c16) {
-                const uint32_t blk = static_cast<uint32_t>(c16 >> 3), chunk = static_cast<uint32_t>(c16 & 7);
-                const uint32_t addr = sP + blk * kBoxBytes + static_cast<uint32_t>(r) * 128u +
-                                      ((chunk ^ static_cast<uint32_t>(r & 7)) << 4);
-                const int cc = c16 >> 2, i0 = (c16 & 3) * 4;
-                st_shared_v4(addr, pk[cc][i0], pk[cc][i0 + 1], pk[cc][i0 + 2], pk[cc][i0 + 3]);
+            if (ok) {
+                ok = mbar_wait(BAR(B_ODONE + g), 0, abort, a.err, E_WAIT_O);
+                ok = __all_sync(0xffffffffu, ok);
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(BAR(B_PFULL));
-        }
-        if (ok) {
-            ok = wait_or_abort(BAR(B_ODONE), static_cast<uint32_t>(n_kv - 1) & 1u, abort, a.err, E_WAIT_O);
-            ok = __all_sync(0xffffffffu, ok);
-        }
-        if (ok) {
-            tc_fence_after();
-            uint32_t o[4][32];
-            const uint32_t ocol = tmem + lane_off + kColO;
+            if (ok) {
+                tc_fence_after();
+                uint32_t o[4][32];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) tmem_ld32(ocol + cc * 32, o[cc]);
-            tmem_wait_ld();
-            const int qrow = q0 + r;
-            if (qrow < S) {
-                const float inv = 1.f / l;
-                const int dim = a.heads * kHD;
-                uint4 *dst;
-                if (qrow < Lw) {
-                    const int g = a.rows[seq0 + qrow].src;
-                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.vid_out) + static_cast<size_t>(g) * dim +
-                                                    head * kHD);
-                } else {
-                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.txt_partial) +
-                                                    (static_cast<size_t>(win) * a.text_len + (qrow - Lw)) * dim +
-                                                    head * kHD);
-                }
+                for (int cc = 0; cc < 4; ++cc) tmem_ld32(ocol + cc * 32, o[cc]);
+                tmem_wait_ld();
+                const int qrow = q0 + g * kBM + r;
+                if (qrow < S) {
+                    const float inv = 1.f / l;
+                    const int dim = a.heads * kHD;
+                    uint4 *dst;
+                    if (qrow < Lw) {
+                        const int gr = a.rows[seq0 + qrow].src;
+                        dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.vid_out) + static_cast<size_t>(gr) * dim +
+                                                        head * kHD);
+                    } else {
+                        dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.txt_partial) +
+                                                        (static_cast<size_t>(win) * a.text_len + (qrow - Lw)) * dim +
+                                                        head * kHD);
+                    }
 #pragma unroll
-                for (int c16 = 0; c16 < 16; ++c16) {
-                    const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
-                    uint4 w;
-                    w.x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
-                    w.y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
-                    w.z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
-                    w.w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
-                    dst[c16] = w;
+                    for (int c16 = 0; c16 < 16; ++c16) {
+                        const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
+                        uint4 w;
+                        w.x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
+                        w.y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
+                        w.z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
+                        w.w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
+                        dst[c16] = w;
+                    }
                 }
             }
         }
@@ -406,6 +445,15 @@ s2_status launch(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, 
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_window_attention: smem attribute: %s", cudaGetErrorString(e));
+        // setmaxnreg.inc waits until the block's launch registers can cover the
+        // softmax groups' request: refuse to launch a build whose register
+        // count at launch is smaller than the split assumes.
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, window_attention_kernel<kF16>) != cudaSuccess ||
+            static_cast<long long>(fa.numRegs) * kThreads < 128LL * (kQT * kRegsSoftmax + kRegsControl))
+            return s2::set_error(S2_INFERENCE_FAILED,
+                                 "s2_window_attention: kernel built with %d registers/thread, register split needs %d",
+                                 fa.numRegs, (128 * (kQT * kRegsSoftmax + kRegsControl) + kThreads - 1) / kThreads);
         configured = true;
     }
     window_attention_kernel<kF16><<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, args);

@@ -17,7 +17,9 @@ void clear_error();
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 // Attention core tiling shared by the planner and the kernel.
-constexpr int kTileM = 128;   // query rows per CTA (one TMEM lane per row)
+constexpr int kTileM = 128;   // query rows per Q tile (one TMEM lane per row)
+constexpr int kQTiles = 2;    // Q tiles per CTA (one softmax warpgroup each)
+constexpr int kCtaRows = kTileM * kQTiles;
 constexpr int kTileN = 128;   // key/value rows per pipeline stage
 
 }  // namespace s2

@@ -131,9 +131,10 @@ extern "C" s2_status s2_build_varlen(int frames, int height, int width,
     return S2_OK;
 }
 
-// Work items (window << 16 | q_tile), costliest first: a window's q-tiles all
-// cost ceil(S_w / kTileN) key tiles, so sorting windows by S_w descending is a
-// longest-processing-time order for the hardware block scheduler.
+// Work items (window << 16 | q_block), one per kCtaRows (256) query rows,
+// costliest first: every q-block of a window costs ceil(S_w / kTileN) key
+// tiles, so sorting windows by S_w descending is a longest-processing-time
+// order for the hardware block scheduler.
 extern "C" s2_status s2_plan_work(const int32_t *cu_seqlens, int n_windows, int32_t *work, int cap, int *n_work)
 {
     if (!cu_seqlens || n_windows <= 0 || !n_work)
@@ -148,7 +149,7 @@ extern "C" s2_status s2_plan_work(const int32_t *cu_seqlens, int n_windows, int3
     int n = 0;
     for (int w : order) {
         const int s = cu_seqlens[w + 1] - cu_seqlens[w];
-        const int tiles = ceil_div(s, s2::kTileM);
+        const int tiles = ceil_div(s, s2::kCtaRows);
         if (tiles > 65535) return s2::set_error(S2_INVALID_ARGUMENT, "s2_plan_work: window %d too long", w);
         for (int qt = 0; qt < tiles; qt++) {
             if (work && n < cap) work[n] = (w << 16) | qt;

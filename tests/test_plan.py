@@ -92,7 +92,7 @@ def test_plan_work_covers_tiles_costliest_first():
     cu, _ = s2b200.build_varlen(6, 45, 80, wins, 58)
     work = s2b200.plan_work(cu)
     S = np.diff(cu)
-    tiles = -(-S // 128)
+    tiles = -(-S // 256)  # one CTA per 256 query rows (two 128-row Q tiles)
     assert len(work) == tiles.sum()
     w, qt = work >> 16, work & 0xFFFF
     cost = S[w]
