@@ -64,15 +64,17 @@ constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + 1 KB alignment slack
 
 enum Bar {
-    B_QFULL = 0,                // [kQT]
-    B_KFULL = B_QFULL + kQT,    // [kStages]
+    B_QFULL = 0,                   // [kQT] Q_i landed
+    B_QEMPTY = B_QFULL + kQT,      // [kQT] last Q_i K^T of an item retired
+    B_KFULL = B_QEMPTY + kQT,      // [kStages]
     B_KEMPTY = B_KFULL + kStages,
     B_VFULL = B_KEMPTY + kStages,
     B_VEMPTY = B_VFULL + kStages,
     B_SFULL = B_VEMPTY + kStages,  // [kQT] S_i(j) ready (and P_i(j-1) V retired)
     B_PFULL = B_SFULL + kQT,       // [kQT] P_i(j) in TMEM, O_i rescaled (128 arrivals)
-    B_ODONE = B_PFULL + kQT,       // [kQT] final P_i V retired
-    B_DRAIN = B_ODONE + kQT,
+    B_ODONE = B_PFULL + kQT,       // [kQT] last P_i V of an item retired
+    B_OFREE = B_ODONE + kQT,       // [kQT] epilogue finished reading O_i (128 arrivals)
+    B_DRAIN = B_OFREE + kQT,
     B_COUNT
 };
 static_assert(8 * B_COUNT + 8 <= 256, "barrier area");
@@ -92,7 +94,8 @@ constexpr uint32_t kColP = 32;                       // P_i offset inside S_i
 constexpr uint32_t kColO = 256;
 
 // device error codes (first failure wins)
-enum : int { E_WAIT_Q = 1, E_WAIT_K = 2, E_WAIT_V = 3, E_WAIT_P = 4, E_WAIT_S = 5, E_WAIT_O = 6, E_DRAIN = 7 };
+enum : int { E_WAIT_Q = 1, E_WAIT_K = 2, E_WAIT_V = 3, E_WAIT_P = 4, E_WAIT_S = 5, E_WAIT_O = 6, E_DRAIN = 7,
+             E_WAIT_OFREE = 8 };
 
 struct AttnArgs {
     const s2_row *rows;
@@ -103,8 +106,30 @@ struct AttnArgs {
     int32_t *err;
     int heads;
     int text_len;
+    int n_items;      // n_work * heads
     float scale_log2;
 };
+
+// One (window, q-block, head) work item.
+struct Item {
+    int head, win, seq0, S, Lw, q0, n_q, n_kv;
+};
+
+__device__ __forceinline__ Item decode_item(const AttnArgs &a, int t)
+{
+    Item it;
+    it.head = t % a.heads;
+    const int w = a.work[t / a.heads];
+    it.win = w >> 16;
+    const int qb = w & 0xFFFF;
+    it.seq0 = a.cu[it.win];
+    it.S = a.cu[it.win + 1] - it.seq0;
+    it.Lw = it.S - a.text_len;
+    it.q0 = qb * (kQT * kBM);
+    it.n_q = min(kQT, (it.S - it.q0 + kBM - 1) / kBM);
+    it.n_kv = (it.S + kBN - 1) / kBN;
+    return it;
+}
 
 __device__ __forceinline__ uint32_t pack_p(float a, float b)
 {
@@ -131,6 +156,8 @@ __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *e
     return mbar_wait(bar, parity, &dummy, err, E_DRAIN);
 }
 
+// Persistent: CTA b processes items b, b + gridDim.x, ... of the cost-ordered
+// list; every barrier's phase counter runs on across items.
 template <bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -147,18 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #define BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int head = blockIdx.x % a.heads;
-    const int item = a.work[blockIdx.x / a.heads];
-    const int win = item >> 16, qp = item & 0xFFFF;
-    const int seq0 = a.cu[win];
-    const int S = a.cu[win + 1] - seq0;
-    const int Lw = S - a.text_len;
-    const int q0 = qp * (kQT * kBM);                     // first query row of tile 0 (window-local)
-    const int n_q = min(kQT, (S - q0 + kBM - 1) / kBM);  // active Q tiles (>= 1)
-    const int n_kv = (S + kBN - 1) / kBN;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), (i >= B_PFULL && i < B_PFULL + kQT) ? 128u : 1u);
+        for (int i = 0; i < B_COUNT; ++i) {
+            const bool wg_arrive = (i >= B_PFULL && i < B_PFULL + kQT) || (i >= B_OFREE && i < B_OFREE + kQT);
+            mbar_init(BAR(i), wg_arrive ? 128u : 1u);
+        }
         *abort = 0;
         fence_mbar_init();
     }
@@ -178,98 +199,129 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            int issued_k[kStages] = {0, 0}, issued_v[kStages] = {0, 0};
-            for (int i = 0; i < n_q; ++i) {
-                const int row_q = seq0 + q0 + i * kBM;
-                mbar_arrive_expect_tx(BAR(B_QFULL + i), kTileBytes);
-                tma_load_3d(sQ + i * kTileBytes, &tmQ, BAR(B_QFULL + i), 0, row_q, head);
-                tma_load_3d(sQ + i * kTileBytes + kBoxBytes, &tmQ, BAR(B_QFULL + i), 64, row_q, head);
+            uint32_t nq[kQT] = {0, 0};   // Q_i loads issued
+            uint32_t kv = 0;             // K/V tiles issued (ring position)
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+                const Item it = decode_item(a, t);
+                for (int i = 0; i < it.n_q; ++i) {
+                    if (!(ok = mbar_wait(BAR(B_QEMPTY + i), (nq[i] & 1u) ^ 1u, abort, a.err, E_WAIT_Q))) break;
+                    const int row_q = it.seq0 + it.q0 + i * kBM;
+                    mbar_arrive_expect_tx(BAR(B_QFULL + i), kTileBytes);
+                    tma_load_3d(sQ + i * kTileBytes, &tmQ, BAR(B_QFULL + i), 0, row_q, it.head);
+                    tma_load_3d(sQ + i * kTileBytes + kBoxBytes, &tmQ, BAR(B_QFULL + i), 64, row_q, it.head);
+                    nq[i]++;
+                }
+                for (int j = 0; ok && j < it.n_kv; ++j, ++kv) {
+                    const uint32_t s = kv & 1u, u = kv >> 1;
+                    const int row_kv = it.seq0 + j * kBN;
+                    if (!(ok = mbar_wait(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K))) break;
+                    mbar_arrive_expect_tx(BAR(B_KFULL + s), kTileBytes);
+                    tma_load_3d(sK + s * kTileBytes, &tmK, BAR(B_KFULL + s), 0, row_kv, it.head);
+                    tma_load_3d(sK + s * kTileBytes + kBoxBytes, &tmK, BAR(B_KFULL + s), 64, row_kv, it.head);
+                    if (!(ok = mbar_wait(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V))) {
+                        ++kv;  // the K half of this tile is in flight
+                        break;
+                    }
+                    mbar_arrive_expect_tx(BAR(B_VFULL + s), kTileBytes);
+                    tma_load_3d(sV + s * kTileBytes, &tmV, BAR(B_VFULL + s), 0, row_kv, it.head);
+                    tma_load_3d(sV + s * kTileBytes + kBoxBytes, &tmV, BAR(B_VFULL + s), 64, row_kv, it.head);
+                }
             }
-            for (int j = 0; j < n_kv; ++j) {
-                const int s = j & 1;
-                const uint32_t u = static_cast<uint32_t>(j >> 1);
-                const int row_kv = seq0 + j * kBN;
-                if (!mbar_wait(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K)) break;
-                mbar_arrive_expect_tx(BAR(B_KFULL + s), kTileBytes);
-                tma_load_3d(sK + s * kTileBytes, &tmK, BAR(B_KFULL + s), 0, row_kv, head);
-                tma_load_3d(sK + s * kTileBytes + kBoxBytes, &tmK, BAR(B_KFULL + s), 64, row_kv, head);
-                issued_k[s]++;
-                if (!mbar_wait(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V)) break;
-                mbar_arrive_expect_tx(BAR(B_VFULL + s), kTileBytes);
-                tma_load_3d(sV + s * kTileBytes, &tmV, BAR(B_VFULL + s), 0, row_kv, head);
-                tma_load_3d(sV + s * kTileBytes + kBoxBytes, &tmV, BAR(B_VFULL + s), 64, row_kv, head);
-                issued_v[s]++;
-            }
-            // No load may still be landing in shared memory when the CTA exits.
-            for (int i = 0; i < n_q; ++i) wait_drain(BAR(B_QFULL + i), 0, a.err);
-            for (int s = 0; s < kStages; ++s) {
-                if (issued_k[s]) wait_drain(BAR(B_KFULL + s), static_cast<uint32_t>(issued_k[s] - 1) & 1u, a.err);
-                if (issued_v[s]) wait_drain(BAR(B_VFULL + s), static_cast<uint32_t>(issued_v[s] - 1) & 1u, a.err);
+            // No load may still be landing in shared memory when the CTA exits:
+            // wait for the last load issued into every buffer.
+            for (int i = 0; i < kQT; ++i)
+                if (nq[i]) wait_drain(BAR(B_QFULL + i), (nq[i] - 1) & 1u, a.err);
+            for (uint32_t s = 0; s < kStages; ++s) {
+                if (kv > s) {
+                    const uint32_t last = (kv - 1 - s) / kStages;  // use count - 1 of stage s
+                    wait_drain(BAR(B_KFULL + s), last & 1u, a.err);
+                    wait_drain(BAR(B_VFULL + s), last & 1u, a.err);
+                }
             }
         }
       } else if (warp == kMmaWarp) {
         if (lane == 0) {
             const uint32_t id_qk = idesc_f16(0u, kBN, 0);  // f16 x f16 -> f32, K-major A and B
             const uint32_t id_pv = idesc_f16(0u, kHD, 1);  // A = P from TMEM, B = V MN-major
-            bool ok = true;
-            // S_i = Q_i K(j)^T into S_i's columns
-            auto qk = [&](int i, int j) {
-                const uint32_t qb = sQ + i * kTileBytes, kb = sK + (j & 1) * kTileBytes;
+            // Descriptor start addresses advance in 16-byte units: +2 per 16-element
+            // K step inside a 128-byte swizzle row, +1024 (16 KB) to the second
+            // 64-element box; V advances 16 key rows (2 KB, +128) per step.
+            const uint64_t dq0 = smem_desc_sw128(sQ, 16, 1024), dk0 = smem_desc_sw128(sK, 16, 1024);
+            const uint64_t dv0 = smem_desc_sw128(sV, kBoxBytes, 1024);
+            // S_i = Q_i K^T (K tile in ring stage s) into S_i's columns
+            auto qk = [&](int i, uint32_t s) {
+                const uint64_t dq = dq0 + static_cast<uint64_t>(i) * (kTileBytes >> 4);
+                const uint64_t dk = dk0 + static_cast<uint64_t>(s) * (kTileBytes >> 4);
                 const uint32_t d = tmem + static_cast<uint32_t>(i) * 128u;
-#pragma unroll
-                for (int ks = 0; ks < kHD / 16; ++ks) {
-                    const uint32_t off = static_cast<uint32_t>(ks >> 2) * kBoxBytes + static_cast<uint32_t>(ks & 3) * 32u;
-                    mma_f16_ss(d, smem_desc_sw128(qb + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), id_qk,
-                               ks > 0 ? 1u : 0u);
+#pragma unroll 1
+                for (uint32_t ks = 0; ks < kHD / 16; ++ks) {
+                    const uint64_t off = (ks >> 2) * (kBoxBytes >> 4) + (ks & 3u) * 2u;
+                    mma_f16_ss(d, dq + off, dk + off, id_qk, ks > 0 ? 1u : 0u);
                 }
             };
-            // O_i (+)= P_i V(j), P_i read from TMEM
-            auto pv = [&](int i, int j) {
-                const uint32_t vb = sV + (j & 1) * kTileBytes;
+            // O_i (+)= P_i V (V tile in ring stage s), P_i read from TMEM
+            auto pv = [&](int i, uint32_t s, bool acc) {
+                const uint64_t dv = dv0 + static_cast<uint64_t>(s) * (kTileBytes >> 4);
                 const uint32_t d = tmem + kColO + static_cast<uint32_t>(i) * 128u;
                 const uint32_t pa = tmem + static_cast<uint32_t>(i) * 128u + kColP;
-#pragma unroll
-                for (int ks = 0; ks < kBN / 16; ++ks)
-                    mma_f16_ts(d, pa + static_cast<uint32_t>(ks) * 8u,
-                               smem_desc_sw128(vb + static_cast<uint32_t>(ks) * 2048u, kBoxBytes, 1024), id_pv,
-                               (j > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll 1
+                for (uint32_t ks = 0; ks < kBN / 16; ++ks)
+                    mma_f16_ts(d, pa + ks * 8u, dv + ks * 128u, id_pv, (acc || ks > 0) ? 1u : 0u);
             };
-            // prologue: S_i(0)
-            ok = mbar_wait(BAR(B_KFULL), 0, abort, a.err, E_WAIT_K);
-            for (int i = 0; ok && i < n_q; ++i) {
-                ok = mbar_wait(BAR(B_QFULL + i), 0, abort, a.err, E_WAIT_Q);
-                if (!ok) break;
-                tc_fence_after();
-                qk(i, 0);
-                mma_commit(BAR(B_SFULL + i));
-            }
-            if (ok) mma_commit(BAR(B_KEMPTY + 0));
-            for (int j = 0; ok && j < n_kv; ++j) {
-                const bool more = j + 1 < n_kv;
-                ok = mbar_wait(BAR(B_VFULL + (j & 1)), static_cast<uint32_t>(j >> 1) & 1u, abort, a.err, E_WAIT_V);
-                bool k_next = false;
-                for (int i = 0; ok && i < n_q; ++i) {
-                    ok = mbar_wait(BAR(B_PFULL + i), static_cast<uint32_t>(j) & 1u, abort, a.err, E_WAIT_P);
-                    if (!ok) break;
+            uint32_t nq[kQT] = {0, 0};   // items seen per Q tile (Q_FULL / Q_EMPTY / O phases)
+            uint32_t np[kQT] = {0, 0};   // P_i tiles consumed (P_FULL phases)
+            uint32_t kv = 0;             // K/V tiles consumed
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+                const Item it = decode_item(a, t);
+                // S_i(0)
+                const uint32_t s0 = kv & 1u;
+                ok = mbar_wait(BAR(B_KFULL + s0), (kv >> 1) & 1u, abort, a.err, E_WAIT_K);
+                for (int i = 0; ok && i < it.n_q; ++i) {
+                    if (!(ok = mbar_wait(BAR(B_QFULL + i), nq[i] & 1u, abort, a.err, E_WAIT_Q))) break;
                     tc_fence_after();
-                    pv(i, j);
-                    if (more && !k_next) {
-                        ok = mbar_wait(BAR(B_KFULL + ((j + 1) & 1)), static_cast<uint32_t>((j + 1) >> 1) & 1u, abort,
-                                       a.err, E_WAIT_K);
-                        if (!ok) break;
-                        tc_fence_after();
-                        k_next = true;
-                    }
-                    if (more) {
-                        qk(i, j + 1);  // overwrites S_i/P_i after P_i V(j): in-order tcgen05 issue
-                        mma_commit(BAR(B_SFULL + i));
-                    } else {
-                        mma_commit(BAR(B_ODONE + i));
-                    }
+                    qk(i, s0);
+                    mma_commit(BAR(B_SFULL + i));
+                    if (it.n_kv == 1) mma_commit(BAR(B_QEMPTY + i));
                 }
                 if (!ok) break;
-                mma_commit(BAR(B_VEMPTY + (j & 1)));
-                if (more) mma_commit(BAR(B_KEMPTY + ((j + 1) & 1)));
+                mma_commit(BAR(B_KEMPTY + s0));
+                for (int j = 0; ok && j < it.n_kv; ++j) {
+                    const uint32_t s = (kv + j) & 1u, sn = (kv + j + 1) & 1u;
+                    const bool more = j + 1 < it.n_kv;
+                    ok = mbar_wait(BAR(B_VFULL + s), ((kv + j) >> 1) & 1u, abort, a.err, E_WAIT_V);
+                    bool k_next = false;
+                    for (int i = 0; ok && i < it.n_q; ++i) {
+                        if (!(ok = mbar_wait(BAR(B_PFULL + i), np[i] & 1u, abort, a.err, E_WAIT_P))) break;
+                        np[i]++;
+                        // the previous item's epilogue must have read O_i before it is overwritten
+                        if (j == 0 && !(ok = mbar_wait(BAR(B_OFREE + i), (nq[i] & 1u) ^ 1u, abort, a.err,
+                                                       E_WAIT_OFREE)))
+                            break;
+                        tc_fence_after();
+                        pv(i, s, j > 0);
+                        if (more) {
+                            if (!k_next) {
+                                if (!(ok = mbar_wait(BAR(B_KFULL + sn), ((kv + j + 1) >> 1) & 1u, abort, a.err,
+                                                     E_WAIT_K)))
+                                    break;
+                                tc_fence_after();
+                                k_next = true;
+                            }
+                            qk(i, sn);  // overwrites S_i/P_i after P_i V: in-order tcgen05 issue
+                            mma_commit(BAR(B_SFULL + i));
+                            if (j + 2 == it.n_kv) mma_commit(BAR(B_QEMPTY + i));
+                        } else {
+                            mma_commit(BAR(B_ODONE + i));
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(BAR(B_VEMPTY + s));
+                    if (more) mma_commit(BAR(B_KEMPTY + sn));
+                }
+                for (int i = 0; i < it.n_q; ++i) nq[i]++;
+                kv += it.n_kv;
             }
             // All issued MMAs must retire before TMEM is released.
             mma_commit(BAR(B_DRAIN));
@@ -286,20 +338,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t pcol = scol + kColP;
         const uint32_t ocol = tmem + lane_off + kColO + static_cast<uint32_t>(g) * 128u;
         const float c = a.scale_log2;
-        if (g < n_q) {
+        const int dim = a.heads * kHD;
+        uint32_t ns = 0, no = 0;  // S_FULL phases consumed, items finished
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+            const Item it = decode_item(a, t);
+            if (g >= it.n_q) continue;
             float m = -INFINITY, l = 0.f;
-            bool ok = true;
-            for (int j = 0; j < n_kv; ++j) {
-                ok = mbar_wait(BAR(B_SFULL + g), static_cast<uint32_t>(j) & 1u, abort, a.err, E_WAIT_S);
+            for (int j = 0; j < it.n_kv; ++j) {
+                ok = mbar_wait(BAR(B_SFULL + g), ns & 1u, abort, a.err, E_WAIT_S);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
+                ns++;
                 tc_fence_after();
                 uint32_t x[4][32];
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) tmem_ld32(scol + cc * 32, x[cc]);
                 tmem_wait_ld();
-                const int valid = min(S - j * kBN, kBN);
-                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                const int valid = min(it.S - j * kBN, kBN);
                 if (valid < kBN) {
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc)
@@ -307,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 32; ++i)
                             if (cc * 32 + i >= valid) x[cc][i] = __float_as_uint(-INFINITY);
                 }
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
@@ -353,40 +410,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 mbar_arrive(BAR(B_PFULL + g));
             }
-            if (ok) {
-                ok = mbar_wait(BAR(B_ODONE + g), 0, abort, a.err, E_WAIT_O);
-                ok = __all_sync(0xffffffffu, ok);
-            }
-            if (ok) {
-                tc_fence_after();
-                uint32_t o[4][32];
+            if (!ok) break;
+            ok = mbar_wait(BAR(B_ODONE + g), no & 1u, abort, a.err, E_WAIT_O);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            no++;
+            tc_fence_after();
+            uint32_t o[4][32];
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) tmem_ld32(ocol + cc * 32, o[cc]);
-                tmem_wait_ld();
-                const int qrow = q0 + g * kBM + r;
-                if (qrow < S) {
-                    const float inv = 1.f / l;
-                    const int dim = a.heads * kHD;
-                    uint4 *dst;
-                    if (qrow < Lw) {
-                        const int gr = a.rows[seq0 + qrow].src;
-                        dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.vid_out) + static_cast<size_t>(gr) * dim +
-                                                        head * kHD);
-                    } else {
-                        dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.txt_partial) +
-                                                        (static_cast<size_t>(win) * a.text_len + (qrow - Lw)) * dim +
-                                                        head * kHD);
-                    }
+            for (int cc = 0; cc < 4; ++cc) tmem_ld32(ocol + cc * 32, o[cc]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(BAR(B_OFREE + g));  // O_i may be overwritten by the next item
+            const int qrow = it.q0 + g * kBM + r;
+            if (qrow < it.S) {
+                const float inv = 1.f / l;
+                uint4 *dst;
+                if (qrow < it.Lw) {
+                    const int gr = a.rows[it.seq0 + qrow].src;
+                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.vid_out) + static_cast<size_t>(gr) * dim +
+                                                    it.head * kHD);
+                } else {
+                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.txt_partial) +
+                                                    (static_cast<size_t>(it.win) * a.text_len + (qrow - it.Lw)) * dim +
+                                                    it.head * kHD);
+                }
 #pragma unroll
-                    for (int c16 = 0; c16 < 16; ++c16) {
-                        const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
-                        uint4 w;
-                        w.x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
-                        w.y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
-                        w.z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
-                        w.w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
-                        dst[c16] = w;
-                    }
+                for (int c16 = 0; c16 < 16; ++c16) {
+                    const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
+                    uint4 w;
+                    w.x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
+                    w.y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
+                    w.z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
+                    w.w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
+                    dst[c16] = w;
                 }
             }
         }
@@ -478,8 +535,12 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
           reinterpret_cast<uintptr_t>(vid_out) | reinterpret_cast<uintptr_t>(txt_partial)) & 15u) != 0)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_window_attention: buffers must be 16-byte aligned");
-    const long long grid = 1LL * n_work * heads;
-    if (grid > 0x7fffffffLL) return s2::set_error(S2_INVALID_ARGUMENT, "s2_window_attention: grid too large");
+    const long long n_items = 1LL * n_work * heads;
+    if (n_items > 0x7fffffffLL) return s2::set_error(S2_INVALID_ARGUMENT, "s2_window_attention: too many work items");
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long grid = n_items < sms ? n_items : sms;  // persistent: one CTA per SM
     const bool f16 = mode == S2_MODE_F16;
     CUtensorMap mq, mk, mv;
     if (!make_map(&mq, q, heads, n_rows) || !make_map(&mk, k, heads, n_rows) || !make_map(&mv, v, heads, n_rows))
@@ -493,6 +554,7 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     args.err = err;
     args.heads = heads;
     args.text_len = text_len;
+    args.n_items = static_cast<int>(n_items);
     args.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e) / sqrt(128)
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return f16 ? launch<true>(st, mq, mk, mv, args, static_cast<int>(grid))
