@@ -244,30 +244,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t id_qk = idesc_f16(0u, kBN, 0);  // f16 x f16 -> f32, K-major A and B
             const uint32_t id_pv = idesc_f16(0u, kHD, 1);  // A = P from TMEM, B = V MN-major
-            // Descriptor start addresses advance in 16-byte units: +2 per 16-element
-            // K step inside a 128-byte swizzle row, +1024 (16 KB) to the second
-            // 64-element box; V advances 16 key rows (2 KB, +128) per step.
+            // Each 128x128x128 tile is 8 straight-line K=16 MMAs (s2_sm100.cuh):
+            // any per-MMA loop or branch overhead in this thread shows up
+            // directly as tensor-core idle time.
             const uint64_t dq0 = smem_desc_sw128(sQ, 16, 1024), dk0 = smem_desc_sw128(sK, 16, 1024);
             const uint64_t dv0 = smem_desc_sw128(sV, kBoxBytes, 1024);
             // S_i = Q_i K^T (K tile in ring stage s) into S_i's columns
             auto qk = [&](int i, uint32_t s) {
-                const uint64_t dq = dq0 + static_cast<uint64_t>(i) * (kTileBytes >> 4);
-                const uint64_t dk = dk0 + static_cast<uint64_t>(s) * (kTileBytes >> 4);
-                const uint32_t d = tmem + static_cast<uint32_t>(i) * 128u;
-#pragma unroll 1
-                for (uint32_t ks = 0; ks < kHD / 16; ++ks) {
-                    const uint64_t off = (ks >> 2) * (kBoxBytes >> 4) + (ks & 3u) * 2u;
-                    mma_f16_ss(d, dq + off, dk + off, id_qk, ks > 0 ? 1u : 0u);
-                }
+                mma_tile_ss_k128(tmem + static_cast<uint32_t>(i) * 128u,
+                                 dq0 + static_cast<uint64_t>(i) * (kTileBytes >> 4),
+                                 dk0 + static_cast<uint64_t>(s) * (kTileBytes >> 4), id_qk, 0u);
             };
             // O_i (+)= P_i V (V tile in ring stage s), P_i read from TMEM
-            auto pv = [&](int i, uint32_t s, bool acc) {
-                const uint64_t dv = dv0 + static_cast<uint64_t>(s) * (kTileBytes >> 4);
-                const uint32_t d = tmem + kColO + static_cast<uint32_t>(i) * 128u;
-                const uint32_t pa = tmem + static_cast<uint32_t>(i) * 128u + kColP;
-#pragma unroll 1
-                for (uint32_t ks = 0; ks < kBN / 16; ++ks)
-                    mma_f16_ts(d, pa + ks * 8u, dv + ks * 128u, id_pv, (acc || ks > 0) ? 1u : 0u);
+            auto pv = [&](int i, uint32_t s, uint32_t acc) {
+                mma_tile_ts_k128(tmem + kColO + static_cast<uint32_t>(i) * 128u,
+                                 tmem + static_cast<uint32_t>(i) * 128u + kColP,
+                                 dv0 + static_cast<uint64_t>(s) * (kTileBytes >> 4), id_pv, acc);
             };
             uint32_t nq[kQT] = {0, 0};   // items seen per Q tile (Q_FULL / Q_EMPTY / O phases)
             uint32_t np[kQT] = {0, 0};   // P_i tiles consumed (P_FULL phases)
@@ -300,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                        E_WAIT_OFREE)))
                             break;
                         tc_fence_after();
-                        pv(i, s, j > 0);
+                        pv(i, s, j > 0 ? 1u : 0u);
                         if (more) {
                             if (!k_next) {
                                 if (!(ok = mbar_wait(BAR(B_KFULL + sn), ((kv + j + 1) >> 1) & 1u, abort, a.err,

@@ -150,6 +150,67 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// One 128x128x128 tile as 8 back-to-back K=16 MMAs in a single asm block,
+// both operands 128B-swizzled K-major in shared memory: the descriptor start
+// address advances +2 (32 B) per step and +1024 (16 KB, the second 64-element
+// box) after four steps. Straight-line issue keeps the tensor core fed (a
+// loop or branch between MMAs of the same accumulator leaves it idle).
+// acc_first = 0 overwrites D with the first product.
+__device__ __forceinline__ void mma_tile_ss_k128(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t acc_first)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b64 a, b;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 1024;\n\tadd.s64 b, %2, 1024;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 1026;\n\tadd.s64 b, %2, 1026;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 1028;\n\tadd.s64 b, %2, 1028;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 1030;\n\tadd.s64 b, %2, 1030;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
+        : "memory");
+}
+
+// One 128x128x128 tile O (+)= P V as 8 K=16 MMAs in a single asm block: A = P
+// in TMEM (8 columns per step), B = V 128B-swizzled MN-major in shared memory
+// (16 key rows = 2 KB = +128 per step).
+__device__ __forceinline__ void mma_tile_ts_k128(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t acc_first)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a;\n\t.reg .b64 b;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+        "add.u32 a, %1, 8;\n\tadd.s64 b, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 16;\n\tadd.s64 b, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc_first)
+        : "memory");
+}
+
 // Arrive on `bar` once all previously issued tcgen05 async ops of this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar)
 {
