@@ -60,8 +60,11 @@ constexpr uint32_t kTileBytes = 2 * kBoxBytes;       // 128 rows x 128 head dims
 constexpr uint32_t kOffQ = 0;                        // kQT tiles
 constexpr uint32_t kOffK = kOffQ + kQT * kTileBytes; // kStages tiles
 constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
+constexpr uint32_t kStageBytes = 16 * 256;            // epilogue staging per softmax warp: 16 rows x 256 B
+constexpr uint32_t kOffStage = kOffV + kStages * kTileBytes;
+constexpr uint32_t kOffBar = kOffStage + 4 * kQT * kStageBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + 1 KB alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 enum Bar {
     B_QFULL = 0,                   // [kQT] Q_i landed
@@ -414,29 +417,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(BAR(B_OFREE + g));  // O_i may be overwritten by the next item
+            // Output rows go out through a per-warp shared staging buffer, 16 rows
+            // at a time, so that each warp store instruction writes two whole
+            // 256-byte rows instead of 32 scattered 16-byte pieces.
             const int qrow = it.q0 + g * kBM + r;
+            uint16_t *dst_row = nullptr;
             if (qrow < it.S) {
-                const float inv = 1.f / l;
-                uint4 *dst;
-                if (qrow < it.Lw) {
-                    const int gr = a.rows[it.seq0 + qrow].src;
-                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.vid_out) + static_cast<size_t>(gr) * dim +
-                                                    it.head * kHD);
-                } else {
-                    dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.txt_partial) +
-                                                    (static_cast<size_t>(it.win) * a.text_len + (qrow - it.Lw)) * dim +
-                                                    it.head * kHD);
-                }
+                if (qrow < it.Lw)
+                    dst_row = static_cast<uint16_t *>(a.vid_out) +
+                              static_cast<size_t>(a.rows[it.seq0 + qrow].src) * dim + it.head * kHD;
+                else
+                    dst_row = static_cast<uint16_t *>(a.txt_partial) +
+                              (static_cast<size_t>(it.win) * a.text_len + (qrow - it.Lw)) * dim + it.head * kHD;
+            }
+            const float inv = 1.f / l;
+            uint4 packed[16];
 #pragma unroll
-                for (int c16 = 0; c16 < 16; ++c16) {
-                    const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
-                    uint4 w;
-                    w.x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
-                    w.y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
-                    w.z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
-                    w.w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
-                    dst[c16] = w;
+            for (int c16 = 0; c16 < 16; ++c16) {
+                const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
+                packed[c16].x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
+                packed[c16].y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
+                packed[c16].z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
+                packed[c16].w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
+            }
+            uint4 *stage = reinterpret_cast<uint4 *>(gbase + kOffStage + static_cast<uint32_t>(warp) * kStageBytes);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int srow = lane - 16 * half;  // this lane's row inside the staged half
+                if (srow >= 0 && srow < 16) {
+#pragma unroll
+                    for (int c16 = 0; c16 < 16; ++c16) stage[srow * 16 + (c16 ^ (srow & 7))] = packed[c16];
                 }
+                __syncwarp();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int row = 2 * k + (lane >> 4), chunk = lane & 15;
+                    const unsigned long long pa =
+                        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst_row), 16 * half + row);
+                    const uint4 v4 = stage[row * 16 + (chunk ^ (row & 7))];
+                    if (pa) reinterpret_cast<uint4 *>(pa)[chunk] = v4;
+                }
+                __syncwarp();
             }
         }
     }

@@ -86,8 +86,10 @@ struct Load8<__nv_bfloat16> {
 // 3e-8. Both attention GEMMs then run as f16 x f16 on the tensor cores.
 __device__ __forceinline__ uint32_t pack2(float a, float b)
 {
-    const __nv_bfloat16 ra = __float2bfloat16_rn(a), rb = __float2bfloat16_rn(b);
-    const __half2 h = __floats2half2_rn(__bfloat162float(ra), __bfloat162float(rb));
+    // one packed bf16x2 conversion (RNE) for both values, then one f16x2 pack
+    const __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(&r);
+    const __half2 h = __floats2half2_rn(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
