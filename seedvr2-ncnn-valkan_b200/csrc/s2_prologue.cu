@@ -8,9 +8,11 @@
 // (seedvr2_dit_block.cpp:942-1028). Every multiply/add of the normalisation
 // and rotation uses explicitly rounded intrinsics so nothing is contracted
 // into an FMA, matching the reference's float arithmetic step by step.
-// Memory: 16 threads per (row, head), each moving 8 consecutive elements with
-// 128-bit loads/stores; consecutive thread groups cover consecutive heads of
-// a row, so a warp reads/writes 2 x 256 contiguous bytes per tensor.
+// Work split: 8 lanes per (row, head), each owning two 8-element chunks of the
+// 128 head dims (so a warp covers 4 heads of a row and every per-(row, head)
+// fixed cost -- the fp64 sum reduction, the IEEE sqrt and divide -- is paid
+// once per 16 elements per lane); every 8-lane group moves full 128-byte lines
+// with 128-bit loads and stores.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -102,15 +104,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
                                                            uint4 *__restrict__ q, uint4 *__restrict__ k,
                                                            uint4 *__restrict__ v)
 {
+    // 8 lanes per (row, head); lane `sub` owns dims [64c + 8 sub, 64c + 8 sub + 8) for c = 0, 1.
     const int dim = heads * kHD;
-    const int sub = threadIdx.x & 15;  // 8-element chunk within the head
+    const int sub = threadIdx.x & 7;
     const long long n_pairs = 1LL * n_rows * heads;
-    const long long stride = 1LL * gridDim.x * (blockDim.x >> 4);
-    // The loop bound is uniform per warp (both 16-lane halves iterate together,
-    // because of the half-warp shuffles); an out-of-range half only skips I/O.
-    const long long half = (threadIdx.x >> 4) & 1;
-    for (long long pr = 1LL * blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4); pr - half < n_pairs;
-         pr += stride) {
+    const long long per_block = blockDim.x >> 3;
+    const long long stride = 1LL * gridDim.x * per_block;
+    const long long lane_grp = (threadIdx.x >> 3) & 3;  // pair slot inside the warp
+    for (long long pr = 1LL * blockIdx.x * per_block + (threadIdx.x >> 3); pr - lane_grp < n_pairs; pr += stride) {
         const bool active = pr < n_pairs;
         const long long prc = active ? pr : n_pairs - 1;
         const int row = static_cast<int>(prc / heads);
@@ -123,66 +124,109 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
         const float *gq = gammas + (text ? 2 : 0) * kHD + sub * 8;
         const float *gk = gq + kHD;
 
-        float xq[8], xk[8], xv[8];
-        Load8<TIn>::run(src, xq);
-        Load8<TIn>::run(src + dim, xk);
-        Load8<TIn>::run(src + 2 * dim, xv);
-
+        float xq[2][8], xk[2][8], xv[2][8];
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            Load8<TIn>::run(src + 64 * c, xq[c]);
+            Load8<TIn>::run(src + dim + 64 * c, xk[c]);
+            Load8<TIn>::run(src + 2 * dim + 64 * c, xv[c]);
+        }
         double sq = 0.0, sk = 0.0;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            sq += static_cast<double>(xq[i]) * xq[i];
-            sk += static_cast<double>(xk[i]) * xk[i];
-        }
+        for (int c = 0; c < 2; c++)
 #pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) {
-            sq += __shfl_xor_sync(0xffffffffu, sq, o, 16);
-            sk += __shfl_xor_sync(0xffffffffu, sk, o, 16);
+            for (int i = 0; i < 8; i++) {
+                sq += static_cast<double>(xq[c][i]) * xq[c][i];
+                sk += static_cast<double>(xk[c][i]) * xk[c][i];
+            }
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o, 8);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o, 8);
         }
         const float inv_q = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(static_cast<float>(sq / kHD), eps)));
         const float inv_k = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(static_cast<float>(sk / kHD), eps)));
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            xq[i] = __fmul_rn(__fmul_rn(xq[i], inv_q), __ldg(gq + i));
-            xk[i] = __fmul_rn(__fmul_rn(xk[i], inv_k), __ldg(gk + i));
-        }
-        // pairs (d, d+1), d = 2 * gp; gp = axis * 21 + p covers gp < 63 (dims 0..125)
+        for (int c = 0; c < 2; c++) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int gp = sub * 4 + i;
-            if (gp < 3 * kPairs) {
-                const int axis = gp / kPairs, pair = gp - axis * kPairs;
-                const int pos = axis == 0 ? rd.pt : (axis == 1 ? rd.ph : rd.pw);
-                const float2 cs = __ldg(table + pos * kPairs + pair);
-                const float a = xq[2 * i], b = xq[2 * i + 1];
-                xq[2 * i] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-                xq[2 * i + 1] = __fadd_rn(__fmul_rn(b, cs.x), __fmul_rn(a, cs.y));
-                const float c = xk[2 * i], d = xk[2 * i + 1];
-                xk[2 * i] = __fsub_rn(__fmul_rn(c, cs.x), __fmul_rn(d, cs.y));
-                xk[2 * i + 1] = __fadd_rn(__fmul_rn(d, cs.x), __fmul_rn(c, cs.y));
+            for (int i = 0; i < 8; i++) {
+                xq[c][i] = __fmul_rn(__fmul_rn(xq[c][i], inv_q), __ldg(gq + 64 * c + i));
+                xk[c][i] = __fmul_rn(__fmul_rn(xk[c][i], inv_k), __ldg(gk + 64 * c + i));
+            }
+            // pairs (d, d+1), d = 2 * gp; gp = axis * 21 + p covers gp < 63 (dims 0..125)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int gp = 32 * c + sub * 4 + i;
+                if (gp < 3 * kPairs) {
+                    const int axis = gp / kPairs, pair = gp - axis * kPairs;
+                    const int pos = axis == 0 ? rd.pt : (axis == 1 ? rd.ph : rd.pw);
+                    const float2 cs = __ldg(table + pos * kPairs + pair);
+                    const float a0 = xq[c][2 * i], b0 = xq[c][2 * i + 1];
+                    xq[c][2 * i] = __fsub_rn(__fmul_rn(a0, cs.x), __fmul_rn(b0, cs.y));
+                    xq[c][2 * i + 1] = __fadd_rn(__fmul_rn(b0, cs.x), __fmul_rn(a0, cs.y));
+                    const float c0 = xk[c][2 * i], d0 = xk[c][2 * i + 1];
+                    xk[c][2 * i] = __fsub_rn(__fmul_rn(c0, cs.x), __fmul_rn(d0, cs.y));
+                    xk[c][2 * i + 1] = __fadd_rn(__fmul_rn(d0, cs.x), __fmul_rn(c0, cs.y));
+                }
             }
         }
         if (!active) continue;
         const size_t o = (static_cast<size_t>(head) * n_rows + row) * (kHD / 8) + sub;
-        q[o] = make_uint4(pack2(xq[0], xq[1]), pack2(xq[2], xq[3]), pack2(xq[4], xq[5]),
-                          pack2(xq[6], xq[7]));
-        k[o] = make_uint4(pack2(xk[0], xk[1]), pack2(xk[2], xk[3]), pack2(xk[4], xk[5]),
-                          pack2(xk[6], xk[7]));
-        v[o] = make_uint4(pack2(xv[0], xv[1]), pack2(xv[2], xv[3]), pack2(xv[4], xv[5]),
-                          pack2(xv[6], xv[7]));
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            q[o + 8 * c] = make_uint4(pack2(xq[c][0], xq[c][1]), pack2(xq[c][2], xq[c][3]), pack2(xq[c][4], xq[c][5]),
+                                      pack2(xq[c][6], xq[c][7]));
+            k[o + 8 * c] = make_uint4(pack2(xk[c][0], xk[c][1]), pack2(xk[c][2], xk[c][3]), pack2(xk[c][4], xk[c][5]),
+                                      pack2(xk[c][6], xk[c][7]));
+            v[o + 8 * c] = make_uint4(pack2(xv[c][0], xv[c][1]), pack2(xv[c][2], xv[c][3]), pack2(xv[c][4], xv[c][5]),
+                                      pack2(xv[c][6], xv[c][7]));
+        }
     }
 }
 
-// txt_out[i] = (sum_w partial[w][i]) * scale, window order, fp32 accumulation.
-template <typename T>
-__global__ void text_window_sum_kernel(const T *__restrict__ partial, int n_windows, long long n, float scale,
-                                       int accumulate, float *__restrict__ out)
+// txt_out[i] = (sum_w partial[w][i]) * scale: windows added in order in fp32,
+// the reference's summation order (seedvr2_dit_block.cpp:1075, :1081-1088).
+// Each thread owns 8 consecutive elements (one 128-bit load per window).
+__device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8], bool f16)
 {
-    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
-        float acc = 0.f;
-        for (int w = 0; w < n_windows; w++) acc = __fadd_rn(acc, static_cast<float>(partial[w * n + i]));
-        acc = __fmul_rn(acc, scale);
-        out[i] = accumulate ? __fadd_rn(out[i], acc) : acc;
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        if (f16) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        } else {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+}
+
+template <bool kF16>
+__global__ void text_window_sum_kernel(const uint4 *__restrict__ partial, int n_windows, long long n8, float scale,
+                                       int accumulate, float4 *__restrict__ out)
+{
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += 256LL * gridDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int w = 0; w < n_windows; w++) {
+            float f[8];
+            unpack8(__ldg(partial + w * n8 + i), f, kF16);
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], f[e]);
+        }
+        float4 lo = make_float4(__fmul_rn(acc[0], scale), __fmul_rn(acc[1], scale), __fmul_rn(acc[2], scale),
+                                __fmul_rn(acc[3], scale));
+        float4 hi = make_float4(__fmul_rn(acc[4], scale), __fmul_rn(acc[5], scale), __fmul_rn(acc[6], scale),
+                                __fmul_rn(acc[7], scale));
+        if (accumulate) {
+            const float4 a = out[2 * i], b = out[2 * i + 1];
+            lo = make_float4(__fadd_rn(a.x, lo.x), __fadd_rn(a.y, lo.y), __fadd_rn(a.z, lo.z), __fadd_rn(a.w, lo.w));
+            hi = make_float4(__fadd_rn(b.x, hi.x), __fadd_rn(b.y, hi.y), __fadd_rn(b.z, hi.z), __fadd_rn(b.w, hi.w));
+        }
+        out[2 * i] = lo;
+        out[2 * i + 1] = hi;
     }
 }
 
@@ -239,7 +283,7 @@ extern "C" s2_status s2_qk_norm_rope(void *stream, const void *vid_qkv, const vo
         return s2::set_error(S2_UNSUPPORTED, "s2_qk_norm_rope: unknown mode %d", (int)mode);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long pairs = 1LL * n_rows * heads;
-    const long long want = (pairs + 15) / 16;
+    const long long want = (pairs + 31) / 32;
     const int grid = static_cast<int>(want < 16LL * sm_count() ? want : 16LL * sm_count());
     auto *Q = static_cast<uint4 *>(q);
     auto *K = static_cast<uint4 *>(k);
@@ -268,15 +312,17 @@ extern "C" s2_status s2_text_window_sum(void *stream, s2_mode mode, const void *
     if (text_len == 0) return S2_OK;
     if (!txt_partial || !txt_out || n_windows <= 0 || text_len < 0 || dim <= 0)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_text_window_sum: invalid arguments");
+    if (dim % 8 != 0 || !aligned16(txt_partial) || !aligned16(txt_out))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_text_window_sum: dim must be a multiple of 8, buffers 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const long long n = 1LL * text_len * dim;
-    const int grid = static_cast<int>((n + 255) / 256 < 4LL * sm_count() ? (n + 255) / 256 : 4LL * sm_count());
+    const long long n8 = 1LL * text_len * dim / 8;
+    const int grid = static_cast<int>((n8 + 255) / 256 < 4LL * sm_count() ? (n8 + 255) / 256 : 4LL * sm_count());
     if (mode == S2_MODE_F16)
-        text_window_sum_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(txt_partial), n_windows, n,
-                                                             scale, accumulate, txt_out);
+        text_window_sum_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4 *>(txt_partial), n_windows, n8,
+                                                           scale, accumulate, reinterpret_cast<float4 *>(txt_out));
     else
-        text_window_sum_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-            static_cast<const __nv_bfloat16 *>(txt_partial), n_windows, n, scale, accumulate, txt_out);
+        text_window_sum_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4 *>(txt_partial), n_windows, n8,
+                                                            scale, accumulate, reinterpret_cast<float4 *>(txt_out));
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_text_window_sum: launch failed: %s", cudaGetErrorString(e));
