@@ -186,47 +186,19 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
 
 // txt_out[i] = (sum_w partial[w][i]) * scale: windows added in order in fp32,
 // the reference's summation order (seedvr2_dit_block.cpp:1075, :1081-1088).
-// Each thread owns 8 consecutive elements (one 128-bit load per window).
-__device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8], bool f16)
+// One element per thread (the most loads in flight for a latency-bound
+// in-order chain); the window loop is unrolled 16 deep so the loads of many
+// windows are issued ahead of the in-order adds.
+template <typename T>
+__global__ void text_window_sum_kernel(const T *__restrict__ partial, int n_windows, long long n, float scale,
+                                       int accumulate, float *__restrict__ out)
 {
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        if (f16) {
-            const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
-            f[2 * i] = t.x;
-            f[2 * i + 1] = t.y;
-        } else {
-            f[2 * i] = __uint_as_float(w[i] << 16);
-            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        }
-    }
-}
-
-template <bool kF16>
-__global__ void text_window_sum_kernel(const uint4 *__restrict__ partial, int n_windows, long long n8, float scale,
-                                       int accumulate, float4 *__restrict__ out)
-{
-    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += 256LL * gridDim.x) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int w = 0; w < n_windows; w++) {
-            float f[8];
-            unpack8(__ldg(partial + w * n8 + i), f, kF16);
-#pragma unroll
-            for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], f[e]);
-        }
-        float4 lo = make_float4(__fmul_rn(acc[0], scale), __fmul_rn(acc[1], scale), __fmul_rn(acc[2], scale),
-                                __fmul_rn(acc[3], scale));
-        float4 hi = make_float4(__fmul_rn(acc[4], scale), __fmul_rn(acc[5], scale), __fmul_rn(acc[6], scale),
-                                __fmul_rn(acc[7], scale));
-        if (accumulate) {
-            const float4 a = out[2 * i], b = out[2 * i + 1];
-            lo = make_float4(__fadd_rn(a.x, lo.x), __fadd_rn(a.y, lo.y), __fadd_rn(a.z, lo.z), __fadd_rn(a.w, lo.w));
-            hi = make_float4(__fadd_rn(b.x, hi.x), __fadd_rn(b.y, hi.y), __fadd_rn(b.z, hi.z), __fadd_rn(b.w, hi.w));
-        }
-        out[2 * i] = lo;
-        out[2 * i + 1] = hi;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+        float acc = 0.f;
+#pragma unroll 16
+        for (int w = 0; w < n_windows; w++) acc = __fadd_rn(acc, static_cast<float>(partial[w * n + i]));
+        acc = __fmul_rn(acc, scale);
+        out[i] = accumulate ? __fadd_rn(out[i], acc) : acc;
     }
 }
 
@@ -312,17 +284,15 @@ extern "C" s2_status s2_text_window_sum(void *stream, s2_mode mode, const void *
     if (text_len == 0) return S2_OK;
     if (!txt_partial || !txt_out || n_windows <= 0 || text_len < 0 || dim <= 0)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_text_window_sum: invalid arguments");
-    if (dim % 8 != 0 || !aligned16(txt_partial) || !aligned16(txt_out))
-        return s2::set_error(S2_INVALID_ARGUMENT, "s2_text_window_sum: dim must be a multiple of 8, buffers 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const long long n8 = 1LL * text_len * dim / 8;
-    const int grid = static_cast<int>((n8 + 255) / 256 < 4LL * sm_count() ? (n8 + 255) / 256 : 4LL * sm_count());
+    const long long n = 1LL * text_len * dim;
+    const int grid = static_cast<int>((n + 255) / 256 < 8LL * sm_count() ? (n + 255) / 256 : 8LL * sm_count());
     if (mode == S2_MODE_F16)
-        text_window_sum_kernel<true><<<grid, 256, 0, st>>>(static_cast<const uint4 *>(txt_partial), n_windows, n8,
-                                                           scale, accumulate, reinterpret_cast<float4 *>(txt_out));
+        text_window_sum_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(txt_partial), n_windows, n,
+                                                             scale, accumulate, txt_out);
     else
-        text_window_sum_kernel<false><<<grid, 256, 0, st>>>(static_cast<const uint4 *>(txt_partial), n_windows, n8,
-                                                            scale, accumulate, reinterpret_cast<float4 *>(txt_out));
+        text_window_sum_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(txt_partial), n_windows, n, scale, accumulate, txt_out);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_text_window_sum: launch failed: %s", cudaGetErrorString(e));
