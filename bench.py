@@ -193,17 +193,6 @@ def workload_config(args):
                         "one clip per rank (weak)"}
 
 
-def lpt_assign(costs, n_ranks):
-    order = np.argsort(-np.asarray(costs), kind="stable")
-    load = np.zeros(n_ranks)
-    owner = np.zeros(len(costs), np.int32)
-    for i in order:
-        r = int(np.argmin(load))
-        owner[i] = r
-        load[r] += costs[i]
-    return owner
-
-
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -231,10 +220,9 @@ def run_ours(args, rank, world, local_rank):
     plans = []
     for shifted in (0, 1):
         wins = s2b200.make_windows(T, H, W, shifted, override)
-        sizes = (wins[:, 1] - wins[:, 0]) * (wins[:, 3] - wins[:, 2]) * (wins[:, 5] - wins[:, 4]) + Lt
         ids = np.arange(len(wins))
         if args.shard and world > 1:
-            ids = np.nonzero(lpt_assign(sizes.astype(np.float64) ** 2, world) == rank)[0]
+            ids = s2b200.shard_windows(wins, Lt, world)[rank]
         local = wins[ids]
         cu, rows = s2b200.build_varlen(T, H, W, local, Lt)
         work = s2b200.plan_work(cu)
@@ -398,9 +386,7 @@ def run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, 
         lay.load_param(shifted=shifted, dim=dim, heads=heads)
         lay.load_model(gam[0], gam[1], fr, gam[2], gam[3])
         if args.shard and world > 1:
-            wins = s2b200.make_windows(T, H, W, shifted, override)
-            sizes = (wins[:, 1] - wins[:, 0]) * (wins[:, 3] - wins[:, 2]) * (wins[:, 5] - wins[:, 4]) + Lt
-            lay.set_window_subset(np.nonzero(lpt_assign(sizes.astype(np.float64) ** 2, world) == rank)[0])
+            lay.set_window_subset(s2b200.shard_windows(s2b200.make_windows(T, H, W, shifted, override), Lt, world)[rank])
         layers.append(lay)
     vid_np, txt_np, _, _ = synth.layer_inputs(grid, heads=heads, text_len=Lt, seed=666 + rank)
     hv = torch.from_numpy(vid_np.astype(np.float16)).pin_memory().numpy()

@@ -149,6 +149,29 @@ def plan_work(cu_seqlens: np.ndarray) -> np.ndarray:
     return work[:n.value]
 
 
+def window_costs(windows: np.ndarray, text_len: int) -> np.ndarray:
+    """Attention cost of each window, proportional to S_w^2 with S_w = L_w + text_len."""
+    w = np.asarray(windows)
+    s = (w[:, 1] - w[:, 0]) * (w[:, 3] - w[:, 2]) * (w[:, 5] - w[:, 4]) + text_len
+    return s.astype(np.float64) ** 2
+
+
+def shard_windows(windows: np.ndarray, text_len: int, n_ranks: int) -> list[np.ndarray]:
+    """Deterministic longest-processing-time assignment of a layer's windows to
+    ranks (cost S_w^2, ties to the lowest rank). Every window goes to exactly one
+    rank, so every video token has exactly one owner; returns the sorted window
+    ids of each rank."""
+    costs = window_costs(windows, text_len)
+    order = np.argsort(-costs, kind="stable")
+    load = np.zeros(n_ranks)
+    owner = np.zeros(len(costs), np.int32)
+    for i in order:
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += costs[i]
+    return [np.nonzero(owner == r)[0].astype(np.int32) for r in range(n_ranks)]
+
+
 # ---- device helpers (torch tensors as plumbing) ------------------------------
 
 def _torch():
