@@ -134,6 +134,14 @@ __device__ __forceinline__ Item decode_item(const AttnArgs &a, int t)
     return it;
 }
 
+// 3-input max (one ALU instruction for two new values)
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t pack_p(float a, float b)
 {
     const __half2 h = __floats2half2_rn(a, b);
@@ -362,7 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(x[cc][i]));
+                    for (int i = 0; i < 32; i += 2)
+                        mx4[(i >> 1) & 3] = max3f(mx4[(i >> 1) & 3], __uint_as_float(x[cc][i]), __uint_as_float(x[cc][i + 1]));
                 const float cand = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * c;
                 float m_use = m, alpha = 1.f;
                 bool rescale = false;
@@ -385,22 +394,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_st32(ocol + cc * 32, o);
                     }
                 }
-                float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+                // packed fp32x2 FMA/add halve the instruction count of the exp loop
+                float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float p0 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i]), c, -m_use));
-                        const float p1 = ex2_approx(fmaf(__uint_as_float(x[cc][2 * i + 1]), c, -m_use));
-                        rs4[(2 * i) & 3] += p0;
-                        rs4[(2 * i + 1) & 3] += p1;
-                        pk[i] = pack_p(p0, p1);
+                        const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(x[cc][2 * i]), __uint_as_float(x[cc][2 * i + 1])), c2, nm2);
+                        float2 p2;
+                        p2.x = ex2_approx(a2.x);
+                        p2.y = ex2_approx(a2.y);
+                        rs2[i & 3] = __fadd2_rn(rs2[i & 3], p2);
+                        pk[i] = pack_p(p2.x, p2.y);
                     }
                     tmem_st16(pcol + cc * 16, pk);
                 }
                 tmem_wait_st();
-                l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+                l = l * alpha + (((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) + ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y)));
                 m = m_use;
                 tc_fence_before();
                 mbar_arrive(BAR(B_PFULL + g));
