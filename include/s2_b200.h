@@ -206,6 +206,52 @@ S2_API int s2_attention_layer_last_launches(const s2_attention_layer *layer);
  * Returns S2_INFERENCE_FAILED when the word is set or the stream failed. */
 S2_API s2_status s2_attention_layer_device_error(s2_attention_layer *layer, int *code);
 
+/* ---- VAE mid-block spatial attention ------------------------------------ */
+
+/* Single-head attention per frame, the core of the VAE mid-block attention
+ * (DynamicFramewiseSpatialAttention::forward,
+ * src/layers/dynamic_framewise_spatial_attention.cpp:149-180; Vulkan
+ * attention pipeline :599-775): for every frame f and query token t,
+ * out[f*tokens + t] = softmax_k(q[f*tokens + t] . k[f*tokens + k] / sqrt(channels)) v.
+ * q, k, v, out: device fp16 [frames*tokens][head_dim] row-major, head_dim =
+ * channels padded to 128, 256 or 512 with zero columns (the padded output
+ * columns come out zero). tcgen05 MMA into TMEM, fp32 accumulation, P fp16.
+ * err: device int32 error word, set on a device-side timeout. */
+S2_API s2_status s2_spatial_attention(void *stream, const void *q, const void *k, const void *v, int channels,
+                                      int head_dim, int frames, int tokens, void *out, int32_t *err);
+
+typedef struct s2_vae_attention s2_vae_attention;
+
+/* load_param (dynamic_framewise_spatial_attention.cpp:50-59): channels must
+ * be a positive multiple of 32 (GroupNorm with 32 groups); this build
+ * supports channels <= 512. */
+S2_API s2_status s2_vae_attention_create(int device, int channels, s2_vae_attention **out);
+S2_API s2_status s2_vae_attention_destroy(s2_vae_attention *layer);
+
+/* load_model (:61-77): host fp32 arrays in the reference's load order;
+ * weights are [out][in] = channels x channels. */
+S2_API s2_status s2_vae_attention_load(s2_vae_attention *layer, const float *norm_bias, const float *norm_weight,
+                                       const float *k_bias, const float *k_weight, const float *out_bias,
+                                       const float *out_weight, const float *q_bias, const float *q_weight,
+                                       const float *v_bias, const float *v_weight);
+
+/* forward (:106-210) on DEVICE buffers in ncnn's 4-D layout: x and y are fp32
+ * [channels][cstep], channel plane = frames x height x width (cstep >=
+ * frames*height*width). GroupNorm(32, eps 1e-6) per frame, Q/K/V 1x1
+ * projections, attention, output projection + residual: y = x + proj(attn).
+ * Stream-ordered, no host synchronisation; x and y must not alias. */
+S2_API s2_status s2_vae_attention_forward(s2_vae_attention *layer, void *stream, const float *x, int frames,
+                                          int height, int width, long long cstep, float *y);
+
+/* Same on HOST buffers (the ncnn::Mat contract); copies in and out and
+ * synchronises `stream`. */
+S2_API s2_status s2_vae_attention_forward_host(s2_vae_attention *layer, void *stream, const float *x, int frames,
+                                               int height, int width, long long cstep, float *y);
+
+/* Kernels launched by the last forward, and the device error word (0 = ok). */
+S2_API int s2_vae_attention_last_launches(const s2_vae_attention *layer);
+S2_API s2_status s2_vae_attention_device_error(s2_vae_attention *layer, int *code);
+
 /* ---- allocation-free variant -------------------------------------------- */
 
 /* Limits of the fixed scratch used by s2_dit_window_attention_noalloc

@@ -70,6 +70,9 @@ class Port(_Lib):
             + [_f32p] * 6)
         L.s2o_vae_attention.restype = ctypes.c_int
         L.s2o_vae_attention.argtypes = [ctypes.c_int] * 4 + [_f32p] * 11 + [ctypes.c_int] * 3 + [_f32p]
+        L.s2o_vae_attention_tokens.restype = ctypes.c_int
+        L.s2o_vae_attention_tokens.argtypes = ([ctypes.c_int] * 4 + [_f32p] * 11 + [ctypes.c_int]
+                                               + [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 2 + [_f32p])
 
     def make_windows(self, T, H, W, shifted, override=(0, 0, 0)):
         n = self.lib.s2o_make_windows(T, H, W, int(shifted), *override, None, 0)
@@ -118,6 +121,22 @@ class Port(_Lib):
                                         int(threads or os.cpu_count() or 1), _ptr(y))
         if rc != 0:
             raise ValueError(f"s2o_vae_attention failed: {rc}")
+        return y
+
+    def vae_attention_tokens(self, x, weights, frame, tokens, threads=0):
+        """y rows [len(tokens), C] of one frame for the selected query tokens (h*W + w)."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        order = ["norm_bias", "norm_weight", "k_bias", "k_weight", "out_bias", "out_weight",
+                 "q_bias", "q_weight", "v_bias", "v_weight"]
+        ws = [_f32(weights[k]) for k in order]
+        sel = np.ascontiguousarray(tokens, dtype=np.int32)
+        y = np.zeros((sel.size, C), np.float32)
+        rc = self.lib.s2o_vae_attention_tokens(C, T, H, W, *[_ptr(w) for w in ws], _ptr(x), int(frame),
+                                               sel.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), int(sel.size),
+                                               int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"s2o_vae_attention_tokens failed: {rc}")
         return y
 
 

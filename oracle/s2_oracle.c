@@ -313,3 +313,93 @@ int s2o_vae_attention(int channels, int frames, int height, int width,
     free(nrm); free(qm); free(km); free(vm); free(att); free(prj);
     return 0;
 }
+
+/* The same layer evaluated for a subset of query tokens of one frame
+ * (dynamic_framewise_spatial_attention.cpp:115-194 restricted to the output
+ * rows `tokens_sel`): GroupNorm statistics and the K/V projections cover the
+ * whole frame, Q, attention, output projection and residual only the listed
+ * tokens. x is dense [C][T][H][W]; y_sel receives [n_sel][C] (token-major).
+ * Exists so that full-size frames (14,400 tokens at C = 512) can be checked
+ * in seconds. */
+int s2o_vae_attention_tokens(int channels, int frames, int height, int width,
+                             const float *norm_bias, const float *norm_weight,
+                             const float *k_bias, const float *k_weight,
+                             const float *out_bias, const float *out_weight,
+                             const float *q_bias, const float *q_weight,
+                             const float *v_bias, const float *v_weight,
+                             const float *x, int frame, const int *tokens_sel, int n_sel, int num_threads,
+                             float *y_sel)
+{
+    if (channels <= 0 || channels % 32 != 0 || frame < 0 || frame >= frames || n_sel <= 0) return -1;
+    const int tokens = height * width;
+    const int cpg = channels / 32;
+    const float scale = 1.f / sqrtf((float)channels);
+    const size_t plane = (size_t)frames * tokens;
+    const size_t n = (size_t)tokens * channels;
+    for (int i = 0; i < n_sel; i++)
+        if (tokens_sel[i] < 0 || tokens_sel[i] >= tokens) return -1;
+    float *nrm = (float *)malloc(sizeof(float) * n);
+    float *km = (float *)malloc(sizeof(float) * n);
+    float *vm = (float *)malloc(sizeof(float) * n);
+    float *qs = (float *)malloc(sizeof(float) * (size_t)n_sel * channels);
+    float *as = (float *)calloc((size_t)n_sel * channels, sizeof(float));
+    float *nsel = (float *)malloc(sizeof(float) * (size_t)n_sel * channels);
+    float *ps = (float *)malloc(sizeof(float) * (size_t)n_sel * channels);
+    for (int g = 0; g < 32; g++) {
+        double sum = 0.0, sq = 0.0;
+        for (int lc = 0; lc < cpg; lc++) {
+            const float *in = x + plane * (size_t)(g * cpg + lc) + (size_t)frame * tokens;
+            for (int t = 0; t < tokens; t++) {
+                sum += in[t];
+                sq += (double)in[t] * in[t];
+            }
+        }
+        const int count = cpg * tokens;
+        const float mean = (float)(sum / count);
+        const float var = (float)(sq / count - (double)mean * mean);
+        const float inv_std = 1.f / sqrtf((var > 0.f ? var : 0.f) + 1e-6f);
+        for (int lc = 0; lc < cpg; lc++) {
+            const int c = g * cpg + lc;
+            const float *in = x + plane * (size_t)c + (size_t)frame * tokens;
+            const float sc = norm_weight[c] * inv_std;
+            const float off = norm_bias[c] - mean * sc;
+            for (int t = 0; t < tokens; t++) nrm[(size_t)t * channels + c] = in[t] * sc + off;
+        }
+    }
+    vae_linear(nrm, km, k_weight, k_bias, tokens, channels, num_threads);
+    vae_linear(nrm, vm, v_weight, v_bias, tokens, channels, num_threads);
+    for (int i = 0; i < n_sel; i++)
+        memcpy(nsel + (size_t)i * channels, nrm + (size_t)tokens_sel[i] * channels, sizeof(float) * channels);
+    vae_linear(nsel, qs, q_weight, q_bias, n_sel, channels, num_threads);
+#pragma omp parallel for num_threads(num_threads > 0 ? num_threads : 1)
+    for (int i = 0; i < n_sel; i++) {
+        float *sc = (float *)malloc(sizeof(float) * (size_t)tokens);
+        float mx = -INFINITY;
+        for (int kt = 0; kt < tokens; kt++) {
+            double s = 0.0;
+            for (int c = 0; c < channels; c++)
+                s += (double)qs[(size_t)i * channels + c] * km[(size_t)kt * channels + c];
+            sc[kt] = (float)s * scale;
+            if (sc[kt] > mx) mx = sc[kt];
+        }
+        double den = 0.0;
+        for (int kt = 0; kt < tokens; kt++) {
+            sc[kt] = expf(sc[kt] - mx);
+            den += sc[kt];
+        }
+        float *orow = as + (size_t)i * channels;
+        for (int kt = 0; kt < tokens; kt++) {
+            const float p = (float)(sc[kt] / den);
+            const float *vr = vm + (size_t)kt * channels;
+            for (int c = 0; c < channels; c++) orow[c] += p * vr[c];
+        }
+        free(sc);
+    }
+    vae_linear(as, ps, out_weight, out_bias, n_sel, channels, num_threads);
+    for (int i = 0; i < n_sel; i++)
+        for (int c = 0; c < channels; c++)
+            y_sel[(size_t)i * channels + c] =
+                ps[(size_t)i * channels + c] + x[plane * (size_t)c + (size_t)frame * tokens + tokens_sel[i]];
+    free(nrm); free(km); free(vm); free(qs); free(as); free(nsel); free(ps);
+    return 0;
+}

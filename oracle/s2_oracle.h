@@ -63,6 +63,17 @@ int s2o_vae_attention(int channels, int frames, int height, int width,
                       const float *v_bias, const float *v_weight,
                       const float *x, int frame_begin, int frame_end, int num_threads, float *y);
 
+/* The same layer for the query tokens tokens_sel[0..n_sel) of one frame only
+ * (full GroupNorm statistics and K/V); y_sel [n_sel][C]. Returns 0 or -1. */
+int s2o_vae_attention_tokens(int channels, int frames, int height, int width,
+                             const float *norm_bias, const float *norm_weight,
+                             const float *k_bias, const float *k_weight,
+                             const float *out_bias, const float *out_weight,
+                             const float *q_bias, const float *q_weight,
+                             const float *v_bias, const float *v_weight,
+                             const float *x, int frame, const int *tokens_sel, int n_sel, int num_threads,
+                             float *y_sel);
+
 #ifdef __cplusplus
 }
 #endif

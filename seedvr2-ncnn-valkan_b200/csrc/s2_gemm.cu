@@ -1,0 +1,284 @@
+// Dense GEMM D = A B^T for sm_100a (tcgen05 MMA into TMEM, TMA-fed 4-stage
+// shared-memory ring), used for the 1x1 projections around the VAE mid-block
+// attention (DynamicFramewiseSpatialAttention's linear(),
+// dynamic_framewise_spatial_attention.cpp:79-103: Q/K/V and the output
+// projection with its residual, :145-147 and :185-194).
+//
+// Tiles are 128 rows x 256 columns with K streamed in 64-element slices
+// (A slice 16 KB + B slice 32 KB per stage); each slice is 4 K=16 MMAs of
+// M128 N256. The CTA is persistent over tiles (row-block major, column block
+// minor, so the 128-row A block is re-read from L2, not HBM, for every column
+// block) and keeps two accumulators in TMEM (2 x 256 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2-5 epilogue (thread <-> accumulator row == TMEM lane).
+// Every wait is bounded (s2dev::mbar_wait): on timeout the CTA records an
+// error code in args.err, drains its in-flight copies and MMAs and exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "s2_gemm.h"
+#include "s2_internal.h"
+#include "s2_sm100.cuh"
+
+using namespace s2dev;
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kOffBar = kStages * kStageBytes;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+
+enum Bar {
+    B_FULL = 0,                     // [kStages] A and B slices landed
+    B_EMPTY = B_FULL + kStages,     // [kStages] MMAs reading the stage retired
+    B_ACCF = B_EMPTY + kStages,     // [2] accumulator complete
+    B_ACCE = B_ACCF + 2,            // [2] epilogue finished reading it (128 arrivals)
+    B_DRAIN = B_ACCE + 2,
+    B_COUNT
+};
+static_assert(8 * B_COUNT + 8 <= 256, "barrier area");
+
+// device error codes of this kernel
+enum : int { E_FULL = 16, E_EMPTY = 17, E_ACCF = 18, E_ACCE = 19, E_DRAIN = 20 };
+
+__device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *err)
+{
+    int dummy = 0;
+    return mbar_wait(bar, parity, &dummy, err, E_DRAIN);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b)
+{
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const s2::GemmArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (base - raw);
+    const uint32_t bar0 = base + kOffBar;
+    volatile int *abort = reinterpret_cast<volatile int *>(gbase + kOffBar + 8 * B_COUNT);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + kOffBar + 8 * B_COUNT + 4);
+#define BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_blocks = (a.N + kBN - 1) / kBN;
+    const int n_tiles = ((a.M + kBM - 1) / kBM) * n_blocks;
+    const int n_k = a.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), (i >= B_ACCE && i < B_ACCE + 2) ? 128u : 1u);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            uint32_t p = 0;  // stage uses issued
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+                const int m0 = (t / n_blocks) * kBM, n0 = (t % n_blocks) * kBN;
+                for (int kc = 0; kc < n_k; ++kc, ++p) {
+                    const uint32_t s = p % kStages, u = p / kStages;
+                    if (!(ok = mbar_wait(BAR(B_EMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_EMPTY))) break;
+                    const uint32_t sa = base + s * kStageBytes;
+                    mbar_arrive_expect_tx(BAR(B_FULL + s), kStageBytes);
+                    tma_load_2d(sa, &tmA, BAR(B_FULL + s), kc * kBK, m0);
+                    tma_load_2d(sa + kABytes, &tmB, BAR(B_FULL + s), kc * kBK, n0);
+                }
+            }
+            // no copy may still be landing when the CTA exits
+            for (uint32_t s = 0; s < kStages; ++s)
+                if (p > s) wait_drain(BAR(B_FULL + s), ((p - 1 - s) / kStages) & 1u, a.err);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(0u, kBN, 0);
+            const uint64_t d0 = smem_desc_sw128(base, 16, 1024);
+            uint32_t p = 0, lt = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
+                const uint32_t b = lt & 1u;
+                if (!(ok = mbar_wait(BAR(B_ACCE + b), ((lt >> 1) & 1u) ^ 1u, abort, a.err, E_ACCE))) break;
+                tc_fence_after();
+                for (int kc = 0; kc < n_k; ++kc, ++p) {
+                    const uint32_t s = p % kStages, u = p / kStages;
+                    if (!(ok = mbar_wait(BAR(B_FULL + s), u & 1u, abort, a.err, E_FULL))) break;
+                    tc_fence_after();
+                    const uint64_t da = d0 + static_cast<uint64_t>((s * kStageBytes) >> 4);
+                    const uint64_t db = da + static_cast<uint64_t>(kABytes >> 4);
+                    mma_chunk_ss_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
+                    mma_commit(BAR(B_EMPTY + s));
+                }
+                if (!ok) break;
+                mma_commit(BAR(B_ACCF + b));
+            }
+            mma_commit(BAR(B_DRAIN));
+            wait_drain(BAR(B_DRAIN), 0, a.err);
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (accumulator rows)
+        const int quad = warp & 3;
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        uint32_t lt = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
+            const int m0 = (t / n_blocks) * kBM, n0 = (t % n_blocks) * kBN;
+            const uint32_t b = lt & 1u;
+            ok = mbar_wait(BAR(B_ACCF + b), (lt >> 1) & 1u, abort, a.err, E_ACCF);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            const int row = m0 + quad * 32 + lane;
+            const bool row_ok = row < a.M;
+            for (int c = 0; c < kBN / 32; ++c) {
+                const int n = n0 + c * 32;
+                if (n >= a.N) break;
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_off + b * kBN + c * 32, r);
+                tmem_wait_ld();
+                if (a.epilogue == s2::GEMM_EPI_SPLIT_F16) {
+                    if (row_ok) {
+                        const int which = n / a.split, col = n - which * a.split;
+                        void *ob = which == 0 ? a.out[0] : (which == 1 ? a.out[1] : a.out[2]);
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(ob) +
+                                                               static_cast<size_t>(row) * a.split + col);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            float f[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                f[e] = __uint_as_float(r[v * 8 + e]) + (a.bias ? __ldg(a.bias + n + v * 8 + e) : 0.f);
+                            dst[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                                pack_h2(f[6], f[7]));
+                        }
+                    }
+                } else {
+                    // channel-major store: for a fixed column the warp's 32 rows are 128 contiguous bytes
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int col = n + e;
+                        if (row_ok && col < a.n_valid) {
+                            const size_t o = static_cast<size_t>(col) * a.ldt + row;
+                            a.y[o] = __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + a.resid[o];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(BAR(B_ACCE + b));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+#undef BAR
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+namespace s2 {
+
+bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                 uint32_t box_inner, uint32_t box_rows)
+{
+    auto encode = get_encode();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs &args)
+{
+    if (!A || !B || args.M <= 0 || args.N <= 0 || args.K <= 0 || args.K % kBK != 0 || !args.err)
+        return set_error(S2_INVALID_ARGUMENT, "gemm: invalid arguments (M %d N %d K %d)", args.M, args.N, args.K);
+    if (((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15u) != 0)
+        return set_error(S2_INVALID_ARGUMENT, "gemm: operands must be 16-byte aligned");
+    if (args.epilogue == GEMM_EPI_SPLIT_F16) {
+        if (args.split <= 0 || args.split % 32 != 0 || args.N % 32 != 0 || (args.N + args.split - 1) / args.split > 3)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad output split %d for N %d", args.split, args.N);
+        for (int i = 0; i < (args.N + args.split - 1) / args.split; ++i)
+            if (!args.out[i] || (reinterpret_cast<uintptr_t>(args.out[i]) & 15u) != 0)
+                return set_error(S2_INVALID_ARGUMENT, "gemm: output %d missing or not 16-byte aligned", i);
+    } else if (args.epilogue == GEMM_EPI_RESID_T_F32) {
+        if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
+    } else {
+        return set_error(S2_UNSUPPORTED, "gemm: unknown epilogue %d", args.epilogue);
+    }
+    CUtensorMap ma, mb;
+    if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM) ||
+        !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK, kBN))
+        return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess)
+            return set_error(S2_INFERENCE_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
+        configured = true;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long tiles = 1LL * ((args.M + kBM - 1) / kBM) * ((args.N + kBN - 1) / kBN);
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, args);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: launch failed: %s", cudaGetErrorString(e));
+    return S2_OK;
+}
+
+}  // namespace s2

@@ -1,0 +1,47 @@
+// Internal interface of the tcgen05 GEMM (s2_gemm.cu) and the shared
+// tensor-map encoder. Not part of the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "s2_b200.h"
+
+namespace s2 {
+
+// 2-D fp16 tensor map over a row-major [rows][inner] matrix (row pitch
+// row_bytes), box = box_inner x box_rows elements, 128-byte swizzle.
+bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                 uint32_t box_inner, uint32_t box_rows);
+
+// Epilogues of D = A B^T (+ bias).
+enum GemmEpilogue : int {
+    // fp16 row-major outputs split by column blocks of `split`: column n goes to
+    // out[n / split][row * split + n % split] (the fused Q|K|V projection).
+    GEMM_EPI_SPLIT_F16 = 0,
+    // fp32 channel-major output with residual: for n < n_valid,
+    // y[n * ldt + row] = acc + bias[n] + resid[n * ldt + row] (1x1 conv back
+    // into an ncnn [C][cstep] blob).
+    GEMM_EPI_RESID_T_F32 = 1,
+};
+
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;      // K a multiple of 64
+    const float *bias = nullptr;  // [N] or null
+    int epilogue = GEMM_EPI_SPLIT_F16;
+    void *out[3] = {nullptr, nullptr, nullptr};
+    int split = 0;
+    const float *resid = nullptr;
+    float *y = nullptr;
+    long long ldt = 0;
+    int n_valid = 0;
+    int32_t *err = nullptr;       // device error word (bounded waits)
+};
+
+// D[M][N] = A[M][K] B[N][K]^T on sm_100a: A and B fp16, K-major (row-major
+// with K contiguous, rows 16-byte aligned), fp32 accumulation in TMEM.
+s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs &args);
+
+}  // namespace s2

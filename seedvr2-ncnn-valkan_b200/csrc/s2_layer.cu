@@ -13,55 +13,15 @@
 #include <cstring>
 #include <vector>
 
+#include "s2_buffers.h"
 #include "s2_internal.h"
 
 namespace s2 {
 s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst);
 }
 
-namespace {
-
-struct DeviceBuffer {
-    void *ptr = nullptr;
-    size_t bytes = 0;
-    bool ensure(size_t want)
-    {
-        if (want <= bytes) return true;
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        bytes = 0;
-        if (cudaMalloc(&ptr, want) != cudaSuccess) {
-            cudaGetLastError();
-            return false;
-        }
-        bytes = want;
-        return true;
-    }
-    void release()
-    {
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        bytes = 0;
-    }
-};
-
-// Restores the caller's current device on scope exit.
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev)
-    {
-        cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard()
-    {
-        int cur = -1;
-        cudaGetDevice(&cur);
-        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-    }
-};
-
-}  // namespace
+using s2::DeviceBuffer;
+using s2::DeviceGuard;
 
 struct s2_attention_layer {
     int device = 0;

@@ -97,6 +97,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
         : "memory");
 }
 
+// 2-D tiled bulk tensor load global -> shared (c0 = innermost coordinate).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int c0, int c1)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
 // ---- tcgen05 ---------------------------------------------------------------
 
 // Allocate `ncols` TMEM columns (power of two >= 32); the warp must be converged.
@@ -177,6 +187,27 @@ __device__ __forceinline__ void mma_tile_ss_k128(uint32_t d_tmem, uint64_t a_des
         "add.s64 a, %1, 1028;\n\tadd.s64 b, %2, 1028;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
         "add.s64 a, %1, 1030;\n\tadd.s64 b, %2, 1030;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
+        : "memory");
+}
+
+// One K=64 slice (a single 128B-swizzled 64-element box of each operand, both
+// K-major) as 4 straight-line K=16 MMAs: descriptor start +2 (32 B) per step.
+// The N extent comes from idesc, so the same helper serves N = 128 and 256.
+__device__ __forceinline__ void mma_chunk_ss_k64(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t acc_first)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b64 a, b;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
         : "memory");

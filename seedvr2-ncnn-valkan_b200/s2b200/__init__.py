@@ -9,6 +9,9 @@ Mirrors the reference's layer surface (czwdysj/seedvr2-ncnn-valkan):
   * ``make_windows``            <- SeedVR2DiTBlock::make_windows (src/layers/seedvr2_dit_block.cpp:827-868)
   * ``SeedVR2DiTBlockAttention`` <- SeedVR2DiTBlock's attention stage: load_param (:643-655),
     load_model norm/freqs part (:657-688), set_runtime_shape (.h:55), attention() (:870-1091)
+  * ``DynamicFramewiseSpatialAttention`` <- the VAE mid-block attention layer
+    (src/layers/dynamic_framewise_spatial_attention.cpp: load_param :50-59,
+    load_model :61-77, forward :106-210)
 """
 from __future__ import annotations
 
@@ -77,6 +80,17 @@ _SIGS = {
     "s2_attention_layer_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_window_attention_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int] + [ctypes.c_int] * 5
                                         + [ctypes.c_float] + [ctypes.c_int] * 4 + [_vp] * 5),
+    "s2_spatial_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, _vp, _vp]),
+    "s2_vae_attention_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_vae_attention_destroy": (ctypes.c_int, [_vp]),
+    "s2_vae_attention_load": (ctypes.c_int, [_vp] + [_f32p] * 10),
+    "s2_vae_attention_forward": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_longlong, _vp]),
+    "s2_vae_attention_forward_host": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.c_longlong, _vp]),
+    "s2_vae_attention_last_launches": (ctypes.c_int, [_vp]),
+    "s2_vae_attention_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
@@ -334,6 +348,103 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
                     stream=None):
     _check(lib().s2_text_window_sum(_stream_ptr(stream), mode, _ptr(txt_partial), n_windows, text_len, dim,
                                     ctypes.c_float(scale), int(accumulate), _ptr(txt_out)), "s2_text_window_sum")
+
+
+def padded_channels(channels: int) -> int:
+    """Head dim the spatial attention runs at: channels padded to 128, 256 or 512."""
+    return 128 if channels <= 128 else (256 if channels <= 256 else 512)
+
+
+def spatial_attention(q, k, v, channels, frames, tokens, out, err, stream=None):
+    """Per-frame single-head attention; q/k/v/out fp16 [frames*tokens, padded_channels(channels)]."""
+    _check(lib().s2_spatial_attention(_stream_ptr(stream), _ptr(q), _ptr(k), _ptr(v), channels, q.shape[1], frames,
+                                      tokens, _ptr(out), _ptr(err)), "s2_spatial_attention")
+
+
+VAE_WEIGHT_ORDER = ("norm_bias", "norm_weight", "k_bias", "k_weight", "out_bias", "out_weight", "q_bias", "q_weight",
+                    "v_bias", "v_weight")
+
+
+class DynamicFramewiseSpatialAttention:
+    """The VAE mid-block attention layer on a B200 (drop-in for the ncnn layer's forward).
+
+    ``load_param(channels)`` / ``load_model(weights)`` take what the reference's
+    ParamDict key 10 and ModelBin hold (weights: a dict by name, or the flat
+    fp32 stream in the reference's load order); ``forward`` takes a device fp32
+    tensor x [C, T, H, W] (or an ncnn [C, cstep] blob with ``shape``) and
+    returns y of the same layout; ``forward_host`` does the same on numpy
+    arrays. Errors raise S2Error with the reference-style status code.
+    """
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        self.handle = None
+        self.channels = 0
+
+    def load_param(self, channels: int):
+        h = ctypes.c_void_p()
+        _check(lib().s2_vae_attention_create(self.device, int(channels), ctypes.byref(h)), "s2_vae_attention_create")
+        self.close()
+        self.handle, self.channels = h, int(channels)
+        return S2_OK
+
+    def load_model(self, weights):
+        C = self.channels
+        if not isinstance(weights, dict):
+            flat = np.ascontiguousarray(weights, np.float32).ravel()
+            sizes = [C if name.endswith("bias") or name == "norm_weight" else C * C for name in VAE_WEIGHT_ORDER]
+            if flat.size != sum(sizes):
+                raise S2Error(S2_INVALID_ARGUMENT, f"load_model: {flat.size} floats, expected {sum(sizes)}")
+            offs = np.cumsum([0] + sizes)
+            weights = {n: flat[offs[i]:offs[i + 1]] for i, n in enumerate(VAE_WEIGHT_ORDER)}
+        arrs = [np.ascontiguousarray(weights[n], np.float32).ravel() for n in VAE_WEIGHT_ORDER]
+        _check(lib().s2_vae_attention_load(self.handle, *[a.ctypes.data_as(_f32p) for a in arrs]),
+               "s2_vae_attention_load")
+        self._keep = arrs
+        return S2_OK
+
+    def forward(self, x, y=None, shape=None, stream=None):
+        """x: device fp32 [C, T, H, W], or [C, cstep] with shape=(T, H, W)."""
+        torch = _torch()
+        if shape is None:
+            C, T, H, W = x.shape
+            cstep = T * H * W
+        else:
+            (T, H, W), C, cstep = shape, x.shape[0], x.shape[1]
+        if y is None:
+            y = torch.empty_like(x)
+        _check(lib().s2_vae_attention_forward(self.handle, _stream_ptr(stream), _ptr(x), T, H, W, cstep, _ptr(y)),
+               "s2_vae_attention_forward")
+        return y
+
+    def forward_host(self, x: np.ndarray, stream=None) -> np.ndarray:
+        """x: host fp32 [C, T, H, W] -> y (copies in and out, synchronises)."""
+        x = np.ascontiguousarray(x, np.float32)
+        C, T, H, W = x.shape
+        y = np.empty_like(x)
+        _check(lib().s2_vae_attention_forward_host(self.handle, _stream_ptr(stream) if stream is not None else None,
+                                                   ctypes.c_void_p(x.ctypes.data), T, H, W, T * H * W,
+                                                   ctypes.c_void_p(y.ctypes.data)), "s2_vae_attention_forward_host")
+        return y
+
+    def last_launches(self) -> int:
+        return lib().s2_vae_attention_last_launches(self.handle)
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_vae_attention_device_error(self.handle, ctypes.byref(code))
+        return code.value
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            lib().s2_vae_attention_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_check(device: int = 0) -> int:

@@ -20,6 +20,8 @@ GRIDS = {
     "cfg2": (6, 45, 80),      # 720p x 21f
     "cfg3": (12, 67, 120),    # 1080p x 45f
 }
+# VAE mid-block attention (config 4): channels, latent frames, height, width.
+VAE_CFG4 = (512, 6, 90, 160)
 # BASELINE.json's explicit window geometries (the reference computes its own).
 OVERRIDES = {"cfg0": (2, 8, 10), "cfg2": (6, 15, 20), "cfg3": (4, 17, 20)}
 
@@ -54,3 +56,31 @@ def prologue_bytes(L: int, text_len: int, n_rows: int, heads: int, in_bytes: int
     text), write the packed q/k/v rows in 16-bit."""
     dim = heads * HEAD_DIM
     return float((L + text_len) * 3 * dim * in_bytes + n_rows * 3 * dim * 2)
+
+
+def vae_inputs(shape=VAE_CFG4, seed=666):
+    """(x [C, T, H, W] f32, weights dict) for the VAE mid-block attention.
+
+    x ~ N(0, 1) stored fp16-representable; projection weights and biases
+    N(0, 0.02); GroupNorm gamma 1 + 0.1 N(0, 1), beta 0.1 N(0, 1)."""
+    C, T, H, W = shape
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((C, T, H, W), dtype=np.float32).astype(np.float16).astype(np.float32)
+    w = {"norm_weight": (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32),
+         "norm_bias": (0.1 * rng.standard_normal(C)).astype(np.float32)}
+    for name in ("q", "k", "v", "out"):
+        w[f"{name}_weight"] = (0.02 * rng.standard_normal(C * C)).astype(np.float32)
+        w[f"{name}_bias"] = (0.02 * rng.standard_normal(C)).astype(np.float32)
+    return x, w
+
+
+def vae_attention_flops(shape) -> float:
+    """Algorithmic FLOPs of the per-frame attention: T * 4 * (H*W)^2 * C."""
+    C, T, H, W = shape
+    return float(T) * 4.0 * float(H * W) ** 2 * C
+
+
+def vae_projection_flops(shape) -> float:
+    """FLOPs of the four 1x1 projections: 4 * 2 * T*H*W * C^2."""
+    C, T, H, W = shape
+    return 8.0 * T * H * W * float(C) * C

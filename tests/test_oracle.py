@@ -92,3 +92,13 @@ def test_restatement_matches_reference_live(port, ref):
         assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
         for k in "qkvo":
             assert np.array_equal(a[2][k], b[2][k])
+
+
+@pytest.mark.parametrize("i", range(len(refcases.VAE_CASES)))
+def test_vae_token_subset_equals_full(port, i):
+    x, w, _ = refcases.vae_case(refcases.VAE_CASES[i])
+    C, T, H, W = x.shape
+    y = port.vae_attention(x, w)
+    for f in range(T):
+        sel = np.arange(H * W)[::-1].copy()
+        assert np.array_equal(port.vae_attention_tokens(x, w, f, sel), y[:, f].reshape(C, -1)[:, sel].T)

@@ -120,3 +120,25 @@ def test_layer_create_without_gpu_reports_unsupported():
     with pytest.raises(s2b200.S2Error) as e:
         layer.load_param(heads=20, dim=2560)
     assert e.value.status == s2b200.S2_UNSUPPORTED
+
+
+def test_vae_layer_channel_checks():
+    """load_param rejects channel counts the reference rejects (not a multiple
+    of the 32 GroupNorm groups) before touching a device."""
+    for bad in (0, 48, -32):
+        with pytest.raises(s2b200.S2Error) as e:
+            s2b200.DynamicFramewiseSpatialAttention().load_param(bad)
+        assert e.value.status == s2b200.S2_INVALID_ARGUMENT
+    with pytest.raises(s2b200.S2Error) as e:
+        s2b200.DynamicFramewiseSpatialAttention().load_param(544)
+    assert e.value.status == s2b200.S2_UNSUPPORTED
+    assert [s2b200.padded_channels(c) for c in (32, 128, 160, 256, 288, 512)] == [128, 128, 256, 256, 512, 512]
+
+
+def test_vae_layer_create_without_gpu_reports_unsupported():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    with pytest.raises(s2b200.S2Error) as e:
+        s2b200.DynamicFramewiseSpatialAttention().load_param(512)
+    assert e.value.status == s2b200.S2_UNSUPPORTED
