@@ -183,14 +183,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 } else {
-                    // channel-major store: for a fixed column the warp's 32 rows are 128 contiguous bytes
+                    // channel-major store: for a fixed column the warp's 32 rows are 128 contiguous bytes.
+                    // All 32 residual loads of the chunk are issued before its stores (y and resid are
+                    // distinct buffers; interleaving them would serialise every load behind a store).
+                    float res[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        res[e] = (row_ok && n + e < a.n_valid) ? __ldg(a.resid + static_cast<size_t>(n + e) * a.ldt + row)
+                                                               : 0.f;
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int col = n + e;
-                        if (row_ok && col < a.n_valid) {
-                            const size_t o = static_cast<size_t>(col) * a.ldt + row;
-                            a.y[o] = __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + a.resid[o];
-                        }
+                        if (row_ok && col < a.n_valid)
+                            a.y[static_cast<size_t>(col) * a.ldt + row] =
+                                __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + res[e];
                     }
                 }
             }

@@ -105,14 +105,19 @@ __global__ void __launch_bounds__(256) gn_apply_kernel(const float *__restrict__
         off[threadIdx.x] = o_;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 64 * 64; i += 256) {
-        const int cc = i >> 6, tt = i & 63;
+    // 16 independent loads per thread in flight (a warp reads 128 contiguous bytes per channel row)
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int i = threadIdx.x + 256 * k, cc = i >> 6, tt = i & 63;
         const int c = c0 + cc, t = t0 + tt;
-        float v = 0.f;
-        if (c < C && t < tokens)
-            v = __fadd_rn(__fmul_rn(x[static_cast<size_t>(c) * cstep + static_cast<size_t>(f) * tokens + t], sc[cc]),
-                          off[cc]);
-        tile[cc][tt] = v;
+        v[k] = (c < C && t < tokens) ? __ldg(x + static_cast<size_t>(c) * cstep + static_cast<size_t>(f) * tokens + t)
+                                     : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int i = threadIdx.x + 256 * k, cc = i >> 6, tt = i & 63;
+        tile[cc][tt] = c0 + cc < C ? __fadd_rn(__fmul_rn(v[k], sc[cc]), off[cc]) : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < 64 * 32; i += 256) {
