@@ -63,9 +63,14 @@ typedef enum s2_dtype {
  *    reference CPU path rounds each window output (seedvr2_dit_block.cpp:1074).
  *  S2_MODE_F16: outputs stored as fp16 without the bf16 rounding (the
  *    reference's Vulkan shader keeps its fp32 result, :416-436). */
+/*  S2_MODE_BF16_F16: outputs rounded to bf16 like S2_MODE_BF16_REF but stored
+ *    as fp16 (exact for |x| in fp16's normal range), so that a following
+ *    f16 x f16 tensor-core GEMM (the block's output projection) reads the
+ *    reference's rounded values directly. */
 typedef enum s2_mode {
     S2_MODE_BF16_REF = 0,
-    S2_MODE_F16 = 1
+    S2_MODE_F16 = 1,
+    S2_MODE_BF16_F16 = 2
 } s2_mode;
 
 /* One 3-D window box, half-open ranges on the (T, H, W) token grid.
@@ -205,6 +210,48 @@ S2_API int s2_attention_layer_last_launches(const s2_attention_layer *layer);
  * (0 = ok; nonzero = a bounded wait inside the attention kernel timed out).
  * Returns S2_INFERENCE_FAILED when the word is set or the stream failed. */
 S2_API s2_status s2_attention_layer_device_error(s2_attention_layer *layer, int *code);
+
+/* ---- the whole DiT block (SeedVR2DiTBlock::forward) ----------------------- */
+
+typedef struct s2_dit_block s2_dit_block;
+
+/* load_param (seedvr2_dit_block.cpp:643-655): block_index, shared, last,
+ * shifted, dim, heads, head_dim (128), mlp_hidden (a multiple of 128), eps;
+ * wt/wh/ww override the window size (0,0,0 = the reference rule). */
+S2_API s2_status s2_dit_block_create(int device, int block_index, int shared, int last, int shifted, int dim,
+                                     int heads, int head_dim, int mlp_hidden, float eps, int wt, int wh, int ww,
+                                     s2_dit_block **out);
+S2_API s2_status s2_dit_block_destroy(s2_dit_block *block);
+
+/* load_model (:657-688): the layer's host fp32 weight stream in the
+ * reference's order -- per branch (video, then text unless shared): attn
+ * shift, scale, gate, mlp shift, scale, gate [dim]; qkv W [3 dim][dim]; proj
+ * W [dim][dim], proj b [dim]; norm_q, norm_k [128]; mlp gate W, in W
+ * [hidden][dim]; out W [dim][hidden] -- then rope freqs [21].
+ * n_floats must equal s2_dit_block_weight_count(block). */
+S2_API size_t s2_dit_block_weight_count(const s2_dit_block *block);
+S2_API s2_status s2_dit_block_load(s2_dit_block *block, const float *weights, size_t n_floats);
+
+/* set_runtime_shape (seedvr2_dit_block.h:55) and window sharding. */
+S2_API s2_status s2_dit_block_set_runtime_shape(s2_dit_block *block, int frames, int height, int width);
+S2_API s2_status s2_dit_block_set_window_subset(s2_dit_block *block, const int32_t *ids, int n);
+
+/* forward (:1114-1267) on DEVICE buffers: vid [L][dim], txt [Lt][dim], emb
+ * [6 dim] (emb[6c + slot]), all fp32 -> vid_out [L][dim], txt_out [Lt][dim]
+ * fp32. RMSNorm + adaLN, QKV / output / SwiGLU MLP projections on the tensor
+ * cores (fp16 operands, fp32 accumulation and residual stream), the windowed
+ * attention of this header, gated residuals, the last block's text rule.
+ * Stream-ordered; outputs must not alias inputs. */
+S2_API s2_status s2_dit_block_forward(s2_dit_block *block, void *stream, const float *vid, int L, const float *txt,
+                                      int Lt, const float *emb, float *vid_out, float *txt_out);
+
+/* Same on HOST buffers with the vid_shape blob (int32 [3]), the ncnn::Mat
+ * contract; synchronises `stream`. */
+S2_API s2_status s2_dit_block_forward_host(s2_dit_block *block, void *stream, const float *vid, int L,
+                                           const float *txt, int Lt, const float *emb, const int32_t *vid_shape,
+                                           float *vid_out, float *txt_out);
+S2_API int s2_dit_block_last_launches(const s2_dit_block *block);
+S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
 
 /* ---- VAE mid-block spatial attention ------------------------------------ */
 

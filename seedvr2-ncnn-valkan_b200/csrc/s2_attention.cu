@@ -148,11 +148,18 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <bool kF16>
+// Output element pair in the mode's type: kOut = S2_MODE_BF16_REF (bf16 RNE),
+// S2_MODE_F16 (fp16 RNE) or S2_MODE_BF16_F16 (bf16 RNE, then stored as fp16:
+// exact in fp16's normal range).
+template <int kOut>
 __device__ __forceinline__ uint32_t pack_out(float a, float b)
 {
-    if constexpr (kF16) {
+    if constexpr (kOut == S2_MODE_F16) {
         const __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<const uint32_t *>(&h);
+    } else if constexpr (kOut == S2_MODE_BF16_F16) {
+        const __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+        const __half2 h = __floats2half2_rn(__low2float(r), __high2float(r));
         return *reinterpret_cast<const uint32_t *>(&h);
     } else {
         const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -169,7 +176,7 @@ __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *e
 
 // Persistent: CTA b processes items b, b + gridDim.x, ... of the cost-ordered
 // list; every barrier's phase counter runs on across items.
-template <bool kF16>
+template <int kOut>
 __global__ void __launch_bounds__(kThreads, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const AttnArgs a)
@@ -447,10 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c16 = 0; c16 < 16; ++c16) {
                 const int cc = c16 >> 2, i0 = (c16 & 3) * 8;
-                packed[c16].x = pack_out<kF16>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
-                packed[c16].y = pack_out<kF16>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
-                packed[c16].z = pack_out<kF16>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
-                packed[c16].w = pack_out<kF16>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
+                packed[c16].x = pack_out<kOut>(__uint_as_float(o[cc][i0 + 0]) * inv, __uint_as_float(o[cc][i0 + 1]) * inv);
+                packed[c16].y = pack_out<kOut>(__uint_as_float(o[cc][i0 + 2]) * inv, __uint_as_float(o[cc][i0 + 3]) * inv);
+                packed[c16].z = pack_out<kOut>(__uint_as_float(o[cc][i0 + 4]) * inv, __uint_as_float(o[cc][i0 + 5]) * inv);
+                packed[c16].w = pack_out<kOut>(__uint_as_float(o[cc][i0 + 6]) * inv, __uint_as_float(o[cc][i0 + 7]) * inv);
             }
             uint4 *stage = reinterpret_cast<uint4 *>(gbase + kOffStage + static_cast<uint32_t>(warp) * kStageBytes);
 #pragma unroll
@@ -517,13 +524,13 @@ bool make_map(CUtensorMap *map, const void *ptr, int heads, int n_rows)
     return r == CUDA_SUCCESS;
 }
 
-template <bool kF16>
+template <int kOut>
 s2_status launch(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                  const AttnArgs &args, int grid)
 {
     static bool configured = false;
     if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(window_attention_kernel<kF16>,
+        const cudaError_t e = cudaFuncSetAttribute(window_attention_kernel<kOut>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_window_attention: smem attribute: %s", cudaGetErrorString(e));
@@ -531,14 +538,14 @@ s2_status launch(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, 
         // softmax groups' request: refuse to launch a build whose register
         // count at launch is smaller than the split assumes.
         cudaFuncAttributes fa;
-        if (cudaFuncGetAttributes(&fa, window_attention_kernel<kF16>) != cudaSuccess ||
+        if (cudaFuncGetAttributes(&fa, window_attention_kernel<kOut>) != cudaSuccess ||
             static_cast<long long>(fa.numRegs) * kThreads < 128LL * (kQT * kRegsSoftmax + kRegsControl))
             return s2::set_error(S2_INFERENCE_FAILED,
                                  "s2_window_attention: kernel built with %d registers/thread, register split needs %d",
                                  fa.numRegs, (128 * (kQT * kRegsSoftmax + kRegsControl) + kThreads - 1) / kThreads);
         configured = true;
     }
-    window_attention_kernel<kF16><<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, args);
+    window_attention_kernel<kOut><<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, args);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_window_attention: launch failed: %s", cudaGetErrorString(e));
@@ -555,7 +562,7 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     if (!q || !k || !v || heads <= 0 || n_rows <= 0 || !cu_seqlens || n_windows <= 0 || text_len < 0 || !rows ||
         !work || n_work <= 0 || !vid_out || (text_len > 0 && !txt_partial) || !err)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_window_attention: invalid arguments");
-    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16)
+    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
         return s2::set_error(S2_UNSUPPORTED, "s2_window_attention: unknown mode %d", (int)mode);
     if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
           reinterpret_cast<uintptr_t>(vid_out) | reinterpret_cast<uintptr_t>(txt_partial)) & 15u) != 0)
@@ -566,7 +573,6 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long grid = n_items < sms ? n_items : sms;  // persistent: one CTA per SM
-    const bool f16 = mode == S2_MODE_F16;
     CUtensorMap mq, mk, mv;
     if (!make_map(&mq, q, heads, n_rows) || !make_map(&mk, k, heads, n_rows) || !make_map(&mv, v, heads, n_rows))
         return s2::set_error(S2_INFERENCE_FAILED, "s2_window_attention: cuTensorMapEncodeTiled failed");
@@ -582,6 +588,9 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     args.n_items = static_cast<int>(n_items);
     args.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e) / sqrt(128)
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return f16 ? launch<true>(st, mq, mk, mv, args, static_cast<int>(grid))
-               : launch<false>(st, mq, mk, mv, args, static_cast<int>(grid));
+    switch (mode) {
+    case S2_MODE_F16: return launch<S2_MODE_F16>(st, mq, mk, mv, args, static_cast<int>(grid));
+    case S2_MODE_BF16_F16: return launch<S2_MODE_BF16_F16>(st, mq, mk, mv, args, static_cast<int>(grid));
+    default: return launch<S2_MODE_BF16_REF>(st, mq, mk, mv, args, static_cast<int>(grid));
+    }
 }

@@ -1,0 +1,461 @@
+// s2_dit_block: one SeedVR2DiTBlock (src/layers/seedvr2_dit_block.cpp:1114-1267)
+// on sm_100a -- the block around the windowed attention:
+//
+//   a_x   = RMSNorm(x) (no gamma, eps) then adaLN shift/scale (slot 0)     :770-805, :1144-1150
+//   qkv_x = a_x W_qkv^T                      (tcgen05 GEMM, fp16 out)     :1152-1154
+//   attn  = s2_attention_layer (prologue + window attention + text mean)  :1168-1171
+//   h_x   = (attn W_proj^T + b) * (emb[6c+2] + attn_gate) + x  (epilogue) :1180-1204
+//   m_x   = RMSNorm(h_x) then shift/scale (slot 3)                        :1206-1208
+//   hid   = silu(m W_gate^T) * (m W_in^T)    (one GEMM, SwiGLU epilogue)   :1093-1112
+//   out_x = (hid W_out^T) * (emb[6c+5] + mlp_gate) + h_x   (epilogue)     :1216
+//
+// for x = video and text (text uses the text branch's weights unless the
+// block shares them). The last block's text skips the adaLN input
+// modulation and gate and returns 2 * (proj + txt) (:1146-1150, :1190-1200,
+// :1220-1240). Activations entering a GEMM are fp16 (RNE); accumulation and
+// residual streams stay fp32. Weights are uploaded once as fp16; the SwiGLU
+// gate and "in" weights are interleaved in 128-row groups so one 256-column
+// GEMM tile holds matching gate and in columns.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "s2_buffers.h"
+#include "s2_gemm.h"
+#include "s2_internal.h"
+
+namespace {
+
+// y = fp16( ada( x * inv_rms(x) ) ), one warp per row.
+//   inv_rms = 1 / sqrt(float(sum x^2 (double) / dim) + eps)           (:770-782)
+//   ada: v * (emb[6c + s + 1] + scale[c]) + emb[6c + s] + shift[c]     (:784-805)
+// emb6 == nullptr skips the modulation (the last block's text input).
+__global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ x, int rows, int dim, float eps,
+                                                      const float *__restrict__ emb6, const float *__restrict__ shift,
+                                                      const float *__restrict__ scale, __half *__restrict__ y)
+{
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(warp) * dim);
+    double ss = 0.0;
+    for (int i = lane; i < dim / 4; i += 32) {
+        const float4 v = __ldg(xr + i);
+        ss += static_cast<double>(v.x) * v.x;
+        ss += static_cast<double>(v.y) * v.y;
+        ss += static_cast<double>(v.z) * v.z;
+        ss += static_cast<double>(v.w) * v.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(static_cast<float>(ss / dim), eps)));
+    __half2 *yr = reinterpret_cast<__half2 *>(y + static_cast<size_t>(warp) * dim);
+    for (int i = lane; i < dim / 4; i += 32) {
+        const float4 v = __ldg(xr + i);
+        float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int c = 4 * i + e;
+            float t = __fmul_rn(f[e], inv);
+            if (emb6) {
+                t = __fmul_rn(t, __fadd_rn(__ldg(emb6 + 6 * c + 1), __ldg(scale + c)));
+                t = __fadd_rn(__fadd_rn(t, __ldg(emb6 + 6 * c)), __ldg(shift + c));
+            }
+            f[e] = t;
+        }
+        yr[2 * i] = __floats2half2_rn(f[0], f[1]);
+        yr[2 * i + 1] = __floats2half2_rn(f[2], f[3]);
+    }
+}
+
+__global__ void f32_to_f16_kernel(const float *__restrict__ x, long long n, __half *__restrict__ y)
+{
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) y[i] = __float2half_rn(x[i]);
+}
+
+struct Branch {
+    s2::DeviceBuffer mod;    // fp32 [6][dim]: attn_shift, attn_scale, attn_gate, mlp_shift, mlp_scale, mlp_gate
+    s2::DeviceBuffer qkv;    // fp16 [3 dim][dim]
+    s2::DeviceBuffer proj;   // fp16 [dim][dim]
+    s2::DeviceBuffer proj_b; // fp32 [dim]
+    s2::DeviceBuffer gu;     // fp16 [2 hidden][dim], gate/in interleaved by 128 rows
+    s2::DeviceBuffer out;    // fp16 [dim][hidden]
+    std::vector<float> norm_q, norm_k;
+    void release()
+    {
+        for (s2::DeviceBuffer *b : {&mod, &qkv, &proj, &proj_b, &gu, &out}) b->release();
+    }
+    const float *m(int k, int dim) const { return static_cast<const float *>(mod.ptr) + static_cast<size_t>(k) * dim; }
+};
+
+bool upload(s2::DeviceBuffer &b, const void *src, size_t bytes)
+{
+    return b.ensure(bytes) && cudaMemcpy(b.ptr, src, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+bool upload_f16(s2::DeviceBuffer &b, const float *src, size_t n)
+{
+    std::vector<__half> h(n);
+    for (size_t i = 0; i < n; ++i) h[i] = __float2half_rn(src[i]);
+    return upload(b, h.data(), n * 2);
+}
+
+}  // namespace
+
+struct s2_dit_block {
+    int device = 0;
+    int block_index = 0, shared = 0, last = 0, shifted = 0;
+    int dim = 2560, heads = 20, head_dim = 128, hidden = 6912;
+    float eps = 1e-5f;
+    bool loaded = false;
+    Branch vid, txt;
+    s2_attention_layer *attn = nullptr;
+    // workspaces
+    s2::DeviceBuffer a_vid, a_txt, qkv_vid, qkv_txt, att_vid, att_txt32, att_txt16, h_vid, h_txt, hid_vid, hid_txt,
+        err;
+    s2::DeviceBuffer hv, ht, he, hov, hot;  // forward_host staging
+    int last_launches = 0;
+    cudaStream_t last_stream = nullptr;
+    const Branch &tb() const { return shared ? vid : txt; }
+};
+
+extern "C" s2_status s2_dit_block_create(int device, int block_index, int shared, int last, int shifted, int dim,
+                                         int heads, int head_dim, int mlp_hidden, float eps, int wt, int wh, int ww,
+                                         s2_dit_block **out)
+{
+    s2::clear_error();
+    if (!out) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_create: out is NULL");
+    *out = nullptr;
+    if (dim != heads * head_dim || heads <= 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_create: dim %d != heads %d * head_dim %d", dim, heads,
+                             head_dim);
+    if (head_dim != S2_HEAD_DIM)
+        return s2::set_error(S2_UNSUPPORTED, "s2_dit_block_create: head_dim %d (only 128)", head_dim);
+    if (mlp_hidden <= 0 || mlp_hidden % 128 != 0)
+        return s2::set_error(S2_UNSUPPORTED, "s2_dit_block_create: mlp_hidden %d must be a multiple of 128", mlp_hidden);
+    auto *b = new s2_dit_block();
+    b->device = device;
+    b->block_index = block_index;
+    b->shared = shared != 0;
+    b->last = last != 0;
+    b->shifted = shifted != 0;
+    b->dim = dim;
+    b->heads = heads;
+    b->head_dim = head_dim;
+    b->hidden = mlp_hidden;
+    b->eps = eps;
+    const s2_status st =
+        s2_attention_layer_create(device, heads, head_dim, eps, shifted, wt, wh, ww, S2_MODE_BF16_F16, &b->attn);
+    if (st != S2_OK) {
+        delete b;
+        return st;
+    }
+    *out = b;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_destroy(s2_dit_block *b)
+{
+    if (!b) return S2_OK;
+    {
+        s2::DeviceGuard guard(b->device);
+        b->vid.release();
+        b->txt.release();
+        for (s2::DeviceBuffer *x : {&b->a_vid, &b->a_txt, &b->qkv_vid, &b->qkv_txt, &b->att_vid, &b->att_txt32,
+                                    &b->att_txt16, &b->h_vid, &b->h_txt, &b->hid_vid, &b->hid_txt, &b->err, &b->hv,
+                                    &b->ht, &b->he, &b->hov, &b->hot})
+            x->release();
+    }
+    s2_attention_layer_destroy(b->attn);
+    delete b;
+    return S2_OK;
+}
+
+// Number of floats of one branch in the weight stream (load_branch, :657-680).
+static size_t branch_floats(const s2_dit_block *b)
+{
+    const size_t d = b->dim, h = b->hidden, hd = b->head_dim;
+    return 6 * d + 3 * d * d + d * d + d + 2 * hd + 2 * h * d + d * h;
+}
+
+extern "C" size_t s2_dit_block_weight_count(const s2_dit_block *b)
+{
+    return b ? branch_floats(b) * (b->shared ? 1 : 2) + S2_ROPE_PAIRS : 0;
+}
+
+extern "C" s2_status s2_dit_block_load(s2_dit_block *b, const float *w, size_t n_floats)
+{
+    s2::clear_error();
+    if (!b || !w) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_load: null argument");
+    if (n_floats != s2_dit_block_weight_count(b))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_load: %zu floats, the layer reads %zu", n_floats,
+                             s2_dit_block_weight_count(b));
+    s2::DeviceGuard guard(b->device);
+    const size_t d = b->dim, h = b->hidden, hd = b->head_dim;
+    auto load_branch = [&](const float *p, Branch &br) -> bool {
+        bool ok = upload(br.mod, p, 6 * d * 4);
+        p += 6 * d;
+        ok = ok && upload_f16(br.qkv, p, 3 * d * d);
+        p += 3 * d * d;
+        ok = ok && upload_f16(br.proj, p, d * d);
+        p += d * d;
+        ok = ok && upload(br.proj_b, p, d * 4);
+        p += d;
+        br.norm_q.assign(p, p + hd);
+        p += hd;
+        br.norm_k.assign(p, p + hd);
+        p += hd;
+        // interleave gate / in rows by groups of 128 -> [2h][d]
+        std::vector<float> gu(2 * h * d);
+        const float *gate = p, *in = p + h * d;
+        for (size_t g = 0; g < h / 128; ++g) {
+            std::memcpy(&gu[(2 * g) * 128 * d], gate + g * 128 * d, 128 * d * 4);
+            std::memcpy(&gu[(2 * g + 1) * 128 * d], in + g * 128 * d, 128 * d * 4);
+        }
+        p += 2 * h * d;
+        ok = ok && upload_f16(br.gu, gu.data(), gu.size());
+        ok = ok && upload_f16(br.out, p, d * h);
+        return ok;
+    };
+    if (!load_branch(w, b->vid))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_load: weight upload failed");
+    const float *freqs = w + branch_floats(b);
+    if (!b->shared) {
+        if (!load_branch(w + branch_floats(b), b->txt))
+            return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_load: weight upload failed");
+        freqs += branch_floats(b);
+    }
+    const Branch &t = b->tb();
+    const s2_status st =
+        s2_attention_layer_load(b->attn, b->vid.norm_q.data(), b->vid.norm_k.data(), t.norm_q.data(), t.norm_k.data(), freqs);
+    if (st != S2_OK) return st;
+    b->loaded = true;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_set_runtime_shape(s2_dit_block *b, int frames, int height, int width)
+{
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_set_runtime_shape: block is NULL");
+    return s2_attention_layer_set_runtime_shape(b->attn, frames, height, width);
+}
+
+extern "C" s2_status s2_dit_block_set_window_subset(s2_dit_block *b, const int32_t *ids, int n)
+{
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_set_window_subset: block is NULL");
+    return s2_attention_layer_set_window_subset(b->attn, ids, n);
+}
+
+namespace {
+
+s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *emb6, const float *shift,
+                  const float *scale, __half *y)
+{
+    if (rows <= 0) return S2_OK;
+    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, emb6, shift, scale, y);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "rms_ada launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt,
+                                          int Lt, const float *emb, float *vid_out, float *txt_out)
+{
+    s2::clear_error();
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: block is NULL");
+    if (!b->loaded) return s2::set_error(S2_NOT_LOADED, "s2_dit_block_forward: weights not loaded");
+    if (!vid || !emb || !vid_out || L <= 0 || Lt < 0 || (Lt > 0 && (!txt || !txt_out)))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: invalid arguments");
+    if (vid == vid_out || (Lt > 0 && txt == txt_out))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: in-place forward is not supported");
+    s2::DeviceGuard guard(b->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int d = b->dim, h = b->hidden;
+    const size_t Lz = static_cast<size_t>(L), Tz = static_cast<size_t>(std::max(Lt, 1));
+    const bool fresh = b->err.ptr == nullptr;
+    if (!b->a_vid.ensure(Lz * d * 2) || !b->a_txt.ensure(Tz * d * 2) || !b->qkv_vid.ensure(Lz * 3 * d * 2) ||
+        !b->qkv_txt.ensure(Tz * 3 * d * 2) || !b->att_vid.ensure(Lz * d * 2) || !b->att_txt32.ensure(Tz * d * 4) ||
+        !b->att_txt16.ensure(Tz * d * 2) || !b->h_vid.ensure(Lz * d * 4) || !b->h_txt.ensure(Tz * d * 4) ||
+        !b->hid_vid.ensure(Lz * h * 2) || !b->hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward: workspace allocation failed");
+    if (fresh && cudaMemsetAsync(b->err.ptr, 0, 4, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: memset failed");
+    int32_t *err = static_cast<int32_t *>(b->err.ptr);
+    const Branch &V = b->vid, &T = b->tb();
+    b->last_stream = st;
+    int launches = 0;
+    s2_status s;
+#define S2_TRY(expr)                 \
+    do {                             \
+        if ((s = (expr)) != S2_OK) { \
+            b->last_launches = launches; \
+            return s;                \
+        }                            \
+        ++launches;                  \
+    } while (0)
+
+    // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
+    S2_TRY(rms_ada(st, vid, L, d, b->eps, emb, V.m(0, d), V.m(1, d), static_cast<__half *>(b->a_vid.ptr)));
+    if (Lt > 0)
+        S2_TRY(rms_ada(st, txt, Lt, d, b->eps, b->last ? nullptr : emb, T.m(0, d), T.m(1, d),
+                       static_cast<__half *>(b->a_txt.ptr)));
+    // QKV projections (no bias)
+    s2::GemmArgs g;
+    g.K = d;
+    g.N = 3 * d;
+    g.split = 3 * d;
+    g.err = err;
+    g.M = L;
+    g.out[0] = b->qkv_vid.ptr;
+    S2_TRY(s2::gemm_f16(st, b->a_vid.ptr, V.qkv.ptr, g));
+    if (Lt > 0) {
+        g.M = Lt;
+        g.out[0] = b->qkv_txt.ptr;
+        S2_TRY(s2::gemm_f16(st, b->a_txt.ptr, T.qkv.ptr, g));
+    }
+    // windowed MM attention (prologue, attention, text mean)
+    if ((s = s2_attention_layer_forward(b->attn, stream, b->qkv_vid.ptr, S2_F16, L, b->qkv_txt.ptr, Lt, b->att_vid.ptr,
+                                        static_cast<float *>(b->att_txt32.ptr))) != S2_OK) {
+        b->last_launches = launches;
+        return s;
+    }
+    launches += s2_attention_layer_last_launches(b->attn);
+    // output projection + gated residual
+    s2::GemmArgs p;
+    p.K = d;
+    p.N = d;
+    p.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+    p.err = err;
+    p.M = L;
+    p.bias = static_cast<const float *>(V.proj_b.ptr);
+    p.emb6 = emb + 2;
+    p.gate = V.m(2, d);
+    p.resid = vid;
+    p.y = static_cast<float *>(b->h_vid.ptr);
+    S2_TRY(s2::gemm_f16(st, b->att_vid.ptr, V.proj.ptr, p));
+    if (Lt > 0) {
+        const long long n = static_cast<long long>(Lt) * d;
+        f32_to_f16_kernel<<<static_cast<unsigned>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
+            static_cast<const float *>(b->att_txt32.ptr), n, static_cast<__half *>(b->att_txt16.ptr));
+        if (cudaGetLastError() != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: convert launch failed");
+        ++launches;
+        p.M = Lt;
+        p.bias = static_cast<const float *>(T.proj_b.ptr);
+        p.resid = txt;
+        if (b->last) {
+            // vid_only modulation: plain residual, and the text output is 2 * (proj + txt)
+            p.emb6 = nullptr;
+            p.gate = nullptr;
+            p.out_scale = 2.f;
+            p.y = txt_out;
+        } else {
+            p.emb6 = emb + 2;
+            p.gate = T.m(2, d);
+            p.y = static_cast<float *>(b->h_txt.ptr);
+        }
+        S2_TRY(s2::gemm_f16(st, b->att_txt16.ptr, T.proj.ptr, p));
+    }
+    // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
+    auto mlp = [&](const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y) -> s2_status {
+        s2_status r = rms_ada(st, hx, rows, d, b->eps, emb + 3, br.m(3, d), br.m(4, d), a16);
+        if (r != S2_OK) return r;
+        ++launches;
+        s2::GemmArgs u;
+        u.M = rows;
+        u.N = 2 * h;
+        u.K = d;
+        u.epilogue = s2::GEMM_EPI_SWIGLU_F16;
+        u.out[0] = hid;
+        u.err = err;
+        if ((r = s2::gemm_f16(st, a16, br.gu.ptr, u)) != S2_OK) return r;
+        ++launches;
+        s2::GemmArgs o;
+        o.M = rows;
+        o.N = d;
+        o.K = h;
+        o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+        o.emb6 = emb + 5;
+        o.gate = br.m(5, d);
+        o.resid = hx;
+        o.y = y;
+        o.err = err;
+        if ((r = s2::gemm_f16(st, hid, br.out.ptr, o)) != S2_OK) return r;
+        ++launches;
+        return S2_OK;
+    };
+    if ((s = mlp(V, static_cast<const float *>(b->h_vid.ptr), L, static_cast<__half *>(b->a_vid.ptr),
+                 static_cast<__half *>(b->hid_vid.ptr), vid_out)) != S2_OK) {
+        b->last_launches = launches;
+        return s;
+    }
+    if (Lt > 0 && !b->last &&
+        (s = mlp(T, static_cast<const float *>(b->h_txt.ptr), Lt, static_cast<__half *>(b->a_txt.ptr),
+                 static_cast<__half *>(b->hid_txt.ptr), txt_out)) != S2_OK) {
+        b->last_launches = launches;
+        return s;
+    }
+#undef S2_TRY
+    b->last_launches = launches;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_forward_host(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt,
+                                               int Lt, const float *emb, const int32_t *vid_shape, float *vid_out,
+                                               float *txt_out)
+{
+    s2::clear_error();
+    if (!b || !vid || !emb || !vid_shape || !vid_out || L <= 0 || Lt < 0 || (Lt > 0 && (!txt || !txt_out)))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward_host: invalid arguments");
+    s2_status s = s2_dit_block_set_runtime_shape(b, vid_shape[0], vid_shape[1], vid_shape[2]);
+    if (s != S2_OK) return s;
+    if (L != vid_shape[0] * vid_shape[1] * vid_shape[2])
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward_host: vid rows %d != T*H*W", L);
+    s2::DeviceGuard guard(b->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t d = b->dim, vb = static_cast<size_t>(L) * d * 4, tbytes = static_cast<size_t>(std::max(Lt, 1)) * d * 4;
+    if (!b->hv.ensure(vb) || !b->ht.ensure(tbytes) || !b->he.ensure(6 * d * 4) || !b->hov.ensure(vb) ||
+        !b->hot.ensure(tbytes))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward_host: staging allocation failed");
+    if (cudaMemcpyAsync(b->hv.ptr, vid, vb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        (Lt > 0 && cudaMemcpyAsync(b->ht.ptr, txt, static_cast<size_t>(Lt) * d * 4, cudaMemcpyHostToDevice, st) !=
+                       cudaSuccess) ||
+        cudaMemcpyAsync(b->he.ptr, emb, 6 * d * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward_host: upload failed");
+    s = s2_dit_block_forward(b, stream, static_cast<const float *>(b->hv.ptr), L, static_cast<const float *>(b->ht.ptr), Lt,
+                             static_cast<const float *>(b->he.ptr), static_cast<float *>(b->hov.ptr),
+                             static_cast<float *>(b->hot.ptr));
+    if (s != S2_OK) return s;
+    if (cudaMemcpyAsync(vid_out, b->hov.ptr, vb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        (Lt > 0 && cudaMemcpyAsync(txt_out, b->hot.ptr, static_cast<size_t>(Lt) * d * 4, cudaMemcpyDeviceToHost, st) !=
+                       cudaSuccess) ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward_host: %s", cudaGetErrorString(cudaGetLastError()));
+    int code = 0;
+    return s2_dit_block_device_error(b, &code);
+}
+
+extern "C" int s2_dit_block_last_launches(const s2_dit_block *b) { return b ? b->last_launches : 0; }
+
+extern "C" s2_status s2_dit_block_device_error(s2_dit_block *b, int *code)
+{
+    if (code) *code = 0;
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_device_error: block is NULL");
+    int c = 0;
+    s2_status s = s2_attention_layer_device_error(b->attn, &c);
+    if (s != S2_OK) {
+        if (code) *code = c;
+        return s;
+    }
+    if (!b->err.ptr) return S2_OK;
+    s2::DeviceGuard guard(b->device);
+    int32_t hcode = 0;
+    if (cudaStreamSynchronize(b->last_stream) != cudaSuccess ||
+        cudaMemcpy(&hcode, b->err.ptr, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block: device failure: %s", cudaGetErrorString(cudaGetLastError()));
+    if (code) *code = hcode;
+    if (hcode != 0) return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block: device wait timed out (code %d)", hcode);
+    return S2_OK;
+}

@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < a.M;
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < kBN / 32 && a.epilogue != s2::GEMM_EPI_SWIGLU_F16; ++c) {
                 const int n = n0 + c * 32;
                 if (n >= a.N) break;
                 uint32_t r[32];
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                 pack_h2(f[6], f[7]));
                         }
                     }
-                } else {
+                } else if (a.epilogue == s2::GEMM_EPI_RESID_T_F32) {
                     // channel-major store: for a fixed column the warp's 32 rows are 128 contiguous bytes.
                     // All 32 residual loads of the chunk are issued before its stores (y and resid are
                     // distinct buffers; interleaving them would serialise every load behind a store).
@@ -197,6 +197,52 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (row_ok && col < a.n_valid)
                             a.y[static_cast<size_t>(col) * a.ldt + row] =
                                 __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + res[e];
+                    }
+                } else if (a.epilogue == s2::GEMM_EPI_GATED_RESID_F32) {
+                    if (row_ok) {
+                        const float4 *rs = reinterpret_cast<const float4 *>(a.resid + static_cast<size_t>(row) * a.N + n);
+                        float4 *yd = reinterpret_cast<float4 *>(a.y + static_cast<size_t>(row) * a.N + n);
+                        float4 res[8];
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) res[v] = __ldg(rs + v);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            float o[4];
+                            const float rv[4] = {res[v].x, res[v].y, res[v].z, res[v].w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int col = n + v * 4 + e;
+                                float t = __uint_as_float(r[v * 4 + e]);
+                                if (a.bias) t = __fadd_rn(t, __ldg(a.bias + col));
+                                if (a.emb6) t = __fmul_rn(t, __fadd_rn(__ldg(a.emb6 + 6 * col), __ldg(a.gate + col)));
+                                o[e] = __fmul_rn(__fadd_rn(t, rv[e]), a.out_scale);
+                            }
+                            yd[v] = make_float4(o[0], o[1], o[2], o[3]);
+                        }
+                    }
+                }
+            }
+            if (a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && ok) {
+                // pairs (gate chunk c, in chunk c + 4) of the 256-column tile
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t gr[32], ur[32];
+                    tmem_ld32(tmem + lane_off + b * kBN + c * 32, gr);
+                    tmem_ld32(tmem + lane_off + b * kBN + 128 + c * 32, ur);
+                    tmem_wait_ld();
+                    if (row_ok) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(a.out[0]) +
+                                                               static_cast<size_t>(row) * (a.N / 2) + n0 / 2 + c * 32);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            float f[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float g = __uint_as_float(gr[v * 8 + e]);
+                                f[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), __uint_as_float(ur[v * 8 + e]));
+                            }
+                            dst[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                                pack_h2(f[6], f[7]));
+                        }
                     }
                 }
             }
@@ -262,6 +308,13 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else if (args.epilogue == GEMM_EPI_RESID_T_F32) {
         if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
+    } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
+        if (!args.y || !args.resid || args.N % 32 != 0 || (args.emb6 && !args.gate) ||
+            ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
+    } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {
+        if (!args.out[0] || args.N % kBN != 0 || (reinterpret_cast<uintptr_t>(args.out[0]) & 15u) != 0)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad SwiGLU output (N %d must be a multiple of 256)", args.N);
     } else {
         return set_error(S2_UNSUPPORTED, "gemm: unknown epilogue %d", args.epilogue);
     }

@@ -145,7 +145,8 @@ extern "C" s2_status s2_attention_layer_create(int device, int heads, int head_d
     if (head_dim != S2_HEAD_DIM)
         return s2::set_error(S2_INVALID_ARGUMENT, "head_dim must be %d (got %d)", S2_HEAD_DIM, head_dim);
     if (heads <= 0 || heads > 64) return s2::set_error(S2_INVALID_ARGUMENT, "heads must be in [1, 64]");
-    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16) return s2::set_error(S2_UNSUPPORTED, "unknown mode");
+    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
+        return s2::set_error(S2_UNSUPPORTED, "unknown mode");
     if ((wt > 0 || wh > 0 || ww > 0) && !(wt > 0 && wh > 0 && ww > 0))
         return s2::set_error(S2_INVALID_ARGUMENT, "window override needs wt, wh, ww > 0");
     const s2_status dc = s2_device_check(device);
@@ -261,7 +262,7 @@ extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void
     if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
     if (!vid_shape || !vid_qkv || !vid_out || (Lt > 0 && (!txt_qkv || !txt_out)) || L <= 0 || Lt < 0)
         return s2::set_error(S2_INVALID_ARGUMENT, "forward_host: NULL buffer or bad size");
-    const s2_dtype mode_dtype = l->mode == S2_MODE_F16 ? S2_F16 : S2_BF16;
+    const s2_dtype mode_dtype = l->mode == S2_MODE_BF16_REF ? S2_BF16 : S2_F16;
     if (io_dtype != S2_F32 && io_dtype != mode_dtype)
         return s2::set_error(S2_UNSUPPORTED, "forward_host: io dtype must be f32 or the mode's 16-bit type");
     // The shape blob is authoritative on this path (the CPU forward reads vid_shape).

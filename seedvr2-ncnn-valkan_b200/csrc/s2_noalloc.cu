@@ -120,7 +120,8 @@ extern "C" s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
     if (!vid_qkv || !gammas || !freqs21 || !vid_out || text_len < 0 || (text_len > 0 && (!txt_qkv || !txt_out)) ||
         heads <= 0 || heads > 64)
         return s2::set_error(S2_INVALID_ARGUMENT, "noalloc: NULL buffer or invalid heads/text_len");
-    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16) return s2::set_error(S2_UNSUPPORTED, "noalloc: unknown mode");
+    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
+        return s2::set_error(S2_UNSUPPORTED, "noalloc: unknown mode");
     s2_window wins[kMaxWindows];
     int n = 0;
     s2_status rc = s2_make_windows(frames, height, width, shifted, wt, wh, ww, wins, kMaxWindows, &n);

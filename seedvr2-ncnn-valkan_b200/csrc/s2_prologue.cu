@@ -251,7 +251,7 @@ extern "C" s2_status s2_qk_norm_rope(void *stream, const void *vid_qkv, const vo
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_qk_norm_rope: invalid arguments");
     if (!aligned16(vid_qkv) || (txt_qkv && !aligned16(txt_qkv)) || !aligned16(q) || !aligned16(k) || !aligned16(v))
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_qk_norm_rope: buffers must be 16-byte aligned");
-    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16)
+    if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
         return s2::set_error(S2_UNSUPPORTED, "s2_qk_norm_rope: unknown mode %d", (int)mode);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long pairs = 1LL * n_rows * heads;
@@ -287,7 +287,7 @@ extern "C" s2_status s2_text_window_sum(void *stream, s2_mode mode, const void *
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long n = 1LL * text_len * dim;
     const int grid = static_cast<int>((n + 255) / 256 < 8LL * sm_count() ? (n + 255) / 256 : 8LL * sm_count());
-    if (mode == S2_MODE_F16)
+    if (mode == S2_MODE_F16 || mode == S2_MODE_BF16_F16)
         text_window_sum_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(txt_partial), n_windows, n,
                                                              scale, accumulate, txt_out);
     else
@@ -305,7 +305,7 @@ s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, fl
 {
     if (n <= 0) return S2_OK;
     const int grid = static_cast<int>((n + 255) / 256 < 8LL * sm_count() ? (n + 255) / 256 : 8LL * sm_count());
-    if (mode == S2_MODE_F16)
+    if (mode == S2_MODE_F16 || mode == S2_MODE_BF16_F16)
         to_f32_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(src), n, dst);
     else
         to_f32_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(src), n, dst);

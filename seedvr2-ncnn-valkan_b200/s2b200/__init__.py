@@ -9,6 +9,8 @@ Mirrors the reference's layer surface (czwdysj/seedvr2-ncnn-valkan):
   * ``make_windows``            <- SeedVR2DiTBlock::make_windows (src/layers/seedvr2_dit_block.cpp:827-868)
   * ``SeedVR2DiTBlockAttention`` <- SeedVR2DiTBlock's attention stage: load_param (:643-655),
     load_model norm/freqs part (:657-688), set_runtime_shape (.h:55), attention() (:870-1091)
+  * ``SeedVR2DiTBlock``          <- the whole block (seedvr2_dit_block.cpp: load_param :643-655,
+    load_model :657-688, forward :1114-1267)
   * ``DynamicFramewiseSpatialAttention`` <- the VAE mid-block attention layer
     (src/layers/dynamic_framewise_spatial_attention.cpp: load_param :50-59,
     load_model :61-77, forward :106-210)
@@ -26,7 +28,7 @@ HEAD_DIM = 128
 
 S2_OK, S2_INVALID_ARGUMENT, S2_NOT_LOADED, S2_INFERENCE_FAILED, S2_UNSUPPORTED, S2_OUT_OF_MEMORY = 0, -1, -2, -5, -6, -7
 S2_F32, S2_F16, S2_BF16 = 0, 1, 2
-MODE_BF16_REF, MODE_F16 = 0, 1
+MODE_BF16_REF, MODE_F16, MODE_BF16_F16 = 0, 1, 2
 
 _STATUS_NAMES = {0: "Ok", -1: "InvalidArgument", -2: "NotLoaded", -5: "InferenceFailed", -6: "UnsupportedBackend",
                  -7: "OutOfMemory"}
@@ -80,6 +82,18 @@ _SIGS = {
     "s2_attention_layer_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_window_attention_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int] + [ctypes.c_int] * 5
                                         + [ctypes.c_float] + [ctypes.c_int] * 4 + [_vp] * 5),
+    "s2_dit_block_create": (ctypes.c_int, [ctypes.c_int] * 9 + [ctypes.c_float] + [ctypes.c_int] * 3
+                            + [ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_dit_block_destroy": (ctypes.c_int, [_vp]),
+    "s2_dit_block_weight_count": (ctypes.c_size_t, [_vp]),
+    "s2_dit_block_load": (ctypes.c_int, [_vp, _f32p, ctypes.c_size_t]),
+    "s2_dit_block_set_runtime_shape": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "s2_dit_block_set_window_subset": (ctypes.c_int, [_vp, _i32p, ctypes.c_int]),
+    "s2_dit_block_forward": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp]),
+    "s2_dit_block_forward_host": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i32p, _vp,
+                                                 _vp]),
+    "s2_dit_block_last_launches": (ctypes.c_int, [_vp]),
+    "s2_dit_block_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_spatial_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_int, _vp, _vp]),
     "s2_vae_attention_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
@@ -210,7 +224,7 @@ def _ptr(t):
 
 def mode_dtype(mode: int):
     torch = _torch()
-    return torch.float16 if mode == MODE_F16 else torch.bfloat16
+    return torch.bfloat16 if mode == MODE_BF16_REF else torch.float16
 
 
 class SeedVR2DiTBlockAttention:
@@ -348,6 +362,93 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
                     stream=None):
     _check(lib().s2_text_window_sum(_stream_ptr(stream), mode, _ptr(txt_partial), n_windows, text_len, dim,
                                     ctypes.c_float(scale), int(accumulate), _ptr(txt_out)), "s2_text_window_sum")
+
+
+class SeedVR2DiTBlock:
+    """One DiT block on a B200 (drop-in for the ncnn layer's forward).
+
+    ``load_param`` takes the reference's ParamDict keys 0..8, ``load_model``
+    the flat fp32 weight stream in the reference's load order,
+    ``set_runtime_shape`` the token grid; ``forward`` takes device fp32
+    tensors vid [L, dim], txt [Lt, dim], emb [6*dim] and returns
+    (vid_out, txt_out); ``forward_host`` the same on numpy arrays with the
+    vid_shape blob. Errors raise S2Error with the reference-style status.
+    """
+
+    def __init__(self, device: int = 0, window_override=(0, 0, 0)):
+        self.device = device
+        self.window_override = tuple(int(x) for x in window_override)
+        self.handle = None
+        self.dim = 0
+
+    def load_param(self, block_index=0, shared=False, last=False, shifted=False, dim=2560, heads=20, head_dim=128,
+                   mlp_hidden=6912, eps=1e-5):
+        h = ctypes.c_void_p()
+        _check(lib().s2_dit_block_create(self.device, block_index, int(shared), int(last), int(shifted), dim, heads,
+                                         head_dim, mlp_hidden, ctypes.c_float(eps), *self.window_override,
+                                         ctypes.byref(h)), "s2_dit_block_create")
+        self.close()
+        self.handle, self.dim = h, dim
+        return S2_OK
+
+    def weight_count(self) -> int:
+        return int(lib().s2_dit_block_weight_count(self.handle))
+
+    def load_model(self, weights):
+        w = np.ascontiguousarray(weights, np.float32).ravel()
+        _check(lib().s2_dit_block_load(self.handle, w.ctypes.data_as(_f32p), w.size), "s2_dit_block_load")
+        return S2_OK
+
+    def set_runtime_shape(self, frames, height, width):
+        _check(lib().s2_dit_block_set_runtime_shape(self.handle, frames, height, width), "set_runtime_shape")
+
+    def set_window_subset(self, ids=None):
+        ids = np.ascontiguousarray([] if ids is None else ids, np.int32)
+        _check(lib().s2_dit_block_set_window_subset(self.handle, ids.ctypes.data_as(_i32p) if ids.size else None,
+                                                    int(ids.size)), "set_window_subset")
+
+    def forward(self, vid, txt, emb, vid_out=None, txt_out=None, stream=None):
+        torch = _torch()
+        L, Lt = vid.shape[0], (txt.shape[0] if txt is not None else 0)
+        if vid_out is None:
+            vid_out = torch.empty_like(vid)
+        if txt_out is None and Lt:
+            txt_out = torch.empty_like(txt)
+        _check(lib().s2_dit_block_forward(self.handle, _stream_ptr(stream), _ptr(vid), L,
+                                          _ptr(txt) if Lt else None, Lt, _ptr(emb), _ptr(vid_out),
+                                          _ptr(txt_out) if Lt else None), "s2_dit_block_forward")
+        return vid_out, txt_out
+
+    def forward_host(self, vid: np.ndarray, txt: np.ndarray, emb: np.ndarray, vid_shape, stream=None):
+        vid, txt, emb = (np.ascontiguousarray(a, np.float32) for a in (vid, txt, emb))
+        vo, to = np.empty_like(vid), np.empty_like(txt)
+        shape = np.ascontiguousarray(vid_shape, np.int32)
+        _check(lib().s2_dit_block_forward_host(self.handle, _stream_ptr(stream) if stream is not None else None,
+                                               ctypes.c_void_p(vid.ctypes.data), vid.shape[0],
+                                               ctypes.c_void_p(txt.ctypes.data), txt.shape[0],
+                                               ctypes.c_void_p(emb.ctypes.data), shape.ctypes.data_as(_i32p),
+                                               ctypes.c_void_p(vo.ctypes.data), ctypes.c_void_p(to.ctypes.data)),
+               "s2_dit_block_forward_host")
+        return vo, to
+
+    def last_launches(self) -> int:
+        return lib().s2_dit_block_last_launches(self.handle)
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_dit_block_device_error(self.handle, ctypes.byref(code))
+        return code.value
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            lib().s2_dit_block_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def padded_channels(channels: int) -> int:

@@ -84,3 +84,44 @@ def vae_projection_flops(shape) -> float:
     """FLOPs of the four 1x1 projections: 4 * 2 * T*H*W * C^2."""
     C, T, H, W = shape
     return 8.0 * T * H * W * float(C) * C
+
+
+def block_weights(dim, heads, mlp_hidden, shared=False, seed=666):
+    """Flat fp32 weight stream of one SeedVR2DiTBlock in the reference's
+    load_model order (seedvr2_dit_block.cpp:657-688): per branch the six adaLN
+    vectors N(0, 0.02), qkv W, proj W + b, mlp gate/in/out W ~ N(0, 0.02),
+    QK-norm gammas 1 + 0.1 N(0, 1); then the RoPE freqs."""
+    rng = np.random.default_rng(seed)
+
+    def branch():
+        parts = [0.02 * rng.standard_normal(dim, dtype=np.float32) for _ in range(6)]
+        parts += [0.02 * rng.standard_normal(3 * dim * dim, dtype=np.float32),
+                  0.02 * rng.standard_normal(dim * dim, dtype=np.float32),
+                  0.02 * rng.standard_normal(dim, dtype=np.float32),
+                  (1.0 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32),
+                  (1.0 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32),
+                  0.02 * rng.standard_normal(mlp_hidden * dim, dtype=np.float32),
+                  0.02 * rng.standard_normal(mlp_hidden * dim, dtype=np.float32),
+                  0.02 * rng.standard_normal(dim * mlp_hidden, dtype=np.float32)]
+        return parts
+
+    stream = branch() if shared else branch() + branch()
+    stream.append(rope_freqs())
+    return np.concatenate([p.astype(np.float32).ravel() for p in stream])
+
+
+def block_activations(grid, dim, text_len=TEXT_LEN, seed=667):
+    """(vid [L, dim], txt [Lt, dim]) ~ N(0, 1) and emb [6 dim] ~ N(0, 0.02)."""
+    T, H, W = grid
+    rng = np.random.default_rng(seed)
+    vid = rng.standard_normal((T * H * W, dim), dtype=np.float32)
+    txt = rng.standard_normal((text_len, dim), dtype=np.float32)
+    emb = (0.02 * rng.standard_normal(6 * dim)).astype(np.float32)
+    return vid, txt, emb
+
+
+def block_gemm_flops(L, text_len, dim, mlp_hidden, last=False):
+    """FLOPs of a block's projections: qkv, proj, SwiGLU (gate + in), out."""
+    per_row = 2.0 * dim * (3 * dim + dim + 2 * mlp_hidden + mlp_hidden)
+    txt_rows = text_len if not last else 0
+    return per_row * L + per_row * txt_rows + (2.0 * dim * 4 * dim * text_len if last else 0.0)

@@ -1,0 +1,101 @@
+"""GPU parity of the whole DiT block (SeedVR2DiTBlock::forward) through the C
+ABI: RMSNorm + adaLN, tcgen05 QKV / projection / SwiGLU MLP GEMMs with fused
+gated-residual and SwiGLU epilogues, and the windowed MM attention.
+
+References: the reference's own CPU block (built from its sources,
+oracle/_ref) on identical seeded inputs, and its runner cases as golden
+fixtures. Gate: outputs within max-abs 2e-3, and the block's contribution
+(out - input) at cosine >= 0.9999 -- the residual stream dominates the
+output, so the contribution is where a wrong GEMM or epilogue would show.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import parity
+import refcases
+import s2b200
+from s2b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    assert s2b200.device_check(0) == 0, s2b200.last_error()
+    return torch
+
+
+def run_gpu(torch, params, w, vid, txt, emb, shape):
+    b = s2b200.SeedVR2DiTBlock()
+    assert b.load_param(**params) == 0
+    b.load_model(w)
+    b.set_runtime_shape(*shape)
+    vo, to = b.forward(torch.from_numpy(vid).cuda(), torch.from_numpy(txt).cuda(), torch.from_numpy(emb).cuda())
+    torch.cuda.synchronize()
+    assert b.device_error() == 0
+    return vo.cpu().numpy(), to.cpu().numpy(), b
+
+
+def check_block(vo, to, evo, eto, vid, txt, what):
+    for name, got, exp, inp in (("vid", vo, evo, vid), ("txt", to, eto, txt)):
+        m = parity.metrics(got, exp)
+        assert m["finite"] and m["max_abs"] <= parity.MAX_ABS, f"{what} {name}: {m}"
+        d = parity.metrics(got - inp, exp - inp)
+        assert d["cosine"] >= parity.COSINE, f"{what} {name} contribution: {d}"
+
+
+@pytest.mark.parametrize("i", range(len(refcases.BLOCK_CASES)))
+def test_runner_cases_vs_reference(torch_cuda, golden, i):
+    params, w, vid, txt, emb, shape, _, _ = refcases.block_case(refcases.BLOCK_CASES[i])
+    vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
+    g = golden("block_runner_cases.npz")
+    check_block(vo, to, g[f"c{i}_vid_out"], g[f"c{i}_txt_out"], vid, txt, f"runner case {i}")
+    # 16 launches: 2 norms, 2 QKV GEMMs, 3 attention, text convert, 2 projections, 2 x (norm + 2 GEMMs);
+    # the last block's text skips its MLP (13)
+    assert b.last_launches() == (13 if params["last"] else 16)
+
+
+@pytest.mark.parametrize("shared,last,shifted", [(False, False, True), (True, False, False), (True, True, True)])
+def test_synthetic_blocks_vs_reference(torch_cuda, ref, shared, last, shifted):
+    dim, heads, mlp, grid = 512, 4, 1024, (2, 16, 30)
+    w = synth.block_weights(dim, heads, mlp, shared, seed=10 + shared + 2 * last)
+    vid, txt, emb = synth.block_activations(grid, dim)
+    params = dict(block_index=12 if shared else 3, shared=shared, last=last, shifted=shifted, dim=dim, heads=heads,
+                  head_dim=128, mlp_hidden=mlp, eps=1e-5)
+    evo, eto = ref.block_forward(params, w, vid, txt, emb, grid)
+    vo, to, _ = run_gpu(torch_cuda, params, w, vid, txt, emb, grid)
+    check_block(vo, to, evo, eto, vid, txt, f"dim 512 shared={shared} last={last}")
+
+
+def test_config1_block_vs_reference(torch_cuda, ref):
+    """one block at 2x16x30 (960 tokens), dim 2560, 20
+    heads, SwiGLU 6912 (the reference's MLP), shifted windows."""
+    dim, heads, mlp, grid = 2560, 20, 6912, synth.GRIDS["cfg0"]
+    w = synth.block_weights(dim, heads, mlp)
+    vid, txt, emb = synth.block_activations(grid, dim)
+    params = dict(block_index=1, shared=False, last=False, shifted=True, dim=dim, heads=heads, head_dim=128,
+                  mlp_hidden=mlp, eps=1e-5)
+    evo, eto = ref.block_forward(params, w, vid, txt, emb, grid)
+    vo, to, _ = run_gpu(torch_cuda, params, w, vid, txt, emb, grid)
+    check_block(vo, to, evo, eto, vid, txt, "config 1")
+
+
+def test_host_forward_matches_device(torch_cuda):
+    params, w, vid, txt, emb, shape, _, _ = refcases.block_case(refcases.BLOCK_CASES[3])
+    vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
+    ho, hto = b.forward_host(vid, txt, emb, shape)
+    assert np.array_equal(ho, vo) and np.array_equal(hto, to)
+
+
+def test_load_rejects_wrong_weight_count(torch_cuda):
+    params, w, *_ = refcases.block_case(refcases.BLOCK_CASES[0])
+    b = s2b200.SeedVR2DiTBlock()
+    b.load_param(**params)
+    assert b.weight_count() == w.size
+    with pytest.raises(s2b200.S2Error) as e:
+        b.load_model(w[:-1])
+    assert e.value.status == s2b200.S2_INVALID_ARGUMENT
