@@ -253,6 +253,52 @@ S2_API s2_status s2_dit_block_forward_host(s2_dit_block *block, void *stream, co
 S2_API int s2_dit_block_last_launches(const s2_dit_block *block);
 S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
 
+/* ---- the DiT model and one Euler step ------------------------------------ */
+
+typedef struct s2_dit s2_dit;
+
+/* SeedVR2DiT (src/model/dit.cpp:277-383): input head, n_blocks blocks, output
+ * head. Reference values: n_blocks 32, dim 2560, heads 20, head_dim 128,
+ * mlp_hidden 6912, eps 1e-5, video_channels 33, text_channels 5120,
+ * sinusoidal_dim 256, out_channels 16 (the embedding is 6 * dim). */
+S2_API s2_status s2_dit_create(int device, int n_blocks, int dim, int heads, int head_dim, int mlp_hidden, float eps,
+                               int video_channels, int text_channels, int sinusoidal_dim, int out_channels, int wt,
+                               int wh, int ww, s2_dit **out);
+S2_API s2_status s2_dit_destroy(s2_dit *model);
+
+/* Weight streams (host fp32) in the reference's load_model orders:
+ * SeedVR2DiTInput (seedvr2_dit_input.cpp:217-224: video, text, time-in,
+ * time-hidden, time-out projections, each W [out][in] then b),
+ * SeedVR2DiTBlock (see s2_dit_block_load; the flags come from the block's
+ * exported param file: shared for index >= 10, shifted for odd index, last
+ * for the final block) and SeedVR2DiTOutput (seedvr2_dit_output.cpp:264-270:
+ * norm weight, shift, scale [dim], projection W [4 oc][dim] then b). */
+S2_API size_t s2_dit_input_weight_count(const s2_dit *model);
+S2_API size_t s2_dit_output_weight_count(const s2_dit *model);
+S2_API s2_status s2_dit_load_input(s2_dit *model, const float *weights, size_t n_floats);
+S2_API s2_status s2_dit_load_block(s2_dit *model, int index, int shared, int last, int shifted, const float *weights,
+                                   size_t n_floats);
+S2_API s2_status s2_dit_load_output(s2_dit *model, const float *weights, size_t n_floats);
+
+/* SeedVR2DiT::forward on DEVICE buffers: latent fp32 [video_channels][T][H][W]
+ * (H, W even), text fp32 [Lt][text_channels], timestep -> prediction fp32
+ * [out_channels][T][H][W]. Stream-ordered, no host synchronisation. */
+S2_API s2_status s2_dit_forward(s2_dit *model, void *stream, const float *latent, int T, int H, int W,
+                                const float *text, int Lt, float timestep, float *prediction);
+
+/* One Euler sampling step as the engine runs it with one step and cfg 1
+ * (src/core/engine.cpp:125-149, 308-343; EulerSampler::endpoint,
+ * src/model/sampler.cpp:276-286): latent = noise || condition || ones,
+ * prediction = DiT(latent, text, timestep), x0 = noise - (timestep/1000) *
+ * prediction. noise, condition, x0: fp32 [out_channels][T][H][W]. */
+S2_API s2_status s2_dit_euler_step(s2_dit *model, void *stream, const float *noise, const float *condition, int T,
+                                   int H, int W, const float *text, int Lt, float timestep, float *x0);
+/* Same on HOST buffers (copies in and out, synchronises `stream`). */
+S2_API s2_status s2_dit_euler_step_host(s2_dit *model, void *stream, const float *noise, const float *condition,
+                                        int T, int H, int W, const float *text, int Lt, float timestep, float *x0);
+S2_API int s2_dit_last_launches(const s2_dit *model);
+S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);
+
 /* ---- VAE mid-block spatial attention ------------------------------------ */
 
 /* Single-head attention per frame, the core of the VAE mid-block attention

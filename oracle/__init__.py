@@ -140,6 +140,31 @@ class Port(_Lib):
         return y
 
 
+def make_dit_input(noise, condition):
+    """33-channel DiT input: noise (16) || condition (16) || ones
+    (make_dit_input, src/core/engine.cpp:125-149)."""
+    noise, condition = _f32(noise), _f32(condition)
+    ones = np.ones((1,) + noise.shape[1:], np.float32)
+    return np.concatenate([noise, condition, ones], axis=0)
+
+
+def flatten_latent(latent):
+    """[C, T, H, W] -> token-major [T*H*W, C] (dit.cpp:70-86)."""
+    C = latent.shape[0]
+    return np.ascontiguousarray(np.asarray(latent, np.float32).reshape(C, -1).T)
+
+
+def unflatten_latent(flat, T, H, W):
+    """token-major [T*H*W, C] -> [C, T, H, W] (dit.cpp:88-101)."""
+    return np.ascontiguousarray(np.asarray(flat, np.float32).T.reshape(-1, T, H, W))
+
+
+def euler_endpoint(prediction, current, timestep):
+    """EulerSampler::endpoint (sampler.cpp:276-286): x - (t / 1000) * pred in fp32."""
+    bt = np.float32(timestep) / np.float32(1000.0)
+    return (_f32(current) - bt * _f32(prediction)).astype(np.float32)
+
+
 class Ref(_Lib):
     """The reference's own CPU code (``oracle/_ref/libs2ref.so``)."""
 
@@ -159,6 +184,12 @@ class Ref(_Lib):
         L.ref_vae_attention.restype = ctypes.c_int
         L.ref_vae_attention.argtypes = [ctypes.c_int] * 4 + [_f32p, ctypes.c_size_t, _f32p,
                                                               ctypes.c_int, _f32p]
+        L.ref_dit_input.restype = ctypes.c_int
+        L.ref_dit_input.argtypes = ([ctypes.c_int] * 5 + [_f32p, ctypes.c_size_t, _f32p] + [ctypes.c_int] * 3
+                                    + [_f32p, ctypes.c_int, ctypes.c_float, ctypes.c_int] + [_f32p] * 3)
+        L.ref_dit_output.restype = ctypes.c_int
+        L.ref_dit_output.argtypes = ([ctypes.c_int] * 2 + [ctypes.c_float, _f32p, ctypes.c_size_t, _f32p]
+                                     + [ctypes.c_int] * 3 + [_f32p, ctypes.c_int, _f32p])
 
     def make_windows(self, T, H, W, shifted):
         n = self.lib.ref_make_windows(T, H, W, int(shifted), None, 0)
@@ -204,6 +235,55 @@ class Ref(_Lib):
         if rc != 0:
             raise ValueError(f"ref_block_forward failed: {rc}")
         return vo, to
+
+    def dit_input(self, params, weights, latent33, text, timestep, threads=0):
+        """SeedVR2DiTInput on latent [vc, T, H, W] (flattened here like
+        SeedVR2DiT::forward, dit.cpp:70-86, 298) and text [Lt, tc].
+        Returns (vid [T*H/2*W/2, dim], txt [Lt, dim], emb [ed])."""
+        p = params
+        latent33, text, weights = _f32(latent33), _f32(text), _f32(weights)
+        vc, T, H, W = latent33.shape
+        flat = np.ascontiguousarray(flatten_latent(latent33))
+        rows = T * (H // 2) * (W // 2)
+        vo = np.zeros((rows, p["dim"]), np.float32)
+        to = np.zeros((text.shape[0], p["dim"]), np.float32)
+        emb = np.zeros(p["embedding_dim"], np.float32)
+        rc = self.lib.ref_dit_input(p["dim"], vc, p["text_channels"], p["sinusoidal_dim"], p["embedding_dim"],
+                                    _ptr(weights), weights.size, _ptr(flat), T, H, W, _ptr(text), text.shape[0],
+                                    ctypes.c_float(timestep), int(threads or os.cpu_count() or 1), _ptr(vo),
+                                    _ptr(to), _ptr(emb))
+        if rc != 0:
+            raise ValueError(f"ref_dit_input failed: {rc}")
+        return vo, to, emb
+
+    def dit_output(self, params, weights, vid, emb, patched_shape, threads=0):
+        """SeedVR2DiTOutput; returns the prediction [oc, T, 2H, 2W] (unflattened
+        like dit.cpp:88-101)."""
+        p = params
+        vid, emb, weights = _f32(vid), _f32(emb), _f32(weights)
+        T, H, W = patched_shape
+        oc = p["out_channels"]
+        flat = np.zeros((T * 2 * H * 2 * W, oc), np.float32)
+        rc = self.lib.ref_dit_output(p["dim"], oc, ctypes.c_float(p.get("eps", 1e-5)), _ptr(weights), weights.size,
+                                     _ptr(vid), T, H, W, _ptr(emb), int(threads or os.cpu_count() or 1), _ptr(flat))
+        if rc != 0:
+            raise ValueError(f"ref_dit_output failed: {rc}")
+        return unflatten_latent(flat, T, 2 * H, 2 * W)
+
+    def euler_step(self, head_params, input_weights, block_params, block_weights, output_weights, noise, condition,
+                   text, timestep=1000.0, threads=0):
+        """One DiT Euler step the way the reference engine runs it with one
+        sampling step and cfg 1 (engine.cpp:308-343): make_dit_input, the DiT
+        forward (input head, blocks in order, output head; dit.cpp:277-383)
+        and EulerSampler::endpoint (sampler.cpp:276-286)."""
+        latent = make_dit_input(noise, condition)
+        vid, txt, emb = self.dit_input(head_params, input_weights, latent, text, timestep, threads)
+        _, T, H, W = latent.shape
+        shape = (T, H // 2, W // 2)
+        for bp, bw in zip(block_params, block_weights):
+            vid, txt = self.block_forward(bp, bw, vid, txt, emb, shape, threads)
+        pred = self.dit_output(head_params, output_weights, vid, emb, shape, threads)
+        return euler_endpoint(pred, noise, timestep), pred
 
     def vae_attention(self, x, weights_flat, threads=0):
         x = _f32(x)

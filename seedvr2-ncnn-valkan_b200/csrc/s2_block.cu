@@ -21,19 +21,23 @@
 
 #include <algorithm>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "s2_buffers.h"
 #include "s2_gemm.h"
 #include "s2_internal.h"
+#include "s2_ops.h"
 
 namespace {
 
-// y = fp16( ada( x * inv_rms(x) ) ), one warp per row.
+// y = fp16( ada( x * inv_rms(x) [* gamma] ) ), one warp per row.
 //   inv_rms = 1 / sqrt(float(sum x^2 (double) / dim) + eps)           (:770-782)
 //   ada: v * (emb[6c + s + 1] + scale[c]) + emb[6c + s] + shift[c]     (:784-805)
-// emb6 == nullptr skips the modulation (the last block's text input).
+// emb6 == nullptr skips the modulation (the last block's text input); gamma
+// is the output head's RMSNorm weight (seedvr2_dit_output.cpp:383).
 __global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ x, int rows, int dim, float eps,
+                                                      const float *__restrict__ gamma,
                                                       const float *__restrict__ emb6, const float *__restrict__ shift,
                                                       const float *__restrict__ scale, __half *__restrict__ y)
 {
@@ -59,6 +63,7 @@ __global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ 
         for (int e = 0; e < 4; ++e) {
             const int c = 4 * i + e;
             float t = __fmul_rn(f[e], inv);
+            if (gamma) t = __fmul_rn(t, __ldg(gamma + c));
             if (emb6) {
                 t = __fmul_rn(t, __fadd_rn(__ldg(emb6 + 6 * c + 1), __ldg(scale + c)));
                 t = __fadd_rn(__fadd_rn(t, __ldg(emb6 + 6 * c)), __ldg(shift + c));
@@ -104,6 +109,20 @@ bool upload_f16(s2::DeviceBuffer &b, const float *src, size_t n)
 
 }  // namespace
 
+// Activation workspaces of a block forward, shareable between blocks that run
+// one after another.
+struct BlockScratch {
+    int device = 0;
+    s2::DeviceBuffer a_vid, a_txt, qkv_vid, qkv_txt, att_vid, att_txt32, att_txt16, h_vid, h_txt, hid_vid, hid_txt;
+    ~BlockScratch()
+    {
+        s2::DeviceGuard guard(device);
+        for (s2::DeviceBuffer *x : {&a_vid, &a_txt, &qkv_vid, &qkv_txt, &att_vid, &att_txt32, &att_txt16, &h_vid, &h_txt,
+                                    &hid_vid, &hid_txt})
+            x->release();
+    }
+};
+
 struct s2_dit_block {
     int device = 0;
     int block_index = 0, shared = 0, last = 0, shifted = 0;
@@ -112,9 +131,8 @@ struct s2_dit_block {
     bool loaded = false;
     Branch vid, txt;
     s2_attention_layer *attn = nullptr;
-    // workspaces
-    s2::DeviceBuffer a_vid, a_txt, qkv_vid, qkv_txt, att_vid, att_txt32, att_txt16, h_vid, h_txt, hid_vid, hid_txt,
-        err;
+    std::shared_ptr<BlockScratch> sc = std::make_shared<BlockScratch>();
+    s2::DeviceBuffer err;
     s2::DeviceBuffer hv, ht, he, hov, hot;  // forward_host staging
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
@@ -137,6 +155,7 @@ extern "C" s2_status s2_dit_block_create(int device, int block_index, int shared
         return s2::set_error(S2_UNSUPPORTED, "s2_dit_block_create: mlp_hidden %d must be a multiple of 128", mlp_hidden);
     auto *b = new s2_dit_block();
     b->device = device;
+    b->sc->device = device;
     b->block_index = block_index;
     b->shared = shared != 0;
     b->last = last != 0;
@@ -163,9 +182,7 @@ extern "C" s2_status s2_dit_block_destroy(s2_dit_block *b)
         s2::DeviceGuard guard(b->device);
         b->vid.release();
         b->txt.release();
-        for (s2::DeviceBuffer *x : {&b->a_vid, &b->a_txt, &b->qkv_vid, &b->qkv_txt, &b->att_vid, &b->att_txt32,
-                                    &b->att_txt16, &b->h_vid, &b->h_txt, &b->hid_vid, &b->hid_txt, &b->err, &b->hv,
-                                    &b->ht, &b->he, &b->hov, &b->hot})
+        for (s2::DeviceBuffer *x : {&b->err, &b->hv, &b->ht, &b->he, &b->hov, &b->hot})
             x->release();
     }
     s2_attention_layer_destroy(b->attn);
@@ -252,13 +269,41 @@ namespace {
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *emb6, const float *shift,
                   const float *scale, __half *y)
 {
+    return s2::rms_ada(st, x, rows, dim, eps, nullptr, emb6, shift, scale, y);
+}
+
+}  // namespace
+
+namespace s2 {
+
+s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,
+                  const float *emb6, const float *shift, const float *scale, void *y)
+{
     if (rows <= 0) return S2_OK;
-    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, emb6, shift, scale, y);
+    if (dim % 4 != 0) return set_error(S2_INVALID_ARGUMENT, "rms_ada: dim %d not a multiple of 4", dim);
+    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, gamma, emb6, shift, scale,
+                                                   static_cast<__half *>(y));
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "rms_ada launch: %s", cudaGetErrorString(e));
 }
 
-}  // namespace
+s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y)
+{
+    if (n <= 0) return S2_OK;
+    f32_to_f16_kernel<<<static_cast<unsigned>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
+        x, n, static_cast<__half *>(y));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "f32_to_f16 launch: %s", cudaGetErrorString(e));
+}
+
+void share_block_scratch(s2_dit_block *dst, const s2_dit_block *src)
+{
+    if (!dst || !src || dst == src) return;
+    dst->sc = src->sc;
+    share_attention_scratch(dst->attn, src->attn);
+}
+
+}  // namespace s2
 
 extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt,
                                           int Lt, const float *emb, float *vid_out, float *txt_out)
@@ -275,10 +320,11 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     const int d = b->dim, h = b->hidden;
     const size_t Lz = static_cast<size_t>(L), Tz = static_cast<size_t>(std::max(Lt, 1));
     const bool fresh = b->err.ptr == nullptr;
-    if (!b->a_vid.ensure(Lz * d * 2) || !b->a_txt.ensure(Tz * d * 2) || !b->qkv_vid.ensure(Lz * 3 * d * 2) ||
-        !b->qkv_txt.ensure(Tz * 3 * d * 2) || !b->att_vid.ensure(Lz * d * 2) || !b->att_txt32.ensure(Tz * d * 4) ||
-        !b->att_txt16.ensure(Tz * d * 2) || !b->h_vid.ensure(Lz * d * 4) || !b->h_txt.ensure(Tz * d * 4) ||
-        !b->hid_vid.ensure(Lz * h * 2) || !b->hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4))
+    BlockScratch &sc = *b->sc;
+    if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) || !sc.qkv_vid.ensure(Lz * 3 * d * 2) ||
+        !sc.qkv_txt.ensure(Tz * 3 * d * 2) || !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
+        !sc.att_txt16.ensure(Tz * d * 2) || !sc.h_vid.ensure(Lz * d * 4) || !sc.h_txt.ensure(Tz * d * 4) ||
+        !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward: workspace allocation failed");
     if (fresh && cudaMemsetAsync(b->err.ptr, 0, 4, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: memset failed");
@@ -297,10 +343,10 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     } while (0)
 
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
-    S2_TRY(rms_ada(st, vid, L, d, b->eps, emb, V.m(0, d), V.m(1, d), static_cast<__half *>(b->a_vid.ptr)));
+    S2_TRY(rms_ada(st, vid, L, d, b->eps, emb, V.m(0, d), V.m(1, d), static_cast<__half *>(sc.a_vid.ptr)));
     if (Lt > 0)
         S2_TRY(rms_ada(st, txt, Lt, d, b->eps, b->last ? nullptr : emb, T.m(0, d), T.m(1, d),
-                       static_cast<__half *>(b->a_txt.ptr)));
+                       static_cast<__half *>(sc.a_txt.ptr)));
     // QKV projections (no bias)
     s2::GemmArgs g;
     g.K = d;
@@ -308,16 +354,16 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     g.split = 3 * d;
     g.err = err;
     g.M = L;
-    g.out[0] = b->qkv_vid.ptr;
-    S2_TRY(s2::gemm_f16(st, b->a_vid.ptr, V.qkv.ptr, g));
+    g.out[0] = sc.qkv_vid.ptr;
+    S2_TRY(s2::gemm_f16(st, sc.a_vid.ptr, V.qkv.ptr, g));
     if (Lt > 0) {
         g.M = Lt;
-        g.out[0] = b->qkv_txt.ptr;
-        S2_TRY(s2::gemm_f16(st, b->a_txt.ptr, T.qkv.ptr, g));
+        g.out[0] = sc.qkv_txt.ptr;
+        S2_TRY(s2::gemm_f16(st, sc.a_txt.ptr, T.qkv.ptr, g));
     }
     // windowed MM attention (prologue, attention, text mean)
-    if ((s = s2_attention_layer_forward(b->attn, stream, b->qkv_vid.ptr, S2_F16, L, b->qkv_txt.ptr, Lt, b->att_vid.ptr,
-                                        static_cast<float *>(b->att_txt32.ptr))) != S2_OK) {
+    if ((s = s2_attention_layer_forward(b->attn, stream, sc.qkv_vid.ptr, S2_F16, L, sc.qkv_txt.ptr, Lt, sc.att_vid.ptr,
+                                        static_cast<float *>(sc.att_txt32.ptr))) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
@@ -333,12 +379,12 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     p.emb6 = emb + 2;
     p.gate = V.m(2, d);
     p.resid = vid;
-    p.y = static_cast<float *>(b->h_vid.ptr);
-    S2_TRY(s2::gemm_f16(st, b->att_vid.ptr, V.proj.ptr, p));
+    p.y = static_cast<float *>(sc.h_vid.ptr);
+    S2_TRY(s2::gemm_f16(st, sc.att_vid.ptr, V.proj.ptr, p));
     if (Lt > 0) {
         const long long n = static_cast<long long>(Lt) * d;
         f32_to_f16_kernel<<<static_cast<unsigned>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
-            static_cast<const float *>(b->att_txt32.ptr), n, static_cast<__half *>(b->att_txt16.ptr));
+            static_cast<const float *>(sc.att_txt32.ptr), n, static_cast<__half *>(sc.att_txt16.ptr));
         if (cudaGetLastError() != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: convert launch failed");
         ++launches;
@@ -354,9 +400,9 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         } else {
             p.emb6 = emb + 2;
             p.gate = T.m(2, d);
-            p.y = static_cast<float *>(b->h_txt.ptr);
+            p.y = static_cast<float *>(sc.h_txt.ptr);
         }
-        S2_TRY(s2::gemm_f16(st, b->att_txt16.ptr, T.proj.ptr, p));
+        S2_TRY(s2::gemm_f16(st, sc.att_txt16.ptr, T.proj.ptr, p));
     }
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
     auto mlp = [&](const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y) -> s2_status {
@@ -386,14 +432,14 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         ++launches;
         return S2_OK;
     };
-    if ((s = mlp(V, static_cast<const float *>(b->h_vid.ptr), L, static_cast<__half *>(b->a_vid.ptr),
-                 static_cast<__half *>(b->hid_vid.ptr), vid_out)) != S2_OK) {
+    if ((s = mlp(V, static_cast<const float *>(sc.h_vid.ptr), L, static_cast<__half *>(sc.a_vid.ptr),
+                 static_cast<__half *>(sc.hid_vid.ptr), vid_out)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
     if (Lt > 0 && !b->last &&
-        (s = mlp(T, static_cast<const float *>(b->h_txt.ptr), Lt, static_cast<__half *>(b->a_txt.ptr),
-                 static_cast<__half *>(b->hid_txt.ptr), txt_out)) != S2_OK) {
+        (s = mlp(T, static_cast<const float *>(sc.h_txt.ptr), Lt, static_cast<__half *>(sc.a_txt.ptr),
+                 static_cast<__half *>(sc.hid_txt.ptr), txt_out)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }

@@ -1,0 +1,485 @@
+// s2_dit: the SeedVR2 DiT (input head, the block stack, output head) and one
+// Euler sampling step on sm_100a -- the device-resident counterpart of
+// SeedVR2DiT::forward (src/model/dit.cpp:277-383) with the engine's one-step
+// sampling (make_dit_input, src/core/engine.cpp:125-149;
+// EulerSampler::endpoint, src/model/sampler.cpp:276-286).
+//
+//   input head (SeedVR2DiTInput, seedvr2_dit_input.cpp:311-405):
+//     patchify 1x2x2 of the vc-channel latent in (dy, dx, c) order -> fp16 rows
+//     (K padded to a multiple of 64), video projection and text projection on
+//     the tensor cores (+ bias, fp32 out); timestep sinusoid -> Linear + SiLU
+//     -> Linear + SiLU -> Linear = the block modulation vector emb [6 dim]
+//     (fp32 matrix-vector kernels: one vector, weight-bandwidth bound).
+//   blocks: s2_dit_block in order, sharing one set of activation workspaces.
+//   output head (SeedVR2DiTOutput, seedvr2_dit_output.cpp:349-431):
+//     RMSNorm * weight, adaLN with emb slots 0/1, projection dim -> 4 oc
+//     (+ bias), unpatchify -- fused with the Euler endpoint x - (t/1000) pred
+//     for a sampling step.
+// Every forward is stream-ordered with no host synchronisation.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "s2_buffers.h"
+#include "s2_gemm.h"
+#include "s2_internal.h"
+#include "s2_ops.h"
+
+namespace {
+
+int round64(int x) { return (x + 63) / 64 * 64; }
+
+// patches[p][col] = latent[c][t][2y + dy][2x + dx], col = (dy * 2 + dx) * vc + c;
+// zero for the padding columns col >= 4 vc (seedvr2_dit_input.cpp:335-353).
+__global__ void patchify_kernel(const float *__restrict__ latent, int vc, int T, int H, int W, int kp,
+                                __half *__restrict__ patches)
+{
+    const int Hp = H / 2, Wp = W / 2;
+    const long long total = 1LL * T * Hp * Wp * kp;
+    const long long plane = 1LL * T * H * W;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int col = static_cast<int>(i % kp);
+        const long long p = i / kp;
+        float v = 0.f;
+        if (col < 4 * vc) {
+            const int x = static_cast<int>(p % Wp), y = static_cast<int>((p / Wp) % Hp), t = static_cast<int>(p / (1LL * Wp * Hp));
+            const int blk = col / vc, c = col - blk * vc, dy = blk >> 1, dx = blk & 1;
+            v = latent[c * plane + (1LL * t * H + 2 * y + dy) * W + 2 * x + dx];
+        }
+        patches[i] = __float2half_rn(v);
+    }
+}
+
+// latent33 = noise (oc) || condition (oc) || ones (engine.cpp:125-149)
+__global__ void make_dit_input_kernel(const float *__restrict__ noise, const float *__restrict__ cond, int oc,
+                                      long long plane, float *__restrict__ latent)
+{
+    const long long total = (2LL * oc + 1) * plane;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const long long c = i / plane, o = i - c * plane;
+        latent[i] = c < oc ? noise[i] : (c < 2 * oc ? cond[(c - oc) * plane + o] : 1.f);
+    }
+}
+
+// text rows fp32 [rows][cols] -> fp16 [rows][ld] (zero padding columns)
+__global__ void pad_to_f16_kernel(const float *__restrict__ x, int rows, int cols, int ld, __half *__restrict__ y)
+{
+    const long long total = 1LL * rows * ld;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int c = static_cast<int>(i % ld);
+        const long long r = i / ld;
+        y[i] = __float2half_rn(c < cols ? x[r * cols + c] : 0.f);
+    }
+}
+
+// s[i] = sin(t f_i), s[i + half] = cos(t f_i), f_i = exp(-log(10000) i / half)
+// (seedvr2_dit_input.cpp:362-372, single-precision like the reference)
+__global__ void sinusoid_kernel(float t, int half, float *__restrict__ s)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= half) return;
+    const float freq = expf(__fdiv_rn(__fmul_rn(-logf(10000.f), static_cast<float>(i)), static_cast<float>(half)));
+    const float v = __fmul_rn(t, freq);
+    s[i] = sinf(v);
+    s[i + half] = cosf(v);
+}
+
+// y[o] = act(b[o] + W[o] . x), one warp per output row, fp32 weights; x staged
+// in shared memory. act = SiLU (x / (1 + exp(-x))) when silu != 0.
+__global__ void __launch_bounds__(256) gemv_kernel(const float *__restrict__ Wm, const float *__restrict__ b,
+                                                   const float *__restrict__ x, int K, int N, int silu,
+                                                   float *__restrict__ y)
+{
+    extern __shared__ float xs[];
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const int o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (o >= N) return;
+    const float *w = Wm + static_cast<size_t>(o) * K;
+    float acc = 0.f;
+    for (int i = lane; i < K; i += 32) acc = fmaf(__ldg(w + i), xs[i], acc);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    if (lane == 0) {
+        float v = __fadd_rn(acc, b[o]);
+        if (silu) v = __fdiv_rn(v, __fadd_rn(1.f, expf(-v)));
+        y[o] = v;
+    }
+}
+
+// out[c][t][Y][X] = proj[p][(dy*2 + dx) * oc + c] with p the patch of (t, Y/2, X/2)
+// (seedvr2_dit_output.cpp:402-418); with `noise`, the Euler endpoint
+// out = noise - (t/1000) * pred (sampler.cpp:276-286).
+__global__ void unpatchify_kernel(const float *__restrict__ proj, int oc, int T, int Hp, int Wp,
+                                  const float *__restrict__ noise, float bt, float *__restrict__ out)
+{
+    const int H = 2 * Hp, W = 2 * Wp;
+    const long long plane = 1LL * T * H * W, total = plane * oc;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int c = static_cast<int>(i / plane);
+        const long long o = i - c * plane;
+        const int X = static_cast<int>(o % W), Y = static_cast<int>((o / W) % H), t = static_cast<int>(o / (1LL * W * H));
+        const long long p = (1LL * t * Hp + Y / 2) * Wp + X / 2;
+        const float pred = proj[p * 4 * oc + ((Y & 1) * 2 + (X & 1)) * oc + c];
+        out[i] = noise ? __fsub_rn(noise[i], __fmul_rn(bt, pred)) : pred;
+    }
+}
+
+unsigned grid_for(long long n) { return static_cast<unsigned>(std::min<long long>((n + 255) / 256, 4096)); }
+
+bool upload(s2::DeviceBuffer &b, const float *src, size_t n)
+{
+    return b.ensure(n * 4) && cudaMemcpy(b.ptr, src, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+// W [rows][cols] fp32 -> fp16 [rows][ld] (zero padding)
+bool upload_f16_pad(s2::DeviceBuffer &b, const float *src, size_t rows, size_t cols, size_t ld)
+{
+    std::vector<__half> h(rows * ld, __float2half_rn(0.f));
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) h[r * ld + c] = __float2half_rn(src[r * cols + c]);
+    return b.ensure(h.size() * 2) && cudaMemcpy(b.ptr, h.data(), h.size() * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+}  // namespace
+
+struct s2_dit {
+    int device = 0;
+    int n_blocks = 32, dim = 2560, heads = 20, head_dim = 128, hidden = 6912;
+    float eps = 1e-5f;
+    int vc = 33, tc = 5120, sd = 256, oc = 16;
+    int wt = 0, wh = 0, ww = 0;
+    int kp = 192, tcp = 5120;
+    bool input_loaded = false, output_loaded = false;
+    std::vector<s2_dit_block *> blocks;
+    // input head
+    s2::DeviceBuffer w_vid, b_vid, w_txt, b_txt, w_t1, b_t1, w_t2, b_t2, w_t3, b_t3;
+    // output head
+    s2::DeviceBuffer o_norm, o_shift, o_scale, w_out, b_out;
+    // workspaces
+    s2::DeviceBuffer latent, patches, txt16, vid_a, vid_b, txt_a, txt_b, sinus, th1, th2, emb, o16, proj, err;
+    s2::DeviceBuffer h_noise, h_cond, h_text, h_x0;  // host-step staging
+    int last_launches = 0;
+    cudaStream_t last_stream = nullptr;
+};
+
+extern "C" s2_status s2_dit_create(int device, int n_blocks, int dim, int heads, int head_dim, int mlp_hidden,
+                                   float eps, int video_channels, int text_channels, int sinusoidal_dim,
+                                   int out_channels, int wt, int wh, int ww, s2_dit **out)
+{
+    s2::clear_error();
+    if (!out) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_create: out is NULL");
+    *out = nullptr;
+    if (n_blocks <= 0 || dim != heads * head_dim || video_channels <= 0 || text_channels <= 0 || sinusoidal_dim <= 0 ||
+        sinusoidal_dim % 2 != 0 || out_channels <= 0 || (4 * out_channels) % 32 != 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_create: invalid configuration");
+    const s2_status st = s2_device_check(device);
+    if (st != S2_OK) return st;
+    auto *d = new s2_dit();
+    d->device = device;
+    d->n_blocks = n_blocks;
+    d->dim = dim;
+    d->heads = heads;
+    d->head_dim = head_dim;
+    d->hidden = mlp_hidden;
+    d->eps = eps;
+    d->vc = video_channels;
+    d->tc = text_channels;
+    d->sd = sinusoidal_dim;
+    d->oc = out_channels;
+    d->wt = wt;
+    d->wh = wh;
+    d->ww = ww;
+    d->kp = round64(4 * video_channels);
+    d->tcp = round64(text_channels);
+    d->blocks.assign(n_blocks, nullptr);
+    *out = d;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_destroy(s2_dit *d)
+{
+    if (!d) return S2_OK;
+    for (s2_dit_block *b : d->blocks) s2_dit_block_destroy(b);
+    s2::DeviceGuard guard(d->device);
+    for (s2::DeviceBuffer *b : {&d->w_vid, &d->b_vid, &d->w_txt, &d->b_txt, &d->w_t1, &d->b_t1, &d->w_t2, &d->b_t2,
+                                &d->w_t3, &d->b_t3, &d->o_norm, &d->o_shift, &d->o_scale, &d->w_out, &d->b_out,
+                                &d->latent, &d->patches, &d->txt16, &d->vid_a, &d->vid_b, &d->txt_a, &d->txt_b,
+                                &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise,
+                                &d->h_cond, &d->h_text, &d->h_x0})
+        b->release();
+    delete d;
+    return S2_OK;
+}
+
+extern "C" size_t s2_dit_input_weight_count(const s2_dit *d)
+{
+    if (!d) return 0;
+    const size_t D = d->dim, ed = 6 * D;
+    return D * 4 * d->vc + D + D * d->tc + D + D * d->sd + D + D * D + D + ed * D + ed;
+}
+
+extern "C" size_t s2_dit_output_weight_count(const s2_dit *d)
+{
+    return d ? 3 * static_cast<size_t>(d->dim) + 4 * static_cast<size_t>(d->oc) * (d->dim + 1) : 0;
+}
+
+extern "C" s2_status s2_dit_load_input(s2_dit *d, const float *w, size_t n)
+{
+    s2::clear_error();
+    if (!d || !w) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_load_input: null argument");
+    if (n != s2_dit_input_weight_count(d))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_load_input: %zu floats, the layer reads %zu", n,
+                             s2_dit_input_weight_count(d));
+    s2::DeviceGuard guard(d->device);
+    const size_t D = d->dim, ed = 6 * D;
+    // load_model order (seedvr2_dit_input.cpp:217-224): each InnerProduct is W [out][in] then b [out]
+    bool ok = upload_f16_pad(d->w_vid, w, D, 4 * d->vc, d->kp) && upload(d->b_vid, w + D * 4 * d->vc, D);
+    w += D * 4 * d->vc + D;
+    ok = ok && upload_f16_pad(d->w_txt, w, D, d->tc, d->tcp) && upload(d->b_txt, w + D * d->tc, D);
+    w += D * d->tc + D;
+    ok = ok && upload(d->w_t1, w, D * d->sd) && upload(d->b_t1, w + D * d->sd, D);
+    w += D * d->sd + D;
+    ok = ok && upload(d->w_t2, w, D * D) && upload(d->b_t2, w + D * D, D);
+    w += D * D + D;
+    ok = ok && upload(d->w_t3, w, ed * D) && upload(d->b_t3, w + ed * D, ed);
+    if (!ok) return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_load_input: weight upload failed");
+    d->input_loaded = true;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_load_output(s2_dit *d, const float *w, size_t n)
+{
+    s2::clear_error();
+    if (!d || !w) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_load_output: null argument");
+    if (n != s2_dit_output_weight_count(d))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_load_output: %zu floats, the layer reads %zu", n,
+                             s2_dit_output_weight_count(d));
+    s2::DeviceGuard guard(d->device);
+    const size_t D = d->dim, N = 4 * d->oc;
+    // load_model order (seedvr2_dit_output.cpp:264-270): norm weight, shift, scale, projection W then b
+    const bool ok = upload(d->o_norm, w, D) && upload(d->o_shift, w + D, D) && upload(d->o_scale, w + 2 * D, D) &&
+                    upload_f16_pad(d->w_out, w + 3 * D, N, D, D) && upload(d->b_out, w + 3 * D + N * D, N);
+    if (!ok) return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_load_output: weight upload failed");
+    d->output_loaded = true;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int last, int shifted, const float *w, size_t n)
+{
+    s2::clear_error();
+    if (!d || !w || index < 0 || index >= d->n_blocks)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_load_block: bad block index %d", index);
+    s2_dit_block *b = nullptr;
+    s2_status st = s2_dit_block_create(d->device, index, shared, last, shifted, d->dim, d->heads, d->head_dim,
+                                       d->hidden, d->eps, d->wt, d->wh, d->ww, &b);
+    if (st != S2_OK) return st;
+    if ((st = s2_dit_block_load(b, w, n)) != S2_OK) {
+        s2_dit_block_destroy(b);
+        return st;
+    }
+    s2_dit_block_destroy(d->blocks[index]);
+    d->blocks[index] = b;
+    // all blocks run one after another on one stream: one set of activation workspaces
+    for (s2_dit_block *o : d->blocks)
+        if (o && o != b) {
+            s2::share_block_scratch(b, o);
+            break;
+        }
+    return S2_OK;
+}
+
+// The DiT forward; with `noise` the output is the Euler endpoint instead of the prediction.
+static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, int T, int H, int W,
+                                         const float *text, int Lt, float timestep, const float *noise, float *out)
+{
+    s2::clear_error();
+    if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_forward: model is NULL");
+    if (!d->input_loaded || !d->output_loaded)
+        return s2::set_error(S2_NOT_LOADED, "s2_dit_forward: input/output heads not loaded");
+    for (int i = 0; i < d->n_blocks; ++i)
+        if (!d->blocks[i]) return s2::set_error(S2_NOT_LOADED, "s2_dit_forward: block %d not loaded", i);
+    if (!latent || !out || T <= 0 || H <= 0 || W <= 0 || H % 2 != 0 || W % 2 != 0 || Lt <= 0 || !text)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_forward: latent needs even H and W, and text tokens");
+    s2::DeviceGuard guard(d->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int Hp = H / 2, Wp = W / 2, rows = T * Hp * Wp, D = d->dim, N = 4 * d->oc;
+    const size_t Rz = static_cast<size_t>(rows), Tz = static_cast<size_t>(Lt);
+    const bool fresh = d->err.ptr == nullptr;
+    if (!d->patches.ensure(Rz * d->kp * 2) || !d->txt16.ensure(Tz * d->tcp * 2) || !d->vid_a.ensure(Rz * D * 4) ||
+        !d->vid_b.ensure(Rz * D * 4) || !d->txt_a.ensure(Tz * D * 4) || !d->txt_b.ensure(Tz * D * 4) ||
+        !d->sinus.ensure(d->sd * 4) || !d->th1.ensure(D * 4) || !d->th2.ensure(D * 4) || !d->emb.ensure(6 * D * 4) ||
+        !d->o16.ensure(Rz * D * 2) || !d->proj.ensure(Rz * N * 4) || !d->err.ensure(4))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_forward: workspace allocation failed");
+    if (fresh && cudaMemsetAsync(d->err.ptr, 0, 4, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_forward: memset failed");
+    int32_t *err = static_cast<int32_t *>(d->err.ptr);
+    d->last_stream = st;
+    int launches = 0;
+    s2_status s;
+    auto check = [&](const char *what) {
+        const cudaError_t e = cudaGetLastError();
+        ++launches;
+        return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "s2_dit_forward: %s: %s", what,
+                                                         cudaGetErrorString(e));
+    };
+#define S2_TRY(expr)                      \
+    do {                                  \
+        if ((s = (expr)) != S2_OK) {      \
+            d->last_launches = launches;  \
+            return s;                     \
+        }                                 \
+    } while (0)
+
+    // ---- input head ----
+    patchify_kernel<<<grid_for(Rz * d->kp), 256, 0, st>>>(latent, d->vc, T, H, W, d->kp,
+                                                          static_cast<__half *>(d->patches.ptr));
+    S2_TRY(check("patchify"));
+    pad_to_f16_kernel<<<grid_for(Tz * d->tcp), 256, 0, st>>>(text, Lt, d->tc, d->tcp, static_cast<__half *>(d->txt16.ptr));
+    S2_TRY(check("text convert"));
+    s2::GemmArgs g;
+    g.epilogue = s2::GEMM_EPI_GATED_RESID_F32;  // no modulation, no residual: acc + bias
+    g.N = D;
+    g.err = err;
+    g.M = rows;
+    g.K = d->kp;
+    g.bias = static_cast<const float *>(d->b_vid.ptr);
+    g.y = static_cast<float *>(d->vid_a.ptr);
+    S2_TRY(s2::gemm_f16(st, d->patches.ptr, d->w_vid.ptr, g));
+    ++launches;
+    g.M = Lt;
+    g.K = d->tcp;
+    g.bias = static_cast<const float *>(d->b_txt.ptr);
+    g.y = static_cast<float *>(d->txt_a.ptr);
+    S2_TRY(s2::gemm_f16(st, d->txt16.ptr, d->w_txt.ptr, g));
+    ++launches;
+    const int half = d->sd / 2;
+    sinusoid_kernel<<<(half + 127) / 128, 128, 0, st>>>(timestep, half, static_cast<float *>(d->sinus.ptr));
+    S2_TRY(check("sinusoid"));
+    auto gemv = [&](const s2::DeviceBuffer &Wm, const s2::DeviceBuffer &bv, const s2::DeviceBuffer &x, int K, int Nn,
+                    int silu, s2::DeviceBuffer &y) {
+        gemv_kernel<<<(Nn + 7) / 8, 256, K * 4, st>>>(static_cast<const float *>(Wm.ptr),
+                                                      static_cast<const float *>(bv.ptr),
+                                                      static_cast<const float *>(x.ptr), K, Nn, silu,
+                                                      static_cast<float *>(y.ptr));
+        return check("time embedding");
+    };
+    S2_TRY(gemv(d->w_t1, d->b_t1, d->sinus, d->sd, D, 1, d->th1));
+    S2_TRY(gemv(d->w_t2, d->b_t2, d->th1, D, D, 1, d->th2));
+    S2_TRY(gemv(d->w_t3, d->b_t3, d->th2, D, 6 * D, 0, d->emb));
+
+    // ---- blocks ----
+    float *vid_cur = static_cast<float *>(d->vid_a.ptr), *vid_nxt = static_cast<float *>(d->vid_b.ptr);
+    float *txt_cur = static_cast<float *>(d->txt_a.ptr), *txt_nxt = static_cast<float *>(d->txt_b.ptr);
+    const float *emb = static_cast<const float *>(d->emb.ptr);
+    for (int i = 0; i < d->n_blocks; ++i) {
+        S2_TRY(s2_dit_block_set_runtime_shape(d->blocks[i], T, Hp, Wp));
+        S2_TRY(s2_dit_block_forward(d->blocks[i], stream, vid_cur, rows, txt_cur, Lt, emb, vid_nxt, txt_nxt));
+        launches += s2_dit_block_last_launches(d->blocks[i]);
+        std::swap(vid_cur, vid_nxt);
+        std::swap(txt_cur, txt_nxt);
+    }
+
+    // ---- output head ----
+    S2_TRY(s2::rms_ada(st, vid_cur, rows, D, d->eps, static_cast<const float *>(d->o_norm.ptr), emb,
+                       static_cast<const float *>(d->o_shift.ptr), static_cast<const float *>(d->o_scale.ptr),
+                       d->o16.ptr));
+    ++launches;
+    s2::GemmArgs o;
+    o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+    o.M = rows;
+    o.N = N;
+    o.K = D;
+    o.bias = static_cast<const float *>(d->b_out.ptr);
+    o.y = static_cast<float *>(d->proj.ptr);
+    o.err = err;
+    S2_TRY(s2::gemm_f16(st, d->o16.ptr, d->w_out.ptr, o));
+    ++launches;
+    const float bt = timestep / 1000.0f;
+    unpatchify_kernel<<<grid_for(1LL * rows * N), 256, 0, st>>>(static_cast<const float *>(d->proj.ptr), d->oc, T, Hp,
+                                                                 Wp, noise, bt, out);
+    S2_TRY(check("unpatchify"));
+#undef S2_TRY
+    d->last_launches = launches;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_forward(s2_dit *d, void *stream, const float *latent, int T, int H, int W,
+                                    const float *text, int Lt, float timestep, float *prediction)
+{
+    return dit_forward_into(d, stream, latent, T, H, W, text, Lt, timestep, nullptr, prediction);
+}
+
+extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noise, const float *condition, int T,
+                                       int H, int W, const float *text, int Lt, float timestep, float *x0)
+{
+    s2::clear_error();
+    if (!d || !noise || !condition || !x0 || T <= 0 || H <= 0 || W <= 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_euler_step: invalid arguments");
+    if (d->vc != 2 * d->oc + 1)
+        return s2::set_error(S2_UNSUPPORTED, "s2_dit_euler_step: video_channels %d != 2 * out_channels + 1", d->vc);
+    s2::DeviceGuard guard(d->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const long long plane = 1LL * T * H * W;
+    if (!d->latent.ensure(static_cast<size_t>(plane) * d->vc * 4))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_euler_step: workspace allocation failed");
+    make_dit_input_kernel<<<grid_for(plane * d->vc), 256, 0, st>>>(noise, condition, d->oc, plane,
+                                                                    static_cast<float *>(d->latent.ptr));
+    if (cudaGetLastError() != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: launch failed");
+    const s2_status s = dit_forward_into(d, stream, static_cast<const float *>(d->latent.ptr), T, H, W, text, Lt,
+                                            timestep, noise, x0);
+    if (s == S2_OK) ++d->last_launches;
+    return s;
+}
+
+extern "C" s2_status s2_dit_euler_step_host(s2_dit *d, void *stream, const float *noise, const float *condition,
+                                            int T, int H, int W, const float *text, int Lt, float timestep, float *x0)
+{
+    s2::clear_error();
+    if (!d || !noise || !condition || !text || !x0 || T <= 0 || H <= 0 || W <= 0 || Lt <= 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_euler_step_host: invalid arguments");
+    s2::DeviceGuard guard(d->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t lat = static_cast<size_t>(T) * H * W * d->oc * 4, txt = static_cast<size_t>(Lt) * d->tc * 4;
+    if (!d->h_noise.ensure(lat) || !d->h_cond.ensure(lat) || !d->h_text.ensure(txt) || !d->h_x0.ensure(lat))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_euler_step_host: staging allocation failed");
+    if (cudaMemcpyAsync(d->h_noise.ptr, noise, lat, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(d->h_cond.ptr, condition, lat, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(d->h_text.ptr, text, txt, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step_host: upload failed");
+    s2_status s = s2_dit_euler_step(d, stream, static_cast<const float *>(d->h_noise.ptr),
+                                    static_cast<const float *>(d->h_cond.ptr), T, H, W,
+                                    static_cast<const float *>(d->h_text.ptr), Lt, timestep,
+                                    static_cast<float *>(d->h_x0.ptr));
+    if (s != S2_OK) return s;
+    if (cudaMemcpyAsync(x0, d->h_x0.ptr, lat, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step_host: %s", cudaGetErrorString(cudaGetLastError()));
+    int code = 0;
+    return s2_dit_device_error(d, &code);
+}
+
+extern "C" int s2_dit_last_launches(const s2_dit *d) { return d ? d->last_launches : 0; }
+
+extern "C" s2_status s2_dit_device_error(s2_dit *d, int *code)
+{
+    if (code) *code = 0;
+    if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_device_error: model is NULL");
+    for (s2_dit_block *b : d->blocks) {
+        if (!b) continue;
+        const s2_status s = s2_dit_block_device_error(b, code);
+        if (s != S2_OK) return s;
+    }
+    if (!d->err.ptr) return S2_OK;
+    s2::DeviceGuard guard(d->device);
+    int32_t h = 0;
+    if (cudaStreamSynchronize(d->last_stream) != cudaSuccess || cudaMemcpy(&h, d->err.ptr, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit: device failure: %s", cudaGetErrorString(cudaGetLastError()));
+    if (code) *code = h;
+    if (h != 0) return s2::set_error(S2_INFERENCE_FAILED, "s2_dit: device wait timed out (code %d)", h);
+    return S2_OK;
+}

@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float4 *yd = reinterpret_cast<float4 *>(a.y + static_cast<size_t>(row) * a.N + n);
                         float4 res[8];
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) res[v] = __ldg(rs + v);
+                        for (int v = 0; v < 8; ++v) res[v] = a.resid ? __ldg(rs + v) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
                             float o[4];
@@ -309,7 +309,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
         if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
     } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
-        if (!args.y || !args.resid || args.N % 32 != 0 || (args.emb6 && !args.gate) ||
+        if (!args.y || args.N % 32 != 0 || (args.emb6 && !args.gate) ||
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {

@@ -28,7 +28,8 @@ enum GemmEpilogue : int {
     // fp32 row-major output with the DiT block's gated residual
     // (apply_ada_output_and_residual, seedvr2_dit_block.cpp:807-825):
     // y[row * N + n] = ((acc + bias[n]) * g[n] + resid[row * N + n]) * out_scale,
-    // g[n] = emb6[6 n] + gate[n] (g = 1 when emb6 is null).
+    // g[n] = emb6[6 n] + gate[n] (g = 1 when emb6 is null; no residual when
+    // resid is null: the plain "+ bias" fp32 projection).
     GEMM_EPI_GATED_RESID_F32 = 2,
     // SwiGLU (apply_mlp, :1093-1112): every 256-column tile holds 128 gate
     // columns then the 128 matching "in" columns; out[0] is fp16

@@ -11,10 +11,12 @@
 
 #include <algorithm>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "s2_buffers.h"
 #include "s2_internal.h"
+#include "s2_ops.h"
 
 namespace s2 {
 s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst);
@@ -22,6 +24,18 @@ s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, fl
 
 using s2::DeviceBuffer;
 using s2::DeviceGuard;
+
+// Packed Q/K/V and per-window text outputs: the layer's large activation
+// buffers, shareable between layers that run one after another.
+struct AttnScratch {
+    int device = 0;
+    DeviceBuffer q, k, v, txt_partial;
+    ~AttnScratch()
+    {
+        DeviceGuard g(device);
+        for (DeviceBuffer *b : {&q, &k, &v, &txt_partial}) b->release();
+    }
+};
 
 struct s2_attention_layer {
     int device = 0;
@@ -43,7 +57,8 @@ struct s2_attention_layer {
     DeviceBuffer d_cu, d_rows, d_work, d_rope;
 
     DeviceBuffer d_weights;  // gammas [4][128] + freqs [21]
-    DeviceBuffer d_q, d_k, d_v, d_txt_partial, d_err;
+    std::shared_ptr<AttnScratch> sc = std::make_shared<AttnScratch>();
+    DeviceBuffer d_err;
     DeviceBuffer d_in_vid, d_in_txt, d_out_vid, d_out_vid32, d_out_txt;  // host-forward staging
     cudaStream_t last_stream = nullptr;
     int last_launches = 0;
@@ -51,8 +66,7 @@ struct s2_attention_layer {
     ~s2_attention_layer()
     {
         DeviceGuard g(device);
-        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_q, &d_k, &d_v, &d_txt_partial,
-                                &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt})
+        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt})
             b->release();
     }
 
@@ -153,6 +167,7 @@ extern "C" s2_status s2_attention_layer_create(int device, int heads, int head_d
     if (dc != S2_OK) return dc;
     auto *l = new s2_attention_layer;
     l->device = device;
+    l->sc->device = device;
     l->heads = heads;
     l->eps = eps;
     l->shifted = shifted ? 1 : 0;
@@ -231,23 +246,23 @@ extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *str
     const int dim = l->heads * S2_HEAD_DIM;
     const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;
     const size_t txt_bytes = static_cast<size_t>(std::max(l->n_local, 1)) * std::max(Lt, 1) * dim * 2;
-    if (!l->d_q.ensure(qkv_bytes) || !l->d_k.ensure(qkv_bytes) || !l->d_v.ensure(qkv_bytes) ||
-        !l->d_txt_partial.ensure(txt_bytes))
+    AttnScratch &sc = *l->sc;
+    if (!sc.q.ensure(qkv_bytes) || !sc.k.ensure(qkv_bytes) || !sc.v.ensure(qkv_bytes) || !sc.txt_partial.ensure(txt_bytes))
         return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: workspace allocation failed");
     if (!l->d_err.ptr && (!l->d_err.ensure(sizeof(int32_t)) || cudaMemset(l->d_err.ptr, 0, sizeof(int32_t)) != cudaSuccess))
         return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: error word allocation failed");
     rc = s2_qk_norm_rope(stream, vid_qkv, txt_qkv, in_dtype, l->heads, l->eps, l->gammas(), l->d_rope.ptr,
-                         static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows, l->mode, l->d_q.ptr, l->d_k.ptr,
-                         l->d_v.ptr);
+                         static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows, l->mode, sc.q.ptr, sc.k.ptr,
+                         sc.v.ptr);
     if (rc != S2_OK) return rc;
-    rc = s2_window_attention(stream, l->mode, l->d_q.ptr, l->d_k.ptr, l->d_v.ptr, l->heads, l->n_rows,
+    rc = s2_window_attention(stream, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
                              static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
                              static_cast<const s2_row *>(l->d_rows.ptr), static_cast<const int32_t *>(l->d_work.ptr),
-                             l->n_work, vid_out, l->d_txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
+                             l->n_work, vid_out, sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
     if (rc != S2_OK) return rc;
     l->last_launches = 2;
     if (Lt > 0) {
-        rc = s2_text_window_sum(stream, l->mode, l->d_txt_partial.ptr, l->n_local, Lt, dim,
+        rc = s2_text_window_sum(stream, l->mode, sc.txt_partial.ptr, l->n_local, Lt, dim,
                                 1.f / static_cast<float>(l->n_total_windows), 0, txt_out);
         if (rc != S2_OK) return rc;
         l->last_launches = 3;
@@ -329,3 +344,10 @@ extern "C" s2_status s2_attention_layer_device_error(s2_attention_layer *l, int 
     }
     return S2_OK;
 }
+
+namespace s2 {
+void share_attention_scratch(s2_attention_layer *dst, const s2_attention_layer *src)
+{
+    if (dst && src && dst != src) dst->sc = src->sc;
+}
+}  // namespace s2

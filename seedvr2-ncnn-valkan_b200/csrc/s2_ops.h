@@ -1,0 +1,23 @@
+// Internal helpers shared between the layer objects of libs2b200 (not part of
+// the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "s2_b200.h"
+
+namespace s2 {
+
+// Let `dst` use the same activation scratch (packed Q/K/V, text partials /
+// block activations) as `src`. Only for objects whose forwards run one after
+// another on one stream, like the blocks of one DiT forward.
+void share_attention_scratch(s2_attention_layer *dst, const s2_attention_layer *src);
+void share_block_scratch(s2_dit_block *dst, const s2_dit_block *src);
+
+// y = fp16( ada( x * inv_rms(x) [* gamma] ) ) per row (s2_block.cu); gamma,
+// emb6 may be null (no gamma / no modulation).
+s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,
+                  const float *emb6, const float *shift, const float *scale, void *y_f16);
+s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y_f16);
+
+}  // namespace s2

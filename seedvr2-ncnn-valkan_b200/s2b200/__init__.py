@@ -9,6 +9,8 @@ Mirrors the reference's layer surface (czwdysj/seedvr2-ncnn-valkan):
   * ``make_windows``            <- SeedVR2DiTBlock::make_windows (src/layers/seedvr2_dit_block.cpp:827-868)
   * ``SeedVR2DiTBlockAttention`` <- SeedVR2DiTBlock's attention stage: load_param (:643-655),
     load_model norm/freqs part (:657-688), set_runtime_shape (.h:55), attention() (:870-1091)
+  * ``SeedVR2DiT``               <- the DiT (src/model/dit.cpp:277-383: input head, 32 blocks,
+    output head) and one Euler step (src/core/engine.cpp:125-149, src/model/sampler.cpp:276-286)
   * ``SeedVR2DiTBlock``          <- the whole block (seedvr2_dit_block.cpp: load_param :643-655,
     load_model :657-688, forward :1114-1267)
   * ``DynamicFramewiseSpatialAttention`` <- the VAE mid-block attention layer
@@ -82,6 +84,21 @@ _SIGS = {
     "s2_attention_layer_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_window_attention_noalloc": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.c_int] + [ctypes.c_int] * 5
                                         + [ctypes.c_float] + [ctypes.c_int] * 4 + [_vp] * 5),
+    "s2_dit_create": (ctypes.c_int, [ctypes.c_int] * 6 + [ctypes.c_float] + [ctypes.c_int] * 7
+                      + [ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_dit_destroy": (ctypes.c_int, [_vp]),
+    "s2_dit_input_weight_count": (ctypes.c_size_t, [_vp]),
+    "s2_dit_output_weight_count": (ctypes.c_size_t, [_vp]),
+    "s2_dit_load_input": (ctypes.c_int, [_vp, _f32p, ctypes.c_size_t]),
+    "s2_dit_load_block": (ctypes.c_int, [_vp] + [ctypes.c_int] * 4 + [_f32p, ctypes.c_size_t]),
+    "s2_dit_load_output": (ctypes.c_int, [_vp, _f32p, ctypes.c_size_t]),
+    "s2_dit_forward": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
+    "s2_dit_euler_step": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3
+                          + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
+    "s2_dit_euler_step_host": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3
+                               + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
+    "s2_dit_last_launches": (ctypes.c_int, [_vp]),
+    "s2_dit_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_block_create": (ctypes.c_int, [ctypes.c_int] * 9 + [ctypes.c_float] + [ctypes.c_int] * 3
                             + [ctypes.POINTER(ctypes.c_void_p)]),
     "s2_dit_block_destroy": (ctypes.c_int, [_vp]),
@@ -362,6 +379,102 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
                     stream=None):
     _check(lib().s2_text_window_sum(_stream_ptr(stream), mode, _ptr(txt_partial), n_windows, text_len, dim,
                                     ctypes.c_float(scale), int(accumulate), _ptr(txt_out)), "s2_text_window_sum")
+
+
+def block_flags(index: int, n_blocks: int = 32) -> dict:
+    """Per-block flags of the exported model (shared weights from block 10 on,
+    odd blocks shifted, the final block last)."""
+    return dict(shared=index >= 10, shifted=index % 2 == 1, last=index == n_blocks - 1)
+
+
+class SeedVR2DiT:
+    """The DiT on a B200: input head, blocks, output head, and one Euler step.
+
+    ``load_input`` / ``load_block`` / ``load_output`` take the host fp32
+    weight streams in the reference's load orders; ``forward`` the 33-channel
+    latent; ``euler_step`` noise + condition latents and the text embedding
+    (device tensors), ``euler_step_host`` the same on numpy arrays.
+    """
+
+    def __init__(self, device=0, n_blocks=32, dim=2560, heads=20, head_dim=128, mlp_hidden=6912, eps=1e-5,
+                 video_channels=33, text_channels=5120, sinusoidal_dim=256, out_channels=16, window_override=(0, 0, 0)):
+        h = ctypes.c_void_p()
+        _check(lib().s2_dit_create(device, n_blocks, dim, heads, head_dim, mlp_hidden, ctypes.c_float(eps),
+                                   video_channels, text_channels, sinusoidal_dim, out_channels,
+                                   *[int(x) for x in window_override], ctypes.byref(h)), "s2_dit_create")
+        self.handle = h
+        self.n_blocks, self.dim, self.out_channels, self.text_channels = n_blocks, dim, out_channels, text_channels
+
+    def input_weight_count(self) -> int:
+        return int(lib().s2_dit_input_weight_count(self.handle))
+
+    def output_weight_count(self) -> int:
+        return int(lib().s2_dit_output_weight_count(self.handle))
+
+    def load_input(self, weights):
+        w = np.ascontiguousarray(weights, np.float32).ravel()
+        _check(lib().s2_dit_load_input(self.handle, w.ctypes.data_as(_f32p), w.size), "s2_dit_load_input")
+
+    def load_block(self, index, weights, shared=None, last=None, shifted=None):
+        f = block_flags(index, self.n_blocks)
+        f.update({k: v for k, v in dict(shared=shared, last=last, shifted=shifted).items() if v is not None})
+        w = np.ascontiguousarray(weights, np.float32).ravel()
+        _check(lib().s2_dit_load_block(self.handle, index, int(f["shared"]), int(f["last"]), int(f["shifted"]),
+                                       w.ctypes.data_as(_f32p), w.size), "s2_dit_load_block")
+
+    def load_output(self, weights):
+        w = np.ascontiguousarray(weights, np.float32).ravel()
+        _check(lib().s2_dit_load_output(self.handle, w.ctypes.data_as(_f32p), w.size), "s2_dit_load_output")
+
+    def forward(self, latent, text, timestep, prediction=None, stream=None):
+        torch = _torch()
+        vc, T, H, W = latent.shape
+        if prediction is None:
+            prediction = torch.empty((self.out_channels, T, H, W), dtype=torch.float32, device=latent.device)
+        _check(lib().s2_dit_forward(self.handle, _stream_ptr(stream), _ptr(latent), T, H, W, _ptr(text),
+                                    text.shape[0], ctypes.c_float(timestep), _ptr(prediction)), "s2_dit_forward")
+        return prediction
+
+    def euler_step(self, noise, condition, text, timestep=1000.0, x0=None, stream=None):
+        torch = _torch()
+        _, T, H, W = noise.shape
+        if x0 is None:
+            x0 = torch.empty_like(noise)
+        _check(lib().s2_dit_euler_step(self.handle, _stream_ptr(stream), _ptr(noise), _ptr(condition), T, H, W,
+                                       _ptr(text), text.shape[0], ctypes.c_float(timestep), _ptr(x0)),
+               "s2_dit_euler_step")
+        return x0
+
+    def euler_step_host(self, noise, condition, text, timestep=1000.0, x0=None, stream=None):
+        noise, condition, text = (np.ascontiguousarray(a, np.float32) for a in (noise, condition, text))
+        _, T, H, W = noise.shape
+        if x0 is None:
+            x0 = np.empty_like(noise)
+        _check(lib().s2_dit_euler_step_host(self.handle, _stream_ptr(stream) if stream is not None else None,
+                                            ctypes.c_void_p(noise.ctypes.data), ctypes.c_void_p(condition.ctypes.data),
+                                            T, H, W, ctypes.c_void_p(text.ctypes.data), text.shape[0],
+                                            ctypes.c_float(timestep), ctypes.c_void_p(x0.ctypes.data)),
+               "s2_dit_euler_step_host")
+        return x0
+
+    def last_launches(self) -> int:
+        return lib().s2_dit_last_launches(self.handle)
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_dit_device_error(self.handle, ctypes.byref(code))
+        return code.value
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            lib().s2_dit_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class SeedVR2DiTBlock:

@@ -125,3 +125,44 @@ def block_gemm_flops(L, text_len, dim, mlp_hidden, last=False):
     per_row = 2.0 * dim * (3 * dim + dim + 2 * mlp_hidden + mlp_hidden)
     txt_rows = text_len if not last else 0
     return per_row * L + per_row * txt_rows + (2.0 * dim * 4 * dim * text_len if last else 0.0)
+
+
+# DiT heads (SeedVR2DiTInput / SeedVR2DiTOutput) and the config-2 latent.
+DIT_CFG2_LATENT = (6, 90, 160)   # T, H, W of the 16-channel latent (720p x 21 frames)
+DIT_HEADS = dict(video_channels=33, text_channels=5120, sinusoidal_dim=256, out_channels=16)
+
+
+def dit_input_weights(dim, video_channels=33, text_channels=5120, sinusoidal_dim=256, seed=668):
+    """SeedVR2DiTInput weight stream (load_model order, seedvr2_dit_input.cpp:217-224):
+    video, text, time-in, time-hidden, time-out projections, each W [out][in]
+    ~ N(0, 0.02) then b ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    ed = 6 * dim
+    parts = []
+    for n_in, n_out in ((4 * video_channels, dim), (text_channels, dim), (sinusoidal_dim, dim), (dim, dim),
+                        (dim, ed)):
+        parts += [0.02 * rng.standard_normal(n_in * n_out, dtype=np.float32),
+                  0.02 * rng.standard_normal(n_out, dtype=np.float32)]
+    return np.concatenate(parts).astype(np.float32)
+
+
+def dit_output_weights(dim, out_channels=16, seed=669):
+    """SeedVR2DiTOutput weight stream (seedvr2_dit_output.cpp:264-270): norm
+    weight 1 + 0.1 N, shift and scale N(0, 0.02), projection W, b ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    n = 4 * out_channels
+    return np.concatenate([(1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32),
+                           0.02 * rng.standard_normal(dim, dtype=np.float32),
+                           0.02 * rng.standard_normal(dim, dtype=np.float32),
+                           0.02 * rng.standard_normal(n * dim, dtype=np.float32),
+                           0.02 * rng.standard_normal(n, dtype=np.float32)]).astype(np.float32)
+
+
+def dit_latents(latent_shape, out_channels=16, text_len=TEXT_LEN, text_channels=5120, seed=670):
+    """(noise, condition [oc, T, H, W] ~ N(0, 1), text [Lt, text_channels] ~ N(0, 1))."""
+    T, H, W = latent_shape
+    rng = np.random.default_rng(seed)
+    noise = rng.standard_normal((out_channels, T, H, W), dtype=np.float32)
+    cond = rng.standard_normal((out_channels, T, H, W), dtype=np.float32)
+    text = rng.standard_normal((text_len, text_channels), dtype=np.float32)
+    return noise, cond, text
