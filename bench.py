@@ -17,6 +17,14 @@ roofline  = the attention kernel alone: FLOPs per launch / mean launch time
 cpu_baseline / --impl reference: the reference's own CPU attention()
             (oracle/_ref, built from the reference sources) on a bounded
             sample of the same workload, on this host's cores.
+euler_step (N = 1): the second half of the metric -- one full DiT Euler step
+            at 720p (33-channel 6x90x160 latent, 58 text
+            tokens x 5120, 32 blocks of dim 2560 / 20 heads / SwiGLU 6912,
+            random-init weights) through s2_dit_euler_step, replayed as a
+            CUDA graph; device ms per step, the same through the host-buffer
+            call (e2e), GEMM throughput, clocks.
+vae_attention (N = 1): the VAE mid-block attention layer at config 4
+            (C 512, 6 frames of 90x160) through s2_vae_attention_forward.
 
 Multi-GPU (torchrun): each rank processes its own clip's windows (weak
 scaling, no data-path collective). --shard instead splits ONE clip's windows
@@ -347,6 +355,12 @@ def run_ours(args, rank, world, local_rank):
         e2e = run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, fr, mode, override,
                       step_flops_all, dist)
 
+    extra = {}
+    if world == 1 and not args.no_euler:
+        extra["euler_step"] = run_euler(args, torch, s2b200, synth, dev)
+    if world == 1 and not args.no_vae:
+        extra["vae_attention"] = run_vae(args, torch, s2b200, synth, dev)
+
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -366,6 +380,7 @@ def run_ours(args, rank, world, local_rank):
                 "clocks": clk.summary()}
         if e2e:
             line["e2e"] = e2e
+        line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_reference_sample(grid, Lt, heads)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -428,6 +443,116 @@ def run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, 
             "path": "s2_attention_layer_forward_host (pinned host buffers)"}
 
 
+def run_euler(args, torch, s2b200, synth, dev):
+    """One DiT Euler step at 720p (config 2) on this GPU; returns a dict."""
+    t0 = time.perf_counter()
+    m = s2b200.SeedVR2DiT(device=dev.index)
+    m.load_input(synth.dit_input_weights(2560))
+    m.load_output(synth.dit_output_weights(2560))
+    for i in range(32):
+        m.load_block(i, synth.block_weights(2560, 20, 6912, s2b200.block_flags(i)["shared"], seed=100 + i))
+    load_s = time.perf_counter() - t0
+    noise, cond, text = synth.dit_latents(synth.DIT_CFG2_LATENT)
+    n, c, t = (torch.from_numpy(a).to(dev) for a in (noise, cond, text))
+    x0 = torch.empty_like(n)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(3, args.warmup)):  # eager, capture, replays
+        m.euler_step(n, c, t, 1000.0, x0, stream=stream)
+    torch.cuda.synchronize()
+    if m.device_error() != 0:
+        raise RuntimeError("DiT device error")
+    steps = max(1, args.euler_steps)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    with ClockSampler(dev.index) as clk:
+        ev[0].record(stream)
+        for i in range(steps):
+            m.euler_step(n, c, t, 1000.0, x0, stream=stream)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    ms = float(np.mean(per))
+    ok = bool(torch.isfinite(x0).all().item())
+    L = 6 * 45 * 80
+    gemm = sum(synth.block_gemm_flops(L, 58, 2560, 6912, last=(i == 31)) for i in range(32))
+    att = 16 * sum(synth.attention_flops(s2b200.make_windows(6, 45, 80, sh), 58, 20) for sh in (0, 1))
+    # end to end: pinned host noise / condition / text in, x0 out, copies inside the timed region
+    hn, hc, ht = (torch.from_numpy(a).pin_memory().numpy() for a in (noise, cond, text))
+    hx = torch.empty(noise.shape, dtype=torch.float32).pin_memory().numpy()
+    m.euler_step_host(hn, hc, ht, 1000.0, hx, stream=stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(steps, args.e2e_steps))
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        m.euler_step_host(hn, hc, ht, 1000.0, hx, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    launches = m.last_launches()
+    m.close()
+    return {"workload": "DiT Euler step at 720p: latent 33x6x90x160 -> 21,600 tokens, 58 text tokens x 5120, "
+                        "32 blocks (dim 2560, 20 heads, SwiGLU 6912), t = 1000, one step, cfg 1",
+            "ms_per_step": ms, "ms_min": float(min(per)), "steps": steps, "higher_is_better": False,
+            "gemm_tflop_per_step": gemm / 1e12, "attention_tflop_per_step": att / 1e12,
+            "tflops_overall": (gemm + att) / (ms * 1e-3) / 1e12, "gpu_launches_per_step": launches,
+            "cuda_graph": True, "finite": ok, "weights_load_s": load_s,
+            "e2e": {"ms_per_step": e2e_ms, "unit": "ms", "steps": e2e_steps,
+                    "h2d_bytes_per_step": int(hn.nbytes + hc.nbytes + ht.nbytes),
+                    "d2h_bytes_per_step": int(hx.nbytes), "path": "s2_dit_euler_step_host (pinned host buffers)"},
+            "clocks": clk.summary()}
+
+
+def run_vae(args, torch, s2b200, synth, dev):
+    """VAE mid-block attention (config 4) on this GPU; returns a dict."""
+    shape = synth.VAE_CFG4
+    x, w = synth.vae_inputs(shape)
+    lay = s2b200.DynamicFramewiseSpatialAttention(device=dev.index)
+    lay.load_param(shape[0])
+    lay.load_model(w)
+    xd = torch.from_numpy(x).to(dev)
+    y = torch.empty_like(xd)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(3, args.warmup)):
+        lay.forward(xd, y, stream=stream)
+    torch.cuda.synchronize()
+    steps = max(1, args.vae_steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(steps):
+            lay.forward(xd, y, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if lay.device_error() != 0:
+        raise RuntimeError("VAE attention device error")
+    # the attention core alone (the same kernel as in the layer), on the layer's own operands
+    C, T, H, W = shape
+    N = H * W
+    q, k, v, o = (torch.randn((T * N, 512), device=dev).half() for _ in range(4))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(2):
+        s2b200.spatial_attention(q, k, v, C, T, N, o, err, stream=stream)
+    e0.record(stream)
+    for _ in range(steps):
+        s2b200.spatial_attention(q, k, v, C, T, N, o, err, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    core_ms = e0.elapsed_time(e1) / steps
+    af = synth.vae_attention_flops(shape)
+    hx = torch.from_numpy(x).pin_memory().numpy()
+    lay.forward_host(hx)
+    t0 = time.perf_counter()
+    lay.forward_host(hx)
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    lay.close()
+    return {"workload": "VAE mid-block attention, C 512, 6 frames x 90x160 = 14,400 tokens per frame",
+            "ms_per_forward": ms, "attention_core_ms": core_ms,
+            "attention_tflops": af / (core_ms * 1e-3) / 1e12, "attention_tflop": af / 1e12,
+            "projection_tflop": synth.vae_projection_flops(shape) / 1e12, "gpu_launches_per_forward": 5,
+            "e2e_ms": e2e_ms, "clocks": clk.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -440,6 +565,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-euler", action="store_true", help="skip the DiT Euler-step measurement")
+    ap.add_argument("--euler-steps", type=int, default=5)
+    ap.add_argument("--no-vae", action="store_true", help="skip the VAE attention measurement")
+    ap.add_argument("--vae-steps", type=int, default=5)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -296,6 +296,11 @@ S2_API s2_status s2_dit_euler_step(s2_dit *model, void *stream, const float *noi
 /* Same on HOST buffers (copies in and out, synchronises `stream`). */
 S2_API s2_status s2_dit_euler_step_host(s2_dit *model, void *stream, const float *noise, const float *condition,
                                         int T, int H, int W, const float *text, int Lt, float timestep, float *x0);
+/* From the second call with the same shapes, buffers and timestep,
+ * s2_dit_euler_step replays the step as one CUDA graph (captured on an
+ * internal stream); enable = 0 keeps every call eager. On by default; a call
+ * on a stream that is itself being captured always runs eagerly. */
+S2_API s2_status s2_dit_set_graph(s2_dit *model, int enable);
 S2_API int s2_dit_last_launches(const s2_dit *model);
 S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);
 

@@ -33,13 +33,14 @@ namespace {
 
 // y = fp16( ada( x * inv_rms(x) [* gamma] ) ), one warp per row.
 //   inv_rms = 1 / sqrt(float(sum x^2 (double) / dim) + eps)           (:770-782)
-//   ada: v * (emb[6c + s + 1] + scale[c]) + emb[6c + s] + shift[c]     (:784-805)
-// emb6 == nullptr skips the modulation (the last block's text input); gamma
-// is the output head's RMSNorm weight (seedvr2_dit_output.cpp:383).
+//   ada: (v * mul[c] + add0[c]) + add1[c] with mul = emb[6c + s + 1] + scale[c],
+//        add0 = emb[6c + s], add1 = shift[c] precomputed (:784-805)
+// mul == nullptr skips the modulation (the last block's text input); gamma is
+// the output head's RMSNorm weight (seedvr2_dit_output.cpp:383).
 __global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ x, int rows, int dim, float eps,
-                                                      const float *__restrict__ gamma,
-                                                      const float *__restrict__ emb6, const float *__restrict__ shift,
-                                                      const float *__restrict__ scale, __half *__restrict__ y)
+                                                      const float *__restrict__ gamma, const float *__restrict__ mul,
+                                                      const float *__restrict__ add0, const float *__restrict__ add1,
+                                                      __half *__restrict__ y)
 {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -58,20 +59,45 @@ __global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ 
     __half2 *yr = reinterpret_cast<__half2 *>(y + static_cast<size_t>(warp) * dim);
     for (int i = lane; i < dim / 4; i += 32) {
         const float4 v = __ldg(xr + i);
-        float f[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int c = 4 * i + e;
-            float t = __fmul_rn(f[e], inv);
-            if (gamma) t = __fmul_rn(t, __ldg(gamma + c));
-            if (emb6) {
-                t = __fmul_rn(t, __fadd_rn(__ldg(emb6 + 6 * c + 1), __ldg(scale + c)));
-                t = __fadd_rn(__fadd_rn(t, __ldg(emb6 + 6 * c)), __ldg(shift + c));
-            }
-            f[e] = t;
+        float f[4] = {__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv)};
+        if (gamma) {
+            const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + i);
+            f[0] = __fmul_rn(f[0], g.x);
+            f[1] = __fmul_rn(f[1], g.y);
+            f[2] = __fmul_rn(f[2], g.z);
+            f[3] = __fmul_rn(f[3], g.w);
+        }
+        if (mul) {
+            const float4 m = __ldg(reinterpret_cast<const float4 *>(mul) + i);
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(add0) + i);
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(add1) + i);
+            f[0] = __fadd_rn(__fadd_rn(__fmul_rn(f[0], m.x), a.x), b.x);
+            f[1] = __fadd_rn(__fadd_rn(__fmul_rn(f[1], m.y), a.y), b.y);
+            f[2] = __fadd_rn(__fadd_rn(__fmul_rn(f[2], m.z), a.z), b.z);
+            f[3] = __fadd_rn(__fadd_rn(__fmul_rn(f[3], m.w), a.w), b.w);
         }
         yr[2 * i] = __floats2half2_rn(f[0], f[1]);
         yr[2 * i + 1] = __floats2half2_rn(f[2], f[3]);
+    }
+}
+
+// Per-forward modulation vectors of a branch from the block input emb and the
+// branch's [6][dim] adaLN parameters (attn shift, scale, gate, mlp shift,
+// scale, gate): out [8][dim] = attn {mul, add0, add1}, mlp {mul, add0, add1},
+// attn gate, mlp gate, with mul = emb[6c + s + 1] + scale, add0 = emb[6c + s],
+// add1 = shift, gate = emb[6c + s + 2] + gate (s = 0 attention, 3 MLP).
+__global__ void modulation_kernel(const float *__restrict__ emb, const float *__restrict__ mod6, int dim,
+                                  float *__restrict__ out)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= dim) return;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int s = 3 * k;
+        out[(3 * k + 0) * dim + c] = __fadd_rn(emb[6 * c + s + 1], mod6[(s + 1) * dim + c]);
+        out[(3 * k + 1) * dim + c] = emb[6 * c + s];
+        out[(3 * k + 2) * dim + c] = mod6[s * dim + c];
+        out[(6 + k) * dim + c] = __fadd_rn(emb[6 * c + s + 2], mod6[(s + 2) * dim + c]);
     }
 }
 
@@ -100,11 +126,25 @@ bool upload(s2::DeviceBuffer &b, const void *src, size_t bytes)
     return b.ensure(bytes) && cudaMemcpy(b.ptr, src, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
 }
 
+__global__ void f32_to_f16_kernel(const float *__restrict__ x, long long n, __half *__restrict__ y);
+
+// fp32 host weights -> fp16 device weights, converted on the device
 bool upload_f16(s2::DeviceBuffer &b, const float *src, size_t n)
 {
-    std::vector<__half> h(n);
-    for (size_t i = 0; i < n; ++i) h[i] = __float2half_rn(src[i]);
-    return upload(b, h.data(), n * 2);
+    if (!b.ensure(n * 2)) return false;
+    void *tmp = nullptr;
+    if (cudaMalloc(&tmp, n * 4) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    bool ok = cudaMemcpy(tmp, src, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (ok) {
+        f32_to_f16_kernel<<<static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 4096)), 256>>>(
+            static_cast<const float *>(tmp), static_cast<long long>(n), static_cast<__half *>(b.ptr));
+        ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    }
+    cudaFree(tmp);
+    return ok;
 }
 
 }  // namespace
@@ -132,6 +172,7 @@ struct s2_dit_block {
     Branch vid, txt;
     s2_attention_layer *attn = nullptr;
     std::shared_ptr<BlockScratch> sc = std::make_shared<BlockScratch>();
+    s2::DeviceBuffer mods;  // fp32 [2 branches][8][dim] modulation vectors of the current forward
     s2::DeviceBuffer err;
     s2::DeviceBuffer hv, ht, he, hov, hot;  // forward_host staging
     int last_launches = 0;
@@ -182,7 +223,7 @@ extern "C" s2_status s2_dit_block_destroy(s2_dit_block *b)
         s2::DeviceGuard guard(b->device);
         b->vid.release();
         b->txt.release();
-        for (s2::DeviceBuffer *x : {&b->err, &b->hv, &b->ht, &b->he, &b->hov, &b->hot})
+        for (s2::DeviceBuffer *x : {&b->mods, &b->err, &b->hv, &b->ht, &b->he, &b->hov, &b->hot})
             x->release();
     }
     s2_attention_layer_destroy(b->attn);
@@ -266,25 +307,31 @@ extern "C" s2_status s2_dit_block_set_window_subset(s2_dit_block *b, const int32
 
 namespace {
 
-s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *emb6, const float *shift,
-                  const float *scale, __half *y)
+s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *mod3, __half *y)
 {
-    return s2::rms_ada(st, x, rows, dim, eps, nullptr, emb6, shift, scale, y);
+    return s2::rms_ada(st, x, rows, dim, eps, nullptr, mod3, mod3 ? mod3 + dim : nullptr,
+                       mod3 ? mod3 + 2 * dim : nullptr, y);
 }
 
 }  // namespace
 
 namespace s2 {
 
-s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,
-                  const float *emb6, const float *shift, const float *scale, void *y)
+s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma, const float *mul,
+                  const float *add0, const float *add1, void *y)
 {
     if (rows <= 0) return S2_OK;
     if (dim % 4 != 0) return set_error(S2_INVALID_ARGUMENT, "rms_ada: dim %d not a multiple of 4", dim);
-    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, gamma, emb6, shift, scale,
-                                                   static_cast<__half *>(y));
+    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, gamma, mul, add0, add1, static_cast<__half *>(y));
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "rms_ada launch: %s", cudaGetErrorString(e));
+}
+
+s2_status modulation_vectors(cudaStream_t st, const float *emb, const float *mod6, int dim, float *out)
+{
+    modulation_kernel<<<(dim + 255) / 256, 256, 0, st>>>(emb, mod6, dim, out);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "modulation launch: %s", cudaGetErrorString(e));
 }
 
 s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y)
@@ -324,7 +371,8 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) || !sc.qkv_vid.ensure(Lz * 3 * d * 2) ||
         !sc.qkv_txt.ensure(Tz * 3 * d * 2) || !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
         !sc.att_txt16.ensure(Tz * d * 2) || !sc.h_vid.ensure(Lz * d * 4) || !sc.h_txt.ensure(Tz * d * 4) ||
-        !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4))
+        !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4) ||
+        !b->mods.ensure(static_cast<size_t>(16) * d * 4))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward: workspace allocation failed");
     if (fresh && cudaMemsetAsync(b->err.ptr, 0, 4, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: memset failed");
@@ -342,11 +390,13 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         ++launches;                  \
     } while (0)
 
+    // modulation vectors of both branches for this emb
+    float *mv = static_cast<float *>(b->mods.ptr), *mt = mv + 8 * static_cast<size_t>(d);
+    S2_TRY(s2::modulation_vectors(st, emb, V.m(0, d), d, mv));
+    if (Lt > 0) S2_TRY(s2::modulation_vectors(st, emb, T.m(0, d), d, mt));
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
-    S2_TRY(rms_ada(st, vid, L, d, b->eps, emb, V.m(0, d), V.m(1, d), static_cast<__half *>(sc.a_vid.ptr)));
-    if (Lt > 0)
-        S2_TRY(rms_ada(st, txt, Lt, d, b->eps, b->last ? nullptr : emb, T.m(0, d), T.m(1, d),
-                       static_cast<__half *>(sc.a_txt.ptr)));
+    S2_TRY(rms_ada(st, vid, L, d, b->eps, mv, static_cast<__half *>(sc.a_vid.ptr)));
+    if (Lt > 0) S2_TRY(rms_ada(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, static_cast<__half *>(sc.a_txt.ptr)));
     // QKV projections (no bias)
     s2::GemmArgs g;
     g.K = d;
@@ -376,8 +426,7 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     p.err = err;
     p.M = L;
     p.bias = static_cast<const float *>(V.proj_b.ptr);
-    p.emb6 = emb + 2;
-    p.gate = V.m(2, d);
+    p.gmul = mv + 6 * static_cast<size_t>(d);
     p.resid = vid;
     p.y = static_cast<float *>(sc.h_vid.ptr);
     S2_TRY(s2::gemm_f16(st, sc.att_vid.ptr, V.proj.ptr, p));
@@ -393,20 +442,19 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         p.resid = txt;
         if (b->last) {
             // vid_only modulation: plain residual, and the text output is 2 * (proj + txt)
-            p.emb6 = nullptr;
-            p.gate = nullptr;
+            p.gmul = nullptr;
             p.out_scale = 2.f;
             p.y = txt_out;
         } else {
-            p.emb6 = emb + 2;
-            p.gate = T.m(2, d);
+            p.gmul = mt + 6 * static_cast<size_t>(d);
             p.y = static_cast<float *>(sc.h_txt.ptr);
         }
         S2_TRY(s2::gemm_f16(st, sc.att_txt16.ptr, T.proj.ptr, p));
     }
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
-    auto mlp = [&](const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y) -> s2_status {
-        s2_status r = rms_ada(st, hx, rows, d, b->eps, emb + 3, br.m(3, d), br.m(4, d), a16);
+    auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid,
+                   float *y) -> s2_status {
+        s2_status r = rms_ada(st, hx, rows, d, b->eps, mb + 3 * static_cast<size_t>(d), a16);
         if (r != S2_OK) return r;
         ++launches;
         s2::GemmArgs u;
@@ -423,8 +471,7 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         o.N = d;
         o.K = h;
         o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
-        o.emb6 = emb + 5;
-        o.gate = br.m(5, d);
+        o.gmul = mb + 7 * static_cast<size_t>(d);
         o.resid = hx;
         o.y = y;
         o.err = err;
@@ -432,13 +479,13 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         ++launches;
         return S2_OK;
     };
-    if ((s = mlp(V, static_cast<const float *>(sc.h_vid.ptr), L, static_cast<__half *>(sc.a_vid.ptr),
+    if ((s = mlp(mv, V, static_cast<const float *>(sc.h_vid.ptr), L, static_cast<__half *>(sc.a_vid.ptr),
                  static_cast<__half *>(sc.hid_vid.ptr), vid_out)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
     if (Lt > 0 && !b->last &&
-        (s = mlp(T, static_cast<const float *>(sc.h_txt.ptr), Lt, static_cast<__half *>(sc.a_txt.ptr),
+        (s = mlp(mt, T, static_cast<const float *>(sc.h_txt.ptr), Lt, static_cast<__half *>(sc.a_txt.ptr),
                  static_cast<__half *>(sc.hid_txt.ptr), txt_out)) != S2_OK) {
         b->last_launches = launches;
         return s;

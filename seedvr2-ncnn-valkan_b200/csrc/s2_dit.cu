@@ -15,7 +15,11 @@
 //     RMSNorm * weight, adaLN with emb slots 0/1, projection dim -> 4 oc
 //     (+ bias), unpatchify -- fused with the Euler endpoint x - (t/1000) pred
 //     for a sampling step.
-// Every forward is stream-ordered with no host synchronisation.
+// Every forward is stream-ordered with no host synchronisation. An Euler step
+// is about 520 launches; from the second call with the same shapes, buffers
+// and timestep it is replayed as one CUDA graph (captured on an internal
+// stream, launched on the caller's), so host launch latency stays off the
+// GPU's critical path.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -158,12 +162,34 @@ struct s2_dit {
     // input head
     s2::DeviceBuffer w_vid, b_vid, w_txt, b_txt, w_t1, b_t1, w_t2, b_t2, w_t3, b_t3;
     // output head
-    s2::DeviceBuffer o_norm, o_shift, o_scale, w_out, b_out;
+    s2::DeviceBuffer o_norm, o_mod6, w_out, b_out;  // o_mod6 [6][dim] = shift, scale, zeros
     // workspaces
-    s2::DeviceBuffer latent, patches, txt16, vid_a, vid_b, txt_a, txt_b, sinus, th1, th2, emb, o16, proj, err;
+    s2::DeviceBuffer latent, patches, txt16, vid_a, vid_b, txt_a, txt_b, sinus, th1, th2, emb, omods, o16, proj, err;
     s2::DeviceBuffer h_noise, h_cond, h_text, h_x0;  // host-step staging
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
+    // Euler-step graph: the call it was captured for and its launch count
+    struct StepKey {
+        int T = 0, H = 0, W = 0, Lt = 0;
+        const void *noise = nullptr, *cond = nullptr, *text = nullptr, *x0 = nullptr;
+        float t = 0.f;
+        bool operator==(const StepKey &o) const
+        {
+            return T == o.T && H == o.H && W == o.W && Lt == o.Lt && noise == o.noise && cond == o.cond &&
+                   text == o.text && x0 == o.x0 && t == o.t;
+        }
+    };
+    bool use_graph = true;
+    StepKey key;
+    bool key_valid = false;
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int graph_launches = 0;
+    void drop_graph()
+    {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+    }
 };
 
 extern "C" s2_status s2_dit_create(int device, int n_blocks, int dim, int heads, int head_dim, int mlp_hidden,
@@ -205,8 +231,10 @@ extern "C" s2_status s2_dit_destroy(s2_dit *d)
     if (!d) return S2_OK;
     for (s2_dit_block *b : d->blocks) s2_dit_block_destroy(b);
     s2::DeviceGuard guard(d->device);
+    d->drop_graph();
+    if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
     for (s2::DeviceBuffer *b : {&d->w_vid, &d->b_vid, &d->w_txt, &d->b_txt, &d->w_t1, &d->b_t1, &d->w_t2, &d->b_t2,
-                                &d->w_t3, &d->b_t3, &d->o_norm, &d->o_shift, &d->o_scale, &d->w_out, &d->b_out,
+                                &d->w_t3, &d->b_t3, &d->o_norm, &d->o_mod6, &d->w_out, &d->b_out, &d->omods,
                                 &d->latent, &d->patches, &d->txt16, &d->vid_a, &d->vid_b, &d->txt_a, &d->txt_b,
                                 &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise,
                                 &d->h_cond, &d->h_text, &d->h_x0})
@@ -261,7 +289,9 @@ extern "C" s2_status s2_dit_load_output(s2_dit *d, const float *w, size_t n)
     s2::DeviceGuard guard(d->device);
     const size_t D = d->dim, N = 4 * d->oc;
     // load_model order (seedvr2_dit_output.cpp:264-270): norm weight, shift, scale, projection W then b
-    const bool ok = upload(d->o_norm, w, D) && upload(d->o_shift, w + D, D) && upload(d->o_scale, w + 2 * D, D) &&
+    std::vector<float> mod6(6 * D, 0.f);
+    std::copy(w + D, w + 3 * D, mod6.begin());  // shift, scale in the adaLN slots 0 and 1
+    const bool ok = upload(d->o_norm, w, D) && upload(d->o_mod6, mod6.data(), 6 * D) &&
                     upload_f16_pad(d->w_out, w + 3 * D, N, D, D) && upload(d->b_out, w + 3 * D + N * D, N);
     if (!ok) return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_load_output: weight upload failed");
     d->output_loaded = true;
@@ -283,6 +313,8 @@ extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int las
     }
     s2_dit_block_destroy(d->blocks[index]);
     d->blocks[index] = b;
+    d->drop_graph();
+    d->key_valid = false;
     // all blocks run one after another on one stream: one set of activation workspaces
     for (s2_dit_block *o : d->blocks)
         if (o && o != b) {
@@ -312,7 +344,8 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     if (!d->patches.ensure(Rz * d->kp * 2) || !d->txt16.ensure(Tz * d->tcp * 2) || !d->vid_a.ensure(Rz * D * 4) ||
         !d->vid_b.ensure(Rz * D * 4) || !d->txt_a.ensure(Tz * D * 4) || !d->txt_b.ensure(Tz * D * 4) ||
         !d->sinus.ensure(d->sd * 4) || !d->th1.ensure(D * 4) || !d->th2.ensure(D * 4) || !d->emb.ensure(6 * D * 4) ||
-        !d->o16.ensure(Rz * D * 2) || !d->proj.ensure(Rz * N * 4) || !d->err.ensure(4))
+        !d->o16.ensure(Rz * D * 2) || !d->proj.ensure(Rz * N * 4) || !d->err.ensure(4) ||
+        !d->omods.ensure(static_cast<size_t>(8) * D * 4))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_forward: workspace allocation failed");
     if (fresh && cudaMemsetAsync(d->err.ptr, 0, 4, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_forward: memset failed");
@@ -384,8 +417,10 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     }
 
     // ---- output head ----
-    S2_TRY(s2::rms_ada(st, vid_cur, rows, D, d->eps, static_cast<const float *>(d->o_norm.ptr), emb,
-                       static_cast<const float *>(d->o_shift.ptr), static_cast<const float *>(d->o_scale.ptr),
+    float *om = static_cast<float *>(d->omods.ptr);
+    S2_TRY(s2::modulation_vectors(st, emb, static_cast<const float *>(d->o_mod6.ptr), D, om));
+    ++launches;
+    S2_TRY(s2::rms_ada(st, vid_cur, rows, D, d->eps, static_cast<const float *>(d->o_norm.ptr), om, om + D, om + 2 * D,
                        d->o16.ptr));
     ++launches;
     s2::GemmArgs o;
@@ -413,6 +448,22 @@ extern "C" s2_status s2_dit_forward(s2_dit *d, void *stream, const float *latent
     return dit_forward_into(d, stream, latent, T, H, W, text, Lt, timestep, nullptr, prediction);
 }
 
+static s2_status euler_step_eager(s2_dit *d, cudaStream_t st, const float *noise, const float *condition, int T,
+                                  int H, int W, const float *text, int Lt, float timestep, float *x0)
+{
+    const long long plane = 1LL * T * H * W;
+    if (!d->latent.ensure(static_cast<size_t>(plane) * d->vc * 4))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_euler_step: workspace allocation failed");
+    make_dit_input_kernel<<<grid_for(plane * d->vc), 256, 0, st>>>(noise, condition, d->oc, plane,
+                                                                    static_cast<float *>(d->latent.ptr));
+    if (cudaGetLastError() != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: launch failed");
+    const s2_status s = dit_forward_into(d, st, static_cast<const float *>(d->latent.ptr), T, H, W, text, Lt,
+                                         timestep, noise, x0);
+    if (s == S2_OK) ++d->last_launches;
+    return s;
+}
+
 extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noise, const float *condition, int T,
                                        int H, int W, const float *text, int Lt, float timestep, float *x0)
 {
@@ -423,17 +474,66 @@ extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noi
         return s2::set_error(S2_UNSUPPORTED, "s2_dit_euler_step: video_channels %d != 2 * out_channels + 1", d->vc);
     s2::DeviceGuard guard(d->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const long long plane = 1LL * T * H * W;
-    if (!d->latent.ensure(static_cast<size_t>(plane) * d->vc * 4))
-        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_euler_step: workspace allocation failed");
-    make_dit_input_kernel<<<grid_for(plane * d->vc), 256, 0, st>>>(noise, condition, d->oc, plane,
-                                                                    static_cast<float *>(d->latent.ptr));
-    if (cudaGetLastError() != cudaSuccess)
-        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: launch failed");
-    const s2_status s = dit_forward_into(d, stream, static_cast<const float *>(d->latent.ptr), T, H, W, text, Lt,
-                                            timestep, noise, x0);
-    if (s == S2_OK) ++d->last_launches;
-    return s;
+    s2_dit::StepKey k;
+    k.T = T, k.H = H, k.W = W, k.Lt = Lt, k.noise = noise, k.cond = condition, k.text = text, k.x0 = x0, k.t = timestep;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (!d->use_graph || cs != cudaStreamCaptureStatusNone)
+        return euler_step_eager(d, st, noise, condition, T, H, W, text, Lt, timestep, x0);
+    if (d->exec && d->key_valid && d->key == k) {
+        if (cudaGraphLaunch(d->exec, st) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: graph launch: %s",
+                                 cudaGetErrorString(cudaGetLastError()));
+        d->last_stream = st;
+        d->last_launches = d->graph_launches;
+        return S2_OK;
+    }
+    if (!d->key_valid || !(d->key == k)) {
+        // first call for these shapes and buffers: run eagerly (plans, workspaces)
+        d->drop_graph();
+        const s2_status s = euler_step_eager(d, st, noise, condition, T, H, W, text, Lt, timestep, x0);
+        d->key = k;
+        d->key_valid = s == S2_OK;
+        return s;
+    }
+    // second call: capture the step once, then replay it
+    if (!d->cap_stream && cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: capture stream");
+    if (cudaStreamBeginCapture(d->cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: begin capture: %s",
+                             cudaGetErrorString(cudaGetLastError()));
+    const s2_status s = euler_step_eager(d, d->cap_stream, noise, condition, T, H, W, text, Lt, timestep, x0);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(d->cap_stream, &g);
+    if (s != S2_OK || ce != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return s != S2_OK ? s
+                          : s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: capture failed: %s",
+                                          cudaGetErrorString(ce));
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&d->exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+        d->exec = nullptr;
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: graph instantiate: %s", cudaGetErrorString(ie));
+    }
+    d->graph_launches = d->last_launches;
+    if (cudaGraphLaunch(d->exec, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: graph launch: %s",
+                             cudaGetErrorString(cudaGetLastError()));
+    d->last_stream = st;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_set_graph(s2_dit *d, int enable)
+{
+    if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_set_graph: model is NULL");
+    s2::DeviceGuard guard(d->device);
+    d->use_graph = enable != 0;
+    d->drop_graph();
+    d->key_valid = false;
+    return S2_OK;
 }
 
 extern "C" s2_status s2_dit_euler_step_host(s2_dit *d, void *stream, const float *noise, const float *condition,
@@ -469,6 +569,11 @@ extern "C" s2_status s2_dit_device_error(s2_dit *d, int *code)
 {
     if (code) *code = 0;
     if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_device_error: model is NULL");
+    {
+        s2::DeviceGuard guard(d->device);
+        if (cudaStreamSynchronize(d->last_stream) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit: device failure: %s", cudaGetErrorString(cudaGetLastError()));
+    }
     for (s2_dit_block *b : d->blocks) {
         if (!b) continue;
         const s2_status s = s2_dit_block_device_error(b, code);

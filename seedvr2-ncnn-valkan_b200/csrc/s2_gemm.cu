@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const int col = n + v * 4 + e;
                                 float t = __uint_as_float(r[v * 4 + e]);
                                 if (a.bias) t = __fadd_rn(t, __ldg(a.bias + col));
-                                if (a.emb6) t = __fmul_rn(t, __fadd_rn(__ldg(a.emb6 + 6 * col), __ldg(a.gate + col)));
+                                if (a.gmul) t = __fmul_rn(t, __ldg(a.gmul + col));
                                 o[e] = __fmul_rn(__fadd_rn(t, rv[e]), a.out_scale);
                             }
                             yd[v] = make_float4(o[0], o[1], o[2], o[3]);
@@ -309,7 +309,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
         if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
     } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
-        if (!args.y || args.N % 32 != 0 || (args.emb6 && !args.gate) ||
+        if (!args.y || args.N % 32 != 0 ||
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {

@@ -27,9 +27,9 @@ enum GemmEpilogue : int {
     GEMM_EPI_RESID_T_F32 = 1,
     // fp32 row-major output with the DiT block's gated residual
     // (apply_ada_output_and_residual, seedvr2_dit_block.cpp:807-825):
-    // y[row * N + n] = ((acc + bias[n]) * g[n] + resid[row * N + n]) * out_scale,
-    // g[n] = emb6[6 n] + gate[n] (g = 1 when emb6 is null; no residual when
-    // resid is null: the plain "+ bias" fp32 projection).
+    // y[row * N + n] = ((acc + bias[n]) * gmul[n] + resid[row * N + n]) * out_scale,
+    // gmul[n] = emb[6 n + slot] + gate[n] precomputed (no multiply when gmul
+    // is null; no residual when resid is null: the plain "+ bias" projection).
     GEMM_EPI_GATED_RESID_F32 = 2,
     // SwiGLU (apply_mlp, :1093-1112): every 256-column tile holds 128 gate
     // columns then the 128 matching "in" columns; out[0] is fp16
@@ -47,8 +47,7 @@ struct GemmArgs {
     float *y = nullptr;
     long long ldt = 0;
     int n_valid = 0;
-    const float *emb6 = nullptr;  // GEMM_EPI_GATED_RESID_F32 modulation (stride 6) or null
-    const float *gate = nullptr;
+    const float *gmul = nullptr;  // GEMM_EPI_GATED_RESID_F32 gate vector [N] or null
     float out_scale = 1.f;
     int32_t *err = nullptr;       // device error word (bounded waits)
 };

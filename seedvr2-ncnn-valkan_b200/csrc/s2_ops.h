@@ -14,10 +14,12 @@ namespace s2 {
 void share_attention_scratch(s2_attention_layer *dst, const s2_attention_layer *src);
 void share_block_scratch(s2_dit_block *dst, const s2_dit_block *src);
 
-// y = fp16( ada( x * inv_rms(x) [* gamma] ) ) per row (s2_block.cu); gamma,
-// emb6 may be null (no gamma / no modulation).
+// y = fp16( (x * inv_rms(x) [* gamma]) * mul + add0 + add1 ) per row
+// (s2_block.cu); gamma and mul may be null (no gamma / no modulation).
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,
-                  const float *emb6, const float *shift, const float *scale, void *y_f16);
+                  const float *mul, const float *add0, const float *add1, void *y_f16);
+// out [8][dim] modulation vectors of one branch (see modulation_kernel).
+s2_status modulation_vectors(cudaStream_t st, const float *emb, const float *mod6, int dim, float *out);
 s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y_f16);
 
 }  // namespace s2

@@ -97,6 +97,7 @@ _SIGS = {
                           + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
     "s2_dit_euler_step_host": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3
                                + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
+    "s2_dit_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
     "s2_dit_last_launches": (ctypes.c_int, [_vp]),
     "s2_dit_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_block_create": (ctypes.c_int, [ctypes.c_int] * 9 + [ctypes.c_float] + [ctypes.c_int] * 3
@@ -456,6 +457,9 @@ class SeedVR2DiT:
                                             ctypes.c_float(timestep), ctypes.c_void_p(x0.ctypes.data)),
                "s2_dit_euler_step_host")
         return x0
+
+    def set_graph(self, enable: bool):
+        _check(lib().s2_dit_set_graph(self.handle, int(enable)), "s2_dit_set_graph")
 
     def last_launches(self) -> int:
         return lib().s2_dit_last_launches(self.handle)

@@ -54,9 +54,10 @@ def test_runner_cases_vs_reference(torch_cuda, golden, i):
     vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
     g = golden("block_runner_cases.npz")
     check_block(vo, to, g[f"c{i}_vid_out"], g[f"c{i}_txt_out"], vid, txt, f"runner case {i}")
-    # 16 launches: 2 norms, 2 QKV GEMMs, 3 attention, text convert, 2 projections, 2 x (norm + 2 GEMMs);
-    # the last block's text skips its MLP (13)
-    assert b.last_launches() == (13 if params["last"] else 16)
+    # 18 launches: 2 modulation vectors, 2 norms, 2 QKV GEMMs, 3 attention, text convert, 2 projections,
+    # 2 x (norm + 2 GEMMs);
+    # the last block's text skips its MLP (15)
+    assert b.last_launches() == (15 if params["last"] else 18)
 
 
 @pytest.mark.parametrize("shared,last,shifted", [(False, False, True), (True, False, False), (True, True, True)])

@@ -132,3 +132,28 @@ def test_load_checks(torch_cuda):
     with pytest.raises(s2b200.S2Error) as e:  # blocks missing
         m.euler_step_host(noise, cond, text)
     assert e.value.status == s2b200.S2_NOT_LOADED
+
+
+def test_graph_replay_matches_eager(torch_cuda):
+    """Calls 1 (eager), 2 (captured) and 3+ (graph replay) of an Euler step on
+    the same buffers give identical results, and so does a model with graphs
+    switched off."""
+    torch = torch_cuda
+    hp, wi, wo, bps, bws = build_case(4, 256, 2, 256, 256, four_block_flags)
+    noise, cond, text = synth.dit_latents((2, 8, 12), 16, 9, 256)
+    n, c, t = (torch.from_numpy(a).cuda() for a in (noise, cond, text))
+    m = make_model(4, 256, 2, 256, 256, wi, wo, bps, bws)
+    x0 = torch.empty_like(n)
+    outs = []
+    for _ in range(4):
+        x0.zero_()
+        m.euler_step(n, c, t, 1000.0, x0)
+        torch.cuda.synchronize()
+        outs.append(x0.cpu().numpy().copy())
+    assert m.device_error() == 0
+    eager = make_model(4, 256, 2, 256, 256, wi, wo, bps, bws)
+    eager.set_graph(False)
+    ref_out = eager.euler_step(n, c, t, 1000.0).cpu().numpy()
+    for o in outs:
+        assert np.array_equal(o, ref_out)
+    assert m.last_launches() == eager.last_launches()
