@@ -107,6 +107,11 @@ S2_API s2_status s2_build_varlen(int frames, int height, int width,
                           const s2_window *windows, int n, int text_len,
                           int32_t *cu_seqlens, s2_row *rows, int *total_rows);
 
+/* Multi-GPU ownership of a layer's windows: owner[i] = rank of window i, by a
+ * deterministic longest-processing-time rule on cost S_w^2 (S_w = L_w +
+ * text_len). Every window has one owner, so every video token has one. */
+S2_API s2_status s2_shard_windows(const s2_window *windows, int n, int text_len, int n_ranks, int32_t *owner);
+
 /* ---- device kernels (explicit buffers) ---------------------------------- */
 
 /* Fused prologue: per (packed row, head) RMSNorm over 128 dims (eps) times
@@ -184,6 +189,14 @@ S2_API s2_status s2_attention_layer_set_runtime_shape(s2_attention_layer *layer,
  * GPUs). ids NULL / n 0 = all windows. */
 S2_API s2_status s2_attention_layer_set_window_subset(s2_attention_layer *layer, const int32_t *ids, int n);
 
+/* With a window subset, let the layer read and write only the subset's video
+ * tokens, compacted in packed order (window by window, (t, y, x) inside a
+ * window): vid_qkv [n][3*dim] and vid_out [n][dim] with n from
+ * s2_attention_layer_local_rows (after load and set_runtime_shape). Used by
+ * the sharded DiT step, where each GPU keeps only its windows' rows. */
+S2_API s2_status s2_attention_layer_set_local_rows(s2_attention_layer *layer, int enable);
+S2_API s2_status s2_attention_layer_local_rows(s2_attention_layer *layer, int Lt, int *n_video);
+
 /* attention() on device buffers: vid_qkv [L][3*dim], txt_qkv [Lt][3*dim] in
  * in_dtype; vid_out [L][dim] in the mode dtype (rows of windows outside the
  * subset are left untouched); txt_out [Lt][dim] fp32 = sum over this layer's
@@ -235,6 +248,9 @@ S2_API s2_status s2_dit_block_load(s2_dit_block *block, const float *weights, si
 /* set_runtime_shape (seedvr2_dit_block.h:55) and window sharding. */
 S2_API s2_status s2_dit_block_set_runtime_shape(s2_dit_block *block, int frames, int height, int width);
 S2_API s2_status s2_dit_block_set_window_subset(s2_dit_block *block, const int32_t *ids, int n);
+/* With a window subset: video rows are the subset's tokens only (see
+ * s2_attention_layer_set_local_rows); vid / vid_out then have that many rows. */
+S2_API s2_status s2_dit_block_set_local_rows(s2_dit_block *block, int enable);
 
 /* forward (:1114-1267) on DEVICE buffers: vid [L][dim], txt [Lt][dim], emb
  * [6 dim] (emb[6c + slot]), all fp32 -> vid_out [L][dim], txt_out [Lt][dim]
@@ -252,6 +268,19 @@ S2_API s2_status s2_dit_block_forward_host(s2_dit_block *block, void *stream, co
                                            float *vid_out, float *txt_out);
 S2_API int s2_dit_block_last_launches(const s2_dit_block *block);
 S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
+
+/* ---- multi-GPU communicator (no counterpart in the reference) ------------ */
+
+/* One rank per GPU; NCCL over NVLink / NVSwitch, loaded on first use
+ * (libnccl.so.2). Rank 0 creates the id, every rank passes the same bytes
+ * (e.g. broadcast through torch.distributed) to s2_comm_init. */
+#define S2_COMM_ID_BYTES 128
+typedef struct s2_comm s2_comm;
+S2_API s2_status s2_comm_unique_id(char *id /* [S2_COMM_ID_BYTES] */);
+S2_API s2_status s2_comm_init(int device, int nranks, int rank, const char *id, s2_comm **out);
+S2_API s2_status s2_comm_destroy(s2_comm *comm);
+S2_API int s2_comm_size(const s2_comm *comm);
+S2_API int s2_comm_rank(const s2_comm *comm);
 
 /* ---- the DiT model and one Euler step ------------------------------------ */
 
@@ -301,6 +330,15 @@ S2_API s2_status s2_dit_euler_step_host(s2_dit *model, void *stream, const float
  * internal stream); enable = 0 keeps every call eager. On by default; a call
  * on a stream that is itself being captured always runs eagerly. */
 S2_API s2_status s2_dit_set_graph(s2_dit *model, int enable);
+
+/* Shard the DiT step over the communicator's ranks (NULL = one GPU). Every
+ * block's windows are split by s2_shard_windows; each rank keeps only its
+ * windows' video rows (text rows replicated), all-reduces each block's text
+ * attention mean, exchanges rows between the plain and shifted window
+ * ownerships of consecutive blocks, and all ranks end with the full output
+ * (disjoint per-rank parts summed). All ranks call forward / euler_step with
+ * the same inputs; the step then runs eagerly (no CUDA graph). */
+S2_API s2_status s2_dit_set_comm(s2_dit *model, s2_comm *comm);
 S2_API int s2_dit_last_launches(const s2_dit *model);
 S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);
 

@@ -307,7 +307,7 @@ extern "C" s2_status s2_dit_block_set_window_subset(s2_dit_block *b, const int32
 
 namespace {
 
-s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *mod3, __half *y)
+s2_status rms_ada3(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *mod3, __half *y)
 {
     return s2::rms_ada(st, x, rows, dim, eps, nullptr, mod3, mod3 ? mod3 + dim : nullptr,
                        mod3 ? mod3 + 2 * dim : nullptr, y);
@@ -355,6 +355,20 @@ void share_block_scratch(s2_dit_block *dst, const s2_dit_block *src)
 extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt,
                                           int Lt, const float *emb, float *vid_out, float *txt_out)
 {
+    return s2::dit_block_forward_ex(b, stream, vid, L, txt, Lt, emb, vid_out, txt_out, nullptr);
+}
+
+s2_attention_layer *s2::dit_block_attention(s2_dit_block *b) { return b ? b->attn : nullptr; }
+
+extern "C" s2_status s2_dit_block_set_local_rows(s2_dit_block *b, int enable)
+{
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_set_local_rows: block is NULL");
+    return s2_attention_layer_set_local_rows(b->attn, enable);
+}
+
+s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt, int Lt,
+                                   const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce)
+{
     s2::clear_error();
     if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: block is NULL");
     if (!b->loaded) return s2::set_error(S2_NOT_LOADED, "s2_dit_block_forward: weights not loaded");
@@ -395,8 +409,8 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     S2_TRY(s2::modulation_vectors(st, emb, V.m(0, d), d, mv));
     if (Lt > 0) S2_TRY(s2::modulation_vectors(st, emb, T.m(0, d), d, mt));
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
-    S2_TRY(rms_ada(st, vid, L, d, b->eps, mv, static_cast<__half *>(sc.a_vid.ptr)));
-    if (Lt > 0) S2_TRY(rms_ada(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, static_cast<__half *>(sc.a_txt.ptr)));
+    S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, static_cast<__half *>(sc.a_vid.ptr)));
+    if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, static_cast<__half *>(sc.a_txt.ptr)));
     // QKV projections (no bias)
     s2::GemmArgs g;
     g.K = d;
@@ -418,6 +432,11 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
         return s;
     }
     launches += s2_attention_layer_last_launches(b->attn);
+    if (reduce && reduce->fn && Lt > 0 &&
+        (s = reduce->fn(reduce->ctx, static_cast<float *>(sc.att_txt32.ptr), static_cast<size_t>(Lt) * d, st)) != S2_OK) {
+        b->last_launches = launches;
+        return s;
+    }
     // output projection + gated residual
     s2::GemmArgs p;
     p.K = d;
@@ -454,7 +473,7 @@ extern "C" s2_status s2_dit_block_forward(s2_dit_block *b, void *stream, const f
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
     auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid,
                    float *y) -> s2_status {
-        s2_status r = rms_ada(st, hx, rows, d, b->eps, mb + 3 * static_cast<size_t>(d), a16);
+        s2_status r = rms_ada3(st, hx, rows, d, b->eps, mb + 3 * static_cast<size_t>(d), a16);
         if (r != S2_OK) return r;
         ++launches;
         s2::GemmArgs u;

@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "s2_buffers.h"
+#include "s2_comm.h"
 #include "s2_gemm.h"
 #include "s2_internal.h"
 #include "s2_ops.h"
@@ -132,6 +133,68 @@ __global__ void unpatchify_kernel(const float *__restrict__ proj, int oc, int T,
     }
 }
 
+// ---- sharded step (one rank per GPU) ----
+
+// patches for a rank's local rows: local row i is patched-grid token tok[i]
+__global__ void patchify_local_kernel(const float *__restrict__ latent, int vc, int T, int H, int W, int kp,
+                                      const int32_t *__restrict__ tok, int n, __half *__restrict__ patches)
+{
+    const int Hp = H / 2, Wp = W / 2;
+    const long long total = 1LL * n * kp, plane = 1LL * T * H * W;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int col = static_cast<int>(i % kp);
+        const int p = tok[i / kp];
+        float v = 0.f;
+        if (col < 4 * vc) {
+            const int x = p % Wp, y = (p / Wp) % Hp, t = p / (Wp * Hp);
+            const int blk = col / vc, c = col - blk * vc, dy = blk >> 1, dx = blk & 1;
+            v = latent[c * plane + (1LL * t * H + 2 * y + dy) * W + 2 * x + dx];
+        }
+        patches[i] = __float2half_rn(v);
+    }
+}
+
+// the rank's output pixels (zero elsewhere) from its local rows' projections
+__global__ void unpatchify_local_kernel(const float *__restrict__ proj, int oc, int T, int Hp, int Wp,
+                                        const int32_t *__restrict__ tok, int n, const float *__restrict__ noise,
+                                        float bt, float *__restrict__ out)
+{
+    const int H = 2 * Hp, W = 2 * Wp;
+    const long long plane = 1LL * T * H * W, total = 1LL * n * 4 * oc;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int col = static_cast<int>(i % (4 * oc));
+        const long long row = i / (4 * oc);
+        const int p = tok[row];
+        const int x = p % Wp, y = (p / Wp) % Hp, t = p / (Wp * Hp);
+        const int blk = col / oc, c = col - blk * oc, dy = blk >> 1, dx = blk & 1;
+        const long long o = c * plane + (1LL * t * H + 2 * y + dy) * W + 2 * x + dx;
+        const float pred = proj[i];
+        out[o] = noise ? __fsub_rn(noise[o], __fmul_rn(bt, pred)) : pred;
+    }
+}
+
+// dst[i] = src[map[i]] (rows of dim floats)
+__global__ void gather_rows_kernel(const float4 *__restrict__ src, const int32_t *__restrict__ map, int n, int dim4,
+                                   float4 *__restrict__ dst)
+{
+    const long long total = 1LL * n * dim4;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const long long r = i / dim4;
+        dst[i] = src[1LL * map[r] * dim4 + (i - r * dim4)];
+    }
+}
+
+// dst[map[i]] = src[i]
+__global__ void scatter_rows_kernel(const float4 *__restrict__ src, const int32_t *__restrict__ map, int n, int dim4,
+                                    float4 *__restrict__ dst)
+{
+    const long long total = 1LL * n * dim4;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const long long r = i / dim4;
+        dst[1LL * map[r] * dim4 + (i - r * dim4)] = src[i];
+    }
+}
+
 unsigned grid_for(long long n) { return static_cast<unsigned>(std::min<long long>((n + 255) / 256, 4096)); }
 
 bool upload(s2::DeviceBuffer &b, const float *src, size_t n)
@@ -168,6 +231,20 @@ struct s2_dit {
     s2::DeviceBuffer h_noise, h_cond, h_text, h_x0;  // host-step staging
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
+    std::vector<int> shifted;  // per block (the window kind of its attention)
+    // sharded step
+    s2_comm *comm = nullptr;
+    struct Shard {
+        bool valid = false;
+        int T = 0, Hp = 0, Wp = 0, Lt = -1;
+        int n_local[2] = {0, 0};
+        std::vector<int32_t> ids[2];
+        s2::DeviceBuffer tok[2];                  // local row -> patched-grid token, per window kind
+        s2::DeviceBuffer send_src[2], recv_dst[2];  // exchange from kind k to kind 1 - k
+        std::vector<size_t> send_off[2], send_bytes[2], recv_off[2], recv_bytes[2];
+        int send_rows[2] = {0, 0};
+    } sh;
+    s2::DeviceBuffer xsend, xrecv;
     // Euler-step graph: the call it was captured for and its launch count
     struct StepKey {
         int T = 0, H = 0, W = 0, Lt = 0;
@@ -222,6 +299,7 @@ extern "C" s2_status s2_dit_create(int device, int n_blocks, int dim, int heads,
     d->kp = round64(4 * video_channels);
     d->tcp = round64(text_channels);
     d->blocks.assign(n_blocks, nullptr);
+    d->shifted.assign(n_blocks, 0);
     *out = d;
     return S2_OK;
 }
@@ -236,7 +314,9 @@ extern "C" s2_status s2_dit_destroy(s2_dit *d)
     for (s2::DeviceBuffer *b : {&d->w_vid, &d->b_vid, &d->w_txt, &d->b_txt, &d->w_t1, &d->b_t1, &d->w_t2, &d->b_t2,
                                 &d->w_t3, &d->b_t3, &d->o_norm, &d->o_mod6, &d->w_out, &d->b_out, &d->omods,
                                 &d->latent, &d->patches, &d->txt16, &d->vid_a, &d->vid_b, &d->txt_a, &d->txt_b,
-                                &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise,
+                                &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise, &d->xsend, &d->xrecv,
+                                &d->sh.tok[0], &d->sh.tok[1], &d->sh.send_src[0], &d->sh.send_src[1],
+                                &d->sh.recv_dst[0], &d->sh.recv_dst[1],
                                 &d->h_cond, &d->h_text, &d->h_x0})
         b->release();
     delete d;
@@ -313,8 +393,10 @@ extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int las
     }
     s2_dit_block_destroy(d->blocks[index]);
     d->blocks[index] = b;
+    d->shifted[index] = shifted != 0;
     d->drop_graph();
     d->key_valid = false;
+    d->sh.valid = false;
     // all blocks run one after another on one stream: one set of activation workspaces
     for (s2_dit_block *o : d->blocks)
         if (o && o != b) {
@@ -322,6 +404,87 @@ extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int las
             break;
         }
     return S2_OK;
+}
+
+// Window ownership of both window kinds, every rank's local row order, and the
+// row-exchange maps between them; sets every block's window subset.
+static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
+{
+    auto &sh = d->sh;
+    if (sh.valid && sh.T == T && sh.Hp == Hp && sh.Wp == Wp && sh.Lt == Lt) return S2_OK;
+    sh.valid = false;
+    const int N = s2_comm_size(d->comm), me = s2_comm_rank(d->comm), L = T * Hp * Wp;
+    std::vector<std::vector<std::vector<int32_t>>> tok(2, std::vector<std::vector<int32_t>>(N));
+    std::vector<std::vector<int32_t>> own_rank(2, std::vector<int32_t>(L, -1)), own_idx(2, std::vector<int32_t>(L, -1));
+    for (int k = 0; k < 2; ++k) {
+        int n = 0;
+        s2_status s = s2_make_windows(T, Hp, Wp, k, d->wt, d->wh, d->ww, nullptr, 0, &n);
+        if (s != S2_OK) return s;
+        std::vector<s2_window> w(n);
+        s2_make_windows(T, Hp, Wp, k, d->wt, d->wh, d->ww, w.data(), n, &n);
+        std::vector<int32_t> owner(n);
+        if ((s = s2_shard_windows(w.data(), n, Lt, N, owner.data())) != S2_OK) return s;
+        sh.ids[k].clear();
+        for (int i = 0; i < n; ++i) {
+            if (owner[i] == me) sh.ids[k].push_back(i);
+            auto &list = tok[k][owner[i]];
+            for (int t = w[i].t0; t < w[i].t1; ++t)
+                for (int y = w[i].h0; y < w[i].h1; ++y)
+                    for (int x = w[i].w0; x < w[i].w1; ++x) {
+                        const int p = (t * Hp + y) * Wp + x;
+                        own_rank[k][p] = owner[i];
+                        own_idx[k][p] = static_cast<int32_t>(list.size());
+                        list.push_back(p);
+                    }
+        }
+        for (int p = 0; p < L; ++p)
+            if (own_rank[k][p] < 0) return s2::set_error(S2_INFERENCE_FAILED, "shard: token %d has no window", p);
+        sh.n_local[k] = static_cast<int>(tok[k][me].size());
+        if (!sh.tok[k].ensure(std::max<size_t>(tok[k][me].size(), 1) * 4) ||
+            cudaMemcpy(sh.tok[k].ptr, tok[k][me].data(), tok[k][me].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
+    }
+    const size_t row_bytes = static_cast<size_t>(d->dim) * 4;
+    for (int k = 0; k < 2; ++k) {
+        const int k2 = 1 - k;
+        std::vector<int32_t> src, dst;
+        sh.send_off[k].assign(N, 0);
+        sh.send_bytes[k].assign(N, 0);
+        sh.recv_off[k].assign(N, 0);
+        sh.recv_bytes[k].assign(N, 0);
+        for (int p2 = 0; p2 < N; ++p2) {  // rows I send to p2, in p2's local order of kind k2
+            sh.send_off[k][p2] = src.size() * row_bytes;
+            for (int p : tok[k2][p2])
+                if (own_rank[k][p] == me) src.push_back(own_idx[k][p]);
+            sh.send_bytes[k][p2] = src.size() * row_bytes - sh.send_off[k][p2];
+        }
+        for (int p1 = 0; p1 < N; ++p1) {  // rows I receive from p1, in my local order of kind k2
+            sh.recv_off[k][p1] = dst.size() * row_bytes;
+            for (size_t i = 0; i < tok[k2][me].size(); ++i)
+                if (own_rank[k][tok[k2][me][i]] == p1) dst.push_back(static_cast<int32_t>(i));
+            sh.recv_bytes[k][p1] = dst.size() * row_bytes - sh.recv_off[k][p1];
+        }
+        sh.send_rows[k] = static_cast<int>(src.size());
+        if (!sh.send_src[k].ensure(std::max<size_t>(src.size(), 1) * 4) ||
+            !sh.recv_dst[k].ensure(std::max<size_t>(dst.size(), 1) * 4) ||
+            cudaMemcpy(sh.send_src[k].ptr, src.data(), src.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(sh.recv_dst[k].ptr, dst.data(), dst.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
+    }
+    for (int i = 0; i < d->n_blocks; ++i) {
+        const auto &ids = sh.ids[d->shifted[i]];
+        s2_status s = s2_dit_block_set_window_subset(d->blocks[i], ids.data(), static_cast<int>(ids.size()));
+        if (s == S2_OK) s = s2_dit_block_set_local_rows(d->blocks[i], 1);
+        if (s != S2_OK) return s;
+    }
+    sh.T = T, sh.Hp = Hp, sh.Wp = Wp, sh.Lt = Lt;
+    sh.valid = true;
+    return S2_OK;
+}
+
+static s2_status text_allreduce(void *ctx, float *buf, size_t n, cudaStream_t st)
+{
+    return s2::comm_allreduce_f32(static_cast<s2_comm *>(ctx), buf, n, st);
 }
 
 // The DiT forward; with `noise` the output is the Euler endpoint instead of the prediction.
@@ -367,9 +530,33 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
         }                                 \
     } while (0)
 
+    // sharded: this rank's video rows of each window kind (rows0: the first block's kind)
+    const bool sharded = d->comm && s2_comm_size(d->comm) > 1;
+    int rows0 = rows;
+    if (sharded) {
+        S2_TRY(build_shard(d, T, Hp, Wp, Lt));
+        rows0 = d->sh.n_local[d->shifted[0]];
+        if (!d->xsend.ensure(Rz * D * 4) || !d->xrecv.ensure(Rz * D * 4))
+            return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_forward: exchange buffers");
+    } else if (d->sh.valid) {
+        for (s2_dit_block *b : d->blocks) {  // back to whole-clip blocks
+            S2_TRY(s2_dit_block_set_window_subset(b, nullptr, 0));
+            S2_TRY(s2_dit_block_set_local_rows(b, 0));
+        }
+        d->sh.valid = false;
+    }
+    s2::TextReduce reduce;
+    reduce.fn = text_allreduce;
+    reduce.ctx = d->comm;
+
     // ---- input head ----
-    patchify_kernel<<<grid_for(Rz * d->kp), 256, 0, st>>>(latent, d->vc, T, H, W, d->kp,
-                                                          static_cast<__half *>(d->patches.ptr));
+    if (sharded)
+        patchify_local_kernel<<<grid_for(1LL * rows0 * d->kp), 256, 0, st>>>(
+            latent, d->vc, T, H, W, d->kp, static_cast<const int32_t *>(d->sh.tok[d->shifted[0]].ptr), rows0,
+            static_cast<__half *>(d->patches.ptr));
+    else
+        patchify_kernel<<<grid_for(Rz * d->kp), 256, 0, st>>>(latent, d->vc, T, H, W, d->kp,
+                                                              static_cast<__half *>(d->patches.ptr));
     S2_TRY(check("patchify"));
     pad_to_f16_kernel<<<grid_for(Tz * d->tcp), 256, 0, st>>>(text, Lt, d->tc, d->tcp, static_cast<__half *>(d->txt16.ptr));
     S2_TRY(check("text convert"));
@@ -377,7 +564,7 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     g.epilogue = s2::GEMM_EPI_GATED_RESID_F32;  // no modulation, no residual: acc + bias
     g.N = D;
     g.err = err;
-    g.M = rows;
+    g.M = rows0;
     g.K = d->kp;
     g.bias = static_cast<const float *>(d->b_vid.ptr);
     g.y = static_cast<float *>(d->vid_a.ptr);
@@ -408,9 +595,28 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     float *vid_cur = static_cast<float *>(d->vid_a.ptr), *vid_nxt = static_cast<float *>(d->vid_b.ptr);
     float *txt_cur = static_cast<float *>(d->txt_a.ptr), *txt_nxt = static_cast<float *>(d->txt_b.ptr);
     const float *emb = static_cast<const float *>(d->emb.ptr);
+    int kind = d->shifted[0], n_rows = rows0;
     for (int i = 0; i < d->n_blocks; ++i) {
+        if (sharded && d->shifted[i] != kind) {
+            // re-partition the hidden rows from this kind's window ownership to the next one's
+            auto &sh = d->sh;
+            const int dim4 = D / 4;
+            gather_rows_kernel<<<grid_for(1LL * sh.send_rows[kind] * dim4), 256, 0, st>>>(
+                reinterpret_cast<const float4 *>(vid_cur), static_cast<const int32_t *>(sh.send_src[kind].ptr),
+                sh.send_rows[kind], dim4, static_cast<float4 *>(d->xsend.ptr));
+            S2_TRY(check("exchange pack"));
+            S2_TRY(s2::comm_exchange(d->comm, d->xsend.ptr, sh.send_off[kind].data(), sh.send_bytes[kind].data(),
+                                     d->xrecv.ptr, sh.recv_off[kind].data(), sh.recv_bytes[kind].data(), st));
+            kind = d->shifted[i];
+            n_rows = sh.n_local[kind];
+            scatter_rows_kernel<<<grid_for(1LL * n_rows * dim4), 256, 0, st>>>(
+                static_cast<const float4 *>(d->xrecv.ptr), static_cast<const int32_t *>(sh.recv_dst[1 - kind].ptr),
+                n_rows, dim4, reinterpret_cast<float4 *>(vid_cur));
+            S2_TRY(check("exchange unpack"));
+        }
         S2_TRY(s2_dit_block_set_runtime_shape(d->blocks[i], T, Hp, Wp));
-        S2_TRY(s2_dit_block_forward(d->blocks[i], stream, vid_cur, rows, txt_cur, Lt, emb, vid_nxt, txt_nxt));
+        S2_TRY(s2::dit_block_forward_ex(d->blocks[i], stream, vid_cur, n_rows, txt_cur, Lt, emb, vid_nxt, txt_nxt,
+                                        sharded ? &reduce : nullptr));
         launches += s2_dit_block_last_launches(d->blocks[i]);
         std::swap(vid_cur, vid_nxt);
         std::swap(txt_cur, txt_nxt);
@@ -420,12 +626,12 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     float *om = static_cast<float *>(d->omods.ptr);
     S2_TRY(s2::modulation_vectors(st, emb, static_cast<const float *>(d->o_mod6.ptr), D, om));
     ++launches;
-    S2_TRY(s2::rms_ada(st, vid_cur, rows, D, d->eps, static_cast<const float *>(d->o_norm.ptr), om, om + D, om + 2 * D,
-                       d->o16.ptr));
+    S2_TRY(s2::rms_ada(st, vid_cur, n_rows, D, d->eps, static_cast<const float *>(d->o_norm.ptr), om, om + D,
+                       om + 2 * D, d->o16.ptr));
     ++launches;
     s2::GemmArgs o;
     o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
-    o.M = rows;
+    o.M = n_rows;
     o.N = N;
     o.K = D;
     o.bias = static_cast<const float *>(d->b_out.ptr);
@@ -434,9 +640,21 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     S2_TRY(s2::gemm_f16(st, d->o16.ptr, d->w_out.ptr, o));
     ++launches;
     const float bt = timestep / 1000.0f;
-    unpatchify_kernel<<<grid_for(1LL * rows * N), 256, 0, st>>>(static_cast<const float *>(d->proj.ptr), d->oc, T, Hp,
-                                                                 Wp, noise, bt, out);
-    S2_TRY(check("unpatchify"));
+    if (sharded) {
+        // every rank writes its own pixels of a zeroed output; the sum over ranks is the full output
+        const size_t plane_bytes = static_cast<size_t>(T) * H * W * d->oc * 4;
+        if (cudaMemsetAsync(out, 0, plane_bytes, st) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_forward: output memset failed");
+        unpatchify_local_kernel<<<grid_for(1LL * n_rows * N), 256, 0, st>>>(
+            static_cast<const float *>(d->proj.ptr), d->oc, T, Hp, Wp,
+            static_cast<const int32_t *>(d->sh.tok[kind].ptr), n_rows, noise, bt, out);
+        S2_TRY(check("unpatchify"));
+        S2_TRY(s2::comm_allreduce_f32(d->comm, out, plane_bytes / 4, st));
+    } else {
+        unpatchify_kernel<<<grid_for(1LL * rows * N), 256, 0, st>>>(static_cast<const float *>(d->proj.ptr), d->oc, T,
+                                                                     Hp, Wp, noise, bt, out);
+        S2_TRY(check("unpatchify"));
+    }
 #undef S2_TRY
     d->last_launches = launches;
     return S2_OK;
@@ -478,7 +696,7 @@ extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noi
     k.T = T, k.H = H, k.W = W, k.Lt = Lt, k.noise = noise, k.cond = condition, k.text = text, k.x0 = x0, k.t = timestep;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
-    if (!d->use_graph || cs != cudaStreamCaptureStatusNone)
+    if (!d->use_graph || cs != cudaStreamCaptureStatusNone || (d->comm && s2_comm_size(d->comm) > 1))
         return euler_step_eager(d, st, noise, condition, T, H, W, text, Lt, timestep, x0);
     if (d->exec && d->key_valid && d->key == k) {
         if (cudaGraphLaunch(d->exec, st) != cudaSuccess)
@@ -523,6 +741,23 @@ extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noi
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: graph launch: %s",
                              cudaGetErrorString(cudaGetLastError()));
     d->last_stream = st;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_set_comm(s2_dit *d, s2_comm *comm)
+{
+    if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_set_comm: model is NULL");
+    d->comm = comm;
+    d->sh.valid = false;
+    s2::DeviceGuard guard(d->device);
+    d->drop_graph();
+    d->key_valid = false;
+    if (!comm || s2_comm_size(comm) == 1)
+        for (s2_dit_block *b : d->blocks)
+            if (b) {
+                s2_dit_block_set_window_subset(b, nullptr, 0);
+                s2_dit_block_set_local_rows(b, 0);
+            }
     return S2_OK;
 }
 

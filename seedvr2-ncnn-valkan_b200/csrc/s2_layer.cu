@@ -48,6 +48,8 @@ struct s2_attention_layer {
     int T = 0, H = 0, W = 0;
     bool shape_valid = false;
     std::vector<int32_t> subset;
+    bool local_rows = false;  // video rows are the subset's tokens, compacted in packed order
+    int n_video = 0;          // video rows the plan reads and writes
 
     // plan
     bool plan_valid = false;
@@ -108,6 +110,14 @@ struct s2_attention_layer {
         s2_plan_work(h_cu.data(), n_local, h_work.data(), nw, &nw);
         int mp = 1;
         for (const s2_row &r : h_rows) mp = std::max(mp, std::max(r.pt, std::max(r.ph, r.pw)) + 1);
+        n_video = T * H * W;
+        if (local_rows) {
+            // the i-th video row of the packed sequence is local row i
+            int next = 0;
+            for (s2_row &r : h_rows)
+                if (r.src >= 0) r.src = next++;
+            n_video = next;
+        }
         n_rows = rows;
         n_work = nw;
         max_pos = mp;
@@ -224,6 +234,26 @@ extern "C" s2_status s2_attention_layer_set_window_subset(s2_attention_layer *l,
     return S2_OK;
 }
 
+extern "C" s2_status s2_attention_layer_set_local_rows(s2_attention_layer *l, int enable)
+{
+    if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    l->local_rows = enable != 0;
+    l->plan_valid = false;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_attention_layer_local_rows(s2_attention_layer *l, int Lt, int *n_video)
+{
+    if (!l || !n_video) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    if (!l->loaded || !l->shape_valid)
+        return s2::set_error(S2_NOT_LOADED, "attention layer: weights or runtime shape not set");
+    s2::DeviceGuard g(l->device);
+    const s2_status rc = l->build_plan(Lt, nullptr);
+    if (rc != S2_OK) return rc;
+    *n_video = l->n_video;
+    return S2_OK;
+}
+
 extern "C" int s2_attention_layer_last_launches(const s2_attention_layer *l) { return l ? l->last_launches : 0; }
 
 extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *stream, const void *vid_qkv,
@@ -234,14 +264,15 @@ extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *str
     l->last_launches = 0;
     if (!l->loaded) return s2::set_error(S2_NOT_LOADED, "attention layer: weights not loaded");
     if (!l->shape_valid) return s2::set_error(S2_NOT_LOADED, "attention layer: runtime shape not set");
-    if (L != l->T * l->H * l->W)
-        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: vid rows %d != T*H*W = %d", L, l->T * l->H * l->W);
     if (Lt < 0 || (Lt > 0 && !txt_qkv) || !vid_qkv || !vid_out || (Lt > 0 && !txt_out))
         return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: NULL buffer");
     DeviceGuard g(l->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     l->last_stream = st;
     s2_status rc = l->build_plan(Lt, st);
+    if (rc == S2_OK && L != l->n_video)
+        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: vid rows %d != %d (%s)", L, l->n_video,
+                             l->local_rows ? "the subset's video tokens" : "T*H*W");
     if (rc != S2_OK) return rc;
     const int dim = l->heads * S2_HEAD_DIM;
     const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;

@@ -14,6 +14,19 @@ namespace s2 {
 void share_attention_scratch(s2_attention_layer *dst, const s2_attention_layer *src);
 void share_block_scratch(s2_dit_block *dst, const s2_dit_block *src);
 
+// Reduction of a block's text attention output across ranks (a sharded DiT
+// step): called between the attention and the output projection with the
+// rank's partial text mean [Lt][dim] fp32, stream-ordered on `st`.
+struct TextReduce {
+    s2_status (*fn)(void *ctx, float *buf, size_t n, cudaStream_t st) = nullptr;
+    void *ctx = nullptr;
+};
+
+// s2_dit_block_forward with an optional text reduction.
+s2_status dit_block_forward_ex(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt, int Lt,
+                               const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce);
+s2_attention_layer *dit_block_attention(s2_dit_block *b);
+
 // y = fp16( (x * inv_rms(x) [* gamma]) * mul + add0 + add1 ) per row
 // (s2_block.cu); gamma and mul may be null (no gamma / no modulation).
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,

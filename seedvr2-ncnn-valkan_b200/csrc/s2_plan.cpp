@@ -159,3 +159,31 @@ extern "C" s2_status s2_plan_work(const int32_t *cu_seqlens, int n_windows, int3
     *n_work = n;
     return S2_OK;
 }
+
+// Longest-processing-time assignment of a layer's windows to ranks: windows in
+// descending cost S_w^2 (S_w = L_w + text_len; ties keep window order), each to
+// the least-loaded rank (ties to the lowest rank). Deterministic, so every rank
+// derives the same ownership without communicating.
+extern "C" s2_status s2_shard_windows(const s2_window *windows, int n, int text_len, int n_ranks, int32_t *owner)
+{
+    if (!windows || !owner || n <= 0 || n_ranks <= 0 || text_len < 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_shard_windows: invalid arguments");
+    std::vector<double> cost(n);
+    for (int i = 0; i < n; ++i) {
+        const s2_window &w = windows[i];
+        const double s = static_cast<double>(w.t1 - w.t0) * (w.h1 - w.h0) * (w.w1 - w.w0) + text_len;
+        cost[i] = s * s;
+    }
+    std::vector<int> order(n);
+    for (int i = 0; i < n; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+    std::vector<double> load(n_ranks, 0.0);
+    for (int i : order) {
+        int r = 0;
+        for (int k = 1; k < n_ranks; ++k)
+            if (load[k] < load[r]) r = k;
+        owner[i] = r;
+        load[r] += cost[i];
+    }
+    return S2_OK;
+}

@@ -61,6 +61,7 @@ _SIGS = {
     "s2_build_varlen": (ctypes.c_int, [ctypes.c_int] * 3 + [ctypes.POINTER(Window), ctypes.c_int, ctypes.c_int,
                                                            _i32p, ctypes.POINTER(Row), _i32p]),
     "s2_plan_work": (ctypes.c_int, [_i32p, ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
+    "s2_shard_windows": (ctypes.c_int, [ctypes.POINTER(Window), ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p]),
     "s2_rope_table_bytes": (ctypes.c_size_t, [ctypes.c_int]),
     "s2_rope_table": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
     "s2_qk_norm_rope": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, _vp,
@@ -98,6 +99,16 @@ _SIGS = {
     "s2_dit_euler_step_host": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3
                                + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
     "s2_dit_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "s2_dit_set_comm": (ctypes.c_int, [_vp, _vp]),
+    "s2_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "s2_comm_init": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                    ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_comm_destroy": (ctypes.c_int, [_vp]),
+    "s2_comm_size": (ctypes.c_int, [_vp]),
+    "s2_comm_rank": (ctypes.c_int, [_vp]),
+    "s2_attention_layer_set_local_rows": (ctypes.c_int, [_vp, ctypes.c_int]),
+    "s2_attention_layer_local_rows": (ctypes.c_int, [_vp, ctypes.c_int, _i32p]),
+    "s2_dit_block_set_local_rows": (ctypes.c_int, [_vp, ctypes.c_int]),
     "s2_dit_last_launches": (ctypes.c_int, [_vp]),
     "s2_dit_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_block_create": (ctypes.c_int, [ctypes.c_int] * 9 + [ctypes.c_float] + [ctypes.c_int] * 3
@@ -216,6 +227,15 @@ def shard_windows(windows: np.ndarray, text_len: int, n_ranks: int) -> list[np.n
         owner[i] = r
         load[r] += costs[i]
     return [np.nonzero(owner == r)[0].astype(np.int32) for r in range(n_ranks)]
+
+
+def shard_owners(windows: np.ndarray, text_len: int, n_ranks: int) -> np.ndarray:
+    """Owner rank of every window as the library assigns it (s2_shard_windows)."""
+    w = np.ascontiguousarray(windows, np.int32)
+    owner = np.zeros(len(w), np.int32)
+    _check(lib().s2_shard_windows(w.ctypes.data_as(ctypes.POINTER(Window)), len(w), text_len, n_ranks,
+                                  owner.ctypes.data_as(_i32p)), "s2_shard_windows")
+    return owner
 
 
 # ---- device helpers (torch tensors as plumbing) ------------------------------
@@ -458,6 +478,11 @@ class SeedVR2DiT:
                "s2_dit_euler_step_host")
         return x0
 
+    def set_comm(self, comm: "Comm | None"):
+        """Shard the step over the communicator's ranks (None: this GPU alone)."""
+        self._comm = comm
+        _check(lib().s2_dit_set_comm(self.handle, comm.handle if comm is not None else None), "s2_dit_set_comm")
+
     def set_graph(self, enable: bool):
         _check(lib().s2_dit_set_graph(self.handle, int(enable)), "s2_dit_set_graph")
 
@@ -559,6 +584,51 @@ class SeedVR2DiTBlock:
     def close(self):
         if self.handle is not None and self.handle.value:
             lib().s2_dit_block_destroy(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+COMM_ID_BYTES = 128
+
+
+class Comm:
+    """One rank of the library's multi-GPU communicator (NCCL, loaded on first use).
+
+    ``Comm.create(device, rank, world, pg=None)`` makes rank 0's unique id and
+    broadcasts it with torch.distributed (the default process group unless
+    ``pg`` is given); pass ``unique_id`` to supply the bytes yourself."""
+
+    def __init__(self, device: int, rank: int, world: int, unique_id: bytes):
+        h = ctypes.c_void_p()
+        _check(lib().s2_comm_init(device, world, rank, ctypes.create_string_buffer(unique_id, COMM_ID_BYTES),
+                                  ctypes.byref(h)), "s2_comm_init")
+        self.handle, self.rank, self.world = h, rank, world
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+        _check(lib().s2_comm_unique_id(buf), "s2_comm_unique_id")
+        return buf.raw
+
+    @classmethod
+    def create(cls, device: int, rank: int, world: int, pg=None):
+        torch = _torch()
+        import torch.distributed as dist
+        uid = cls.unique_id() if rank == 0 else bytes(COMM_ID_BYTES)
+        t = torch.tensor(list(uid), dtype=torch.uint8)
+        if dist.get_backend(pg) == "nccl":
+            t = t.cuda(device)
+        dist.broadcast(t, 0, group=pg)
+        return cls(device, rank, world, bytes(t.cpu().tolist()))
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            lib().s2_comm_destroy(self.handle)
         self.handle = None
 
     def __del__(self):

@@ -77,3 +77,15 @@ def test_shard_windows_partitions_and_balances(grid, shifted, n):
     # LPT bound: no rank exceeds the mean by more than the largest single window
     assert loads.max() <= loads.mean() + cost.max() + 1e-9
     assert s2b200.shard_windows(wins, 58, n)[0].tolist() == parts[0].tolist()  # deterministic
+
+
+@pytest.mark.parametrize("grid,shifted,n", [((6, 45, 80), 0, 2), ((6, 45, 80), 1, 8), ((12, 67, 120), 1, 4),
+                                            ((2, 16, 30), 0, 3)])
+def test_library_sharding_matches_python_lpt(grid, shifted, n):
+    """The library's ownership (used by the sharded DiT step) is the same LPT
+    assignment as the Python helper used by the layer-level sharding."""
+    wins = s2b200.make_windows(*grid, shifted)
+    owner = s2b200.shard_owners(wins, 58, n)
+    parts = s2b200.shard_windows(wins, 58, n)
+    for r in range(n):
+        assert np.nonzero(owner == r)[0].tolist() == parts[r].tolist()
