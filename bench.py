@@ -17,12 +17,13 @@ roofline  = the attention kernel alone: FLOPs per launch / mean launch time
 cpu_baseline / --impl reference: the reference's own CPU attention()
             (oracle/_ref, built from the reference sources) on a bounded
             sample of the same workload, on this host's cores.
-euler_step (N = 1): the second half of the metric -- one full DiT Euler step
+euler_step: the second half of the metric -- one full DiT Euler step
             at 720p (33-channel 6x90x160 latent, 58 text
             tokens x 5120, 32 blocks of dim 2560 / 20 heads / SwiGLU 6912,
             random-init weights) through s2_dit_euler_step, replayed as a
             CUDA graph; device ms per step, the same through the host-buffer
-            call (e2e), GEMM throughput, clocks.
+            call (e2e), GEMM throughput, clocks. At N > 1 the ONE step is
+            sharded by window over the ranks (strong scaling, max over ranks).
 vae_attention (N = 1): the VAE mid-block attention layer at config 4
             (C 512, 6 frames of 90x160) through s2_vae_attention_forward.
 
@@ -356,8 +357,8 @@ def run_ours(args, rank, world, local_rank):
                       step_flops_all, dist)
 
     extra = {}
-    if world == 1 and not args.no_euler:
-        extra["euler_step"] = run_euler(args, torch, s2b200, synth, dev)
+    if not args.no_euler:
+        extra["euler_step"] = run_euler(args, torch, s2b200, synth, dev, rank, world, dist)
     if world == 1 and not args.no_vae:
         extra["vae_attention"] = run_vae(args, torch, s2b200, synth, dev)
 
@@ -443,14 +444,21 @@ def run_e2e(args, torch, s2b200, synth, dev, rank, world, grid, heads, Lt, gam, 
             "path": "s2_attention_layer_forward_host (pinned host buffers)"}
 
 
-def run_euler(args, torch, s2b200, synth, dev):
-    """One DiT Euler step at 720p (config 2) on this GPU; returns a dict."""
+def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
+    """One DiT Euler step at 720p (config 2): on this GPU (N = 1), or sharded by
+    window over all ranks (N > 1: strong scaling, one step split across GPUs).
+    Returns a dict (on every rank; rank 0 prints it)."""
     t0 = time.perf_counter()
     m = s2b200.SeedVR2DiT(device=dev.index)
     m.load_input(synth.dit_input_weights(2560))
     m.load_output(synth.dit_output_weights(2560))
     for i in range(32):
-        m.load_block(i, synth.block_weights(2560, 20, 6912, s2b200.block_flags(i)["shared"], seed=100 + i))
+        m.load_block(i, synth.block_weights_device(2560, 20, 6912, s2b200.block_flags(i)["shared"], seed=100 + i,
+                                                   device=dev))
+    comm = None
+    if world > 1:
+        comm = s2b200.Comm.create(dev.index, rank, world)
+        m.set_comm(comm)
     load_s = time.perf_counter() - t0
     noise, cond, text = synth.dit_latents(synth.DIT_CFG2_LATENT)
     n, c, t = (torch.from_numpy(a).to(dev) for a in (noise, cond, text))
@@ -463,6 +471,9 @@ def run_euler(args, torch, s2b200, synth, dev):
         raise RuntimeError("DiT device error")
     steps = max(1, args.euler_steps)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
     with ClockSampler(dev.index) as clk:
         ev[0].record(stream)
         for i in range(steps):
@@ -471,6 +482,11 @@ def run_euler(args, torch, s2b200, synth, dev):
         torch.cuda.synchronize()
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
     ms = float(np.mean(per))
+    if dist:
+        ms_t = torch.tensor([ms, float(min(per))], dtype=torch.float64, device=dev)
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        ms = float(ms_t[0].item())
+        per = [float(ms_t[1].item())]
     ok = bool(torch.isfinite(x0).all().item())
     L = 6 * 45 * 80
     gemm = sum(synth.block_gemm_flops(L, 58, 2560, 6912, last=(i == 31)) for i in range(32))
@@ -481,6 +497,8 @@ def run_euler(args, torch, s2b200, synth, dev):
     m.euler_step_host(hn, hc, ht, 1000.0, hx, stream=stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = max(1, min(steps, args.e2e_steps))
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(e2e_steps):
@@ -488,14 +506,23 @@ def run_euler(args, torch, s2b200, synth, dev):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if dist:
+        e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(e_t.item())
     launches = m.last_launches()
     m.close()
+    if comm is not None:
+        comm.close()
     return {"workload": "DiT Euler step at 720p: latent 33x6x90x160 -> 21,600 tokens, 58 text tokens x 5120, "
                         "32 blocks (dim 2560, 20 heads, SwiGLU 6912), t = 1000, one step, cfg 1",
             "ms_per_step": ms, "ms_min": float(min(per)), "steps": steps, "higher_is_better": False,
             "gemm_tflop_per_step": gemm / 1e12, "attention_tflop_per_step": att / 1e12,
             "tflops_overall": (gemm + att) / (ms * 1e-3) / 1e12, "gpu_launches_per_step": launches,
-            "cuda_graph": True, "finite": ok, "weights_load_s": load_s,
+            "cuda_graph": world == 1, "n_gpus": world,
+            "sharding": "one step split by window across the GPUs (NCCL text all-reduce + row exchange at every "
+                        "plain/shifted boundary), strong scaling" if world > 1 else "one GPU",
+            "finite": ok, "weights_load_s": load_s,
             "e2e": {"ms_per_step": e2e_ms, "unit": "ms", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(hn.nbytes + hc.nbytes + ht.nbytes),
                     "d2h_bytes_per_step": int(hx.nbytes), "path": "s2_dit_euler_step_host (pinned host buffers)"},

@@ -166,3 +166,25 @@ def dit_latents(latent_shape, out_channels=16, text_len=TEXT_LEN, text_channels=
     cond = rng.standard_normal((out_channels, T, H, W), dtype=np.float32)
     text = rng.standard_normal((text_len, text_channels), dtype=np.float32)
     return noise, cond, text
+
+
+def block_weights_device(dim, heads, mlp_hidden, shared=False, seed=666, device="cuda"):
+    """The block_weights layout and distributions drawn with torch's device RNG
+    (identical on every GPU for the same seed), returned as a host fp32 numpy
+    array -- fast enough to build a 32-block model on each of several ranks."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def nrm(n, std, mean=0.0):
+        return (torch.randn(n, generator=g, device=device) * std + mean)
+
+    def branch():
+        parts = [nrm(dim, 0.02) for _ in range(6)]
+        parts += [nrm(3 * dim * dim, 0.02), nrm(dim * dim, 0.02), nrm(dim, 0.02), nrm(HEAD_DIM, 0.1, 1.0),
+                  nrm(HEAD_DIM, 0.1, 1.0), nrm(mlp_hidden * dim, 0.02), nrm(mlp_hidden * dim, 0.02),
+                  nrm(dim * mlp_hidden, 0.02)]
+        return parts
+
+    parts = branch() if shared else branch() + branch()
+    parts.append(torch.from_numpy(rope_freqs()).to(device))
+    return torch.cat(parts).float().cpu().numpy()
