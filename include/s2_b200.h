@@ -337,7 +337,8 @@ S2_API s2_status s2_dit_set_graph(s2_dit *model, int enable);
  * attention mean, exchanges rows between the plain and shifted window
  * ownerships of consecutive blocks, and all ranks end with the full output
  * (disjoint per-rank parts summed). All ranks call forward / euler_step with
- * the same inputs; the step then runs eagerly (no CUDA graph). */
+ * the same inputs, in the same order (the graph of a sharded step holds the
+ * NCCL calls: destroy the model before the communicator). */
 S2_API s2_status s2_dit_set_comm(s2_dit *model, s2_comm *comm);
 S2_API int s2_dit_last_launches(const s2_dit *model);
 S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);

@@ -696,7 +696,7 @@ extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noi
     k.T = T, k.H = H, k.W = W, k.Lt = Lt, k.noise = noise, k.cond = condition, k.text = text, k.x0 = x0, k.t = timestep;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
-    if (!d->use_graph || cs != cudaStreamCaptureStatusNone || (d->comm && s2_comm_size(d->comm) > 1))
+    if (!d->use_graph || cs != cudaStreamCaptureStatusNone)
         return euler_step_eager(d, st, noise, condition, T, H, W, text, Lt, timestep, x0);
     if (d->exec && d->key_valid && d->key == k) {
         if (cudaGraphLaunch(d->exec, st) != cudaSuccess)

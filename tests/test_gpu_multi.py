@@ -53,8 +53,10 @@ def _rank(rank, world, port, out_dir):
     flags, wi, wo, bws, noise, cond, text = _case()
     m = _model(rank, flags, wi, wo, bws)
     m.set_comm(comm)
-    x0 = m.euler_step(*(torch.from_numpy(a).cuda(rank) for a in (noise, cond, text)))
-    x0b = m.euler_step(*(torch.from_numpy(a).cuda(rank) for a in (noise, cond, text)))
+    args = [torch.from_numpy(a).cuda(rank) for a in (noise, cond, text)]
+    x0 = m.euler_step(*args)        # eager
+    for _ in range(3):              # captured once (NCCL calls inside the graph), then replayed
+        x0b = m.euler_step(*args, x0=torch.empty_like(x0))
     torch.cuda.synchronize()
     assert m.device_error() == 0
     np.save(os.path.join(out_dir, f"x0_{rank}.npy"), x0.cpu().numpy())
