@@ -379,7 +379,9 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     s2::DeviceGuard guard(b->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int d = b->dim, h = b->hidden;
-    const size_t Lz = static_cast<size_t>(L), Tz = static_cast<size_t>(std::max(Lt, 1));
+    // With shared weights the text rows ride along as rows L .. L+Lt of the video GEMMs.
+    const bool merged = b->shared && Lt > 0;
+    const size_t Lz = static_cast<size_t>(L) + static_cast<size_t>(std::max(Lt, 0)), Tz = static_cast<size_t>(std::max(Lt, 1));
     const bool fresh = b->err.ptr == nullptr;
     BlockScratch &sc = *b->sc;
     if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) || !sc.qkv_vid.ensure(Lz * 3 * d * 2) ||
@@ -403,30 +405,42 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         }                            \
         ++launches;                  \
     } while (0)
+    const size_t dz = static_cast<size_t>(d);
+    __half *a_vid = static_cast<__half *>(sc.a_vid.ptr);
+    __half *a_txt = merged ? a_vid + static_cast<size_t>(L) * dz : static_cast<__half *>(sc.a_txt.ptr);
+    __half *qkv_vid = static_cast<__half *>(sc.qkv_vid.ptr);
+    __half *qkv_txt = merged ? qkv_vid + static_cast<size_t>(L) * 3 * dz : static_cast<__half *>(sc.qkv_txt.ptr);
+    __half *att_vid = static_cast<__half *>(sc.att_vid.ptr);
+    __half *att_txt16 = merged ? att_vid + static_cast<size_t>(L) * dz : static_cast<__half *>(sc.att_txt16.ptr);
+    float *h_vid = static_cast<float *>(sc.h_vid.ptr);
+    float *h_txt = merged ? h_vid + static_cast<size_t>(L) * dz : static_cast<float *>(sc.h_txt.ptr);
 
-    // modulation vectors of both branches for this emb
-    float *mv = static_cast<float *>(b->mods.ptr), *mt = mv + 8 * static_cast<size_t>(d);
+    // modulation vectors: video branch, and the text branch when it has its own weights and uses them
+    float *mv = static_cast<float *>(b->mods.ptr), *mt = mv;
     S2_TRY(s2::modulation_vectors(st, emb, V.m(0, d), d, mv));
-    if (Lt > 0) S2_TRY(s2::modulation_vectors(st, emb, T.m(0, d), d, mt));
+    if (Lt > 0 && !b->shared && !b->last) {
+        mt = mv + 8 * dz;
+        S2_TRY(s2::modulation_vectors(st, emb, T.m(0, d), d, mt));
+    }
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
-    S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, static_cast<__half *>(sc.a_vid.ptr)));
-    if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, static_cast<__half *>(sc.a_txt.ptr)));
+    S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid));
+    if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, a_txt));
     // QKV projections (no bias)
     s2::GemmArgs g;
     g.K = d;
     g.N = 3 * d;
     g.split = 3 * d;
     g.err = err;
-    g.M = L;
-    g.out[0] = sc.qkv_vid.ptr;
-    S2_TRY(s2::gemm_f16(st, sc.a_vid.ptr, V.qkv.ptr, g));
-    if (Lt > 0) {
+    g.M = merged ? L + Lt : L;
+    g.out[0] = qkv_vid;
+    S2_TRY(s2::gemm_f16(st, a_vid, V.qkv.ptr, g));
+    if (Lt > 0 && !merged) {
         g.M = Lt;
-        g.out[0] = sc.qkv_txt.ptr;
-        S2_TRY(s2::gemm_f16(st, sc.a_txt.ptr, T.qkv.ptr, g));
+        g.out[0] = qkv_txt;
+        S2_TRY(s2::gemm_f16(st, a_txt, T.qkv.ptr, g));
     }
     // windowed MM attention (prologue, attention, text mean)
-    if ((s = s2_attention_layer_forward(b->attn, stream, sc.qkv_vid.ptr, S2_F16, L, sc.qkv_txt.ptr, Lt, sc.att_vid.ptr,
+    if ((s = s2_attention_layer_forward(b->attn, stream, qkv_vid, S2_F16, L, qkv_txt, Lt, att_vid,
                                         static_cast<float *>(sc.att_txt32.ptr))) != S2_OK) {
         b->last_launches = launches;
         return s;
@@ -437,43 +451,55 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         b->last_launches = launches;
         return s;
     }
+    if (Lt > 0) {
+        const long long n = static_cast<long long>(Lt) * d;
+        f32_to_f16_kernel<<<static_cast<unsigned>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
+            static_cast<const float *>(sc.att_txt32.ptr), n, att_txt16);
+        if (cudaGetLastError() != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: convert launch failed");
+        ++launches;
+    }
     // output projection + gated residual
+    const bool merged_rest = merged && !b->last;
     s2::GemmArgs p;
     p.K = d;
     p.N = d;
     p.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
     p.err = err;
-    p.M = L;
+    p.M = merged_rest ? L + Lt : L;
     p.bias = static_cast<const float *>(V.proj_b.ptr);
-    p.gmul = mv + 6 * static_cast<size_t>(d);
+    p.gmul = mv + 6 * dz;
     p.resid = vid;
-    p.y = static_cast<float *>(sc.h_vid.ptr);
-    S2_TRY(s2::gemm_f16(st, sc.att_vid.ptr, V.proj.ptr, p));
-    if (Lt > 0) {
-        const long long n = static_cast<long long>(Lt) * d;
-        f32_to_f16_kernel<<<static_cast<unsigned>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
-            static_cast<const float *>(sc.att_txt32.ptr), n, static_cast<__half *>(sc.att_txt16.ptr));
-        if (cudaGetLastError() != cudaSuccess)
-            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: convert launch failed");
-        ++launches;
-        p.M = Lt;
-        p.bias = static_cast<const float *>(T.proj_b.ptr);
-        p.resid = txt;
+    p.y = h_vid;
+    if (merged_rest) {
+        p.split_row = L;
+        p.resid2 = txt;
+        p.y2 = h_txt;
+    }
+    S2_TRY(s2::gemm_f16(st, att_vid, V.proj.ptr, p));
+    if (Lt > 0 && !merged_rest) {
+        s2::GemmArgs q;
+        q.K = d;
+        q.N = d;
+        q.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+        q.err = err;
+        q.M = Lt;
+        q.bias = static_cast<const float *>(T.proj_b.ptr);
+        q.resid = txt;
         if (b->last) {
             // vid_only modulation: plain residual, and the text output is 2 * (proj + txt)
-            p.gmul = nullptr;
-            p.out_scale = 2.f;
-            p.y = txt_out;
+            q.out_scale = 2.f;
+            q.y = txt_out;
         } else {
-            p.gmul = mt + 6 * static_cast<size_t>(d);
-            p.y = static_cast<float *>(sc.h_txt.ptr);
+            q.gmul = mt + 6 * dz;
+            q.y = h_txt;
         }
-        S2_TRY(s2::gemm_f16(st, sc.att_txt16.ptr, T.proj.ptr, p));
+        S2_TRY(s2::gemm_f16(st, att_txt16, T.proj.ptr, q));
     }
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
-    auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid,
-                   float *y) -> s2_status {
-        s2_status r = rms_ada3(st, hx, rows, d, b->eps, mb + 3 * static_cast<size_t>(d), a16);
+    auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y,
+                   int split, float *y2) -> s2_status {
+        s2_status r = rms_ada3(st, hx, rows, d, b->eps, mb + 3 * dz, a16);
         if (r != S2_OK) return r;
         ++launches;
         s2::GemmArgs u;
@@ -490,22 +516,27 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         o.N = d;
         o.K = h;
         o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
-        o.gmul = mb + 7 * static_cast<size_t>(d);
+        o.gmul = mb + 7 * dz;
         o.resid = hx;
         o.y = y;
+        if (split > 0) {
+            o.split_row = split;
+            o.resid2 = hx + static_cast<size_t>(split) * dz;
+            o.y2 = y2;
+        }
         o.err = err;
         if ((r = s2::gemm_f16(st, hid, br.out.ptr, o)) != S2_OK) return r;
         ++launches;
         return S2_OK;
     };
-    if ((s = mlp(mv, V, static_cast<const float *>(sc.h_vid.ptr), L, static_cast<__half *>(sc.a_vid.ptr),
-                 static_cast<__half *>(sc.hid_vid.ptr), vid_out)) != S2_OK) {
+    if ((s = mlp(mv, V, h_vid, merged_rest ? L + Lt : L, a_vid, static_cast<__half *>(sc.hid_vid.ptr), vid_out,
+                 merged_rest ? L : 0, txt_out)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
-    if (Lt > 0 && !b->last &&
-        (s = mlp(mt, T, static_cast<const float *>(sc.h_txt.ptr), Lt, static_cast<__half *>(sc.a_txt.ptr),
-                 static_cast<__half *>(sc.hid_txt.ptr), txt_out)) != S2_OK) {
+    if (Lt > 0 && !b->last && !merged_rest &&
+        (s = mlp(mt, T, h_txt, Lt, static_cast<__half *>(sc.a_txt.ptr), static_cast<__half *>(sc.hid_txt.ptr), txt_out,
+                 0, nullptr)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }

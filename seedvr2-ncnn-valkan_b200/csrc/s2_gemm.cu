@@ -200,11 +200,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else if (a.epilogue == s2::GEMM_EPI_GATED_RESID_F32) {
                     if (row_ok) {
-                        const float4 *rs = reinterpret_cast<const float4 *>(a.resid + static_cast<size_t>(row) * a.N + n);
-                        float4 *yd = reinterpret_cast<float4 *>(a.y + static_cast<size_t>(row) * a.N + n);
+                        const bool second = a.split_row > 0 && row >= a.split_row;
+                        const int rr = second ? row - a.split_row : row;
+                        const float *rbase = second ? a.resid2 : a.resid;
+                        const float4 *rs = reinterpret_cast<const float4 *>(rbase + static_cast<size_t>(rr) * a.N + n);
+                        float4 *yd = reinterpret_cast<float4 *>((second ? a.y2 : a.y) + static_cast<size_t>(rr) * a.N + n);
                         float4 res[8];
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) res[v] = a.resid ? __ldg(rs + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int v = 0; v < 8; ++v) res[v] = rbase ? __ldg(rs + v) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
                             float o[4];
@@ -309,7 +312,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
         if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
     } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
-        if (!args.y || args.N % 32 != 0 ||
+        if (!args.y || args.N % 32 != 0 || (args.split_row > 0 && (!args.y2 || (args.resid && !args.resid2))) ||
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {

@@ -48,6 +48,12 @@ struct GemmArgs {
     long long ldt = 0;
     int n_valid = 0;
     const float *gmul = nullptr;  // GEMM_EPI_GATED_RESID_F32 gate vector [N] or null
+    // GEMM_EPI_GATED_RESID_F32 row split (0 = none): rows >= split_row read
+    // resid2 and write y2 at row - split_row (video and text rows of a block
+    // with shared weights in one GEMM)
+    int split_row = 0;
+    const float *resid2 = nullptr;
+    float *y2 = nullptr;
     float out_scale = 1.f;
     int32_t *err = nullptr;       // device error word (bounded waits)
 };
