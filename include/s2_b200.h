@@ -343,6 +343,34 @@ S2_API s2_status s2_dit_set_comm(s2_dit *model, s2_comm *comm);
 S2_API int s2_dit_last_launches(const s2_dit *model);
 S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);
 
+/* ---- the reference's exported model files (host only) -------------------- */
+
+/* Readers for the model directory written by the reference's exporter
+ * (tools/export_seedvr2_dit_ncnn.py; loaded by SeedVR2DiT::load,
+ * src/model/dit.cpp:119-214): per layer an ncnn .param text graph and a .bin
+ * of weight blobs (raw fp32 vectors; InnerProduct weights tagged fp16
+ * 0x01306B47 or fp32 0). Each reader parses the layer's ParamDict and decodes
+ * the .bin into the fp32 stream that layer's s2_*_load takes; weights NULL
+ * returns the float count in *n. */
+typedef struct s2_block_params {
+    int block_index, shared, last, shifted, dim, heads, head_dim, mlp_hidden;
+    float eps;
+} s2_block_params;
+typedef struct s2_head_params {
+    int dim, video_channels, text_channels, sinusoidal_dim, embedding_dim, out_channels;
+    float eps;
+} s2_head_params;
+S2_API s2_status s2_ncnn_read_block(const char *param_path, const char *bin_path, s2_block_params *params,
+                                    float *weights, size_t cap, size_t *n);
+S2_API s2_status s2_ncnn_read_input(const char *param_path, const char *bin_path, s2_head_params *params,
+                                    float *weights, size_t cap, size_t *n);
+S2_API s2_status s2_ncnn_read_output(const char *param_path, const char *bin_path, s2_head_params *params,
+                                     float *weights, size_t cap, size_t *n);
+/* Loads seedvr2_dit_input / seedvr2_dit_output / seedvr2_dit_block_NN
+ * (.ncnn.param + .ncnn.bin) from `dir` into the model (block flags from the
+ * block files). */
+S2_API s2_status s2_dit_load_dir(s2_dit *model, const char *dir);
+
 /* ---- VAE mid-block spatial attention ------------------------------------ */
 
 /* Single-head attention per frame, the core of the VAE mid-block attention

@@ -42,6 +42,16 @@ class S2Error(RuntimeError):
         self.status = status
 
 
+class BlockParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("block_index", "shared", "last", "shifted", "dim", "heads", "head_dim",
+                                            "mlp_hidden")] + [("eps", ctypes.c_float)]
+
+
+class HeadParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("dim", "video_channels", "text_channels", "sinusoidal_dim",
+                                            "embedding_dim", "out_channels")] + [("eps", ctypes.c_float)]
+
+
 class Window(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
 
@@ -100,6 +110,13 @@ _SIGS = {
                                + [_vp, ctypes.c_int, ctypes.c_float, _vp]),
     "s2_dit_set_graph": (ctypes.c_int, [_vp, ctypes.c_int]),
     "s2_dit_set_comm": (ctypes.c_int, [_vp, _vp]),
+    "s2_ncnn_read_block": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(BlockParams), _f32p,
+                                          ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "s2_ncnn_read_input": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(HeadParams), _f32p,
+                                          ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "s2_ncnn_read_output": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(HeadParams), _f32p,
+                                           ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "s2_dit_load_dir": (ctypes.c_int, [_vp, ctypes.c_char_p]),
     "s2_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "s2_comm_init": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
                                     ctypes.POINTER(ctypes.c_void_p)]),
@@ -447,6 +464,10 @@ class SeedVR2DiT:
         w = np.ascontiguousarray(weights, np.float32).ravel()
         _check(lib().s2_dit_load_output(self.handle, w.ctypes.data_as(_f32p), w.size), "s2_dit_load_output")
 
+    def load_dir(self, model_dir: str):
+        """Loads the reference's exported model directory (SeedVR2DiT::load)."""
+        _check(lib().s2_dit_load_dir(self.handle, os.fsencode(model_dir)), "s2_dit_load_dir")
+
     def forward(self, latent, text, timestep, prediction=None, stream=None):
         torch = _torch()
         vc, T, H, W = latent.shape
@@ -636,6 +657,29 @@ class Comm:
             self.close()
         except Exception:
             pass
+
+
+def _read_ncnn(fn, ptype, param_path, bin_path):
+    p = ptype()
+    n = ctypes.c_size_t(0)
+    _check(fn(os.fsencode(param_path), os.fsencode(bin_path), ctypes.byref(p), None, 0, ctypes.byref(n)), fn.__name__)
+    w = np.zeros(n.value, np.float32)
+    _check(fn(os.fsencode(param_path), os.fsencode(bin_path), ctypes.byref(p), w.ctypes.data_as(_f32p), w.size,
+              ctypes.byref(n)), fn.__name__)
+    return {f: getattr(p, f) for f, _ in ptype._fields_}, w
+
+
+def read_ncnn_block(param_path, bin_path):
+    """(ParamDict values, fp32 weight stream) of an exported SeedVR2DiTBlock."""
+    return _read_ncnn(lib().s2_ncnn_read_block, BlockParams, param_path, bin_path)
+
+
+def read_ncnn_input(param_path, bin_path):
+    return _read_ncnn(lib().s2_ncnn_read_input, HeadParams, param_path, bin_path)
+
+
+def read_ncnn_output(param_path, bin_path):
+    return _read_ncnn(lib().s2_ncnn_read_output, HeadParams, param_path, bin_path)
 
 
 def padded_channels(channels: int) -> int:

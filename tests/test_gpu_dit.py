@@ -157,3 +157,27 @@ def test_graph_replay_matches_eager(torch_cuda):
     for o in outs:
         assert np.array_equal(o, ref_out)
     assert m.last_launches() == eager.last_launches()
+
+
+def test_load_exported_model_dir(torch_cuda, tmp_path):
+    """A model directory in the reference's exported layout (fp16-tagged
+    InnerProduct weights) loads through s2_dit_load_dir and gives exactly the
+    step of the same weights loaded as streams."""
+    import ncnn_files
+    dim, heads, mlp, tc, n_blocks = 256, 2, 256, 256, 4
+    ei = ncnn_files.write_input(tmp_path, synth.dit_input_weights(dim, 33, tc, 256), dim, tc)
+    eo = ncnn_files.write_output(tmp_path, synth.dit_output_weights(dim), dim)
+    ebs = []
+    for i in range(n_blocks):
+        f = s2b200.block_flags(i, n_blocks)
+        ebs.append(ncnn_files.write_block(tmp_path, i, synth.block_weights(dim, heads, mlp, f["shared"], seed=40 + i),
+                                          dim, heads, mlp, f["shared"], f["last"], f["shifted"]))
+    a = s2b200.SeedVR2DiT(n_blocks=n_blocks, dim=dim, heads=heads, mlp_hidden=mlp, text_channels=tc)
+    a.load_dir(str(tmp_path))
+    b = s2b200.SeedVR2DiT(n_blocks=n_blocks, dim=dim, heads=heads, mlp_hidden=mlp, text_channels=tc)
+    b.load_input(ei)
+    b.load_output(eo)
+    for i in range(n_blocks):
+        b.load_block(i, ebs[i])
+    noise, cond, text = synth.dit_latents((2, 8, 10), 16, 5, tc)
+    assert np.array_equal(a.euler_step_host(noise, cond, text), b.euler_step_host(noise, cond, text))
