@@ -21,6 +21,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "s2_gemm.h"
@@ -36,7 +37,9 @@ constexpr int kStages = 4;
 constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kOffBar = kStages * kStageBytes;
+constexpr uint32_t kOffStage = kStages * kStageBytes;  // fp16 epilogue staging: 4 warps x 2 x (32 rows x 64 B)
+constexpr uint32_t kStageChunk = 32 * 64;
+constexpr uint32_t kOffBar = kOffStage + 4 * 2 * kStageChunk;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 constexpr int kThreads = 192;
@@ -69,7 +72,8 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const s2::GemmArgs a)
+                const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
+                const __grid_constant__ CUtensorMap tmO2, const s2::GemmArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -149,6 +153,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (accumulator rows)
         const int quad = warp & 3;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        // fp16 outputs leave through shared memory as TMA bulk stores of 32 rows x 32 columns
+        const uint32_t stg0 = base + kOffStage + static_cast<uint32_t>(warp - 2) * 2 * kStageChunk;
+        uint8_t *stg0_g = gbase + kOffStage + static_cast<uint32_t>(warp - 2) * 2 * kStageChunk;
+        uint32_t sb = 0;
+        auto store_chunk = [&](const CUtensorMap *map, const uint4 (&v)[4], int col, int row) {
+            if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+            __syncwarp();
+            uint4 *dst = reinterpret_cast<uint4 *>(stg0_g + sb * kStageChunk + lane * 64);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[k] = v[k];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(map, stg0 + sb * kStageChunk, col, row);
+                bulk_commit_group();
+            }
+            sb ^= 1u;
+        };
         uint32_t lt = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
@@ -167,21 +189,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(tmem + lane_off + b * kBN + c * 32, r);
                 tmem_wait_ld();
                 if (a.epilogue == s2::GEMM_EPI_SPLIT_F16) {
-                    if (row_ok) {
-                        const int which = n / a.split, col = n - which * a.split;
-                        void *ob = which == 0 ? a.out[0] : (which == 1 ? a.out[1] : a.out[2]);
-                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(ob) +
-                                                               static_cast<size_t>(row) * a.split + col);
+                    const int which = n / a.split, col = n - which * a.split;
+                    uint4 v4[4];
 #pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            float f[8];
+                    for (int v = 0; v < 4; ++v) {
+                        float f[8];
 #pragma unroll
-                            for (int e = 0; e < 8; ++e)
-                                f[e] = __uint_as_float(r[v * 8 + e]) + (a.bias ? __ldg(a.bias + n + v * 8 + e) : 0.f);
-                            dst[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                                                pack_h2(f[6], f[7]));
-                        }
+                        for (int e = 0; e < 8; ++e)
+                            f[e] = __uint_as_float(r[v * 8 + e]) + (a.bias ? __ldg(a.bias + n + v * 8 + e) : 0.f);
+                        v4[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                           pack_h2(f[6], f[7]));
                     }
+                    store_chunk(which == 0 ? &tmO0 : (which == 1 ? &tmO1 : &tmO2), v4, col, m0 + quad * 32);
                 } else if (a.epilogue == s2::GEMM_EPI_RESID_T_F32) {
                     // channel-major store: for a fixed column the warp's 32 rows are 128 contiguous bytes.
                     // All 32 residual loads of the chunk are issued before its stores (y and resid are
@@ -232,26 +251,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tmem + lane_off + b * kBN + c * 32, gr);
                     tmem_ld32(tmem + lane_off + b * kBN + 128 + c * 32, ur);
                     tmem_wait_ld();
-                    if (row_ok) {
-                        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(a.out[0]) +
-                                                               static_cast<size_t>(row) * (a.N / 2) + n0 / 2 + c * 32);
+                    uint4 v4[4];
 #pragma unroll
-                        for (int v = 0; v < 4; ++v) {
-                            float f[8];
+                    for (int v = 0; v < 4; ++v) {
+                        float f[8];
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const float g = __uint_as_float(gr[v * 8 + e]);
-                                f[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), __uint_as_float(ur[v * 8 + e]));
-                            }
-                            dst[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                                                pack_h2(f[6], f[7]));
+                        for (int e = 0; e < 8; ++e) {
+                            const float g = __uint_as_float(gr[v * 8 + e]);
+                            f[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), __uint_as_float(ur[v * 8 + e]));
                         }
+                        v4[v] = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                           pack_h2(f[6], f[7]));
                     }
+                    store_chunk(&tmO0, v4, n0 / 2 + c * 32, m0 + quad * 32);
                 }
             }
             tc_fence_before();
             mbar_arrive(BAR(B_ACCE + b));
         }
+        if (lane == 0) bulk_wait_group_all();  // every bulk store of this warp has landed
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -296,6 +315,20 @@ bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t row
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_2d_plain(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_rows)
+{
+    auto encode = get_encode();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs &args)
 {
     if (!A || !B || args.M <= 0 || args.N <= 0 || args.K <= 0 || args.K % kBK != 0 || !args.err)
@@ -321,10 +354,24 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else {
         return set_error(S2_UNSUPPORTED, "gemm: unknown epilogue %d", args.epilogue);
     }
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mo[3];
     if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM) ||
         !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK, kBN))
         return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");
+    // fp16 outputs: 32 x 32 store boxes, no swizzle (the unused maps repeat the first valid one)
+    std::memset(mo, 0, sizeof(mo));
+    if (args.epilogue == GEMM_EPI_SPLIT_F16 || args.epilogue == GEMM_EPI_SWIGLU_F16) {
+        const int n_out = args.epilogue == GEMM_EPI_SWIGLU_F16 ? 1 : (args.N + args.split - 1) / args.split;
+        const uint64_t cols = args.epilogue == GEMM_EPI_SWIGLU_F16 ? static_cast<uint64_t>(args.N / 2)
+                                                                   : static_cast<uint64_t>(args.split);
+        for (int i = 0; i < 3; ++i) {
+            const void *ptr = args.out[i < n_out ? i : 0];
+            if (!make_map_2d_plain(&mo[i], ptr, cols, args.M, cols * 2, 32, 32))
+                return set_error(S2_INFERENCE_FAILED, "gemm: output tensor map failed");
+        }
+    } else {
+        mo[0] = mo[1] = mo[2] = ma;  // not used by the fp32 epilogues
+    }
     static bool configured = false;
     if (!configured) {
         const cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -337,7 +384,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long tiles = 1LL * ((args.M + kBM - 1) / kBM) * ((args.N + kBN - 1) / kBN);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, args);
+    gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: launch failed: %s", cudaGetErrorString(e));
     return S2_OK;

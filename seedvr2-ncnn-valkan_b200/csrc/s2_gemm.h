@@ -15,6 +15,9 @@ namespace s2 {
 // row_bytes), box = box_inner x box_rows elements, 128-byte swizzle.
 bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
                  uint32_t box_inner, uint32_t box_rows);
+// The same without swizzle (TMA stores from a plain row-major staging tile).
+bool make_map_2d_plain(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_rows);
 
 // Epilogues of D = A B^T (+ bias).
 enum GemmEpilogue : int {

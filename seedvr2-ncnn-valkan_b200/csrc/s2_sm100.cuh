@@ -107,6 +107,25 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint
         : "memory");
 }
 
+// 2-D tiled bulk tensor store shared -> global (bulk async group). Elements
+// outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int c0, int c1)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N bulk groups of this thread still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all bulk groups of this thread have completed.
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---- tcgen05 ---------------------------------------------------------------
 
 // Allocate `ncols` TMEM columns (power of two >= 32); the warp must be converged.
