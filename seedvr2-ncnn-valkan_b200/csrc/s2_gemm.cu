@@ -37,8 +37,8 @@ constexpr int kStages = 4;
 constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kOffStage = kStages * kStageBytes;  // fp16 epilogue staging: 4 warps x 2 x (32 rows x 64 B)
-constexpr uint32_t kStageChunk = 32 * 64;
+constexpr uint32_t kOffStage = kStages * kStageBytes;  // epilogue staging: 4 warps x 2 x (32 rows x 32 columns)
+constexpr uint32_t kStageChunk = 32 * 32 * 4;            // sized for fp32 (fp16 chunks use the first half)
 constexpr uint32_t kOffBar = kOffStage + 4 * 2 * kStageChunk;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -171,6 +171,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             sb ^= 1u;
         };
+        // fp32: 32 rows x 128 B per chunk, 128B-swizzled (16-byte chunk k of row r at k ^ (r % 8)),
+        // which the output map's swizzle mode undoes; conflict-free shared stores
+        auto store_chunk32 = [&](const CUtensorMap *map, const float4 (&v)[8], int col, int row) {
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            float4 *dst = reinterpret_cast<float4 *>(stg0_g + sb * kStageChunk + lane * 128);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) dst[k ^ (lane & 7)] = v[k];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(map, stg0 + sb * kStageChunk, col, row);
+                bulk_commit_group();
+            }
+            sb ^= 1u;
+        };
         uint32_t lt = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
@@ -218,12 +234,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + res[e];
                     }
                 } else if (a.epilogue == s2::GEMM_EPI_GATED_RESID_F32) {
+                    // rows below the split (or all rows) leave by TMA store through the y map, which
+                    // clips at that row count; rows past the split go to y2 with per-thread stores
+                    const bool second = a.split_row > 0 && row >= a.split_row;
+                    const int rr = second ? row - a.split_row : row;
+                    const float *rbase = second ? a.resid2 : a.resid;
+                    float4 outv[8];
                     if (row_ok) {
-                        const bool second = a.split_row > 0 && row >= a.split_row;
-                        const int rr = second ? row - a.split_row : row;
-                        const float *rbase = second ? a.resid2 : a.resid;
                         const float4 *rs = reinterpret_cast<const float4 *>(rbase + static_cast<size_t>(rr) * a.N + n);
-                        float4 *yd = reinterpret_cast<float4 *>((second ? a.y2 : a.y) + static_cast<size_t>(rr) * a.N + n);
                         float4 res[8];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) res[v] = rbase ? __ldg(rs + v) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -239,9 +257,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if (a.gmul) t = __fmul_rn(t, __ldg(a.gmul + col));
                                 o[e] = __fmul_rn(__fadd_rn(t, rv[e]), a.out_scale);
                             }
-                            yd[v] = make_float4(o[0], o[1], o[2], o[3]);
+                            outv[v] = make_float4(o[0], o[1], o[2], o[3]);
+                        }
+                        if (second) {
+                            float4 *yd = reinterpret_cast<float4 *>(a.y2 + static_cast<size_t>(rr) * a.N + n);
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) yd[v] = outv[v];
                         }
                     }
+                    const int y_rows = a.split_row > 0 ? a.split_row : a.M;
+                    if (m0 + quad * 32 < y_rows) store_chunk32(&tmO0, outv, n, m0 + quad * 32);
                 }
             }
             if (a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && ok) {
@@ -329,6 +354,20 @@ bool make_map_2d_plain(CUtensorMap *map, const void *ptr, uint64_t inner, uint64
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_2d_plain_f32(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                           uint32_t box_inner, uint32_t box_rows)
+{
+    auto encode = get_encode();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs &args)
 {
     if (!A || !B || args.M <= 0 || args.N <= 0 || args.K <= 0 || args.K % kBK != 0 || !args.err)
@@ -369,8 +408,13 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             if (!make_map_2d_plain(&mo[i], ptr, cols, args.M, cols * 2, 32, 32))
                 return set_error(S2_INFERENCE_FAILED, "gemm: output tensor map failed");
         }
+    } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
+        const uint64_t rows = args.split_row > 0 ? static_cast<uint64_t>(args.split_row) : static_cast<uint64_t>(args.M);
+        if (!make_map_2d_plain_f32(&mo[0], args.y, args.N, rows, static_cast<uint64_t>(args.N) * 4, 32, 32))
+            return set_error(S2_INFERENCE_FAILED, "gemm: output tensor map failed");
+        mo[1] = mo[2] = mo[0];
     } else {
-        mo[0] = mo[1] = mo[2] = ma;  // not used by the fp32 epilogues
+        mo[0] = mo[1] = mo[2] = ma;  // not used by the channel-major epilogue
     }
     static bool configured = false;
     if (!configured) {

@@ -15,9 +15,12 @@ namespace s2 {
 // row_bytes), box = box_inner x box_rows elements, 128-byte swizzle.
 bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
                  uint32_t box_inner, uint32_t box_rows);
-// The same without swizzle (TMA stores from a plain row-major staging tile).
+// Maps for TMA stores from a staging tile: fp16 without swizzle, fp32 with
+// 128-byte swizzle (box inner extent 32 floats).
 bool make_map_2d_plain(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
                        uint32_t box_inner, uint32_t box_rows);
+bool make_map_2d_plain_f32(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                           uint32_t box_inner, uint32_t box_rows);
 
 // Epilogues of D = A B^T (+ bias).
 enum GemmEpilogue : int {
