@@ -118,15 +118,37 @@ struct Item {
     int head, win, seq0, S, Lw, q0, n_q, n_kv;
 };
 
-__device__ __forceinline__ Item decode_item(const AttnArgs &a, int t)
+// Item decode in two steps, so that every role issues the loads of its next
+// item while it works on the current one: the work word two items ahead and
+// the window bounds one item ahead (two dependent global loads per item would
+// otherwise stall each role at every item boundary).
+struct ItemPrefetch {
+    int t, w, c0, c1;
+};
+
+__device__ __forceinline__ int load_work(const AttnArgs &a, int t)
+{
+    return t < a.n_items ? __ldg(a.work + t / a.heads) : 0;
+}
+
+__device__ __forceinline__ ItemPrefetch prefetch_item(const AttnArgs &a, int t, int w)
+{
+    ItemPrefetch p{t, w, 0, 0};
+    if (t < a.n_items) {
+        p.c0 = __ldg(a.cu + (w >> 16));
+        p.c1 = __ldg(a.cu + (w >> 16) + 1);
+    }
+    return p;
+}
+
+__device__ __forceinline__ Item finish_item(const AttnArgs &a, const ItemPrefetch &p)
 {
     Item it;
-    it.head = t % a.heads;
-    const int w = a.work[t / a.heads];
-    it.win = w >> 16;
-    const int qb = w & 0xFFFF;
-    it.seq0 = a.cu[it.win];
-    it.S = a.cu[it.win + 1] - it.seq0;
+    it.head = p.t % a.heads;
+    it.win = p.w >> 16;
+    const int qb = p.w & 0xFFFF;
+    it.seq0 = p.c0;
+    it.S = p.c1 - p.c0;
     it.Lw = it.S - a.text_len;
     it.q0 = qb * (kQT * kBM);
     it.n_q = min(kQT, (it.S - it.q0 + kBM - 1) / kBM);
@@ -220,8 +242,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t nq[kQT] = {0, 0};   // Q_i loads issued
             uint32_t kv = 0;             // K/V tiles issued (ring position)
             bool ok = true;
+            ItemPrefetch pf_next = prefetch_item(a, blockIdx.x, load_work(a, blockIdx.x));
+            int w_next = load_work(a, blockIdx.x + gridDim.x);
             for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
-                const Item it = decode_item(a, t);
+                const Item it = finish_item(a, pf_next);
+                pf_next = prefetch_item(a, t + gridDim.x, w_next);
+                w_next = load_work(a, t + 2 * gridDim.x);
                 for (int i = 0; i < it.n_q; ++i) {
                     if (!(ok = mbar_wait(BAR(B_QEMPTY + i), (nq[i] & 1u) ^ 1u, abort, a.err, E_WAIT_Q))) break;
                     const int row_q = it.seq0 + it.q0 + i * kBM;
@@ -283,8 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t np[kQT] = {0, 0};   // P_i tiles consumed (P_FULL phases)
             uint32_t kv = 0;             // K/V tiles consumed
             bool ok = true;
+            ItemPrefetch pf_next = prefetch_item(a, blockIdx.x, load_work(a, blockIdx.x));
+            int w_next = load_work(a, blockIdx.x + gridDim.x);
             for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
-                const Item it = decode_item(a, t);
+                const Item it = finish_item(a, pf_next);
+                pf_next = prefetch_item(a, t + gridDim.x, w_next);
+                w_next = load_work(a, t + 2 * gridDim.x);
                 // S_i(0)
                 const uint32_t s0 = kv & 1u;
                 ok = mbar_wait(BAR(B_KFULL + s0), (kv >> 1) & 1u, abort, a.err, E_WAIT_K);
@@ -351,8 +381,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int dim = a.heads * kHD;
         uint32_t ns = 0, no = 0;  // S_FULL phases consumed, items finished
         bool ok = true;
+        ItemPrefetch pf_next = prefetch_item(a, blockIdx.x, load_work(a, blockIdx.x));
+        int w_next = load_work(a, blockIdx.x + gridDim.x);
         for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
-            const Item it = decode_item(a, t);
+            const Item it = finish_item(a, pf_next);
+            pf_next = prefetch_item(a, t + gridDim.x, w_next);
+            w_next = load_work(a, t + 2 * gridDim.x);
             if (g >= it.n_q) continue;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < it.n_kv; ++j) {

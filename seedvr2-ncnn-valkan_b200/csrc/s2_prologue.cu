@@ -256,7 +256,22 @@ extern "C" s2_status s2_qk_norm_rope(void *stream, const void *vid_qkv, const vo
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long pairs = 1LL * n_rows * heads;
     const long long want = (pairs + 31) / 32;
-    const int grid = static_cast<int>(want < 16LL * sm_count() ? want : 16LL * sm_count());
+    // exactly the resident blocks: every block grid-strides to the end, so no
+    // partial last wave of blocks runs at a fraction of the occupancy
+    static int resident_per_sm[3] = {0, 0, 0};  // per input dtype, queried once
+    const int di = in_dtype == S2_F32 ? 0 : in_dtype == S2_F16 ? 1 : 2;
+    int per_sm = resident_per_sm[di];
+    if (per_sm <= 0) {
+        switch (in_dtype) {
+        case S2_F32: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<float>, 256, 0); break;
+        case S2_F16: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__half>, 256, 0); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__nv_bfloat16>, 256, 0); break;
+        }
+        if (per_sm <= 0) per_sm = 1;
+        resident_per_sm[di] = per_sm;
+    }
+    const long long resident = 1LL * per_sm * sm_count();
+    const int grid = static_cast<int>(want < resident ? want : resident);
     auto *Q = static_cast<uint4 *>(q);
     auto *K = static_cast<uint4 *>(k);
     auto *V = static_cast<uint4 *>(v);
