@@ -325,6 +325,42 @@ S2_API s2_status s2_dit_euler_step(s2_dit *model, void *stream, const float *noi
 /* Same on HOST buffers (copies in and out, synchronises `stream`). */
 S2_API s2_status s2_dit_euler_step_host(s2_dit *model, void *stream, const float *noise, const float *condition,
                                         int T, int H, int W, const float *text, int Lt, float timestep, float *x0);
+/* The engine's sampling loop on the device (src/core/engine.cpp:308-347 with
+ * EulerSampler, src/model/sampler.cpp:181-286): x = noise; for each of
+ * `steps` timesteps t_i = 1000 (1 - i/steps): prediction = DiT(x || condition
+ * || ones, positive_text, t_i); when cfg_scale != 1 also the negative
+ * prediction, guided = neg + cfg_scale (pos - neg), rescaled by cfg_rescale *
+ * std(pos) / std(guided) + (1 - cfg_rescale) when cfg_rescale != 0; then
+ * x = step_to(x, t_i, t_{i+1}), or the endpoint x - (t/1000) prediction at the
+ * last step. noise, condition, out: DEVICE fp32 [out_channels][T][H][W]
+ * (out may alias noise); texts fp32 [Lt][text_channels] (negative_text may be
+ * NULL when cfg_scale == 1). Stream-ordered; runs the forwards eagerly (no
+ * graph), so it also works on a sharded model (s2_dit_set_comm). */
+S2_API s2_status s2_dit_sample(s2_dit *model, void *stream, const float *noise, const float *condition, int T, int H,
+                               int W, const float *positive_text, const float *negative_text, int Lt, int steps,
+                               float cfg_scale, float cfg_rescale, float *out);
+
+/* Sampler pieces on DEVICE fp32 tensors of n elements (sampler.cpp):
+ * timesteps of an n-step schedule (host; :181-187); classifier-free guidance
+ * (:200-238; workspace of s2_apply_cfg_workspace_bytes(), 16-byte aligned,
+ * needed only when rescale != 0); Euler step_to (:240-265) and endpoint
+ * (:267-286). Outputs may alias inputs. */
+S2_API s2_status s2_sampler_timesteps(int steps, float *timesteps);
+S2_API size_t s2_apply_cfg_workspace_bytes(void);
+S2_API s2_status s2_apply_cfg(void *stream, const float *positive, const float *negative, long long n, float scale,
+                              float rescale, void *workspace, float *output);
+S2_API s2_status s2_euler_step_to(void *stream, const float *prediction, const float *current, long long n,
+                                  float timestep, float next_timestep, float *output);
+S2_API s2_status s2_euler_endpoint(void *stream, const float *prediction, const float *current, long long n,
+                                   float timestep, float *output);
+/* Condition latent from the VAE encoding and augmentation noise
+ * (make_condition_latent, src/core/engine.cpp:79-121): condition =
+ * (1 - r) encoded + r noise with r = s2_condition_ratio(noise_scale, T, H, W)
+ * (the shifted condition timestep / 1000 of a latent of T frames, H x W). */
+S2_API float s2_condition_ratio(float noise_scale, int latent_frames, int latent_height, int latent_width);
+S2_API s2_status s2_make_condition(void *stream, const float *encoded, const float *noise, int C, int T, int H, int W,
+                                   float noise_scale, float *condition);
+
 /* From the second call with the same shapes, buffers and timestep,
  * s2_dit_euler_step replays the step as one CUDA graph (captured on an
  * internal stream); enable = 0 keeps every call eager. On by default; a call

@@ -285,6 +285,32 @@ class Ref(_Lib):
         pred = self.dit_output(head_params, output_weights, vid, emb, shape, threads)
         return euler_endpoint(pred, noise, timestep), pred
 
+    def sample(self, head_params, input_weights, block_params, block_weights, output_weights, noise, condition,
+               positive_text, negative_text=None, steps=1, cfg_scale=1.0, cfg_rescale=0.0, threads=0):
+        """The engine's sampling loop (engine.cpp:308-347) on the reference's
+        own code: make_dit_input (restated), the DiT forward layer by layer,
+        and EulerSampler (apply_cfg, step_to, endpoint) from sampler.cpp."""
+        s = SamplerRef(self.lib)
+        ts = s.timesteps(steps)
+        latent = _f32(noise)
+        _, T, H, W = latent.shape
+        shape = (T, H // 2, W // 2)
+
+        def predict(text, t):
+            vid, txt, emb = self.dit_input(head_params, input_weights, make_dit_input(latent, condition), text, t,
+                                           threads)
+            for bp, bw in zip(block_params, block_weights):
+                vid, txt = self.block_forward(bp, bw, vid, txt, emb, shape, threads)
+            return self.dit_output(head_params, output_weights, vid, emb, shape, threads)
+
+        for i, t in enumerate(ts):
+            pred = predict(positive_text, float(t))
+            if cfg_scale != 1.0:
+                pred = s.apply_cfg(pred, predict(negative_text, float(t)), cfg_scale, cfg_rescale)
+            latent = s.step_to(pred, latent, float(t), float(ts[i + 1])) if i + 1 < len(ts) else \
+                s.endpoint(pred, latent, float(t))
+        return latent
+
     def vae_attention(self, x, weights_flat, threads=0):
         x = _f32(x)
         C, T, H, W = x.shape
@@ -295,6 +321,110 @@ class Ref(_Lib):
         if rc != 0:
             raise ValueError(f"ref_vae_attention failed: {rc}")
         return y
+
+
+def _sampler_port_init(L):
+    L.s2o_sampler_timesteps.restype = None
+    L.s2o_sampler_timesteps.argtypes = [ctypes.c_int, _f32p]
+    L.s2o_apply_cfg.restype = None
+    L.s2o_apply_cfg.argtypes = [_f32p, _f32p, ctypes.c_size_t, ctypes.c_float, ctypes.c_float, _f32p]
+    L.s2o_euler_step_to.restype = None
+    L.s2o_euler_step_to.argtypes = [_f32p, _f32p, ctypes.c_size_t, ctypes.c_float, ctypes.c_float, _f32p]
+    L.s2o_euler_endpoint.restype = None
+    L.s2o_euler_endpoint.argtypes = [_f32p, _f32p, ctypes.c_size_t, ctypes.c_float, _f32p]
+    L.s2o_condition_ratio.restype = ctypes.c_float
+    L.s2o_condition_ratio.argtypes = [ctypes.c_float] + [ctypes.c_int] * 3
+    L.s2o_make_condition.restype = None
+    L.s2o_make_condition.argtypes = [_f32p, _f32p, ctypes.c_size_t, ctypes.c_float, _f32p]
+
+
+class SamplerPort:
+    """EulerSampler restated in C (oracle/s2_oracle.c; sampler.cpp:19-62,
+    181-286) and the condition builder (engine.cpp:79-121)."""
+
+    def __init__(self, port_lib):
+        self.lib = port_lib
+        _sampler_port_init(port_lib)
+
+    def timesteps(self, steps):
+        out = np.zeros(max(int(steps), 1), np.float32)
+        self.lib.s2o_sampler_timesteps(int(steps), _ptr(out))
+        return out
+
+    def apply_cfg(self, pos, neg, scale, rescale=0.0):
+        pos, neg = _f32(pos), _f32(neg)
+        out = np.empty_like(pos)
+        self.lib.s2o_apply_cfg(_ptr(pos), _ptr(neg), pos.size, ctypes.c_float(scale), ctypes.c_float(rescale), _ptr(out))
+        return out
+
+    def step_to(self, pred, cur, t, t_next):
+        pred, cur = _f32(pred), _f32(cur)
+        out = np.empty_like(cur)
+        self.lib.s2o_euler_step_to(_ptr(pred), _ptr(cur), cur.size, ctypes.c_float(t), ctypes.c_float(t_next), _ptr(out))
+        return out
+
+    def endpoint(self, pred, cur, t):
+        pred, cur = _f32(pred), _f32(cur)
+        out = np.empty_like(cur)
+        self.lib.s2o_euler_endpoint(_ptr(pred), _ptr(cur), cur.size, ctypes.c_float(t), _ptr(out))
+        return out
+
+    def condition_ratio(self, noise_scale, frames, height, width):
+        return float(self.lib.s2o_condition_ratio(ctypes.c_float(noise_scale), frames, height, width))
+
+    def make_condition(self, encoded, noise, noise_scale):
+        encoded, noise = _f32(encoded), _f32(noise)
+        _, T, H, W = encoded.shape
+        out = np.empty_like(encoded)
+        self.lib.s2o_make_condition(_ptr(encoded), _ptr(noise), encoded.size,
+                                    ctypes.c_float(self.condition_ratio(noise_scale, T, H, W)), _ptr(out))
+        return out
+
+
+class SamplerRef:
+    """The reference's own EulerSampler (src/model/sampler.cpp, compiled into
+    oracle/_ref/libs2ref.so by oracle/ref_sampler.cpp)."""
+
+    def __init__(self, ref_lib):
+        L = self.lib = ref_lib
+        L.ref_sampler_timesteps.restype = ctypes.c_int
+        L.ref_sampler_timesteps.argtypes = [ctypes.c_int, _f32p]
+        L.ref_apply_cfg.restype = ctypes.c_int
+        L.ref_apply_cfg.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_float, _f32p]
+        L.ref_step_to.restype = ctypes.c_int
+        L.ref_step_to.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_float, _f32p]
+        L.ref_endpoint.restype = ctypes.c_int
+        L.ref_endpoint.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, _f32p]
+
+    def timesteps(self, steps):
+        out = np.zeros(max(int(steps), 1), np.float32)
+        n = self.lib.ref_sampler_timesteps(int(steps), _ptr(out))
+        return out[:n]
+
+    def apply_cfg(self, pos, neg, scale, rescale=0.0):
+        pos, neg = _f32(pos), _f32(neg)
+        out = np.empty_like(pos)
+        rc = self.lib.ref_apply_cfg(_ptr(pos), _ptr(neg), *pos.shape, ctypes.c_float(scale), ctypes.c_float(rescale),
+                                    _ptr(out))
+        if rc != 0:
+            raise ValueError(f"ref_apply_cfg failed: {rc}")
+        return out
+
+    def step_to(self, pred, cur, t, t_next):
+        pred, cur = _f32(pred), _f32(cur)
+        out = np.empty_like(cur)
+        rc = self.lib.ref_step_to(_ptr(pred), _ptr(cur), *cur.shape, ctypes.c_float(t), ctypes.c_float(t_next), _ptr(out))
+        if rc != 0:
+            raise ValueError(f"ref_step_to failed: {rc}")
+        return out
+
+    def endpoint(self, pred, cur, t):
+        pred, cur = _f32(pred), _f32(cur)
+        out = np.empty_like(cur)
+        rc = self.lib.ref_endpoint(_ptr(pred), _ptr(cur), *cur.shape, ctypes.c_float(t), _ptr(out))
+        if rc != 0:
+            raise ValueError(f"ref_endpoint failed: {rc}")
+        return out
 
 
 def port() -> Port:

@@ -403,3 +403,84 @@ int s2o_vae_attention_tokens(int channels, int frames, int height, int width,
     free(nrm); free(km); free(vm); free(qs); free(as); free(nsel); free(ps);
     return 0;
 }
+
+
+/* ---- sampler (src/model/sampler.cpp) ---------------------------------------- */
+
+/* EulerSampler::EulerSampler (sampler.cpp:181-187) */
+void s2o_sampler_timesteps(int steps, float *timesteps)
+{
+    if (steps < 1) steps = 1;
+    for (int i = 0; i < steps; i++) timesteps[i] = 1000.0f * (1.0f - (float)i / steps);
+}
+
+/* standard_deviation (sampler.cpp:41-62): sequential fp64 sum and sum of squares */
+static double sampler_std(const float *v, size_t n)
+{
+    double sum = 0.0, square_sum = 0.0;
+    for (size_t i = 0; i < n; i++) {
+        sum += v[i];
+        square_sum += (double)v[i] * v[i];
+    }
+    if (n <= 1) return 0.0;
+    double variance = (square_sum - sum * sum / n) / (n - 1);
+    if (variance < 0.0) variance = 0.0;
+    return sqrt(variance);
+}
+
+/* EulerSampler::apply_cfg (sampler.cpp:200-238) */
+void s2o_apply_cfg(const float *positive, const float *negative, size_t n, float scale, float rescale, float *output)
+{
+    for (size_t i = 0; i < n; i++) output[i] = negative[i] + scale * (positive[i] - negative[i]);
+    if (rescale != 0.0f) {
+        const double cfg_std = sampler_std(output, n);
+        if (cfg_std > 0.0) {
+            const float factor = (float)(rescale * sampler_std(positive, n) / cfg_std + (1.0f - rescale));
+            for (size_t i = 0; i < n; i++) output[i] *= factor;
+        }
+    }
+}
+
+/* EulerSampler::step_to (sampler.cpp:240-265) */
+void s2o_euler_step_to(const float *prediction, const float *current, size_t n, float timestep, float next_timestep,
+                       float *output)
+{
+    const float bt = timestep / 1000.0f;
+    const float at = 1.0f - bt;
+    float bs = next_timestep / 1000.0f;
+    bs = bs < 0.0f ? 0.0f : (bs > 1.0f ? 1.0f : bs);
+    const float as = 1.0f - bs;
+    for (size_t i = 0; i < n; i++) {
+        const float x0 = current[i] - bt * prediction[i];
+        const float xT = current[i] + at * prediction[i];
+        output[i] = as * x0 + bs * xT;
+    }
+}
+
+/* EulerSampler::endpoint (sampler.cpp:267-286) */
+void s2o_euler_endpoint(const float *prediction, const float *current, size_t n, float timestep, float *output)
+{
+    const float bt = timestep / 1000.0f;
+    for (size_t i = 0; i < n; i++) output[i] = current[i] - bt * prediction[i];
+}
+
+/* transformed_condition_timestep(noise_scale, latent) / 1000 (engine.cpp:79-92, 108) */
+float s2o_condition_ratio(float noise_scale, int latent_frames, int latent_height, int latent_width)
+{
+    const float timestep = noise_scale * 1000.0f;
+    if (timestep == 0.0f) return 0.0f;
+    const float frames = (float)((latent_frames - 1) * 4 + 1);
+    const float height = (float)(latent_height * 8);
+    const float width = (float)(latent_width * 8);
+    const float x1 = 256.0f * 256.0f * 37.0f;
+    const float x2 = 1280.0f * 720.0f * 145.0f;
+    const float shift = 1.0f + (height * width * frames - x1) * (5.0f - 1.0f) / (x2 - x1);
+    const float normalized = timestep / 1000.0f;
+    return 1000.0f * shift * normalized / (1.0f + (shift - 1.0f) * normalized) / 1000.0f;
+}
+
+/* make_condition_latent (engine.cpp:106-121) */
+void s2o_make_condition(const float *encoded, const float *noise, size_t n, float ratio, float *output)
+{
+    for (size_t i = 0; i < n; i++) output[i] = (1.0f - ratio) * encoded[i] + ratio * noise[i];
+}

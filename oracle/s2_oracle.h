@@ -8,6 +8,12 @@
  *                            (bf16 RNE helper :68-79)
  *   s2o_vae_attention     <- DynamicFramewiseSpatialAttention::forward
  *                            src/layers/dynamic_framewise_spatial_attention.cpp:79-210
+ *   s2o_sampler_*         <- EulerSampler (timesteps, apply_cfg, step_to, endpoint)
+ *                            src/model/sampler.cpp:19-62, 181-286
+ *   s2o_condition_ratio / s2o_make_condition
+ *                         <- transformed_condition_timestep / make_condition_latent
+ *                            src/core/engine.cpp:79-121 (restated only: engine.cpp
+ *                            is not part of the reference build under oracle/_ref)
  * Every float/double conversion point follows the reference so that, built with
  * the same flags as oracle/_ref (the reference's own code), results match bit
  * for bit; tests/test_oracle.py pins this against tests/golden/.
@@ -73,6 +79,17 @@ int s2o_vae_attention_tokens(int channels, int frames, int height, int width,
                              const float *v_bias, const float *v_weight,
                              const float *x, int frame, const int *tokens_sel, int n_sel, int num_threads,
                              float *y_sel);
+
+/* Sampler on fp32 tensors of n elements, summed / transformed in storage
+ * order (the reference walks channel, frame, row, x of a dense 4D Mat, which is
+ * the same order). */
+void s2o_sampler_timesteps(int steps, float *timesteps);
+void s2o_apply_cfg(const float *positive, const float *negative, size_t n, float scale, float rescale, float *output);
+void s2o_euler_step_to(const float *prediction, const float *current, size_t n, float timestep, float next_timestep,
+                       float *output);
+void s2o_euler_endpoint(const float *prediction, const float *current, size_t n, float timestep, float *output);
+float s2o_condition_ratio(float noise_scale, int latent_frames, int latent_height, int latent_width);
+void s2o_make_condition(const float *encoded, const float *noise, size_t n, float ratio, float *output);
 
 #ifdef __cplusplus
 }

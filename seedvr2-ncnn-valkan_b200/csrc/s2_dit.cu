@@ -229,6 +229,7 @@ struct s2_dit {
     // workspaces
     s2::DeviceBuffer latent, patches, txt16, vid_a, vid_b, txt_a, txt_b, sinus, th1, th2, emb, omods, o16, proj, err;
     s2::DeviceBuffer h_noise, h_cond, h_text, h_x0;  // host-step staging
+    s2::DeviceBuffer pred_pos, pred_neg, cfg_ws;     // sampling loop: predictions, guidance statistics
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
     std::vector<int> shifted;  // per block (the window kind of its attention)
@@ -740,6 +741,60 @@ extern "C" s2_status s2_dit_euler_step(s2_dit *d, void *stream, const float *noi
     if (cudaGraphLaunch(d->exec, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_euler_step: graph launch: %s",
                              cudaGetErrorString(cudaGetLastError()));
+    d->last_stream = st;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_sample(s2_dit *d, void *stream, const float *noise, const float *condition, int T,
+                                   int H, int W, const float *positive_text, const float *negative_text, int Lt,
+                                   int steps, float cfg_scale, float cfg_rescale, float *out)
+{
+    s2::clear_error();
+    const bool guide = cfg_scale != 1.0f;  // the engine runs the negative branch only then (engine.cpp:319)
+    if (!d || !noise || !condition || !positive_text || !out || T <= 0 || H <= 0 || W <= 0 || Lt <= 0 ||
+        steps <= 0 || (guide && !negative_text))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_sample: invalid arguments");
+    if (d->vc != 2 * d->oc + 1)
+        return s2::set_error(S2_UNSUPPORTED, "s2_dit_sample: video_channels %d != 2 * out_channels + 1", d->vc);
+    s2::DeviceGuard guard(d->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const long long plane = 1LL * T * H * W, n = plane * d->oc;
+    const bool rescale = guide && cfg_rescale != 0.0f;
+    if (!d->latent.ensure(static_cast<size_t>(plane) * d->vc * 4) || !d->pred_pos.ensure(static_cast<size_t>(n) * 4) ||
+        (guide && !d->pred_neg.ensure(static_cast<size_t>(n) * 4)) ||
+        (rescale && !d->cfg_ws.ensure(s2::cfg_workspace_bytes())))
+        return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_sample: workspace allocation failed");
+    std::vector<float> ts(steps);
+    s2_sampler_timesteps(steps, ts.data());
+    float *pos = static_cast<float *>(d->pred_pos.ptr), *neg = static_cast<float *>(d->pred_neg.ptr);
+    float *lat = static_cast<float *>(d->latent.ptr);
+    const float *x = noise;
+    int launches = 0;
+    for (int i = 0; i < steps; ++i) {
+        make_dit_input_kernel<<<grid_for(plane * d->vc), 256, 0, st>>>(x, condition, d->oc, plane, lat);
+        if (cudaGetLastError() != cudaSuccess) return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_sample: launch failed");
+        s2_status s = dit_forward_into(d, st, lat, T, H, W, positive_text, Lt, ts[i], nullptr, pos);
+        if (s != S2_OK) return s;
+        launches += d->last_launches + 1;
+        float *factor = nullptr;
+        if (guide) {
+            s = dit_forward_into(d, st, lat, T, H, W, negative_text, Lt, ts[i], nullptr, neg);
+            if (s != S2_OK) return s;
+            launches += d->last_launches;
+            if (rescale) {
+                s = s2::cfg_factor(st, pos, neg, n, cfg_scale, cfg_rescale, d->cfg_ws.ptr, &factor);
+                if (s != S2_OK) return s;
+                launches += 2;
+            }
+        }
+        const bool final_step = i + 1 == steps;
+        s = s2::sampler_update(st, x, pos, guide ? neg : nullptr, cfg_scale, factor, n, ts[i],
+                               final_step ? 0.f : ts[i + 1], final_step ? 1 : 0, out);
+        if (s != S2_OK) return s;
+        ++launches;
+        x = out;
+    }
+    d->last_launches = launches;
     d->last_stream = st;
     return S2_OK;
 }

@@ -35,4 +35,16 @@ s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps,
 s2_status modulation_vectors(cudaStream_t st, const float *emb, const float *mod6, int dim, float *out);
 s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y_f16);
 
+// Sampler pieces (s2_sampler.cu). Guidance rescale factor of (pos, neg) into
+// device memory inside `workspace` (cfg_workspace_bytes(), 16-byte aligned);
+// *factor points at it.
+size_t cfg_workspace_bytes();
+s2_status cfg_factor(cudaStream_t st, const float *pos, const float *neg, long long n, float scale, float rescale,
+                     void *workspace, float **factor);
+// out = step_to / endpoint of x with the prediction pos, guided by neg when
+// neg != null and scaled by *factor when factor != null.
+s2_status sampler_update(cudaStream_t st, const float *x, const float *pos, const float *neg, float scale,
+                         const float *factor, long long n, float timestep, float next_timestep, int final_step,
+                         float *out);
+
 }  // namespace s2

@@ -151,6 +151,15 @@ _SIGS = {
                                                      ctypes.c_longlong, _vp]),
     "s2_vae_attention_last_launches": (ctypes.c_int, [_vp]),
     "s2_vae_attention_device_error": (ctypes.c_int, [_vp, _i32p]),
+    "s2_dit_sample": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp, _vp, ctypes.c_int, ctypes.c_int,
+                                                                             ctypes.c_float, ctypes.c_float, _vp]),
+    "s2_sampler_timesteps": (ctypes.c_int, [ctypes.c_int, _f32p]),
+    "s2_apply_cfg_workspace_bytes": (ctypes.c_size_t, []),
+    "s2_apply_cfg": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_float, _vp, _vp]),
+    "s2_euler_step_to": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_float, _vp]),
+    "s2_euler_endpoint": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_float, _vp]),
+    "s2_condition_ratio": (ctypes.c_float, [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "s2_make_condition": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 4 + [ctypes.c_float, _vp]),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
@@ -221,6 +230,65 @@ def plan_work(cu_seqlens: np.ndarray) -> np.ndarray:
     _check(lib().s2_plan_work(cu.ctypes.data_as(_i32p), len(cu) - 1, work.ctypes.data_as(_i32p), n.value,
                               ctypes.byref(n)), "s2_plan_work")
     return work[:n.value]
+
+
+# ---- sampler (EulerSampler, src/model/sampler.cpp) ---------------------------
+
+def sampler_timesteps(steps: int) -> np.ndarray:
+    """Timesteps of an n-step Euler schedule, 1000 (1 - i / steps)."""
+    out = np.zeros(max(int(steps), 1), np.float32)
+    _check(lib().s2_sampler_timesteps(int(steps), out.ctypes.data_as(_f32p)), "s2_sampler_timesteps")
+    return out
+
+
+def condition_ratio(noise_scale: float, frames: int, height: int, width: int) -> float:
+    """Mixing ratio of the augmentation noise into the condition latent."""
+    return float(lib().s2_condition_ratio(ctypes.c_float(noise_scale), frames, height, width))
+
+
+def apply_cfg(positive, negative, scale, rescale=0.0, out=None, stream=None):
+    """Classifier-free guidance on device fp32 tensors (EulerSampler::apply_cfg)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(positive)
+    ws = None
+    if rescale != 0.0:
+        ws = torch.empty(int(lib().s2_apply_cfg_workspace_bytes()), dtype=torch.uint8, device=positive.device)
+    _check(lib().s2_apply_cfg(_stream_ptr(stream), _ptr(positive), _ptr(negative), positive.numel(),
+                              ctypes.c_float(scale), ctypes.c_float(rescale), _ptr(ws), _ptr(out)), "s2_apply_cfg")
+    return out
+
+
+def euler_step_to(prediction, current, timestep, next_timestep, out=None, stream=None):
+    """EulerSampler::step_to on device fp32 tensors."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(current)
+    _check(lib().s2_euler_step_to(_stream_ptr(stream), _ptr(prediction), _ptr(current), current.numel(),
+                                  ctypes.c_float(timestep), ctypes.c_float(next_timestep), _ptr(out)),
+           "s2_euler_step_to")
+    return out
+
+
+def euler_endpoint(prediction, current, timestep, out=None, stream=None):
+    """EulerSampler::endpoint on device fp32 tensors."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(current)
+    _check(lib().s2_euler_endpoint(_stream_ptr(stream), _ptr(prediction), _ptr(current), current.numel(),
+                                   ctypes.c_float(timestep), _ptr(out)), "s2_euler_endpoint")
+    return out
+
+
+def make_condition(encoded, noise, noise_scale, out=None, stream=None):
+    """Condition latent (1 - r) encoded + r noise on device fp32 [C, T, H, W]."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(encoded)
+    C, T, H, W = encoded.shape
+    _check(lib().s2_make_condition(_stream_ptr(stream), _ptr(encoded), _ptr(noise), C, T, H, W,
+                                   ctypes.c_float(noise_scale), _ptr(out)), "s2_make_condition")
+    return out
 
 
 def window_costs(windows: np.ndarray, text_len: int) -> np.ndarray:
@@ -498,6 +566,22 @@ class SeedVR2DiT:
                                             ctypes.c_float(timestep), ctypes.c_void_p(x0.ctypes.data)),
                "s2_dit_euler_step_host")
         return x0
+
+    def sample(self, noise, condition, positive_text, negative_text=None, steps=1, cfg_scale=1.0, cfg_rescale=0.0,
+               out=None, stream=None):
+        """The engine's sampling loop (engine.cpp:308-347): ``steps`` Euler
+        steps from ``noise``, with classifier-free guidance against
+        ``negative_text`` when ``cfg_scale != 1``. Device fp32 tensors; returns
+        the final latent (x0)."""
+        torch = _torch()
+        _, T, H, W = noise.shape
+        if out is None:
+            out = torch.empty_like(noise)
+        _check(lib().s2_dit_sample(self.handle, _stream_ptr(stream), _ptr(noise), _ptr(condition), T, H, W,
+                                   _ptr(positive_text), _ptr(negative_text), positive_text.shape[0], int(steps),
+                                   ctypes.c_float(cfg_scale), ctypes.c_float(cfg_rescale), _ptr(out)),
+               "s2_dit_sample")
+        return out
 
     def set_comm(self, comm: "Comm | None"):
         """Shard the step over the communicator's ranks (None: this GPU alone)."""
