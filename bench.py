@@ -77,6 +77,18 @@ def profile_traffic(name):
     return None
 
 
+def preroll_steps(step_ms, dist, dev, target_ms=400.0):
+    """Untimed steps of the same work run inside the clock sampler before the
+    timed region, so that a short timed region still has clock samples taken
+    under load; the same count on every rank (the steps hold collectives)."""
+    import torch
+    n = torch.tensor([float(max(1, int(np.ceil(target_ms / max(step_ms, 1e-3)))))], dtype=torch.float64,
+                     device=dev)
+    if dist:
+        dist.all_reduce(n, op=dist.ReduceOp.MAX)
+    return int(min(n.item(), 1000))
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle samples during the timed region."""
 
@@ -85,9 +97,20 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
-        self.dev = device_index
+        self.dev = self._physical(device_index)
         self.proc = None
         self.lines = []
+
+    @staticmethod
+    def _physical(index):
+        """nvidia-smi ignores CUDA_VISIBLE_DEVICES: map the process's device
+        index to the physical index (or UUID) it names."""
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            if 0 <= index < len(ids):
+                return ids[index]
+        return str(index)
 
     def __enter__(self):
         try:
@@ -96,6 +119,11 @@ class ClockSampler:
                  "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a moment to start: wait for its first sample so a
+            # short timed region is still sampled
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+                time.sleep(0.02)
         except OSError:
             self.proc = None
         return self
@@ -116,7 +144,8 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        # the first sample is taken before the work starts (the sampler waits for it)
+        for ln in self.lines[1:]:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -296,10 +325,12 @@ def run_ours(args, rank, world, local_rank):
             dist.all_reduce(txt_out)
 
     layers_per_step = 32
+    t_w = time.time()
     for _ in range(args.warmup):
         for i in range(layers_per_step):
             layer(i)
     torch.cuda.synchronize()
+    n_pre = preroll_steps((time.time() - t_w) * 1e3 / max(1, args.warmup), dist, dev)
     if int(err.item()) != 0:
         raise RuntimeError(f"attention kernel device error {int(err.item())}")
 
@@ -310,6 +341,9 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
+        for _ in range(n_pre):
+            for i in range(layers_per_step):
+                layer(i)
         start.record(stream)
         for s in range(args.steps):
             for i in range(layers_per_step):
@@ -467,6 +501,10 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
     for _ in range(max(3, args.warmup)):  # eager, capture, replays
         m.euler_step(n, c, t, 1000.0, x0, stream=stream)
     torch.cuda.synchronize()
+    t_w = time.time()
+    m.euler_step(n, c, t, 1000.0, x0, stream=stream)
+    torch.cuda.synchronize()
+    n_pre = preroll_steps((time.time() - t_w) * 1e3, dist, dev)
     if m.device_error() != 0:
         raise RuntimeError("DiT device error")
     steps = max(1, args.euler_steps)
@@ -475,6 +513,8 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clk:
+        for _ in range(n_pre):
+            m.euler_step(n, c, t, 1000.0, x0, stream=stream)
         ev[0].record(stream)
         for i in range(steps):
             m.euler_step(n, c, t, 1000.0, x0, stream=stream)
@@ -539,12 +579,16 @@ def run_vae(args, torch, s2b200, synth, dev):
     xd = torch.from_numpy(x).to(dev)
     y = torch.empty_like(xd)
     stream = torch.cuda.current_stream()
+    t_w = time.time()
     for _ in range(max(3, args.warmup)):
         lay.forward(xd, y, stream=stream)
     torch.cuda.synchronize()
+    n_pre = preroll_steps((time.time() - t_w) * 1e3 / max(3, args.warmup), None, dev)
     steps = max(1, args.vae_steps)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
+        for _ in range(n_pre):
+            lay.forward(xd, y, stream=stream)
         e0.record(stream)
         for _ in range(steps):
             lay.forward(xd, y, stream=stream)
