@@ -32,23 +32,31 @@ using namespace s2dev;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
+constexpr int kBM = 128, kBK = 64;
 constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kOffStage = kStages * kStageBytes;  // epilogue staging: 4 warps x 2 x (32 rows x 32 columns)
-constexpr uint32_t kStageChunk = 32 * 32 * 4;            // sized for fp32 (fp16 chunks use the first half)
-constexpr uint32_t kOffBar = kOffStage + 4 * 2 * kStageChunk;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+constexpr uint32_t kStageChunk = 32 * 32 * 4;  // epilogue staging chunk, sized for fp32 (fp16 uses the first half)
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 512;
 
+// Tile shape: 128 x BN with BN = 256 (the default) or 128 (twice the tiles,
+// for GEMMs too small to fill the grid with 256-wide tiles).
+template <int BN>
+struct Tile {
+    static constexpr int kBN = BN;
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr uint32_t kBBytes = BN * kBK * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kOffStage = kStages * kStageBytes;  // epilogue staging: 4 warps x 2 chunks
+    static constexpr uint32_t kOffBar = kOffStage + 4 * 2 * kStageChunk;
+    static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
+    static constexpr uint32_t kTmemCols = 2 * BN;                 // two accumulators
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+constexpr int kMaxStages = 6;
 enum Bar {
     B_FULL = 0,                     // [kStages] A and B slices landed
-    B_EMPTY = B_FULL + kStages,     // [kStages] MMAs reading the stage retired
-    B_ACCF = B_EMPTY + kStages,     // [2] accumulator complete
+    B_EMPTY = B_FULL + kMaxStages,  // [kStages] MMAs reading the stage retired
+    B_ACCF = B_EMPTY + kMaxStages,  // [2] accumulator complete
     B_ACCE = B_ACCF + 2,            // [2] epilogue finished reading it (128 arrivals)
     B_DRAIN = B_ACCE + 2,
     B_COUNT
@@ -70,11 +78,16 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
                 const __grid_constant__ CUtensorMap tmO2, const s2::GemmArgs a)
 {
+    using T = Tile<BN>;
+    constexpr int kBN = T::kBN, kStages = T::kStages;
+    constexpr uint32_t kStageBytes = T::kStageBytes, kOffStage = T::kOffStage, kOffBar = T::kOffBar;
+    constexpr uint32_t kTmemCols = T::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -269,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (m0 + quad * 32 < y_rows) store_chunk32(&tmO0, outv, n, m0 + quad * 32);
                 }
             }
-            if (a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && ok) {
+            if (kBN == 256 && a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && ok) {
                 // pairs (gate chunk c, in chunk c + 4) of the 256-column tile
                 for (int c = 0; c < 4; ++c) {
                     uint32_t gr[32], ur[32];
@@ -388,14 +401,32 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {
-        if (!args.out[0] || args.N % kBN != 0 || (reinterpret_cast<uintptr_t>(args.out[0]) & 15u) != 0)
+        if (!args.out[0] || args.N % 256 != 0 || (reinterpret_cast<uintptr_t>(args.out[0]) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad SwiGLU output (N %d must be a multiple of 256)", args.N);
     } else {
         return set_error(S2_UNSUPPORTED, "gemm: unknown epilogue %d", args.epilogue);
     }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // Tile width: 256 unless 128-wide tiles fill the persistent grid's waves
+    // much better. A 128 x 128 tile runs at ~0.76-0.81 of a 128 x 256 tile's
+    // rate (its QK-style MMA reads 128 B of shared memory per clock, the
+    // limit), so in practice this picks 128 only for a few dozen rows (the
+    // text rows of a block), where twice the CTAs cut the latency by ~15 %.
+    const long long mt = (args.M + kBM - 1) / kBM;
+    auto fill = [&](int bn) {
+        const long long t = mt * ((args.N + bn - 1) / bn);
+        const long long waves = (t + sms - 1) / sms;
+        return static_cast<double>(t) / static_cast<double>(waves * sms);
+    };
+    int bn = args.bn;
+    if (bn == 0) bn = (args.epilogue != GEMM_EPI_SWIGLU_F16 && args.N % 128 == 0 && fill(128) * 0.75 > fill(256)) ? 128 : 256;
+    if ((bn != 128 && bn != 256) || (bn == 128 && args.epilogue == GEMM_EPI_SWIGLU_F16))
+        return set_error(S2_INVALID_ARGUMENT, "gemm: tile width %d not available for this epilogue", bn);
     CUtensorMap ma, mb, mo[3];
     if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM) ||
-        !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK, kBN))
+        !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK, static_cast<uint32_t>(bn)))
         return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");
     // fp16 outputs: 32 x 32 store boxes, no swizzle (the unused maps repeat the first valid one)
     std::memset(mo, 0, sizeof(mo));
@@ -416,19 +447,24 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else {
         mo[0] = mo[1] = mo[2] = ma;  // not used by the channel-major epilogue
     }
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    static bool configured[2] = {false, false};
+    const int ci = bn == 256 ? 0 : 1;
+    if (!configured[ci]) {
+        const cudaError_t e =
+            bn == 256 ? cudaFuncSetAttribute(gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Tile<256>::kSmemBytes)
+                      : cudaFuncSetAttribute(gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Tile<128>::kSmemBytes);
         if (e != cudaSuccess)
             return set_error(S2_INFERENCE_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-        configured = true;
+        configured[ci] = true;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long tiles = 1LL * ((args.M + kBM - 1) / kBM) * ((args.N + kBN - 1) / kBN);
+    const long long tiles = mt * ((args.N + bn - 1) / bn);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+    if (bn == 256)
+        gemm_kernel<256><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+    else
+        gemm_kernel<128><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: launch failed: %s", cudaGetErrorString(e));
     return S2_OK;

@@ -61,6 +61,7 @@ struct GemmArgs {
     const float *resid2 = nullptr;
     float *y2 = nullptr;
     float out_scale = 1.f;
+    int bn = 0;                   // tile width 256 or 128 (0: chosen from the wave fill)
     int32_t *err = nullptr;       // device error word (bounded waits)
 };
 
