@@ -20,6 +20,9 @@
 
 namespace s2 {
 s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst);
+s2_status qk_norm_rope_range(void *stream, const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype, int heads,
+                             float eps, const float *gammas, const void *rope_table, const s2_row *rows, int n_rows,
+                             s2_mode mode, int src_lo, int src_hi, int do_text, void *q, void *k, void *v);
 }
 
 using s2::DeviceBuffer;
@@ -65,11 +68,106 @@ struct s2_attention_layer {
     cudaStream_t last_stream = nullptr;
     int last_launches = 0;
 
+    // Host-buffer forward pipeline: the windows grouped by their frame range
+    // (the t-slabs of the tiling), each with its own work list, so that the
+    // upload of slab s+1, the compute of slab s and the download of slab s-1
+    // overlap. Built with the plan (whole window set only).
+    struct Slab {
+        int t0 = 0, t1 = 0;      // frames [t0, t1)
+        int work_off = 0, n_work = 0;
+    };
+    std::vector<Slab> slabs;
+    bool slabs_valid = false;
+    DeviceBuffer d_slab_work;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    std::vector<cudaEvent_t> ev_in, ev_cmp;
+    cudaEvent_t ev_start = nullptr, ev_out = nullptr;
+
     ~s2_attention_layer()
     {
         DeviceGuard g(device);
-        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt})
+        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt, &d_slab_work})
             b->release();
+        for (cudaEvent_t e : ev_in) cudaEventDestroy(e);
+        for (cudaEvent_t e : ev_cmp) cudaEventDestroy(e);
+        if (ev_start) cudaEventDestroy(ev_start);
+        if (ev_out) cudaEventDestroy(ev_out);
+        if (s_in) cudaStreamDestroy(s_in);
+        if (s_out) cudaStreamDestroy(s_out);
+    }
+
+    // Slab work lists (window index << 16 | q-block, costliest window first
+    // within a slab, as s2_plan_work) for the current plan; false when the
+    // windows do not split into full-frame slabs (then the forward is serial).
+    bool build_slabs()
+    {
+        if (slabs_valid) return !slabs.empty();
+        slabs.clear();
+        slabs_valid = true;
+        if (!subset.empty() || local_rows) return false;
+        int count = 0;
+        if (s2_make_windows(T, H, W, shifted, wt, wh, ww, nullptr, 0, &count) != S2_OK || count != n_local) return false;
+        std::vector<s2_window> all(count);
+        s2_make_windows(T, H, W, shifted, wt, wh, ww, all.data(), count, &count);
+        std::vector<std::pair<int, int>> ranges;
+        for (const s2_window &w : all)
+            if (std::find(ranges.begin(), ranges.end(), std::make_pair(w.t0, w.t1)) == ranges.end())
+                ranges.emplace_back(w.t0, w.t1);
+        std::sort(ranges.begin(), ranges.end());
+        // the ranges must tile [0, T) and every slab's windows cover its frames entirely
+        for (size_t i = 0; i < ranges.size(); ++i)
+            if (ranges[i].first != (i == 0 ? 0 : ranges[i - 1].second)) return false;
+        if (ranges.empty() || ranges.back().second != T) return false;
+        std::vector<int32_t> h_work;
+        for (const auto &rg : ranges) {
+            std::vector<int> ids;
+            long long cover = 0;
+            for (int i = 0; i < count; ++i)
+                if (all[i].t0 == rg.first && all[i].t1 == rg.second) {
+                    ids.push_back(i);
+                    cover += 1LL * (all[i].h1 - all[i].h0) * (all[i].w1 - all[i].w0) * (all[i].t1 - all[i].t0);
+                }
+            if (cover != 1LL * (rg.second - rg.first) * H * W) return false;
+            std::stable_sort(ids.begin(), ids.end(), [&](int a, int b) {
+                return h_cu[a + 1] - h_cu[a] > h_cu[b + 1] - h_cu[b];
+            });
+            Slab sl;
+            sl.t0 = rg.first;
+            sl.t1 = rg.second;
+            sl.work_off = static_cast<int>(h_work.size());
+            for (int w : ids) {
+                const int seq = h_cu[w + 1] - h_cu[w];
+                for (int qb = 0; qb * s2::kCtaRows < seq; ++qb) h_work.push_back((w << 16) | qb);
+            }
+            sl.n_work = static_cast<int>(h_work.size()) - sl.work_off;
+            slabs.push_back(sl);
+        }
+        if (!d_slab_work.ensure(h_work.size() * sizeof(int32_t)) ||
+            cudaMemcpy(d_slab_work.ptr, h_work.data(), h_work.size() * sizeof(int32_t), cudaMemcpyHostToDevice) !=
+                cudaSuccess) {
+            slabs.clear();
+            return false;
+        }
+        return true;
+    }
+
+    bool ensure_pipeline_objects(size_t n)
+    {
+        if (!s_in && cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) != cudaSuccess) return false;
+        if (!s_out && cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) != cudaSuccess) return false;
+        if (!ev_start && cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) != cudaSuccess) return false;
+        if (!ev_out && cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming) != cudaSuccess) return false;
+        while (ev_in.size() < n) {
+            cudaEvent_t a = nullptr, b = nullptr;
+            if (cudaEventCreateWithFlags(&a, cudaEventDisableTiming) != cudaSuccess) return false;
+            if (cudaEventCreateWithFlags(&b, cudaEventDisableTiming) != cudaSuccess) {
+                cudaEventDestroy(a);
+                return false;
+            }
+            ev_in.push_back(a);
+            ev_cmp.push_back(b);
+        }
+        return true;
     }
 
     const float *gammas() const { return static_cast<const float *>(d_weights.ptr); }
@@ -79,6 +177,7 @@ struct s2_attention_layer {
     {
         if (plan_valid && plan_T == T && plan_H == H && plan_W == W && plan_Lt == Lt) return S2_OK;
         plan_valid = false;
+        slabs_valid = false;
         int count = 0;
         s2_status rc = s2_make_windows(T, H, W, shifted, wt, wh, ww, nullptr, 0, &count);
         if (rc != S2_OK) return rc;
@@ -301,6 +400,96 @@ extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *str
     return S2_OK;
 }
 
+// The host-buffer forward as a three-stream pipeline over the frame slabs:
+// upload (text rows, then slab by slab) on s_in; per slab, once its rows have
+// landed, the prologue for the slab's video rows (text rows with the first
+// slab) and the attention of the slab's windows on the caller's stream; the
+// download of the slab's output rows (a contiguous block of frames) on s_out.
+// The text mean follows the last slab. Same kernels, same arithmetic and the
+// same results as the serial path; only the copies overlap the compute.
+static s2_status forward_host_pipelined(s2_attention_layer *l, cudaStream_t st, const void *vid_qkv,
+                                        const void *txt_qkv, s2_dtype io_dtype, int L, int Lt, void *vid_out,
+                                        float *txt_out)
+{
+    const int dim = l->heads * S2_HEAD_DIM;
+    const size_t esz = io_dtype == S2_F32 ? 4 : 2;
+    const size_t row_in = static_cast<size_t>(3) * dim * esz;
+    const size_t row_out = static_cast<size_t>(dim) * (io_dtype == S2_F32 ? 4 : 2);
+    const int hw = l->H * l->W;
+    AttnScratch &sc = *l->sc;
+    const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;
+    const size_t txt_bytes = static_cast<size_t>(std::max(l->n_local, 1)) * std::max(Lt, 1) * dim * 2;
+    if (!sc.q.ensure(qkv_bytes) || !sc.k.ensure(qkv_bytes) || !sc.v.ensure(qkv_bytes) || !sc.txt_partial.ensure(txt_bytes))
+        return s2::set_error(S2_OUT_OF_MEMORY, "forward_host: workspace allocation failed");
+    if (!l->d_err.ptr && (!l->d_err.ensure(sizeof(int32_t)) || cudaMemset(l->d_err.ptr, 0, sizeof(int32_t)) != cudaSuccess))
+        return s2::set_error(S2_OUT_OF_MEMORY, "forward_host: error word allocation failed");
+    l->last_stream = st;
+    l->last_launches = 0;
+    auto *in = static_cast<char *>(l->d_in_vid.ptr);
+    const auto *hin = static_cast<const char *>(vid_qkv);
+    auto *hout = static_cast<char *>(vid_out);
+    const void *dout = io_dtype == S2_F32 ? l->d_out_vid32.ptr : l->d_out_vid.ptr;
+    bool ok = cudaEventRecord(l->ev_start, st) == cudaSuccess && cudaStreamWaitEvent(l->s_in, l->ev_start, 0) == cudaSuccess &&
+              cudaStreamWaitEvent(l->s_out, l->ev_start, 0) == cudaSuccess;
+    if (ok && Lt > 0)
+        ok = cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, static_cast<size_t>(Lt) * row_in, cudaMemcpyHostToDevice,
+                             l->s_in) == cudaSuccess;
+    for (size_t i = 0; ok && i < l->slabs.size(); ++i) {
+        const auto &sl = l->slabs[i];
+        const size_t r0 = static_cast<size_t>(sl.t0) * hw, nr = static_cast<size_t>(sl.t1 - sl.t0) * hw;
+        ok = cudaMemcpyAsync(in + r0 * row_in, hin + r0 * row_in, nr * row_in, cudaMemcpyHostToDevice, l->s_in) ==
+                 cudaSuccess &&
+             cudaEventRecord(l->ev_in[i], l->s_in) == cudaSuccess;
+    }
+    if (!ok) return s2::set_error(S2_INFERENCE_FAILED, "forward_host: upload failed");
+    for (size_t i = 0; i < l->slabs.size(); ++i) {
+        const auto &sl = l->slabs[i];
+        const size_t r0 = static_cast<size_t>(sl.t0) * hw, nr = static_cast<size_t>(sl.t1 - sl.t0) * hw;
+        if (cudaStreamWaitEvent(st, l->ev_in[i], 0) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream wait failed");
+        s2_status rc = s2::qk_norm_rope_range(st, in, l->d_in_txt.ptr, io_dtype, l->heads, l->eps, l->gammas(),
+                                              l->d_rope.ptr, static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows,
+                                              l->mode, static_cast<int>(r0), static_cast<int>(r0 + nr), i == 0 ? 1 : 0,
+                                              sc.q.ptr, sc.k.ptr, sc.v.ptr);
+        if (rc != S2_OK) return rc;
+        rc = s2_window_attention(st, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
+                                 static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
+                                 static_cast<const s2_row *>(l->d_rows.ptr),
+                                 static_cast<const int32_t *>(l->d_slab_work.ptr) + sl.work_off, sl.n_work,
+                                 l->d_out_vid.ptr, sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
+        if (rc != S2_OK) return rc;
+        l->last_launches += 2;
+        if (io_dtype == S2_F32) {
+            rc = s2::to_f32(st, l->mode, static_cast<const char *>(l->d_out_vid.ptr) + r0 * dim * 2,
+                            static_cast<long long>(nr) * dim, static_cast<float *>(l->d_out_vid32.ptr) + r0 * dim);
+            if (rc != S2_OK) return rc;
+            l->last_launches++;
+        }
+        if (cudaEventRecord(l->ev_cmp[i], st) != cudaSuccess || cudaStreamWaitEvent(l->s_out, l->ev_cmp[i], 0) != cudaSuccess ||
+            cudaMemcpyAsync(hout + r0 * row_out, static_cast<const char *>(dout) + r0 * row_out, nr * row_out,
+                            cudaMemcpyDeviceToHost, l->s_out) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "forward_host: download failed");
+    }
+    if (Lt > 0) {
+        const s2_status rc = s2_text_window_sum(st, l->mode, sc.txt_partial.ptr, l->n_local, Lt, dim,
+                                                1.f / static_cast<float>(l->n_total_windows), 0,
+                                                static_cast<float *>(l->d_out_txt.ptr));
+        if (rc != S2_OK) return rc;
+        l->last_launches++;
+        if (cudaMemcpyAsync(txt_out, l->d_out_txt.ptr, static_cast<size_t>(Lt) * dim * 4, cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "forward_host: text download failed");
+    }
+    if (cudaEventRecord(l->ev_out, l->s_out) != cudaSuccess || cudaStreamWaitEvent(st, l->ev_out, 0) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream join failed");
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream failed: %s", cudaGetErrorString(e));
+    (void)L;
+    int code = 0;
+    return s2_attention_layer_device_error(l, &code);
+}
+
 extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void *stream, const void *vid_qkv,
                                                      const void *txt_qkv, s2_dtype io_dtype, int L, int Lt,
                                                      const int32_t *vid_shape, void *vid_out, float *txt_out)
@@ -326,6 +515,12 @@ extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void
         !l->d_out_vid.ensure(out_vid16) || !l->d_out_txt.ensure(std::max<size_t>(static_cast<size_t>(Lt) * dim * 4, 16)) ||
         (io_dtype == S2_F32 && !l->d_out_vid32.ensure(static_cast<size_t>(L) * dim * 4)))
         return s2::set_error(S2_OUT_OF_MEMORY, "forward_host: staging allocation failed");
+    if (!l->loaded || !l->shape_valid)
+        return s2::set_error(S2_NOT_LOADED, "attention layer: weights or runtime shape not set");
+    rc = l->build_plan(Lt, st);
+    if (rc != S2_OK) return rc;
+    if (l->build_slabs() && l->ensure_pipeline_objects(l->slabs.size()))
+        return forward_host_pipelined(l, st, vid_qkv, txt_qkv, io_dtype, L, Lt, vid_out, txt_out);
     if (cudaMemcpyAsync(l->d_in_vid.ptr, vid_qkv, in_vid, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (Lt > 0 && cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, in_txt, cudaMemcpyHostToDevice, st) != cudaSuccess))
         return s2::set_error(S2_INFERENCE_FAILED, "forward_host: H2D copy failed");

@@ -101,9 +101,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
                                                            const float *__restrict__ gammas,
                                                            const float2 *__restrict__ table,
                                                            const s2_row *__restrict__ rows, int n_rows,
+                                                           int src_lo, int src_hi, int do_text,
                                                            uint4 *__restrict__ q, uint4 *__restrict__ k,
                                                            uint4 *__restrict__ v)
 {
+    // Only video rows whose source token is in [src_lo, src_hi) (and the text
+    // rows when do_text) are processed; the others neither load nor store (a
+    // host-buffer forward runs one pass per frame slab as its rows arrive).
     // 8 lanes per (row, head); lane `sub` owns dims [64c + 8 sub, 64c + 8 sub + 8) for c = 0, 1.
     const int dim = heads * kHD;
     const int sub = threadIdx.x & 7;
@@ -118,6 +122,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
         const int head = static_cast<int>(prc - 1LL * row * heads);
         const s2_row rd = rows[row];
         const bool text = rd.src < 0;
+        const bool use = active && (text ? do_text != 0 : (rd.src >= src_lo && rd.src < src_hi));
         const TIn *src = text ? txt_qkv + static_cast<size_t>(-rd.src - 1) * 3 * dim
                               : vid_qkv + static_cast<size_t>(rd.src) * 3 * dim;
         src += head * kHD + sub * 8;
@@ -127,9 +132,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
         float xq[2][8], xk[2][8], xv[2][8];
 #pragma unroll
         for (int c = 0; c < 2; c++) {
-            Load8<TIn>::run(src + 64 * c, xq[c]);
-            Load8<TIn>::run(src + dim + 64 * c, xk[c]);
-            Load8<TIn>::run(src + 2 * dim + 64 * c, xv[c]);
+            if (use) {
+                Load8<TIn>::run(src + 64 * c, xq[c]);
+                Load8<TIn>::run(src + dim + 64 * c, xk[c]);
+                Load8<TIn>::run(src + 2 * dim + 64 * c, xv[c]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) xq[c][i] = xk[c][i] = xv[c][i] = 1.f;
+            }
         }
         double sq = 0.0, sk = 0.0;
 #pragma unroll
@@ -170,7 +180,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
                 }
             }
         }
-        if (!active) continue;
+        if (!use) continue;
         const size_t o = (static_cast<size_t>(head) * n_rows + row) * (kHD / 8) + sub;
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -243,9 +253,26 @@ extern "C" s2_status s2_rope_table(void *stream, const float *freqs21, int max_p
     return S2_OK;
 }
 
+namespace s2 {
+
+s2_status qk_norm_rope_range(void *stream, const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype, int heads,
+                             float eps, const float *gammas, const void *rope_table, const s2_row *rows, int n_rows,
+                             s2_mode mode, int src_lo, int src_hi, int do_text, void *q, void *k, void *v);
+
+}  // namespace s2
+
 extern "C" s2_status s2_qk_norm_rope(void *stream, const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype,
                                      int heads, float eps, const float *gammas, const void *rope_table,
                                      const s2_row *rows, int n_rows, s2_mode mode, void *q, void *k, void *v)
+{
+    return s2::qk_norm_rope_range(stream, vid_qkv, txt_qkv, in_dtype, heads, eps, gammas, rope_table, rows, n_rows,
+                                  mode, 0, 0x7fffffff, 1, q, k, v);
+}
+
+s2_status s2::qk_norm_rope_range(void *stream, const void *vid_qkv, const void *txt_qkv, s2_dtype in_dtype,
+                                 int heads, float eps, const float *gammas, const void *rope_table,
+                                 const s2_row *rows, int n_rows, s2_mode mode, int src_lo, int src_hi, int do_text,
+                                 void *q, void *k, void *v)
 {
     if (heads <= 0 || heads > 64 || n_rows <= 0 || !vid_qkv || !gammas || !rows || !rope_table || !q || !k || !v)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_qk_norm_rope: invalid arguments");
@@ -279,7 +306,7 @@ extern "C" s2_status s2_qk_norm_rope(void *stream, const void *vid_qkv, const vo
 #define S2_LAUNCH(TIN)                                                                                              \
     qk_norm_rope_kernel<TIN><<<grid, 256, 0, st>>>(static_cast<const TIN *>(vid_qkv),                               \
                                                    static_cast<const TIN *>(txt_qkv), heads, eps, gammas, T, rows, \
-                                                   n_rows, Q, K, V)
+                                                   n_rows, src_lo, src_hi, do_text, Q, K, V)
     switch (in_dtype) {
     case S2_F32: S2_LAUNCH(float); break;
     case S2_F16: S2_LAUNCH(__half); break;

@@ -230,6 +230,35 @@ def test_host_buffer_forward_matches_device(torch_cuda):
     np.testing.assert_allclose(hv16.astype(np.float32), dv, atol=8e-3)
 
 
+@pytest.mark.parametrize("grid,shifted", [((6, 24, 40), 0), ((6, 24, 40), 1), ((5, 16, 30), 1)])
+@pytest.mark.parametrize("io", ["f32", "f16"])
+def test_pipelined_host_forward_matches_device(torch_cuda, grid, shifted, io):
+    """The host-buffer forward overlaps uploads, compute and downloads slab by
+    slab of frames; its outputs must equal the device-buffer forward's exactly,
+    and a window-subset layer (serial host path) must agree too."""
+    torch = torch_cuda
+    vid, txt, gam, fr = synth.layer_inputs(grid, heads=4, seed=9)
+    mode = s2b200.MODE_F16 if io == "f16" else s2b200.MODE_BF16_REF
+    io_dtype = s2b200.S2_F16 if io == "f16" else s2b200.S2_F32
+    cast = (lambda a: a.astype(np.float16)) if io == "f16" else (lambda a: a)
+    dev_layer = make_layer(4, gam, fr, grid, shifted, mode=mode)
+    dvo, dto = dev_layer.forward(torch.from_numpy(cast(vid)).cuda(), torch.from_numpy(cast(txt)).cuda())
+    torch.cuda.synchronize()
+    dvo, dto = dvo.float().cpu().numpy(), dto.cpu().numpy()
+    layer = make_layer(4, gam, fr, grid, shifted, mode=mode)
+    for _ in range(2):  # the second call reuses the pipeline's streams and events
+        hv, ht = layer.forward_host(cast(vid), cast(txt), np.array(grid, np.int32), io_dtype=io_dtype)
+        assert np.array_equal(hv.astype(np.float32), dvo) and np.array_equal(ht, dto)
+    n = len(s2b200.make_windows(*grid, shifted))
+    acc_v = np.zeros_like(dvo)
+    for r in range(2):
+        sub = make_layer(4, gam, fr, grid, shifted, mode=mode)
+        sub.set_window_subset(np.arange(r, n, 2))
+        sv, _ = sub.forward_host(cast(vid), cast(txt), np.array(grid, np.int32), io_dtype=io_dtype)
+        acc_v += sv.astype(np.float32)
+    assert np.array_equal(acc_v, dvo)
+
+
 def test_shape_mismatch_returns_invalid_argument(torch_cuda):
     torch = torch_cuda
     grid = (2, 4, 4)
