@@ -95,7 +95,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <typename TIn>
+template <typename TIn, bool kRange>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict__ vid_qkv,
                                                            const TIn *__restrict__ txt_qkv, int heads, float eps,
                                                            const float *__restrict__ gammas,
@@ -105,9 +105,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
                                                            uint4 *__restrict__ q, uint4 *__restrict__ k,
                                                            uint4 *__restrict__ v)
 {
-    // Only video rows whose source token is in [src_lo, src_hi) (and the text
-    // rows when do_text) are processed; the others neither load nor store (a
-    // host-buffer forward runs one pass per frame slab as its rows arrive).
+    // kRange: only video rows whose source token is in [src_lo, src_hi) (and the
+    // text rows when do_text) are processed; the others neither load nor store
+    // (a host-buffer forward runs one pass per frame slab as its rows arrive).
+    // Without kRange the loads stay unconditional, as the fastest schedule.
     // 8 lanes per (row, head); lane `sub` owns dims [64c + 8 sub, 64c + 8 sub + 8) for c = 0, 1.
     const int dim = heads * kHD;
     const int sub = threadIdx.x & 7;
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
         const int head = static_cast<int>(prc - 1LL * row * heads);
         const s2_row rd = rows[row];
         const bool text = rd.src < 0;
-        const bool use = active && (text ? do_text != 0 : (rd.src >= src_lo && rd.src < src_hi));
+        const bool use = !kRange || (active && (text ? do_text != 0 : (rd.src >= src_lo && rd.src < src_hi)));
         const TIn *src = text ? txt_qkv + static_cast<size_t>(-rd.src - 1) * 3 * dim
                               : vid_qkv + static_cast<size_t>(rd.src) * 3 * dim;
         src += head * kHD + sub * 8;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
         float xq[2][8], xk[2][8], xv[2][8];
 #pragma unroll
         for (int c = 0; c < 2; c++) {
-            if (use) {
+            if (!kRange || use) {
                 Load8<TIn>::run(src + 64 * c, xq[c]);
                 Load8<TIn>::run(src + dim + 64 * c, xk[c]);
                 Load8<TIn>::run(src + 2 * dim + 64 * c, xv[c]);
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const TIn *__restrict
                 }
             }
         }
-        if (!use) continue;
+        if (!active || !use) continue;
         const size_t o = (static_cast<size_t>(head) * n_rows + row) * (kHD / 8) + sub;
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -281,6 +282,7 @@ s2_status s2::qk_norm_rope_range(void *stream, const void *vid_qkv, const void *
     if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
         return s2::set_error(S2_UNSUPPORTED, "s2_qk_norm_rope: unknown mode %d", (int)mode);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool ranged = !(src_lo <= 0 && src_hi == 0x7fffffff && do_text);
     const long long pairs = 1LL * n_rows * heads;
     const long long want = (pairs + 31) / 32;
     // exactly the resident blocks: every block grid-strides to the end, so no
@@ -290,9 +292,9 @@ s2_status s2::qk_norm_rope_range(void *stream, const void *vid_qkv, const void *
     int per_sm = resident_per_sm[di];
     if (per_sm <= 0) {
         switch (in_dtype) {
-        case S2_F32: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<float>, 256, 0); break;
-        case S2_F16: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__half>, 256, 0); break;
-        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__nv_bfloat16>, 256, 0); break;
+        case S2_F32: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<float, false>, 256, 0); break;
+        case S2_F16: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__half, false>, 256, 0); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qk_norm_rope_kernel<__nv_bfloat16, false>, 256, 0); break;
         }
         if (per_sm <= 0) per_sm = 1;
         resident_per_sm[di] = per_sm;
@@ -304,9 +306,14 @@ s2_status s2::qk_norm_rope_range(void *stream, const void *vid_qkv, const void *
     auto *V = static_cast<uint4 *>(v);
     const auto *T = static_cast<const float2 *>(rope_table);
 #define S2_LAUNCH(TIN)                                                                                              \
-    qk_norm_rope_kernel<TIN><<<grid, 256, 0, st>>>(static_cast<const TIN *>(vid_qkv),                               \
-                                                   static_cast<const TIN *>(txt_qkv), heads, eps, gammas, T, rows, \
-                                                   n_rows, src_lo, src_hi, do_text, Q, K, V)
+    if (ranged)                                                                                                     \
+        qk_norm_rope_kernel<TIN, true><<<grid, 256, 0, st>>>(static_cast<const TIN *>(vid_qkv),                     \
+                                                             static_cast<const TIN *>(txt_qkv), heads, eps, gammas, \
+                                                             T, rows, n_rows, src_lo, src_hi, do_text, Q, K, V);    \
+    else                                                                                                            \
+        qk_norm_rope_kernel<TIN, false><<<grid, 256, 0, st>>>(static_cast<const TIN *>(vid_qkv),                    \
+                                                              static_cast<const TIN *>(txt_qkv), heads, eps,        \
+                                                              gammas, T, rows, n_rows, 0, 0, 1, Q, K, V)
     switch (in_dtype) {
     case S2_F32: S2_LAUNCH(float); break;
     case S2_F16: S2_LAUNCH(__half); break;
