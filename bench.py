@@ -612,9 +612,10 @@ def run_vae(args, torch, s2b200, synth, dev):
     core_ms = e0.elapsed_time(e1) / steps
     af = synth.vae_attention_flops(shape)
     hx = torch.from_numpy(x).pin_memory().numpy()
-    lay.forward_host(hx)
+    hy = torch.empty(x.shape, dtype=torch.float32).pin_memory().numpy()
+    lay.forward_host(hx, y=hy)
     t0 = time.perf_counter()
-    lay.forward_host(hx)
+    lay.forward_host(hx, y=hy)
     e2e_ms = (time.perf_counter() - t0) * 1e3
     lay.close()
     return {"workload": "VAE mid-block attention, C 512, 6 frames x 90x160 = 14,400 tokens per frame",

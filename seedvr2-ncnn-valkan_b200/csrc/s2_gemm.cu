@@ -37,14 +37,19 @@ constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
 constexpr uint32_t kStageChunk = 32 * 32 * 4;  // epilogue staging chunk, sized for fp32 (fp16 uses the first half)
 constexpr int kThreads = 192;
 
-// Tile shape: 128 x BN with BN = 256 (the default) or 128 (twice the tiles,
-// for GEMMs too small to fill the grid with 256-wide tiles).
-template <int BN>
+// Tile shape: 128 x BN per CTA with BN = 256 (the default) or 128 (twice the
+// tiles, for GEMMs too small to fill the grid with 256-wide tiles); with kPair a
+// cluster of two CTAs computes a 256 x 256 tile with tcgen05 cta_group::2 MMAs
+// (each CTA holds its 128 rows of A, half of the tile's B rows, and its 128 rows
+// of the accumulator), halving the B bytes each CTA loads and reads per FLOP.
+template <int BN, bool kPair = false>
 struct Tile {
     static constexpr int kBN = BN;
-    static constexpr int kStages = BN == 256 ? 4 : 6;
-    static constexpr uint32_t kBBytes = BN * kBK * 2;
+    static constexpr int kBRows = kPair ? BN / 2 : BN;  // B rows this CTA loads per slice
+    static constexpr int kTileRows = kPair ? 2 * kBM : kBM;
+    static constexpr uint32_t kBBytes = kBRows * kBK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = kStageBytes > 32768 ? 4 : 6;
     static constexpr uint32_t kOffStage = kStages * kStageBytes;  // epilogue staging: 4 warps x 2 chunks
     static constexpr uint32_t kOffBar = kOffStage + 4 * 2 * kStageChunk;
     static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/flags + alignment slack
@@ -78,16 +83,20 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int BN>
+template <int BN, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1,
                 const __grid_constant__ CUtensorMap tmO2, const s2::GemmArgs a)
 {
-    using T = Tile<BN>;
-    constexpr int kBN = T::kBN, kStages = T::kStages;
+    using T = Tile<BN, kPair>;
+    constexpr int kBN = T::kBN, kStages = T::kStages, kTileRows = T::kTileRows;
     constexpr uint32_t kStageBytes = T::kStageBytes, kOffStage = T::kOffStage, kOffBar = T::kOffBar;
     constexpr uint32_t kTmemCols = T::kTmemCols;
+    // CTA pair: rank 0 issues the MMAs; tiles are distributed over clusters
+    const uint32_t rank = kPair ? cluster_rank() : 0u;
+    const int unit = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int n_units = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -99,20 +108,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = (a.N + kBN - 1) / kBN;
-    const int n_tiles = ((a.M + kBM - 1) / kBM) * n_blocks;
+    const int n_tiles = ((a.M + kTileRows - 1) / kTileRows) * n_blocks;
     const int n_k = a.K / kBK;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), (i >= B_ACCE && i < B_ACCE + 2) ? 128u : 1u);
+        // a pair's accumulator-empty barrier (rank 0's) counts both CTAs' epilogue threads
+        for (int i = 0; i < B_COUNT; ++i)
+            mbar_init(BAR(i), (i >= B_ACCE && i < B_ACCE + 2) ? (kPair ? 256u : 128u) : 1u);
         *abort = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -122,28 +139,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmB);
             uint32_t p = 0;  // stage uses issued
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
-                const int m0 = (t / n_blocks) * kBM, n0 = (t % n_blocks) * kBN;
+            for (int t = unit; ok && t < n_tiles; t += n_units) {
+                const int m0 = (t / n_blocks) * kTileRows + static_cast<int>(rank) * kBM;
+                const int n0 = (t % n_blocks) * kBN + static_cast<int>(rank) * T::kBRows;
                 for (int kc = 0; kc < n_k; ++kc, ++p) {
                     const uint32_t s = p % kStages, u = p / kStages;
                     if (!(ok = mbar_wait(BAR(B_EMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_EMPTY))) break;
                     const uint32_t sa = base + s * kStageBytes;
-                    mbar_arrive_expect_tx(BAR(B_FULL + s), kStageBytes);
-                    tma_load_2d(sa, &tmA, BAR(B_FULL + s), kc * kBK, m0);
-                    tma_load_2d(sa + kABytes, &tmB, BAR(B_FULL + s), kc * kBK, n0);
+                    if constexpr (kPair) {
+                        // both CTAs' slices are counted on rank 0's full barrier
+                        if (rank == 0) mbar_arrive_expect_tx(BAR(B_FULL + s), 2 * kStageBytes);
+                        const uint32_t fb = cluster_map(BAR(B_FULL + s), 0);
+                        tma_load_2d_pair(sa, &tmA, fb, kc * kBK, m0);
+                        tma_load_2d_pair(sa + kABytes, &tmB, fb, kc * kBK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(BAR(B_FULL + s), kStageBytes);
+                        tma_load_2d(sa, &tmA, BAR(B_FULL + s), kc * kBK, m0);
+                        tma_load_2d(sa + kABytes, &tmB, BAR(B_FULL + s), kc * kBK, n0);
+                    }
                 }
             }
-            // no copy may still be landing when the CTA exits
+            // No copy may still be landing when the CTA exits. A pair's loads complete on
+            // rank 0's barriers, which rank 0 drains; rank 1 waits for its last stages to be
+            // released by rank 0's MMAs (each release follows the loads that filled it).
             for (uint32_t s = 0; s < kStages; ++s)
-                if (p > s) wait_drain(BAR(B_FULL + s), ((p - 1 - s) / kStages) & 1u, a.err);
+                if (p > s) {
+                    if (!kPair || rank == 0)
+                        wait_drain(BAR(B_FULL + s), ((p - 1 - s) / kStages) & 1u, a.err);
+                    else
+                        wait_drain(BAR(B_EMPTY + s), ((p - 1 - s) / kStages) & 1u, a.err);
+                }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16(0u, kBN, 0);
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = idesc_f16(0u, kBN, 0, kPair ? 256u : 128u);
             const uint64_t d0 = smem_desc_sw128(base, 16, 1024);
+            // a pair's commits arrive on the barrier in each CTA
+            auto commit = [&](uint32_t bar) {
+                if constexpr (kPair) {
+                    mma_commit_pair(cluster_map(bar, 0));
+                    mma_commit_pair(cluster_map(bar, 1));
+                } else {
+                    mma_commit(bar);
+                }
+            };
             uint32_t p = 0, lt = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
+            for (int t = unit; ok && t < n_tiles; t += n_units, ++lt) {
                 const uint32_t b = lt & 1u;
                 if (!(ok = mbar_wait(BAR(B_ACCE + b), ((lt >> 1) & 1u) ^ 1u, abort, a.err, E_ACCE))) break;
                 tc_fence_after();
@@ -153,13 +195,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint64_t da = d0 + static_cast<uint64_t>((s * kStageBytes) >> 4);
                     const uint64_t db = da + static_cast<uint64_t>(kABytes >> 4);
-                    mma_chunk_ss_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
-                    mma_commit(BAR(B_EMPTY + s));
+                    if constexpr (kPair)
+                        mma_chunk_pair_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
+                    else
+                        mma_chunk_ss_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
+                    commit(BAR(B_EMPTY + s));
                 }
                 if (!ok) break;
-                mma_commit(BAR(B_ACCF + b));
+                commit(BAR(B_ACCF + b));
             }
-            mma_commit(BAR(B_DRAIN));
+            if constexpr (kPair)
+                mma_commit_pair(cluster_map(BAR(B_DRAIN), 0));
+            else
+                mma_commit(BAR(B_DRAIN));
             wait_drain(BAR(B_DRAIN), 0, a.err);
         }
     } else {
@@ -202,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         uint32_t lt = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++lt) {
-            const int m0 = (t / n_blocks) * kBM, n0 = (t % n_blocks) * kBN;
+        for (int t = unit; ok && t < n_tiles; t += n_units, ++lt) {
+            const int m0 = (t / n_blocks) * kTileRows + static_cast<int>(rank) * kBM, n0 = (t % n_blocks) * kBN;
             const uint32_t b = lt & 1u;
             ok = mbar_wait(BAR(B_ACCF + b), (lt >> 1) & 1u, abort, a.err, E_ACCF);
             ok = __all_sync(0xffffffffu, ok);
@@ -305,7 +353,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(BAR(B_ACCE + b));
+            if constexpr (kPair) {
+                if (rank == 0)
+                    mbar_arrive(BAR(B_ACCE + b));
+                else
+                    mbar_arrive_remote(cluster_map(BAR(B_ACCE + b), 0));  // rank 0's barrier counts both CTAs
+            } else {
+                mbar_arrive(BAR(B_ACCE + b));
+            }
         }
         if (lane == 0) bulk_wait_group_all();  // every bulk store of this warp has landed
         __syncwarp();
@@ -313,9 +368,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    // the pair's MMAs write both CTAs' TMEM and its epilogue signals rank 0: neither CTA
+    // releases TMEM or exits before the other is done
+    if constexpr (kPair) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (kPair)
+            tmem_dealloc_pair(tmem, kTmemCols);
+        else
+            tmem_dealloc(tmem, kTmemCols);
     }
 #undef BAR
 }
@@ -424,9 +485,19 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     if (bn == 0) bn = (args.epilogue != GEMM_EPI_SWIGLU_F16 && args.N % 128 == 0 && fill(128) * 0.75 > fill(256)) ? 128 : 256;
     if ((bn != 128 && bn != 256) || (bn == 128 && args.epilogue == GEMM_EPI_SWIGLU_F16))
         return set_error(S2_INVALID_ARGUMENT, "gemm: tile width %d not available for this epilogue", bn);
+    // CTA pairs (256 x 256 tiles over two SMs, a third fewer operand bytes per
+    // FLOP) for 256-wide tiles: measured 2-8 % faster on the DiT block GEMMs at
+    // 10-20 k rows (SwiGLU +7.6 %), but slower for short K (the VAE projections,
+    // K = 512: -6 %) and a few thousand rows (-6 % on a 2.7 k-row QKV), so only
+    // for M >= 4096 and K >= 1024. Needs N a multiple of 256.
+    bool pair = args.pair > 0 ||
+                (args.pair < 0 && bn == 256 && args.M >= 4096 && args.K >= 1024 && args.N % 256 == 0 && sms >= 2);
+    if (pair && (bn != 256 || args.N % 256 != 0 || sms < 2))
+        return set_error(S2_INVALID_ARGUMENT, "gemm: CTA pairs need 256-wide tiles and N %% 256 == 0 (N %d)", args.N);
     CUtensorMap ma, mb, mo[3];
     if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM) ||
-        !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK, static_cast<uint32_t>(bn)))
+        !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK,
+                     static_cast<uint32_t>(pair ? bn / 2 : bn)))
         return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");
     // fp16 outputs: 32 x 32 store boxes, no swizzle (the unused maps repeat the first valid one)
     std::memset(mo, 0, sizeof(mo));
@@ -447,24 +518,46 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else {
         mo[0] = mo[1] = mo[2] = ma;  // not used by the channel-major epilogue
     }
-    static bool configured[2] = {false, false};
-    const int ci = bn == 256 ? 0 : 1;
+    static bool configured[3] = {false, false, false};
+    const int ci = pair ? 2 : (bn == 256 ? 0 : 1);
     if (!configured[ci]) {
         const cudaError_t e =
-            bn == 256 ? cudaFuncSetAttribute(gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            ci == 2   ? cudaFuncSetAttribute(gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Tile<256, true>::kSmemBytes)
+            : ci == 0 ? cudaFuncSetAttribute(gemm_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Tile<256>::kSmemBytes)
-                      : cudaFuncSetAttribute(gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                      : cudaFuncSetAttribute(gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Tile<128>::kSmemBytes);
         if (e != cudaSuccess)
             return set_error(S2_INFERENCE_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
         configured[ci] = true;
     }
-    const long long tiles = mt * ((args.N + bn - 1) / bn);
-    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    if (bn == 256)
-        gemm_kernel<256><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
-    else
-        gemm_kernel<128><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+    if (pair) {
+        const long long tiles = ((args.M + 255) / 256) * (args.N / 256);
+        const long long pairs = tiles < sms / 2 ? tiles : sms / 2;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Tile<256, true>::kSmemBytes;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_kernel<256, true>, ma, mb, mo[0], mo[1], mo[2], args);
+        if (le != cudaSuccess)
+            return set_error(S2_INFERENCE_FAILED, "gemm: pair launch failed: %s", cudaGetErrorString(le));
+    } else {
+        const long long tiles = mt * ((args.N + bn - 1) / bn);
+        const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+        if (bn == 256)
+            gemm_kernel<256, false><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+        else
+            gemm_kernel<128, false><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: launch failed: %s", cudaGetErrorString(e));
     return S2_OK;

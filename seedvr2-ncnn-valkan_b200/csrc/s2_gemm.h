@@ -62,6 +62,7 @@ struct GemmArgs {
     float *y2 = nullptr;
     float out_scale = 1.f;
     int bn = 0;                   // tile width 256 or 128 (0: chosen from the wave fill)
+    int pair = -1;                // CTA pairs (256 x 256 tiles on two SMs): 1 on, 0 off, -1 chosen by shape
     int32_t *err = nullptr;       // device error word (bounded waits)
 };
 

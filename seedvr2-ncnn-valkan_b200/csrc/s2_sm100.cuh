@@ -145,6 +145,91 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) --------------------------
+// The pair's MMAs are issued by CTA rank 0 and cover both CTAs' shared-memory
+// operands and TMEM accumulators. No load here uses cluster multicast.
+
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// arrive on an mbarrier of another CTA of the cluster
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair (the leader's)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap, uint32_t cluster_bar, int c0, int c1)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// commit of the pair's MMAs to one mbarrier (any CTA of the pair, cluster address)
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+
+// One K=64 slice of a pair tile D[256][N] (+)= A[256][64] B[N][64]^T: four K=16
+// MMAs; A rows 0-127 / 128-255 and B rows 0-N/2-1 / N/2-N-1 live at the same
+// shared-memory offsets of CTA rank 0 / 1.
+__device__ __forceinline__ void mma_chunk_pair_k64(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t acc_first)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b64 a, b;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %3, t;\n\t"
+        "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -270,13 +355,13 @@ __device__ __forceinline__ void mma_commit(uint32_t bar)
 
 // Instruction descriptor, kind::f16: D f32, A/B bf16 (fmt 1) or f16 (fmt 0),
 // M = 128, N = n; b_mn_major selects an MN-major B operand.
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t n, uint32_t b_mn_major)
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t n, uint32_t b_mn_major, uint32_t m = 128u)
 {
     return (1u << 4)                 // D format f32
            | (fmt << 7) | (fmt << 10) // A, B formats
            | (b_mn_major << 16)       // B major
            | ((n >> 3) << 17)         // N >> 3
-           | ((128u >> 4) << 24);     // M >> 4
+           | ((m >> 4) << 24);        // M >> 4 (128, or 256 for a CTA pair)
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.

@@ -833,11 +833,15 @@ class DynamicFramewiseSpatialAttention:
                "s2_vae_attention_forward")
         return y
 
-    def forward_host(self, x: np.ndarray, stream=None) -> np.ndarray:
-        """x: host fp32 [C, T, H, W] -> y (copies in and out, synchronises)."""
+    def forward_host(self, x: np.ndarray, stream=None, y: np.ndarray | None = None) -> np.ndarray:
+        """x: host fp32 [C, T, H, W] -> y (copies in and out, synchronises);
+        y may be given (e.g. pinned host memory)."""
         x = np.ascontiguousarray(x, np.float32)
         C, T, H, W = x.shape
-        y = np.empty_like(x)
+        if y is None:
+            y = np.empty_like(x)
+        elif y.shape != x.shape or y.dtype != np.float32 or not y.flags["C_CONTIGUOUS"]:
+            raise ValueError("y must be a contiguous fp32 array of x's shape")
         _check(lib().s2_vae_attention_forward_host(self.handle, _stream_ptr(stream) if stream is not None else None,
                                                    ctypes.c_void_p(x.ctypes.data), T, H, W, T * H * W,
                                                    ctypes.c_void_p(y.ctypes.data)), "s2_vae_attention_forward_host")
