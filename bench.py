@@ -204,6 +204,43 @@ def cpu_reference_sample(grid, text_len, heads_total, seed=666):
                       f"{flops / 1e9:.1f} GFLOP algorithmic"}
 
 
+def cpu_euler_estimate(seed=666):
+    """The reference's own CPU code for the config-2 Euler step, estimated from
+    two timed blocks: oracle/_ref's SeedVR2DiTBlock::forward (the reference's
+    source compiled against the ncnn shim, whose InnerProduct is this
+    repository's fp32 GEMM, not ncnn's) for one plain and one shifted block on
+    all host cores, times 16 each (the step's 16 plain + 16 shifted blocks; the
+    DiT heads are < 1 % and left out). The reference's attention() alone on
+    the same two layers is timed beside it, so that the part of the estimate
+    that is the reference's own arithmetic is stated separately."""
+    import oracle
+    from s2b200 import synth
+    ref = oracle.ref()
+    if ref is None:
+        return {"unavailable": "oracle/_ref (the reference build) is not present"}
+    grid, dim, heads, mlp = synth.GRIDS["cfg2"], 2560, 20, 6912
+    cores = os.cpu_count() or 1
+    vid, txt, emb = synth.block_activations(grid, dim, seed=seed)
+    qv, qt, gam, fr = synth.layer_inputs(grid, heads=heads, seed=seed)
+    out = {"cores": cores, "kind": "reference", "extrapolated": True}
+    for name, idx, shifted in (("plain", 0, 0), ("shifted", 1, 1)):
+        w = synth.block_weights(dim, heads, mlp, shared=False, seed=100 + idx)
+        params = dict(block_index=idx, shared=False, last=False, shifted=bool(shifted), dim=dim, heads=heads,
+                      head_dim=128, mlp_hidden=mlp, eps=1e-5)
+        t0 = time.perf_counter()
+        ref.block_forward(params, w, vid, txt, emb, grid, threads=cores)
+        out[f"block_{name}_s"] = time.perf_counter() - t0
+        del w
+        t0 = time.perf_counter()
+        ref.attention(qv, qt, grid, heads, list(gam), fr, shifted, threads=cores)
+        out[f"attention_{name}_s"] = time.perf_counter() - t0
+    out["ms_per_step"] = 16e3 * (out["block_plain_s"] + out["block_shifted_s"])
+    out["attention_ms_per_step"] = 16e3 * (out["attention_plain_s"] + out["attention_shifted_s"])
+    out["sample"] = ("blocks 0 (plain) and 1 (shifted) of the config-2 step through the reference's block code, "
+                     f"{cores} threads; step = 16 x (plain + shifted)")
+    return out
+
+
 def run_reference_arm(args, rank):
     if rank != 0:
         return
@@ -569,6 +606,7 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
     m.close()
     if comm is not None:
         comm.close()
+    cpu_ref = cpu_euler_estimate() if (args.cpu_euler and rank == 0 and world == 1) else None
     return {"workload": "DiT Euler step at 720p: latent 33x6x90x160 -> 21,600 tokens, 58 text tokens x 5120, "
                         "32 blocks (dim 2560, 20 heads, SwiGLU 6912), t = 1000, one step, cfg 1",
             "ms_per_step": ms, "ms_min": float(min(per)), "steps": steps, "higher_is_better": False,
@@ -581,7 +619,7 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
             "e2e": {"ms_per_step": e2e_ms, "unit": "ms", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(hn.nbytes + hc.nbytes + ht.nbytes),
                     "d2h_bytes_per_step": int(hx.nbytes), "path": "s2_dit_euler_step_host (pinned host buffers)"},
-            "clocks": clk.summary()}
+            "clocks": clk.summary(), **({"cpu_reference": cpu_ref} if cpu_ref else {})}
 
 
 def run_vae(args, torch, s2b200, synth, dev):
@@ -654,6 +692,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-euler", action="store_true", help="skip the DiT Euler-step measurement")
     ap.add_argument("--euler-steps", type=int, default=5)
+    ap.add_argument("--cpu-euler", action="store_true",
+                    help="also time the reference's CPU block code on the Euler-step shape (about 3 min, N = 1)")
     ap.add_argument("--no-vae", action="store_true", help="skip the VAE attention measurement")
     ap.add_argument("--vae-steps", type=int, default=5)
     args = ap.parse_args()
