@@ -175,6 +175,15 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
+// Relaxed arrive on another CTA's mbarrier, for hand-offs of TMEM data that the
+// arriving thread has already completed (tcgen05.wait::st) and fenced
+// (tcgen05.fence::before_thread_sync): the release form orders this thread's
+// memory operations at cluster scope and costs ~1,000 cycles per arrive.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_bar)
+{
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 // 2-D tiled load into this CTA's shared memory whose completion is counted on
 // an mbarrier of the pair (the leader's)
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap, uint32_t cluster_bar, int c0, int c1)
@@ -227,6 +236,35 @@ __device__ __forceinline__ void mma_chunk_pair_k64(uint32_t d_tmem, uint64_t a_d
         "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
+        : "memory");
+}
+
+// A 128-key P V tile of a pair: D[256][N] (+)= P[256][128] V[128][N] with P in
+// each CTA's TMEM (8 packed columns per K=16 step) and each CTA holding N/2
+// columns of V, MN-major (16 keys = 2 KB per step; 64-column blocks LBO apart).
+__device__ __forceinline__ void mma_tile_ts_pair_k128(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                      uint32_t idesc, uint32_t acc_first)
+{
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a;\n\t.reg .b64 b;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+        "add.u32 a, %1, 8;\n\tadd.s64 b, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 16;\n\tadd.s64 b, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t"
+        "add.u32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a], b, %3, t;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc_first)
         : "memory");
 }
 

@@ -22,6 +22,18 @@
 // previous P V to retire. The epilogue divides by the row sum and stores fp16
 // rows into out[token][d] (columns of this half).
 //
+// CTA pairs (head dim 256 and 512): a cluster of two CTAs takes two
+// consecutive query tiles of a frame (an M = 256 item) and runs tcgen05
+// cta_group::2 MMAs issued by rank 0: each CTA keeps its own Q tile and loads
+// only half of every K tile (64 keys, B split by N for Q K^T) and half of the
+// item's V columns (128 of 256, B split by N for P V), while S, P and O stay
+// per CTA (split by M). Every query tile re-reads its frame's whole K/V
+// stream from L2, ~22 MB per item at d = 512; the pair halves those bytes per
+// FLOP, which bound the single-CTA kernel near the L2-to-SM bandwidth
+// (~7.7 TB/s of a measured ~9.4). Both CTAs' loads complete on rank 0's
+// barriers; rank 0's commits arrive in both CTAs; rank 1's softmax warps
+// announce P on rank 0's barrier. No load uses cluster multicast.
+//
 // Roles (192 threads): warps 0-3 softmax + epilogue (thread r <-> query row r
 // <-> TMEM lane r), warp 4 TMA producer, warp 5 TMEM allocator + MMA issuer.
 // Every wait is bounded (s2dev::mbar_wait); on timeout the CTA records an
@@ -61,7 +73,7 @@ enum Bar {
     B_FULL,                         // [kSlots]
     B_EMPTY = B_FULL + kSlots,      // [kSlots]
     B_SFULL = B_EMPTY + kSlots,     // [2] S buffer b holds the next S tile
-    B_PFULL = B_SFULL + 2,          // P(j) in TMEM (128 arrivals)
+    B_PFULL = B_SFULL + 2,          // P(j) in TMEM (128 thread arrivals; pairs: 8 warp arrivals on rank 0)
     B_ORDY,                         // one phase per retired P V
     B_ODONE,                        // last P V of an item retired
     B_DRAIN,
@@ -78,14 +90,14 @@ struct SpArgs {
     int cpad;        // head dim (128, 256 or 512)
     int dout;        // output columns per item
     int n_half;      // cpad / dout
-    int n_qt;        // query tiles per frame
+    int n_qt;        // query units per frame: 128-row tiles, or tile pairs in pair mode
     int n_kv;        // key tiles per frame
     int n_items;
     float scale_log2;
 };
 
 struct Item {
-    int frame, qt, half;
+    int frame, qt, half;  // qt: query unit (a tile, or a pair of tiles)
 };
 
 __device__ __forceinline__ Item decode(const SpArgs &a, int t)
@@ -116,6 +128,7 @@ __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *e
     return mbar_wait(bar, parity, &dummy, err, E_DRAIN);
 }
 
+template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     spatial_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const SpArgs a)
@@ -131,20 +144,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #define BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kc = a.cpad / 64;       // K slices per key tile
-    const int vc = a.dout / 64;       // V slices per key tile (even)
+    const uint32_t rank = kPair ? cluster_rank() : 0u;
+    const int unit = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int n_units = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+    const int kc = a.cpad / 64;                         // Q slices
+    const int ks = kPair ? kc / 2 : kc;                 // ring slots per K tile (pairs: 64 keys x 128 dims)
+    const int vc = kPair ? a.dout / 128 : a.dout / 64;  // ring slots per V tile (this CTA's columns; even)
+    // this CTA's 128-row query tile within the item's query unit
+    auto cta_tile = [&](int qt) { return kPair ? 2 * qt + static_cast<int>(rank) : qt; };
+    // a pair's loads complete on rank 0's barriers
+    auto lead_bar = [&](uint32_t bar) { return kPair ? cluster_map(bar, 0) : bar; };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), i == B_PFULL ? 128u : 1u);
+        for (int i = 0; i < B_COUNT; ++i) mbar_init(BAR(i), i == B_PFULL ? (kPair ? 8u : 128u) : 1u);
         *abort = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -155,26 +182,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmV);
             uint32_t p = 0, nq = 0;
             bool ok = true;
-            auto slot = [&](const CUtensorMap *map, int c0, int c1) {
+            auto load = [&](uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1) {
+                if constexpr (kPair)
+                    tma_load_2d_pair(dst, map, lead_bar(bar), c0, c1);
+                else
+                    tma_load_2d(dst, map, bar, c0, c1);
+            };
+            // one ring slot: a 16 KB box (a V slice, or a single-CTA K slice) or, for a
+            // pair's K, 64 keys x 128 dims as two 8 KB boxes
+            auto slot = [&](const CUtensorMap *map, int c0, int c1, bool two) {
                 const uint32_t s = p % kSlots, u = p / kSlots;
                 if (!(ok = mbar_wait(BAR(B_EMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_EMPTY))) return;
-                mbar_arrive_expect_tx(BAR(B_FULL + s), kBox);
-                tma_load_2d(sRing + s * kBox, map, BAR(B_FULL + s), c0, c1);
+                if (!kPair || rank == 0) mbar_arrive_expect_tx(BAR(B_FULL + s), kPair ? 2 * kBox : kBox);
+                load(sRing + s * kBox, map, BAR(B_FULL + s), c0, c1);
+                if (two) load(sRing + s * kBox + kBox / 2, map, BAR(B_FULL + s), c0 + 64, c1);
                 ++p;
             };
-            for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+            for (int t = unit; ok && t < a.n_items; t += n_units) {
                 const Item it = decode(a, t);
                 const int row0 = it.frame * a.tokens;
                 if (!(ok = mbar_wait(BAR(B_QEMPTY), (nq & 1u) ^ 1u, abort, a.err, E_Q))) break;
-                mbar_arrive_expect_tx(BAR(B_QFULL), kBox * kc);
+                if (!kPair || rank == 0) mbar_arrive_expect_tx(BAR(B_QFULL), (kPair ? 2 : 1) * kBox * kc);
                 for (int c = 0; c < kc; ++c)
-                    tma_load_2d(sQ + c * kBox, &tmQ, BAR(B_QFULL), c * 64, row0 + it.qt * kBM);
+                    load(sQ + c * kBox, &tmQ, BAR(B_QFULL), c * 64, row0 + cta_tile(it.qt) * kBM);
                 ++nq;
                 auto load_k = [&](int j) {
-                    for (int c = 0; ok && c < kc; ++c) slot(&tmK, c * 64, row0 + j * kBN);
+                    if constexpr (kPair) {
+                        for (int c = 0; ok && c < ks; ++c)
+                            slot(&tmK, c * 128, row0 + j * kBN + static_cast<int>(rank) * (kBN / 2), true);
+                    } else {
+                        for (int c = 0; ok && c < ks; ++c) slot(&tmK, c * 64, row0 + j * kBN, false);
+                    }
                 };
                 auto load_v = [&](int j) {
-                    for (int c = 0; ok && c < vc; ++c) slot(&tmV, it.half * a.dout + c * 64, row0 + j * kBN);
+                    const int col0 = it.half * a.dout + (kPair ? static_cast<int>(rank) * (a.dout / 2) : 0);
+                    for (int c = 0; ok && c < vc; ++c) slot(&tmV, col0 + c * 64, row0 + j * kBN, false);
                 };
                 load_k(0);
                 if (a.n_kv > 1) load_k(1);
@@ -183,43 +225,70 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (j + 2 < a.n_kv) load_k(j + 2);
                 }
             }
-            if (nq) wait_drain(BAR(B_QFULL), (nq - 1) & 1u, a.err);
-            for (uint32_t s = 0; s < kSlots; ++s)
-                if (p > s) wait_drain(BAR(B_FULL + s), ((p - 1 - s) / kSlots) & 1u, a.err);
+            // No load may still be landing when the CTA exits. A pair's loads complete on rank
+            // 0's barriers, which rank 0 drains; rank 1 waits until rank 0's MMAs released the
+            // buffers its last loads filled (each release follows the loads it consumed).
+            if (!kPair || rank == 0) {
+                if (nq) wait_drain(BAR(B_QFULL), (nq - 1) & 1u, a.err);
+                for (uint32_t s = 0; s < kSlots; ++s)
+                    if (p > s) wait_drain(BAR(B_FULL + s), ((p - 1 - s) / kSlots) & 1u, a.err);
+            } else {
+                if (nq) wait_drain(BAR(B_QEMPTY), (nq - 1) & 1u, a.err);
+                for (uint32_t s = 0; s < kSlots; ++s)
+                    if (p > s) wait_drain(BAR(B_EMPTY + s), ((p - 1 - s) / kSlots) & 1u, a.err);
+            }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
-            const uint32_t id_qk = idesc_f16(0u, kBN, 0);
-            const uint32_t id_pv = idesc_f16(0u, 128, 1);
+        if (lane == 0 && rank == 0) {
+            const uint32_t id_qk = idesc_f16(0u, kBN, 0, kPair ? 256u : 128u);
+            const uint32_t id_pv = kPair ? idesc_f16(0u, static_cast<uint32_t>(a.dout), 1, 256u) : idesc_f16(0u, 128, 1);
             const uint64_t dq0 = smem_desc_sw128(sQ, 16, 1024);
             const uint64_t dk0 = smem_desc_sw128(sRing, 16, 1024);
             const uint64_t dv0 = smem_desc_sw128(sRing, kBox, 1024);  // MN-major: 64-column blocks one slot apart
             uint32_t p = 0, nq = 0, np = 0, g = 0;
             bool ok = true;
+            // a pair's commits arrive in both CTAs
+            auto commit = [&](uint32_t bar) {
+                if constexpr (kPair) {
+                    mma_commit_pair(cluster_map(bar, 0));
+                    mma_commit_pair(cluster_map(bar, 1));
+                } else {
+                    mma_commit(bar);
+                }
+            };
             auto wait_slot = [&](uint32_t q) {
                 ok = mbar_wait(BAR(B_FULL + q % kSlots), (q / kSlots) & 1u, abort, a.err, E_SLOT);
                 return ok;
             };
-            // S(b) = Q K(tile)^T, K streamed as kc ring slots
+            // S(b) = Q K(tile)^T, K streamed as ks ring slots
             auto qk = [&](uint32_t b) {
-                for (int c = 0; c < kc; ++c, ++p) {
+                for (int c = 0; c < ks; ++c, ++p) {
                     if (!wait_slot(p)) return;
                     tc_fence_after();
                     const uint32_t s = p % kSlots;
-                    mma_chunk_ss_k64(tmem + b * 128u, dq0 + static_cast<uint64_t>((c * kBox) >> 4),
-                                     dk0 + static_cast<uint64_t>((s * kBox) >> 4), id_qk, c > 0 ? 1u : 0u);
-                    mma_commit(BAR(B_EMPTY + s));
+                    const uint64_t dk = dk0 + static_cast<uint64_t>((s * kBox) >> 4);
+                    if constexpr (kPair) {
+                        // 128 dims: Q slices 2c, 2c+1 against the slot's two 8 KB boxes
+                        mma_chunk_pair_k64(tmem + b * 128u, dq0 + static_cast<uint64_t>((2 * c * kBox) >> 4), dk, id_qk,
+                                           c > 0 ? 1u : 0u);
+                        mma_chunk_pair_k64(tmem + b * 128u, dq0 + static_cast<uint64_t>(((2 * c + 1) * kBox) >> 4),
+                                           dk + static_cast<uint64_t>((kBox / 2) >> 4), id_qk, 1u);
+                    } else {
+                        mma_chunk_ss_k64(tmem + b * 128u, dq0 + static_cast<uint64_t>((c * kBox) >> 4), dk, id_qk,
+                                         c > 0 ? 1u : 0u);
+                    }
+                    commit(BAR(B_EMPTY + s));
                 }
-                mma_commit(BAR(B_SFULL + b));
+                commit(BAR(B_SFULL + b));
             };
-            for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+            for (int t = unit; ok && t < a.n_items; t += n_units) {
                 if (!(ok = mbar_wait(BAR(B_QFULL), nq & 1u, abort, a.err, E_Q))) break;
                 ++nq;
                 tc_fence_after();
                 qk(g & 1u);
                 if (ok && a.n_kv > 1) qk((g + 1) & 1u);
                 if (!ok) break;
-                if (a.n_kv <= 2) mma_commit(BAR(B_QEMPTY));
+                if (a.n_kv <= 2) commit(BAR(B_QEMPTY));
                 for (int j = 0; ok && j < a.n_kv; ++j) {
                     const uint32_t b = (g + j) & 1u;
                     if (!(ok = mbar_wait(BAR(B_PFULL), np & 1u, abort, a.err, E_P))) break;
@@ -229,23 +298,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!wait_slot(p) || !wait_slot(p + 1)) break;
                         tc_fence_after();
                         const uint32_t s = p % kSlots;
-                        mma_tile_ts_k128(tmem + kColO + gr * 128u, tmem + b * 128u + kColP,
-                                         dv0 + static_cast<uint64_t>((s * kBox) >> 4), id_pv, j > 0 ? 1u : 0u);
-                        mma_commit(BAR(B_EMPTY + s));
-                        mma_commit(BAR(B_EMPTY + s + 1));
+                        const uint64_t dv = dv0 + static_cast<uint64_t>((s * kBox) >> 4);
+                        if constexpr (kPair)
+                            mma_tile_ts_pair_k128(tmem + kColO, tmem + b * 128u + kColP, dv, id_pv, j > 0 ? 1u : 0u);
+                        else
+                            mma_tile_ts_k128(tmem + kColO + gr * 128u, tmem + b * 128u + kColP, dv, id_pv,
+                                             j > 0 ? 1u : 0u);
+                        commit(BAR(B_EMPTY + s));
+                        commit(BAR(B_EMPTY + s + 1));
                     }
                     if (!ok) break;
-                    mma_commit(BAR(B_ORDY));
+                    commit(BAR(B_ORDY));
                     if (j + 2 < a.n_kv) {
                         qk(b);  // S buffer b is free once P(j) V(j) has read it: in-order issue
-                        if (ok && j + 3 == a.n_kv) mma_commit(BAR(B_QEMPTY));
+                        if (ok && j + 3 == a.n_kv) commit(BAR(B_QEMPTY));
                     }
                 }
                 if (!ok) break;
-                mma_commit(BAR(B_ODONE));
+                commit(BAR(B_ODONE));
                 g += a.n_kv;
             }
-            mma_commit(BAR(B_DRAIN));
+            if constexpr (kPair)
+                mma_commit_pair(cluster_map(BAR(B_DRAIN), 0));
+            else
+                mma_commit(BAR(B_DRAIN));
             wait_drain(BAR(B_DRAIN), 0, a.err);
         }
     } else {
@@ -255,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float c = a.scale_log2;
         uint32_t g = 0, no = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < a.n_items; t += gridDim.x) {
+        for (int t = unit; ok && t < a.n_items; t += n_units) {
             const Item it = decode(a, t);
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < a.n_kv; ++j) {
@@ -328,7 +404,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l = l * alpha + (((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) + ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y)));
                 m = m_use;
                 tc_fence_before();
-                mbar_arrive(BAR(B_PFULL));
+                if constexpr (kPair) {
+                    // one arrival per warp on rank 0's barrier (8 = 4 warps x 2 CTAs)
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0)
+                            mbar_arrive(BAR(B_PFULL));
+                        else
+                            mbar_arrive_remote_relaxed(cluster_map(BAR(B_PFULL), 0));
+                    }
+                } else {
+                    mbar_arrive(BAR(B_PFULL));
+                }
             }
             if (!ok) break;
             g += a.n_kv;
@@ -338,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++no;
             tc_fence_after();
             // O is read before this group's next P_FULL lets the next item's first P V overwrite it
-            const int q = it.qt * kBM + r;
+            const int q = cta_tile(it.qt) * kBM + r;
             __half *dst = q < a.tokens
                               ? a.out + (static_cast<size_t>(it.frame) * a.tokens + q) * a.cpad + it.half * a.dout
                               : nullptr;
@@ -365,9 +452,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    // the pair's MMAs write both CTAs' TMEM and rank 1 signals rank 0: neither CTA
+    // releases TMEM or exits before the other is done
+    if constexpr (kPair) cluster_sync();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (kPair)
+            tmem_dealloc_pair(tmem, kTmemCols);
+        else
+            tmem_dealloc(tmem, kTmemCols);
     }
 #undef BAR
 }
@@ -396,7 +489,15 @@ extern "C" s2_status s2_spatial_attention(void *stream, const void *q, const voi
     a.cpad = head_dim;
     a.dout = head_dim < 256 ? head_dim : 256;
     a.n_half = head_dim / a.dout;
-    a.n_qt = (tokens + kBM - 1) / kBM;
+    const int n_tiles = (tokens + kBM - 1) / kBM;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // CTA pairs for 256-wide output halves (head dim 256 or 512) once a frame has at
+    // least two query tiles; an odd tile count leaves the last pair's second tile past
+    // the frame (rows whose outputs are not stored)
+    const bool pair = a.dout == 256 && n_tiles >= 2 && sms >= 2;
+    a.n_qt = pair ? (n_tiles + 1) / 2 : n_tiles;
     a.n_kv = (tokens + kBN - 1) / kBN;
     const long long items = 1LL * frames * a.n_qt * a.n_half;
     if (items > 0x7fffffffLL) return s2::set_error(S2_INVALID_ARGUMENT, "s2_spatial_attention: too many items");
@@ -404,22 +505,41 @@ extern "C" s2_status s2_spatial_attention(void *stream, const void *q, const voi
     a.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(channels)));
     CUtensorMap mq, mk, mv;
     const uint64_t pitch = static_cast<uint64_t>(head_dim) * 2;
-    if (!s2::make_map_2d(&mq, q, head_dim, rows, pitch, 64, kBM) || !s2::make_map_2d(&mk, k, head_dim, rows, pitch, 64, kBN) ||
+    // a pair's CTA loads 64 keys of each K tile
+    if (!s2::make_map_2d(&mq, q, head_dim, rows, pitch, 64, kBM) ||
+        !s2::make_map_2d(&mk, k, head_dim, rows, pitch, 64, pair ? kBN / 2 : kBN) ||
         !s2::make_map_2d(&mv, v, head_dim, rows, pitch, 64, kBN))
         return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: cuTensorMapEncodeTiled failed");
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(spatial_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    static bool configured[2] = {false, false};
+    if (!configured[pair]) {
+        const cudaError_t e = cudaFuncSetAttribute(pair ? spatial_attention_kernel<true> : spatial_attention_kernel<false>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: smem attribute: %s", cudaGetErrorString(e));
-        configured = true;
+        configured[pair] = true;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = static_cast<int>(items < sms ? items : sms);
-    spatial_attention_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, a);
+    if (pair) {
+        const long long pairs = items < sms / 2 ? items : sms / 2;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t le = cudaLaunchKernelEx(&cfg, spatial_attention_kernel<true>, mq, mk, mv, a);
+        if (le != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: pair launch failed: %s",
+                                 cudaGetErrorString(le));
+    } else {
+        const int grid = static_cast<int>(items < sms ? items : sms);
+        spatial_attention_kernel<false><<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(mq, mk, mv, a);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: launch failed: %s", cudaGetErrorString(e));
