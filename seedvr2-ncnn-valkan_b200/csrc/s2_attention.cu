@@ -40,10 +40,12 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
 #include "s2_internal.h"
+#include "s2_launch.h"
 #include "s2_sm100.cuh"
 
 using namespace s2dev;
@@ -562,8 +564,8 @@ template <int kOut>
 s2_status launch(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                  const AttnArgs &args, int grid)
 {
-    static bool configured = false;
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};
+    const s2_status cs = s2::once_per_device(configured, [] {
         const cudaError_t e = cudaFuncSetAttribute(window_attention_kernel<kOut>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess)
@@ -577,8 +579,9 @@ s2_status launch(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, 
             return s2::set_error(S2_INFERENCE_FAILED,
                                  "s2_window_attention: kernel built with %d registers/thread, register split needs %d",
                                  fa.numRegs, (128 * (kQT * kRegsSoftmax + kRegsControl) + kThreads - 1) / kThreads);
-        configured = true;
-    }
+        return S2_OK;
+    });
+    if (cs != S2_OK) return cs;
     window_attention_kernel<kOut><<<grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, args);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)

@@ -20,12 +20,14 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
 
 #include "s2_gemm.h"
 #include "s2_internal.h"
+#include "s2_launch.h"
 #include "s2_sm100.cuh"
 
 using namespace s2dev;
@@ -518,9 +520,9 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else {
         mo[0] = mo[1] = mo[2] = ma;  // not used by the channel-major epilogue
     }
-    static bool configured[3] = {false, false, false};
+    static std::atomic<uint64_t> configured[3] = {};
     const int ci = pair ? 2 : (bn == 256 ? 0 : 1);
-    if (!configured[ci]) {
+    const s2_status cs = once_per_device(configured[ci], [ci] {
         const cudaError_t e =
             ci == 2   ? cudaFuncSetAttribute(gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Tile<256, true>::kSmemBytes)
@@ -528,10 +530,10 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
                                              Tile<256>::kSmemBytes)
                       : cudaFuncSetAttribute(gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Tile<128>::kSmemBytes);
-        if (e != cudaSuccess)
-            return set_error(S2_INFERENCE_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-        configured[ci] = true;
-    }
+        if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
+        return S2_OK;
+    });
+    if (cs != S2_OK) return cs;
     if (pair) {
         const long long tiles = ((args.M + 255) / 256) * (args.N / 256);
         const long long pairs = tiles < sms / 2 ? tiles : sms / 2;

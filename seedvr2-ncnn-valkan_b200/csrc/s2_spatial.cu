@@ -43,10 +43,12 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <atomic>
 #include <cstdint>
 
 #include "s2_gemm.h"
 #include "s2_internal.h"
+#include "s2_launch.h"
 #include "s2_sm100.cuh"
 
 using namespace s2dev;
@@ -510,14 +512,15 @@ extern "C" s2_status s2_spatial_attention(void *stream, const void *q, const voi
         !s2::make_map_2d(&mk, k, head_dim, rows, pitch, 64, pair ? kBN / 2 : kBN) ||
         !s2::make_map_2d(&mv, v, head_dim, rows, pitch, 64, kBN))
         return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: cuTensorMapEncodeTiled failed");
-    static bool configured[2] = {false, false};
-    if (!configured[pair]) {
+    static std::atomic<uint64_t> configured[2] = {};
+    const s2_status cs = s2::once_per_device(configured[pair ? 1 : 0], [pair] {
         const cudaError_t e = cudaFuncSetAttribute(pair ? spatial_attention_kernel<true> : spatial_attention_kernel<false>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_spatial_attention: smem attribute: %s", cudaGetErrorString(e));
-        configured[pair] = true;
-    }
+        return S2_OK;
+    });
+    if (cs != S2_OK) return cs;
     if (pair) {
         const long long pairs = items < sms / 2 ? items : sms / 2;
         cudaLaunchConfig_t cfg = {};
