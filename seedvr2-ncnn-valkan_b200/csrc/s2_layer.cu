@@ -72,9 +72,16 @@ struct s2_attention_layer {
     // (the t-slabs of the tiling), each with its own work list, so that the
     // upload of slab s+1, the compute of slab s and the download of slab s-1
     // overlap. Built with the plan (whole window set only).
+    // A slab is uploaded, computed and downloaded in parts: rows [h0, h1) of
+    // each of its frames, holding the windows of one height range (they span
+    // the full width); one part of all rows when the height ranges do not tile.
+    struct Part {
+        int h0 = 0, h1 = 0;
+        int work_off = 0, n_work = 0;
+    };
     struct Slab {
         int t0 = 0, t1 = 0;      // frames [t0, t1)
-        int work_off = 0, n_work = 0;
+        std::vector<Part> parts;
     };
     std::vector<Slab> slabs;
     bool slabs_valid = false;
@@ -97,8 +104,11 @@ struct s2_attention_layer {
     }
 
     // Slab work lists (window index << 16 | q-block, costliest window first
-    // within a slab, as s2_plan_work) for the current plan; false when the
+    // within a part, as s2_plan_work) for the current plan; false when the
     // windows do not split into full-frame slabs (then the forward is serial).
+    // Each slab is split into parts by the windows' height ranges, so that every
+    // part's download overlaps the next part's upload and only the last part's
+    // compute and download remain after the last upload.
     bool build_slabs()
     {
         if (slabs_valid) return !slabs.empty();
@@ -131,15 +141,41 @@ struct s2_attention_layer {
             std::stable_sort(ids.begin(), ids.end(), [&](int a, int b) {
                 return h_cu[a + 1] - h_cu[a] > h_cu[b + 1] - h_cu[b];
             });
+            // height ranges of the slab's windows; each must cover full rows of the slab
+            std::vector<std::pair<int, int>> hr;
+            {
+                for (int i : ids)
+                    if (std::find(hr.begin(), hr.end(), std::make_pair(all[i].h0, all[i].h1)) == hr.end())
+                        hr.emplace_back(all[i].h0, all[i].h1);
+                std::sort(hr.begin(), hr.end());
+                bool tiles = !hr.empty() && hr.front().first == 0 && hr.back().second == H;
+                for (size_t k = 1; tiles && k < hr.size(); ++k) tiles = hr[k].first == hr[k - 1].second;
+                for (size_t k = 0; tiles && k < hr.size(); ++k) {
+                    long long area = 0;
+                    for (int i : ids)
+                        if (all[i].h0 == hr[k].first && all[i].h1 == hr[k].second)
+                            area += 1LL * (all[i].h1 - all[i].h0) * (all[i].w1 - all[i].w0);
+                    tiles = area == 1LL * (hr[k].second - hr[k].first) * W;
+                }
+                if (!tiles) hr.clear();
+            }
+            if (hr.empty()) hr.emplace_back(0, H);
             Slab sl;
             sl.t0 = rg.first;
             sl.t1 = rg.second;
-            sl.work_off = static_cast<int>(h_work.size());
-            for (int w : ids) {
-                const int seq = h_cu[w + 1] - h_cu[w];
-                for (int qb = 0; qb * s2::kCtaRows < seq; ++qb) h_work.push_back((w << 16) | qb);
+            for (const auto &h : hr) {
+                Part pt;
+                pt.h0 = h.first;
+                pt.h1 = h.second;
+                pt.work_off = static_cast<int>(h_work.size());
+                for (int w : ids) {
+                    if (hr.size() > 1 && (all[w].h0 != h.first || all[w].h1 != h.second)) continue;
+                    const int seq = h_cu[w + 1] - h_cu[w];
+                    for (int qb = 0; qb * s2::kCtaRows < seq; ++qb) h_work.push_back((w << 16) | qb);
+                }
+                pt.n_work = static_cast<int>(h_work.size()) - pt.work_off;
+                sl.parts.push_back(pt);
             }
-            sl.n_work = static_cast<int>(h_work.size()) - sl.work_off;
             slabs.push_back(sl);
         }
         if (!d_slab_work.ensure(h_work.size() * sizeof(int32_t)) ||
@@ -151,6 +187,14 @@ struct s2_attention_layer {
         return true;
     }
 
+    size_t n_parts() const
+    {
+        size_t n = 0;
+        for (const Slab &sl : slabs) n += sl.parts.size();
+        return n;
+    }
+
+    // n: the number of parts (one upload event per slab, one compute event per part)
     bool ensure_pipeline_objects(size_t n)
     {
         if (!s_in && cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) != cudaSuccess) return false;
@@ -434,41 +478,80 @@ static s2_status forward_host_pipelined(s2_attention_layer *l, cudaStream_t st, 
     if (ok && Lt > 0)
         ok = cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, static_cast<size_t>(Lt) * row_in, cudaMemcpyHostToDevice,
                              l->s_in) == cudaSuccess;
-    for (size_t i = 0; ok && i < l->slabs.size(); ++i) {
-        const auto &sl = l->slabs[i];
-        const size_t r0 = static_cast<size_t>(sl.t0) * hw, nr = static_cast<size_t>(sl.t1 - sl.t0) * hw;
-        ok = cudaMemcpyAsync(in + r0 * row_in, hin + r0 * row_in, nr * row_in, cudaMemcpyHostToDevice, l->s_in) ==
-                 cudaSuccess &&
-             cudaEventRecord(l->ev_in[i], l->s_in) == cudaSuccess;
+    // A part's rows: one range per frame, or the whole slab at once when the part is the slab.
+    auto n_pieces = [&](const s2_attention_layer::Slab &sl, const s2_attention_layer::Part &pt) {
+        return pt.h0 == 0 && pt.h1 == l->H ? 1 : sl.t1 - sl.t0;
+    };
+    auto piece = [&](const s2_attention_layer::Slab &sl, const s2_attention_layer::Part &pt, int k, size_t &a,
+                     size_t &n) {
+        if (pt.h0 == 0 && pt.h1 == l->H) {
+            a = static_cast<size_t>(sl.t0) * hw, n = static_cast<size_t>(sl.t1 - sl.t0) * hw;
+        } else {
+            a = static_cast<size_t>(sl.t0 + k) * hw + static_cast<size_t>(pt.h0) * l->W;
+            n = static_cast<size_t>(pt.h1 - pt.h0) * l->W;
+        }
+    };
+    {
+        size_t pi = 0;
+        for (size_t i = 0; ok && i < l->slabs.size(); ++i)
+            for (const auto &pt : l->slabs[i].parts) {
+                for (int k = 0; ok && k < n_pieces(l->slabs[i], pt); ++k) {
+                    size_t a = 0, n = 0;
+                    piece(l->slabs[i], pt, k, a, n);
+                    ok = cudaMemcpyAsync(in + a * row_in, hin + a * row_in, n * row_in, cudaMemcpyHostToDevice,
+                                         l->s_in) == cudaSuccess;
+                }
+                ok = ok && cudaEventRecord(l->ev_in[pi++], l->s_in) == cudaSuccess;
+            }
     }
     if (!ok) return s2::set_error(S2_INFERENCE_FAILED, "forward_host: upload failed");
+    size_t part_idx = 0;
+    bool text_done = false;
     for (size_t i = 0; i < l->slabs.size(); ++i) {
         const auto &sl = l->slabs[i];
-        const size_t r0 = static_cast<size_t>(sl.t0) * hw, nr = static_cast<size_t>(sl.t1 - sl.t0) * hw;
-        if (cudaStreamWaitEvent(st, l->ev_in[i], 0) != cudaSuccess)
-            return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream wait failed");
-        s2_status rc = s2::qk_norm_rope_range(st, in, l->d_in_txt.ptr, io_dtype, l->heads, l->eps, l->gammas(),
-                                              l->d_rope.ptr, static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows,
-                                              l->mode, static_cast<int>(r0), static_cast<int>(r0 + nr), i == 0 ? 1 : 0,
-                                              sc.q.ptr, sc.k.ptr, sc.v.ptr);
-        if (rc != S2_OK) return rc;
-        rc = s2_window_attention(st, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
-                                 static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
-                                 static_cast<const s2_row *>(l->d_rows.ptr),
-                                 static_cast<const int32_t *>(l->d_slab_work.ptr) + sl.work_off, sl.n_work,
-                                 l->d_out_vid.ptr, sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
-        if (rc != S2_OK) return rc;
-        l->last_launches += 2;
-        if (io_dtype == S2_F32) {
-            rc = s2::to_f32(st, l->mode, static_cast<const char *>(l->d_out_vid.ptr) + r0 * dim * 2,
-                            static_cast<long long>(nr) * dim, static_cast<float *>(l->d_out_vid32.ptr) + r0 * dim);
+        for (const auto &pt : sl.parts) {
+            if (cudaStreamWaitEvent(st, l->ev_in[part_idx], 0) != cudaSuccess)
+                return s2::set_error(S2_INFERENCE_FAILED, "forward_host: stream wait failed");
+            s2_status rc = S2_OK;
+            for (int k = 0; k < n_pieces(sl, pt); ++k) {
+                size_t a = 0, n = 0;
+                piece(sl, pt, k, a, n);
+                rc = s2::qk_norm_rope_range(st, in, l->d_in_txt.ptr, io_dtype, l->heads, l->eps, l->gammas(),
+                                            l->d_rope.ptr, static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows,
+                                            l->mode, static_cast<int>(a), static_cast<int>(a + n), text_done ? 0 : 1,
+                                            sc.q.ptr, sc.k.ptr, sc.v.ptr);
+                if (rc != S2_OK) return rc;
+                text_done = true;
+                l->last_launches++;
+            }
+            rc = s2_window_attention(st, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
+                                     static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
+                                     static_cast<const s2_row *>(l->d_rows.ptr),
+                                     static_cast<const int32_t *>(l->d_slab_work.ptr) + pt.work_off, pt.n_work,
+                                     l->d_out_vid.ptr, sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
             if (rc != S2_OK) return rc;
             l->last_launches++;
+            if (io_dtype == S2_F32) {
+                for (int k = 0; k < n_pieces(sl, pt); ++k) {
+                    size_t a = 0, n = 0;
+                    piece(sl, pt, k, a, n);
+                    rc = s2::to_f32(st, l->mode, static_cast<const char *>(l->d_out_vid.ptr) + a * dim * 2,
+                                    static_cast<long long>(n) * dim, static_cast<float *>(l->d_out_vid32.ptr) + a * dim);
+                    if (rc != S2_OK) return rc;
+                    l->last_launches++;
+                }
+            }
+            bool ok2 = cudaEventRecord(l->ev_cmp[part_idx], st) == cudaSuccess &&
+                       cudaStreamWaitEvent(l->s_out, l->ev_cmp[part_idx], 0) == cudaSuccess;
+            ++part_idx;
+            for (int k = 0; ok2 && k < n_pieces(sl, pt); ++k) {
+                size_t a = 0, n = 0;
+                piece(sl, pt, k, a, n);
+                ok2 = cudaMemcpyAsync(hout + a * row_out, static_cast<const char *>(dout) + a * row_out, n * row_out,
+                                      cudaMemcpyDeviceToHost, l->s_out) == cudaSuccess;
+            }
+            if (!ok2) return s2::set_error(S2_INFERENCE_FAILED, "forward_host: download failed");
         }
-        if (cudaEventRecord(l->ev_cmp[i], st) != cudaSuccess || cudaStreamWaitEvent(l->s_out, l->ev_cmp[i], 0) != cudaSuccess ||
-            cudaMemcpyAsync(hout + r0 * row_out, static_cast<const char *>(dout) + r0 * row_out, nr * row_out,
-                            cudaMemcpyDeviceToHost, l->s_out) != cudaSuccess)
-            return s2::set_error(S2_INFERENCE_FAILED, "forward_host: download failed");
     }
     if (Lt > 0) {
         const s2_status rc = s2_text_window_sum(st, l->mode, sc.txt_partial.ptr, l->n_local, Lt, dim,
@@ -519,7 +602,7 @@ extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void
         return s2::set_error(S2_NOT_LOADED, "attention layer: weights or runtime shape not set");
     rc = l->build_plan(Lt, st);
     if (rc != S2_OK) return rc;
-    if (l->build_slabs() && l->ensure_pipeline_objects(l->slabs.size()))
+    if (l->build_slabs() && l->ensure_pipeline_objects(l->n_parts()))
         return forward_host_pipelined(l, st, vid_qkv, txt_qkv, io_dtype, L, Lt, vid_out, txt_out);
     if (cudaMemcpyAsync(l->d_in_vid.ptr, vid_qkv, in_vid, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (Lt > 0 && cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, in_txt, cudaMemcpyHostToDevice, st) != cudaSuccess))
