@@ -143,6 +143,30 @@ struct s2_vae_attention {
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
     s2::DeviceBuffer hx, hy;  // device staging for forward_host
+    // forward_host's frame pipeline: upload and download streams, one upload and
+    // one compute event per frame
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_out = nullptr;
+    std::vector<cudaEvent_t> ev_in, ev_cmp;
+
+    bool ensure_pipeline(int frames)
+    {
+        if (!s_in && cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) != cudaSuccess) return false;
+        if (!s_out && cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) != cudaSuccess) return false;
+        if (!ev_start && cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) != cudaSuccess) return false;
+        if (!ev_out && cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming) != cudaSuccess) return false;
+        while (static_cast<int>(ev_in.size()) < frames) {
+            cudaEvent_t a = nullptr, b = nullptr;
+            if (cudaEventCreateWithFlags(&a, cudaEventDisableTiming) != cudaSuccess) return false;
+            if (cudaEventCreateWithFlags(&b, cudaEventDisableTiming) != cudaSuccess) {
+                cudaEventDestroy(a);
+                return false;
+            }
+            ev_in.push_back(a);
+            ev_cmp.push_back(b);
+        }
+        return true;
+    }
 };
 
 extern "C" s2_status s2_vae_attention_create(int device, int channels, s2_vae_attention **out)
@@ -172,6 +196,12 @@ extern "C" s2_status s2_vae_attention_destroy(s2_vae_attention *l)
     for (s2::DeviceBuffer *b : {&l->w_qkv, &l->b_qkv, &l->w_o, &l->b_o, &l->gn, &l->part, &l->xn, &l->q, &l->k, &l->v,
                                 &l->att, &l->err, &l->hx, &l->hy})
         b->release();
+    for (cudaEvent_t e : l->ev_in) cudaEventDestroy(e);
+    for (cudaEvent_t e : l->ev_cmp) cudaEventDestroy(e);
+    if (l->ev_start) cudaEventDestroy(l->ev_start);
+    if (l->ev_out) cudaEventDestroy(l->ev_out);
+    if (l->s_in) cudaStreamDestroy(l->s_in);
+    if (l->s_out) cudaStreamDestroy(l->s_out);
     delete l;
     return S2_OK;
 }
@@ -218,6 +248,14 @@ extern "C" s2_status s2_vae_attention_load(s2_vae_attention *l, const float *nor
     return S2_OK;
 }
 
+// Workspaces of a forward over `frames` frames of `rows` tokens in total.
+static bool ensure_workspace(s2_vae_attention *l, int frames, long long rows)
+{
+    const size_t act = static_cast<size_t>(rows) * l->cpad * 2;
+    return l->part.ensure(sizeof(double2) * frames * l->C) && l->xn.ensure(act) && l->q.ensure(act) &&
+           l->k.ensure(act) && l->v.ensure(act) && l->att.ensure(act) && l->err.ensure(4);
+}
+
 extern "C" s2_status s2_vae_attention_forward(s2_vae_attention *l, void *stream, const float *x, int frames,
                                               int height, int width, long long cstep, float *y)
 {
@@ -233,10 +271,8 @@ extern "C" s2_status s2_vae_attention_forward(s2_vae_attention *l, void *stream,
     s2::DeviceGuard guard(l->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int C = l->C, P = l->cpad;
-    const size_t act = static_cast<size_t>(rows) * P * 2;
     bool fresh_err = l->err.ptr == nullptr;
-    if (!l->part.ensure(sizeof(double2) * frames * C) || !l->xn.ensure(act) || !l->q.ensure(act) ||
-        !l->k.ensure(act) || !l->v.ensure(act) || !l->att.ensure(act) || !l->err.ensure(4))
+    if (!ensure_workspace(l, frames, rows))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_vae_attention_forward: workspace allocation failed");
     if (fresh_err && cudaMemsetAsync(l->err.ptr, 0, 4, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward: memset failed");
@@ -297,17 +333,45 @@ extern "C" s2_status s2_vae_attention_forward_host(s2_vae_attention *l, void *st
     s2::clear_error();
     if (!l || !x || !y || frames <= 0 || height <= 0 || width <= 0 || cstep < 1LL * frames * height * width)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_vae_attention_forward_host: invalid arguments");
+    if (!l->loaded) return s2::set_error(S2_NOT_LOADED, "s2_vae_attention_forward_host: weights not loaded");
     s2::DeviceGuard guard(l->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t bytes = static_cast<size_t>(cstep) * l->C * sizeof(float);
-    if (!l->hx.ensure(bytes) || !l->hy.ensure(bytes))
+    const long long tokens = 1LL * height * width;
+    // Every part of the layer works frame by frame (GroupNorm statistics, the
+    // attention, and the row-wise projections), so the frames are pipelined: the
+    // upload of frame f + 1, the forward of frame f and the download of frame f - 1
+    // run on three streams. A frame is one strided copy of the [C][cstep] blob
+    // (C rows of H*W floats, cstep apart). Each frame's forward is the same
+    // arithmetic as the whole blob's, so the result is the same bit for bit.
+    const bool fresh_err = l->err.ptr == nullptr;
+    if (!l->hx.ensure(bytes) || !l->hy.ensure(bytes) || !ensure_workspace(l, 1, tokens) || !l->ensure_pipeline(frames))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_vae_attention_forward_host: staging allocation failed");
-    if (cudaMemcpyAsync(l->hx.ptr, x, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess)
-        return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: upload failed");
-    const s2_status s = s2_vae_attention_forward(l, stream, static_cast<const float *>(l->hx.ptr), frames, height, width,
-                                                 cstep, static_cast<float *>(l->hy.ptr));
-    if (s != S2_OK) return s;
-    if (cudaMemcpyAsync(y, l->hy.ptr, bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+    if (fresh_err && cudaMemsetAsync(l->err.ptr, 0, 4, st) != cudaSuccess)
+        return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: memset failed");
+    auto *dx = static_cast<float *>(l->hx.ptr), *dy = static_cast<float *>(l->hy.ptr);
+    const size_t pitch = static_cast<size_t>(cstep) * sizeof(float), width_b = static_cast<size_t>(tokens) * sizeof(float);
+    bool ok = cudaEventRecord(l->ev_start, st) == cudaSuccess && cudaStreamWaitEvent(l->s_in, l->ev_start, 0) == cudaSuccess &&
+              cudaStreamWaitEvent(l->s_out, l->ev_start, 0) == cudaSuccess;
+    for (int f = 0; ok && f < frames; ++f)
+        ok = cudaMemcpy2DAsync(dx + f * tokens, pitch, x + f * tokens, pitch, width_b, l->C, cudaMemcpyHostToDevice,
+                               l->s_in) == cudaSuccess &&
+             cudaEventRecord(l->ev_in[f], l->s_in) == cudaSuccess;
+    if (!ok) return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: upload failed");
+    int launches = 0;
+    for (int f = 0; f < frames; ++f) {
+        if (cudaStreamWaitEvent(st, l->ev_in[f], 0) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: stream wait failed");
+        const s2_status s = s2_vae_attention_forward(l, stream, dx + f * tokens, 1, height, width, cstep, dy + f * tokens);
+        if (s != S2_OK) return s;
+        launches += l->last_launches;
+        if (cudaEventRecord(l->ev_cmp[f], st) != cudaSuccess || cudaStreamWaitEvent(l->s_out, l->ev_cmp[f], 0) != cudaSuccess ||
+            cudaMemcpy2DAsync(y + f * tokens, pitch, dy + f * tokens, pitch, width_b, l->C, cudaMemcpyDeviceToHost,
+                              l->s_out) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: download failed");
+    }
+    l->last_launches = launches;
+    if (cudaEventRecord(l->ev_out, l->s_out) != cudaSuccess || cudaStreamWaitEvent(st, l->ev_out, 0) != cudaSuccess ||
         cudaStreamSynchronize(st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: %s",
                              cudaGetErrorString(cudaGetLastError()));

@@ -9,6 +9,8 @@ fp32 attention for the attention core alone.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -106,6 +108,30 @@ def test_host_forward_and_determinism(torch_cuda):
     y_dev = run_gpu(torch_cuda, x, w)
     assert np.array_equal(y_host, y_host2)
     assert np.array_equal(y_host, y_dev)
+
+
+@pytest.mark.parametrize("shape", [(96, 5, 9, 14), (256, 3, 12, 20)])
+def test_host_forward_frame_pipeline(torch_cuda, shape):
+    """The host-buffer forward runs frame by frame (upload, forward and download of
+    consecutive frames overlapped on three streams). It must equal the device
+    forward bit for bit, for a dense blob and for a channel step padded past
+    T*H*W, whose padding in y it leaves untouched."""
+    x, w = synth.vae_inputs(shape, seed=21)
+    C, T, H, W = x.shape
+    n = T * H * W
+    layer = make_layer(C, w)
+    y_dev = run_gpu(torch_cuda, x, w)
+    assert np.array_equal(layer.forward_host(x), y_dev)
+    cstep = n + 37
+    blob = np.full((C, cstep), 7.0, np.float32)
+    blob[:, :n] = x.reshape(C, n)
+    yb = np.full((C, cstep), -3.0, np.float32)
+    for _ in range(2):
+        rc = s2b200.lib().s2_vae_attention_forward_host(layer.handle, None, ctypes.c_void_p(blob.ctypes.data), T, H, W,
+                                                        cstep, ctypes.c_void_p(yb.ctypes.data))
+        assert rc == 0, s2b200.last_error()
+        assert np.array_equal(yb[:, :n].reshape(x.shape), y_dev)
+        assert np.all(yb[:, n:] == -3.0)
 
 
 def test_cstep_padded_blob(torch_cuda, port):
