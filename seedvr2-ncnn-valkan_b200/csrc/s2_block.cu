@@ -154,11 +154,15 @@ bool upload_f16(s2::DeviceBuffer &b, const float *src, size_t n)
 struct BlockScratch {
     int device = 0;
     s2::DeviceBuffer a_vid, a_txt, qkv_vid, qkv_txt, att_vid, att_txt32, att_txt16, h_vid, h_txt, hid_vid, hid_txt;
+    // split-K partial sums of the projections of a few dozen rows (the text rows):
+    // at most 128 rows x 256 columns per CTA of the grid
+    s2::DeviceBuffer splitk;
+    static constexpr size_t kSplitKFloats = static_cast<size_t>(128) * 256 * 160;
     ~BlockScratch()
     {
         s2::DeviceGuard guard(device);
         for (s2::DeviceBuffer *x : {&a_vid, &a_txt, &qkv_vid, &qkv_txt, &att_vid, &att_txt32, &att_txt16, &h_vid, &h_txt,
-                                    &hid_vid, &hid_txt})
+                                    &hid_vid, &hid_txt, &splitk})
             x->release();
     }
 };
@@ -388,6 +392,7 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         !sc.qkv_txt.ensure(Tz * 3 * d * 2) || !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
         !sc.att_txt16.ensure(Tz * d * 2) || !sc.h_vid.ensure(Lz * d * 4) || !sc.h_txt.ensure(Tz * d * 4) ||
         !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4) ||
+        !sc.splitk.ensure(BlockScratch::kSplitKFloats * sizeof(float)) ||
         !b->mods.ensure(static_cast<size_t>(16) * d * 4))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward: workspace allocation failed");
     if (fresh && cudaMemsetAsync(b->err.ptr, 0, 4, st) != cudaSuccess)
@@ -426,11 +431,17 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid));
     if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, a_txt));
     // QKV projections (no bias)
+    float *splitk = static_cast<float *>(sc.splitk.ptr);
+    int extra = 0;  // split-K finish kernels
+    const size_t splitk_cap = BlockScratch::kSplitKFloats;
     s2::GemmArgs g;
     g.K = d;
     g.N = 3 * d;
     g.split = 3 * d;
     g.err = err;
+    g.partial = splitk;
+    g.partial_floats = splitk_cap;
+    g.extra_launches = &extra;
     g.M = merged ? L + Lt : L;
     g.out[0] = qkv_vid;
     S2_TRY(s2::gemm_f16(st, a_vid, V.qkv.ptr, g));
@@ -466,6 +477,9 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     p.N = d;
     p.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
     p.err = err;
+    p.partial = splitk;
+    p.partial_floats = splitk_cap;
+    p.extra_launches = &extra;
     p.M = merged_rest ? L + Lt : L;
     p.bias = static_cast<const float *>(V.proj_b.ptr);
     p.gmul = mv + 6 * dz;
@@ -483,6 +497,9 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         q.N = d;
         q.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
         q.err = err;
+        q.partial = splitk;
+        q.partial_floats = splitk_cap;
+        q.extra_launches = &extra;
         q.M = Lt;
         q.bias = static_cast<const float *>(T.proj_b.ptr);
         q.resid = txt;
@@ -509,6 +526,9 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         u.epilogue = s2::GEMM_EPI_SWIGLU_F16;
         u.out[0] = hid;
         u.err = err;
+        u.partial = splitk;
+        u.partial_floats = splitk_cap;
+        u.extra_launches = &extra;
         if ((r = s2::gemm_f16(st, a16, br.gu.ptr, u)) != S2_OK) return r;
         ++launches;
         s2::GemmArgs o;
@@ -517,6 +537,9 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         o.K = h;
         o.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
         o.gmul = mb + 7 * dz;
+        o.partial = splitk;
+        o.partial_floats = splitk_cap;
+        o.extra_launches = &extra;
         o.resid = hx;
         o.y = y;
         if (split > 0) {
@@ -541,7 +564,7 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         return s;
     }
 #undef S2_TRY
-    b->last_launches = launches;
+    b->last_launches = launches + extra;
     return S2_OK;
 }
 

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -112,6 +113,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_blocks = (a.N + kBN - 1) / kBN;
     const int n_tiles = ((a.M + kTileRows - 1) / kTileRows) * n_blocks;
     const int n_k = a.K / kBK;
+    // split-K: work unit t = (tile t / ks, K range t % ks), the K slices [kc_lo, kc_hi)
+    const int ks = kPair ? 1 : (a.ksplit > 1 ? a.ksplit : 1);
+    const int n_work = n_tiles * ks;
+    auto kc_lo = [&](int t) { return static_cast<int>((1LL * (t % ks) * n_k) / ks); };
+    auto kc_hi = [&](int t) { return static_cast<int>((1LL * (t % ks + 1) * n_k) / ks); };
 
     if (threadIdx.x == 0) {
         // a pair's accumulator-empty barrier (rank 0's) counts both CTAs' epilogue threads
@@ -141,10 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmB);
             uint32_t p = 0;  // stage uses issued
             bool ok = true;
-            for (int t = unit; ok && t < n_tiles; t += n_units) {
-                const int m0 = (t / n_blocks) * kTileRows + static_cast<int>(rank) * kBM;
-                const int n0 = (t % n_blocks) * kBN + static_cast<int>(rank) * T::kBRows;
-                for (int kc = 0; kc < n_k; ++kc, ++p) {
+            for (int t = unit; ok && t < n_work; t += n_units) {
+                const int tile = t / ks;
+                const int m0 = (tile / n_blocks) * kTileRows + static_cast<int>(rank) * kBM;
+                const int n0 = (tile % n_blocks) * kBN + static_cast<int>(rank) * T::kBRows;
+                for (int kc = kc_lo(t); kc < kc_hi(t); ++kc, ++p) {
                     const uint32_t s = p % kStages, u = p / kStages;
                     if (!(ok = mbar_wait(BAR(B_EMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_EMPTY))) break;
                     const uint32_t sa = base + s * kStageBytes;
@@ -187,20 +194,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             uint32_t p = 0, lt = 0;
             bool ok = true;
-            for (int t = unit; ok && t < n_tiles; t += n_units, ++lt) {
+            for (int t = unit; ok && t < n_work; t += n_units, ++lt) {
                 const uint32_t b = lt & 1u;
                 if (!(ok = mbar_wait(BAR(B_ACCE + b), ((lt >> 1) & 1u) ^ 1u, abort, a.err, E_ACCE))) break;
                 tc_fence_after();
-                for (int kc = 0; kc < n_k; ++kc, ++p) {
+                const int k0 = kc_lo(t);
+                for (int kc = k0; kc < kc_hi(t); ++kc, ++p) {
                     const uint32_t s = p % kStages, u = p / kStages;
                     if (!(ok = mbar_wait(BAR(B_FULL + s), u & 1u, abort, a.err, E_FULL))) break;
                     tc_fence_after();
                     const uint64_t da = d0 + static_cast<uint64_t>((s * kStageBytes) >> 4);
                     const uint64_t db = da + static_cast<uint64_t>(kABytes >> 4);
                     if constexpr (kPair)
-                        mma_chunk_pair_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
+                        mma_chunk_pair_k64(tmem + b * kBN, da, db, idesc, kc > k0 ? 1u : 0u);
                     else
-                        mma_chunk_ss_k64(tmem + b * kBN, da, db, idesc, kc > 0 ? 1u : 0u);
+                        mma_chunk_ss_k64(tmem + b * kBN, da, db, idesc, kc > k0 ? 1u : 0u);
                     commit(BAR(B_EMPTY + s));
                 }
                 if (!ok) break;
@@ -252,8 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         uint32_t lt = 0;
         bool ok = true;
-        for (int t = unit; ok && t < n_tiles; t += n_units, ++lt) {
-            const int m0 = (t / n_blocks) * kTileRows + static_cast<int>(rank) * kBM, n0 = (t % n_blocks) * kBN;
+        for (int t = unit; ok && t < n_work; t += n_units, ++lt) {
+            const int tile = t / ks;
+            const int m0 = (tile / n_blocks) * kTileRows + static_cast<int>(rank) * kBM, n0 = (tile % n_blocks) * kBN;
             const uint32_t b = lt & 1u;
             ok = mbar_wait(BAR(B_ACCF + b), (lt >> 1) & 1u, abort, a.err, E_ACCF);
             ok = __all_sync(0xffffffffu, ok);
@@ -261,13 +270,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < a.M;
-            for (int c = 0; c < kBN / 32 && a.epilogue != s2::GEMM_EPI_SWIGLU_F16; ++c) {
+            const bool split_k = ks > 1;
+            for (int c = 0; c < kBN / 32 && (split_k || a.epilogue != s2::GEMM_EPI_SWIGLU_F16); ++c) {
                 const int n = n0 + c * 32;
                 if (n >= a.N) break;
                 uint32_t r[32];
                 tmem_ld32(tmem + lane_off + b * kBN + c * 32, r);
                 tmem_wait_ld();
-                if (a.epilogue == s2::GEMM_EPI_SPLIT_F16) {
+                if (split_k) {
+                    // raw fp32 partial sums of this K range; the finish kernel applies the epilogue
+                    if (row_ok) {
+                        float4 *dst = reinterpret_cast<float4 *>(
+                            a.partial + (static_cast<size_t>(t % ks) * a.M + row) * a.N + n);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                    }
+                } else if (a.epilogue == s2::GEMM_EPI_SPLIT_F16) {
                     const int which = n / a.split, col = n - which * a.split;
                     uint4 v4[4];
 #pragma unroll
@@ -332,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (m0 + quad * 32 < y_rows) store_chunk32(&tmO0, outv, n, m0 + quad * 32);
                 }
             }
-            if (kBN == 256 && a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && ok) {
+            if (kBN == 256 && a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && !split_k && ok) {
                 // pairs (gate chunk c, in chunk c + 4) of the 256-column tile
                 for (int c = 0; c < 4; ++c) {
                     uint32_t gr[32], ur[32];
@@ -381,6 +401,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_dealloc(tmem, kTmemCols);
     }
 #undef BAR
+}
+
+// Split-K finish: out = epilogue(sum over splits of partial[split][row][n]), the
+// splits added in order (deterministic), then the same per-element arithmetic as
+// gemm_kernel's epilogues. One thread per output element (per hidden element
+// for SwiGLU).
+__global__ void __launch_bounds__(256) splitk_finish_kernel(const s2::GemmArgs a, int ks)
+{
+    const bool swiglu = a.epilogue == s2::GEMM_EPI_SWIGLU_F16;
+    const int n_out = swiglu ? a.N / 2 : a.N;
+    const long long total = 1LL * a.M * n_out;
+    const size_t slab = static_cast<size_t>(a.M) * a.N;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+        const int row = static_cast<int>(i / n_out), j = static_cast<int>(i - 1LL * row * n_out);
+        auto sum = [&](int n) {
+            const float *p = a.partial + static_cast<size_t>(row) * a.N + n;
+            float acc = p[0];
+            for (int s = 1; s < ks; ++s) acc = __fadd_rn(acc, p[s * slab]);
+            return acc;
+        };
+        if (swiglu) {
+            // hidden column j: gate at tile column (j / 128) * 256 + j % 128, "in" 128 columns on
+            const int n = (j / 128) * 256 + (j % 128);
+            const float g = sum(n), u = sum(n + 128);
+            const float f = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+            static_cast<__half *>(a.out[0])[static_cast<size_t>(row) * n_out + j] = __float2half_rn(f);
+        } else if (a.epilogue == s2::GEMM_EPI_SPLIT_F16) {
+            const float f = sum(j) + (a.bias ? __ldg(a.bias + j) : 0.f);
+            const int which = j / a.split, col = j - which * a.split;
+            static_cast<__half *>(a.out[which])[static_cast<size_t>(row) * a.split + col] = __float2half_rn(f);
+        } else {  // GEMM_EPI_GATED_RESID_F32
+            const bool second = a.split_row > 0 && row >= a.split_row;
+            const int rr = second ? row - a.split_row : row;
+            const float *rbase = second ? a.resid2 : a.resid;
+            float t = sum(j);
+            if (a.bias) t = __fadd_rn(t, __ldg(a.bias + j));
+            if (a.gmul) t = __fmul_rn(t, __ldg(a.gmul + j));
+            const float rv = rbase ? __ldg(rbase + static_cast<size_t>(rr) * a.N + j) : 0.f;
+            (second ? a.y2 : a.y)[static_cast<size_t>(rr) * a.N + j] = __fmul_rn(__fadd_rn(t, rv), a.out_scale);
+        }
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode()
@@ -494,6 +555,17 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     // for M >= 4096 and K >= 1024. Needs N a multiple of 256.
     bool pair = args.pair > 0 ||
                 (args.pair < 0 && bn == 256 && args.M >= 4096 && args.K >= 1024 && args.N % 256 == 0 && sms >= 2);
+    // Split-K for a few dozen rows (the text rows of a block): the tiles alone would
+    // occupy a small part of the grid while each streams its whole weight slab; with
+    // the K range split, up to 8 CTAs per tile stream it together (each split keeps
+    // at least 4 K slices). Not for the channel-major epilogue (the VAE, many rows).
+    int ks = 1;
+    const long long tiles_k = mt * ((args.N + bn - 1) / bn);
+    if (args.partial && !pair && args.M <= kBM && args.epilogue != GEMM_EPI_RESID_T_F32 && tiles_k * 2 <= sms) {
+        ks = static_cast<int>(std::min<long long>({8LL, sms / tiles_k, (args.K / kBK) / 4}));
+        while (ks > 1 && static_cast<size_t>(ks) * args.M * args.N > args.partial_floats) --ks;
+        if (ks < 2) ks = 1;
+    }
     if (pair && (bn != 256 || args.N % 256 != 0 || sms < 2))
         return set_error(S2_INVALID_ARGUMENT, "gemm: CTA pairs need 256-wide tiles and N %% 256 == 0 (N %d)", args.N);
     CUtensorMap ma, mb, mo[3];
@@ -553,12 +625,20 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
         if (le != cudaSuccess)
             return set_error(S2_INFERENCE_FAILED, "gemm: pair launch failed: %s", cudaGetErrorString(le));
     } else {
-        const long long tiles = mt * ((args.N + bn - 1) / bn);
-        const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+        GemmArgs ka = args;
+        ka.ksplit = ks;
+        const long long units = mt * ((args.N + bn - 1) / bn) * ks;
+        const int grid = static_cast<int>(units < sms ? units : sms);
         if (bn == 256)
-            gemm_kernel<256, false><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+            gemm_kernel<256, false><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], ka);
         else
-            gemm_kernel<128, false><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
+            gemm_kernel<128, false><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], ka);
+        if (ks > 1) {
+            const long long outs = 1LL * args.M * (args.epilogue == GEMM_EPI_SWIGLU_F16 ? args.N / 2 : args.N);
+            const int fgrid = static_cast<int>(std::min<long long>((outs + 255) / 256, 4LL * sms));
+            splitk_finish_kernel<<<fgrid, 256, 0, st>>>(ka, ks);
+            if (args.extra_launches) ++*args.extra_launches;
+        }
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(S2_INFERENCE_FAILED, "gemm: launch failed: %s", cudaGetErrorString(e));

@@ -63,6 +63,14 @@ struct GemmArgs {
     float out_scale = 1.f;
     int bn = 0;                   // tile width 256 or 128 (0: chosen from the wave fill)
     int pair = -1;                // CTA pairs (256 x 256 tiles on two SMs): 1 on, 0 off, -1 chosen by shape
+    // Split-K workspace: with `partial` set, a GEMM of at most 128 rows whose tiles
+    // fill less than half of the grid splits K over up to 8 CTAs per tile; each writes
+    // fp32 partial sums [split][M][N] here (capacity `partial_floats`) and a second
+    // kernel adds them in split order and applies the epilogue. Set by gemm_f16.
+    float *partial = nullptr;
+    size_t partial_floats = 0;
+    int ksplit = 0;
+    int *extra_launches = nullptr;  // if set, incremented per kernel launched beyond the GEMM itself
     int32_t *err = nullptr;       // device error word (bounded waits)
 };
 
