@@ -269,6 +269,47 @@ S2_API s2_status s2_dit_block_forward_host(s2_dit_block *block, void *stream, co
 S2_API int s2_dit_block_last_launches(const s2_dit_block *block);
 S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
 
+/* ---- the block's projections (ncnn InnerProduct replacement) ------------- */
+
+/* y = x W^T (+ b) as the block runs its InnerProduct layers (created at
+ * seedvr2_dit_block.cpp:28-56, applied :1114-1267) on sm_100a tcgen05:
+ * a [M][K] and b [N][K] fp16 row-major (K contiguous, K a multiple of 64,
+ * rows 16-byte aligned), fp32 accumulation in TMEM, fused epilogues:
+ *  S2_GEMM_SPLIT_F16: fp16 out[n / split][m * split + n % split] (out0..2;
+ *    the fused Q|K|V projection with split = dim);
+ *  S2_GEMM_GATED_RESID_F32: fp32 y[m][n] = ((acc + bias[n]) * gmul[n] +
+ *    resid[m][n]) * out_scale (gmul / resid may be NULL: no gate / no
+ *    residual); with split_row > 0, rows m >= split_row read resid2 and write
+ *    y2 at row m - split_row (apply_ada_output_and_residual :807-825);
+ *  S2_GEMM_SWIGLU_F16: every 256 columns of W hold 128 gate rows then the
+ *    matching 128 "in" rows; fp16 out0[m][(n / 256) * 128 + j] =
+ *    silu(gate_j) * in_j (apply_mlp :1093-1112).
+ * workspace (device fp32, workspace_floats) lets a GEMM of at most 128 rows
+ * that would fill less than half the GPU split K over up to 8 CTAs per tile
+ * (deterministic: partial sums added in split order by a second kernel);
+ * NULL = never split. A split result differs from the unsplit one within
+ * fp32 rounding (another summation order). *extra_launches (may be NULL)
+ * receives the kernels launched beyond the GEMM itself. err: device int32
+ * error word (bounded waits), may be NULL. Stream-ordered. */
+typedef enum s2_gemm_epilogue {
+    S2_GEMM_SPLIT_F16 = 0,
+    S2_GEMM_GATED_RESID_F32 = 2,
+    S2_GEMM_SWIGLU_F16 = 3
+} s2_gemm_epilogue;
+typedef struct s2_gemm_desc {
+    int epilogue, M, N, K;
+    const void *a, *b;
+    const float *bias, *gmul, *resid, *resid2;
+    void *out0, *out1, *out2;
+    float *y, *y2;
+    int split, split_row;
+    float out_scale;
+    float *workspace;
+    size_t workspace_floats;
+    int32_t *err;
+} s2_gemm_desc;
+S2_API s2_status s2_gemm(void *stream, const s2_gemm_desc *desc, int *extra_launches);
+
 /* ---- multi-GPU communicator (no counterpart in the reference) ------------ */
 
 /* One rank per GPU; NCCL over NVLink / NVSwitch, loaded on first use

@@ -28,10 +28,28 @@ _i32p = ctypes.POINTER(ctypes.c_int)
 _u8p = ctypes.POINTER(ctypes.c_ubyte)
 
 
-def build(ref_root: str = "/root/reference") -> None:
+def reference_root() -> str | None:
+    """Root of the reference source tree: $S2_REFERENCE_ROOT, else the
+    ``reference_path`` recorded in the repository's BASELINE.json; None when
+    neither names an existing tree (e.g. on a GPU box, which uses the
+    prebuilt oracle/_ref)."""
+    root = os.environ.get("S2_REFERENCE_ROOT")
+    if not root:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(os.path.join(root, "src")) else None
+
+
+def build(ref_root: str | None = None) -> None:
     """Compile the restatement, and the reference build when its tree exists."""
-    subprocess.run(["make", "-s", "-C", HERE, "port", f"REF={ref_root}"], check=True)
-    subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
+    ref_root = ref_root or reference_root()
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
+    if ref_root:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
 
 
 def _ptr(a, t=_f32p):

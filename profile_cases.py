@@ -2,8 +2,8 @@
 kernel in isolation (an ncu capture with several passes needs a program that
 holds a few GB at most; the 32-block Euler step holds far more).
 
-    PYTHONPATH=seedvr2-ncnn-valkan_b200 python -m s2b200.cases block720p
-    PYTHONPATH=seedvr2-ncnn-valkan_b200 python -m s2b200.cases vae_cfg4
+    python profile_cases.py block720p
+    python profile_cases.py vae_cfg4
 
 block720p: one unshared, plain-window DiT block (dim 2560, 20 heads, SwiGLU
     6912) over the 720p token grid 6x45x80 plus 58 text rows, random-init
@@ -19,8 +19,12 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
-from . import DynamicFramewiseSpatialAttention, SeedVR2DiTBlock, synth
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "seedvr2-ncnn-valkan_b200"))
+
+from s2b200 import DynamicFramewiseSpatialAttention, SeedVR2DiTBlock, synth  # noqa: E402
 
 CASES = ("block720p", "vae_cfg4")
 

@@ -155,9 +155,16 @@ struct BlockScratch {
     int device = 0;
     s2::DeviceBuffer a_vid, a_txt, qkv_vid, qkv_txt, att_vid, att_txt32, att_txt16, h_vid, h_txt, hid_vid, hid_txt;
     // split-K partial sums of the projections of a few dozen rows (the text rows):
-    // at most 128 rows x 256 columns per CTA of the grid
+    // gemm_f16 splits only GEMMs of at most 128 rows and keeps splits x tiles <=
+    // the SM count, each split holding at most 128 rows x 256 columns, so
+    // 128 x 256 x SMs floats bound every split GEMM of the device.
     s2::DeviceBuffer splitk;
-    static constexpr size_t kSplitKFloats = static_cast<size_t>(128) * 256 * 160;
+    static size_t splitk_floats(int device)
+    {
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        return static_cast<size_t>(128) * 256 * static_cast<size_t>(std::max(sms, 1));
+    }
     ~BlockScratch()
     {
         s2::DeviceGuard guard(device);
@@ -388,11 +395,18 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     const size_t Lz = static_cast<size_t>(L) + static_cast<size_t>(std::max(Lt, 0)), Tz = static_cast<size_t>(std::max(Lt, 1));
     const bool fresh = b->err.ptr == nullptr;
     BlockScratch &sc = *b->sc;
+    // gemm_f16 can split K only for GEMMs of at most 128 rows with at least 8
+    // K slices of 64 (K >= 512): the text rows of an unshared block or of the
+    // last block's projection, or a block of few video rows. Otherwise no
+    // workspace is allocated or passed.
+    const int gemm_rows_min = Lt > 0 ? std::min(L, Lt) : L;
+    const bool need_splitk = gemm_rows_min <= 128 && std::max(d, h) >= 512;
+    const size_t splitk_cap = need_splitk ? BlockScratch::splitk_floats(b->device) : 0;
     if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) || !sc.qkv_vid.ensure(Lz * 3 * d * 2) ||
         !sc.qkv_txt.ensure(Tz * 3 * d * 2) || !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
         !sc.att_txt16.ensure(Tz * d * 2) || !sc.h_vid.ensure(Lz * d * 4) || !sc.h_txt.ensure(Tz * d * 4) ||
         !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4) ||
-        !sc.splitk.ensure(BlockScratch::kSplitKFloats * sizeof(float)) ||
+        (need_splitk && !sc.splitk.ensure(splitk_cap * sizeof(float))) ||
         !b->mods.ensure(static_cast<size_t>(16) * d * 4))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward: workspace allocation failed");
     if (fresh && cudaMemsetAsync(b->err.ptr, 0, 4, st) != cudaSuccess)
@@ -431,9 +445,8 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid));
     if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, a_txt));
     // QKV projections (no bias)
-    float *splitk = static_cast<float *>(sc.splitk.ptr);
+    float *splitk = need_splitk ? static_cast<float *>(sc.splitk.ptr) : nullptr;
     int extra = 0;  // split-K finish kernels
-    const size_t splitk_cap = BlockScratch::kSplitKFloats;
     s2::GemmArgs g;
     g.K = d;
     g.N = 3 * d;

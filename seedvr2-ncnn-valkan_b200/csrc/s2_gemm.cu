@@ -646,3 +646,42 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
 }
 
 }  // namespace s2
+
+extern "C" s2_status s2_gemm(void *stream, const s2_gemm_desc *d, int *extra_launches)
+{
+    s2::clear_error();
+    if (!d || !d->a || !d->b || d->M <= 0 || d->N <= 0 || d->K <= 0 || d->K % 64 != 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: NULL operand or bad shape (K must be a multiple of 64)");
+    if (d->epilogue != S2_GEMM_SPLIT_F16 && d->epilogue != S2_GEMM_GATED_RESID_F32 && d->epilogue != S2_GEMM_SWIGLU_F16)
+        return s2::set_error(S2_UNSUPPORTED, "s2_gemm: unknown epilogue %d", d->epilogue);
+    if (d->epilogue == S2_GEMM_SPLIT_F16 && (d->split <= 0 || d->split % 8 != 0 || !d->out0 ||
+                                             (d->N > d->split && !d->out1) || (d->N > 2 * d->split && !d->out2) ||
+                                             d->N > 3 * d->split))
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: split output needs split %% 8 == 0 and one buffer per part");
+    s2::GemmArgs g;
+    g.M = d->M;
+    g.N = d->N;
+    g.K = d->K;
+    g.bias = d->bias;
+    g.epilogue = d->epilogue;
+    g.out[0] = d->out0;
+    g.out[1] = d->out1;
+    g.out[2] = d->out2;
+    g.split = d->split;
+    g.gmul = d->gmul;
+    g.resid = d->resid;
+    g.y = d->y;
+    g.split_row = d->split_row;
+    g.resid2 = d->resid2;
+    g.y2 = d->y2;
+    g.out_scale = d->out_scale;
+    g.partial = d->workspace;
+    g.partial_floats = d->workspace ? d->workspace_floats : 0;
+    g.err = d->err;
+    int extra = 0;
+    g.extra_launches = &extra;
+    const s2_status s = s2::gemm_f16(static_cast<cudaStream_t>(stream), d->a, d->b, g);
+    if (extra_launches) *extra_launches = extra;
+    return s;
+}
+

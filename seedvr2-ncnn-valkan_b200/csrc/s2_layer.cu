@@ -573,6 +573,9 @@ static s2_status forward_host_pipelined(s2_attention_layer *l, cudaStream_t st, 
     return s2_attention_layer_device_error(l, &code);
 }
 
+static s2_status forward_host_serial(s2_attention_layer *l, cudaStream_t st, const void *vid_qkv, const void *txt_qkv,
+                                     s2_dtype io_dtype, int L, int Lt, void *vid_out, float *txt_out);
+
 extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void *stream, const void *vid_qkv,
                                                      const void *txt_qkv, s2_dtype io_dtype, int L, int Lt,
                                                      const int32_t *vid_shape, void *vid_out, float *txt_out)
@@ -602,8 +605,33 @@ extern "C" s2_status s2_attention_layer_forward_host(s2_attention_layer *l, void
         return s2::set_error(S2_NOT_LOADED, "attention layer: weights or runtime shape not set");
     rc = l->build_plan(Lt, st);
     if (rc != S2_OK) return rc;
+    // Once a copy touching the caller's host buffers is queued, an error return
+    // first waits for the copies in flight, so the caller may free its buffers
+    // as soon as the call returns.
+    auto drain = [&](s2_status s) {
+        if (s != S2_OK) {
+            if (l->s_in) cudaStreamSynchronize(l->s_in);
+            if (l->s_out) cudaStreamSynchronize(l->s_out);
+            cudaStreamSynchronize(st);
+        }
+        return s;
+    };
     if (l->build_slabs() && l->ensure_pipeline_objects(l->n_parts()))
-        return forward_host_pipelined(l, st, vid_qkv, txt_qkv, io_dtype, L, Lt, vid_out, txt_out);
+        return drain(forward_host_pipelined(l, st, vid_qkv, txt_qkv, io_dtype, L, Lt, vid_out, txt_out));
+    return drain(forward_host_serial(l, st, vid_qkv, txt_qkv, io_dtype, L, Lt, vid_out, txt_out));
+}
+
+// The host-buffer forward without the pipeline (window subsets): copies in,
+// the device forward, copies out, one stream.
+static s2_status forward_host_serial(s2_attention_layer *l, cudaStream_t st, const void *vid_qkv, const void *txt_qkv,
+                                     s2_dtype io_dtype, int L, int Lt, void *vid_out, float *txt_out)
+{
+    const int dim = l->heads * S2_HEAD_DIM;
+    const size_t esz = io_dtype == S2_F32 ? 4 : 2;
+    const size_t in_vid = static_cast<size_t>(L) * 3 * dim * esz, in_txt = static_cast<size_t>(Lt) * 3 * dim * esz;
+    const size_t out_vid16 = static_cast<size_t>(L) * dim * 2;
+    void *stream = st;
+    s2_status rc = S2_OK;
     if (cudaMemcpyAsync(l->d_in_vid.ptr, vid_qkv, in_vid, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (Lt > 0 && cudaMemcpyAsync(l->d_in_txt.ptr, txt_qkv, in_txt, cudaMemcpyHostToDevice, st) != cudaSuccess))
         return s2::set_error(S2_INFERENCE_FAILED, "forward_host: H2D copy failed");

@@ -76,19 +76,39 @@ s2_status scratch_address(void **out)
     return S2_OK;
 }
 
-// Packed row table from the window list (the device-side counterpart of
-// s2_build_varlen, so no host-side row array is needed).
-__global__ void build_rows_kernel(const s2_window *__restrict__ wins, const int32_t *__restrict__ cu, int n_windows,
-                                  int n_rows, int height, int width, int text_len, s2_row *__restrict__ rows)
+// The whole plan of one call, passed BY VALUE as a kernel parameter (about
+// 17 KB, under the 32,764-byte parameter limit of sm_70+ with CUDA 12.1+), so
+// the launch carries its own copy and no host pointer outlives the call.
+struct NoallocPlan {
+    s2_window wins[kMaxWindows];
+    int32_t cu[kMaxWindows + 1];
+    int32_t work[kMaxWork];
+    int32_t n_windows, n_work;
+};
+static_assert(sizeof(NoallocPlan) <= 32000, "plan must fit the kernel parameter space");
+
+// Writes the plan tables into the scratch array, clears the error word and
+// builds the packed row table (the device-side counterpart of s2_build_varlen,
+// so no host-side row array is needed).
+__global__ void plan_rows_kernel(const NoallocPlan p, int n_rows, int height, int width, int text_len,
+                                 s2_window *__restrict__ d_win, int32_t *__restrict__ d_cu,
+                                 int32_t *__restrict__ d_work, int32_t *__restrict__ d_err,
+                                 s2_row *__restrict__ rows)
 {
-    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n_rows; r += gridDim.x * blockDim.x) {
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
+    for (int i = tid; i < p.n_windows; i += nthr) d_win[i] = p.wins[i];
+    for (int i = tid; i <= p.n_windows; i += nthr) d_cu[i] = p.cu[i];
+    for (int i = tid; i < p.n_work; i += nthr) d_work[i] = p.work[i];
+    if (tid == 0) *d_err = 0;
+    const int n_windows = p.n_windows;
+    for (int r = tid; r < n_rows; r += nthr) {
         int lo = 0, hi = n_windows - 1;  // last window with cu[w] <= r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if (cu[mid] <= r) lo = mid; else hi = mid - 1;
+            if (p.cu[mid] <= r) lo = mid; else hi = mid - 1;
         }
-        const s2_window b = wins[lo];
-        const int i = r - cu[lo];
+        const s2_window b = p.wins[lo];
+        const int i = r - p.cu[lo];
         const int lh = b.h1 - b.h0, lw = b.w1 - b.w0;
         const int lvid = (b.t1 - b.t0) * lh * lw;
         s2_row o;
@@ -116,20 +136,27 @@ extern "C" s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
                                                      const float *freqs21, void *vid_out, float *txt_out,
                                                      int32_t *err)
 {
-    // ---- host-side validation and planning (stack arrays only) ----
+    // ---- host-side validation and planning (host memory only) ----
     if (!vid_qkv || !gammas || !freqs21 || !vid_out || text_len < 0 || (text_len > 0 && (!txt_qkv || !txt_out)) ||
         heads <= 0 || heads > 64)
         return s2::set_error(S2_INVALID_ARGUMENT, "noalloc: NULL buffer or invalid heads/text_len");
     if (mode != S2_MODE_BF16_REF && mode != S2_MODE_F16 && mode != S2_MODE_BF16_F16)
         return s2::set_error(S2_UNSUPPORTED, "noalloc: unknown mode");
-    s2_window wins[kMaxWindows];
+    // The plan lives in one struct that the launch below copies as its
+    // parameter (static: ~17 KB is too large for some callers' thread stacks;
+    // the mutex serialises host threads that plan at the same time).
+    static std::mutex plan_mu;
+    std::lock_guard<std::mutex> plan_lock(plan_mu);
+    static NoallocPlan plan;
+    s2_window *wins = plan.wins;
+    int32_t *cu = plan.cu;
+    int32_t *work = plan.work;
     int n = 0;
     s2_status rc = s2_make_windows(frames, height, width, shifted, wt, wh, ww, wins, kMaxWindows, &n);
     if (rc != S2_OK) return rc;
     if (n > kMaxWindows)
         return s2::set_error(S2_INVALID_ARGUMENT, "noalloc: %d windows exceed the fixed scratch limit of %d", n,
                              kMaxWindows);
-    int32_t cu[kMaxWindows + 1];
     long long rows = 0;
     int max_pos = std::max(text_len, 1);
     for (int w = 0; w < n; w++) {
@@ -150,7 +177,6 @@ extern "C" s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
     if (max_pos > kMaxPos)
         return s2::set_error(S2_INVALID_ARGUMENT, "noalloc: RoPE position %d exceeds the limit of %d", max_pos - 1,
                              kMaxPos - 1);
-    int32_t work[kMaxWork];
     int n_work = 0;
     rc = s2_plan_work(cu, n, work, kMaxWork, &n_work);
     if (rc != S2_OK) return rc;
@@ -167,16 +193,12 @@ extern "C" s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
     auto *d_work = reinterpret_cast<int32_t *>(sc + kOffWork);
     auto *d_err = err ? err : reinterpret_cast<int32_t *>(sc + kOffErr);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // Pageable (stack) sources: cudaMemcpyAsync stages them before returning.
-    if (cudaMemcpyAsync(d_win, wins, sizeof(s2_window) * n, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(d_cu, cu, sizeof(int32_t) * (n + 1), cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(d_work, work, sizeof(int32_t) * n_work, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess)
-        return s2::set_error(S2_INFERENCE_FAILED, "noalloc: plan upload failed");
+    plan.n_windows = n;
+    plan.n_work = n_work;
     const int n_rows = static_cast<int>(rows);
-    build_rows_kernel<<<std::min((n_rows + 255) / 256, 1184), 256, 0, st>>>(d_win, d_cu, n, n_rows, height, width,
-                                                                           text_len, d_rows);
-    if (cudaGetLastError() != cudaSuccess) return s2::set_error(S2_INFERENCE_FAILED, "noalloc: row-table launch failed");
+    plan_rows_kernel<<<std::max(1, std::min((n_rows + 255) / 256, 1184)), 256, 0, st>>>(
+        plan, n_rows, height, width, text_len, d_win, d_cu, d_work, d_err, d_rows);
+    if (cudaGetLastError() != cudaSuccess) return s2::set_error(S2_INFERENCE_FAILED, "noalloc: plan launch failed");
     void *rope = sc + kOffRope;
     rc = s2_rope_table(stream, freqs21, max_pos, rope);
     if (rc != S2_OK) return rc;

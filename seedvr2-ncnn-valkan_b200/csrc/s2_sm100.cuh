@@ -72,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             if (*abort) return false;
             if (global_timer_ns() - t0 > kWaitTimeoutNs) {
                 *abort = 1;
-                atomicCAS(err, 0, code);
+                if (err) atomicCAS(err, 0, code);
                 return false;
             }
         }

@@ -351,24 +351,33 @@ extern "C" s2_status s2_vae_attention_forward_host(s2_vae_attention *l, void *st
         return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: memset failed");
     auto *dx = static_cast<float *>(l->hx.ptr), *dy = static_cast<float *>(l->hy.ptr);
     const size_t pitch = static_cast<size_t>(cstep) * sizeof(float), width_b = static_cast<size_t>(tokens) * sizeof(float);
+    // After the first copy is queued, every error return first waits for the
+    // copies in flight on the caller's host buffers, so the caller may free
+    // them as soon as the call returns.
+    auto drain = [&](s2_status s) {
+        cudaStreamSynchronize(l->s_in);
+        cudaStreamSynchronize(l->s_out);
+        cudaStreamSynchronize(st);
+        return s;
+    };
     bool ok = cudaEventRecord(l->ev_start, st) == cudaSuccess && cudaStreamWaitEvent(l->s_in, l->ev_start, 0) == cudaSuccess &&
               cudaStreamWaitEvent(l->s_out, l->ev_start, 0) == cudaSuccess;
     for (int f = 0; ok && f < frames; ++f)
         ok = cudaMemcpy2DAsync(dx + f * tokens, pitch, x + f * tokens, pitch, width_b, l->C, cudaMemcpyHostToDevice,
                                l->s_in) == cudaSuccess &&
              cudaEventRecord(l->ev_in[f], l->s_in) == cudaSuccess;
-    if (!ok) return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: upload failed");
+    if (!ok) return drain(s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: upload failed"));
     int launches = 0;
     for (int f = 0; f < frames; ++f) {
         if (cudaStreamWaitEvent(st, l->ev_in[f], 0) != cudaSuccess)
-            return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: stream wait failed");
+            return drain(s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: stream wait failed"));
         const s2_status s = s2_vae_attention_forward(l, stream, dx + f * tokens, 1, height, width, cstep, dy + f * tokens);
-        if (s != S2_OK) return s;
+        if (s != S2_OK) return drain(s);
         launches += l->last_launches;
         if (cudaEventRecord(l->ev_cmp[f], st) != cudaSuccess || cudaStreamWaitEvent(l->s_out, l->ev_cmp[f], 0) != cudaSuccess ||
             cudaMemcpy2DAsync(y + f * tokens, pitch, dy + f * tokens, pitch, width_b, l->C, cudaMemcpyDeviceToHost,
                               l->s_out) != cudaSuccess)
-            return s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: download failed");
+            return drain(s2::set_error(S2_INFERENCE_FAILED, "s2_vae_attention_forward_host: download failed"));
     }
     l->last_launches = launches;
     if (cudaEventRecord(l->ev_out, l->s_out) != cudaSuccess || cudaStreamWaitEvent(st, l->ev_out, 0) != cudaSuccess ||

@@ -52,6 +52,18 @@ class HeadParams(ctypes.Structure):
                                             "embedding_dim", "out_channels")] + [("eps", ctypes.c_float)]
 
 
+class GemmDesc(ctypes.Structure):
+    """s2_gemm_desc (include/s2_b200.h)."""
+    _fields_ = ([(n, ctypes.c_int) for n in ("epilogue", "M", "N", "K")]
+                + [(n, ctypes.c_void_p) for n in ("a", "b", "bias", "gmul", "resid", "resid2", "out0", "out1", "out2",
+                                                  "y", "y2")]
+                + [("split", ctypes.c_int), ("split_row", ctypes.c_int), ("out_scale", ctypes.c_float),
+                   ("workspace", ctypes.c_void_p), ("workspace_floats", ctypes.c_size_t), ("err", ctypes.c_void_p)])
+
+
+GEMM_SPLIT_F16, GEMM_GATED_RESID_F32, GEMM_SWIGLU_F16 = 0, 2, 3
+
+
 class Window(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
 
@@ -160,6 +172,7 @@ _SIGS = {
     "s2_euler_endpoint": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_float, _vp]),
     "s2_condition_ratio": (ctypes.c_float, [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "s2_make_condition": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 4 + [ctypes.c_float, _vp]),
+    "s2_gemm": (ctypes.c_int, [_vp, ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int)]),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
@@ -485,6 +498,27 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
                     stream=None):
     _check(lib().s2_text_window_sum(_stream_ptr(stream), mode, _ptr(txt_partial), n_windows, text_len, dim,
                                     ctypes.c_float(scale), int(accumulate), _ptr(txt_out)), "s2_text_window_sum")
+
+
+def gemm(epilogue, a, b, *, bias=None, gmul=None, resid=None, resid2=None, outs=(), y=None, y2=None, split=0,
+         split_row=0, out_scale=1.0, workspace=None, err=None, stream=None) -> int:
+    """s2_gemm: the block's InnerProduct on tcgen05 (a [M][K], b [N][K] fp16 CUDA
+    tensors). Returns the number of extra kernels launched (split-K finish)."""
+    M, K = a.shape
+    N = b.shape[0]
+    o = list(outs) + [None] * (3 - len(outs))
+
+    def _ptr(t):
+        return None if t is None else t.data_ptr()
+
+    d = GemmDesc(epilogue=int(epilogue), M=M, N=N, K=K, a=_ptr(a), b=_ptr(b), bias=_ptr(bias), gmul=_ptr(gmul),
+                 resid=_ptr(resid), resid2=_ptr(resid2), out0=_ptr(o[0]), out1=_ptr(o[1]), out2=_ptr(o[2]),
+                 y=_ptr(y), y2=_ptr(y2), split=int(split), split_row=int(split_row), out_scale=float(out_scale),
+                 workspace=_ptr(workspace), workspace_floats=0 if workspace is None else workspace.numel(),
+                 err=_ptr(err))
+    extra = ctypes.c_int(0)
+    _check(lib().s2_gemm(_stream_ptr(stream), ctypes.byref(d), ctypes.byref(extra)), "s2_gemm")
+    return extra.value
 
 
 def block_flags(index: int, n_blocks: int = 32) -> dict:

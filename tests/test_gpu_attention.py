@@ -168,6 +168,58 @@ def test_cfg3_1080p_ragged_sampled(torch_cuda, port, shifted):
     _sampled(torch_cuda, port, "cfg3", shifted, n_win=2, heads_pick=(19,))
 
 
+@pytest.mark.parametrize("shifted", [0, 1])
+def test_bench_path_cfg2_full_vs_unrounded_oracle(torch_cuda, port, shifted):
+    """Exactly the configuration bench.py times: the 720p layer (27 plain / 64
+    shifted windows) in S2_MODE_F16 with fp16 QKV in and fp16 out -- every
+    window, every head and the text mean against the oracle's unrounded
+    variant (the reference's Vulkan output semantics,
+    seedvr2_dit_block.cpp:416-436; arithmetic :1045-1079)."""
+    torch = torch_cuda
+    grid = synth.GRIDS["cfg2"]
+    vid, txt, gam, fr = synth.layer_inputs(grid, heads=20, seed=41 + shifted)
+    vo, to = run_gpu(torch, vid, txt, gam, fr, grid, 20, shifted, mode=s2b200.MODE_F16, in_dtype=torch.float16)
+    ro, rt, _ = port.window_attention(vid, txt, grid, 20, list(gam), fr, shifted, round_out=False)
+    m = parity.check(vo, ro, False, f"cfg2 shifted={shifted} vid")
+    parity.check(to, rt, False, f"cfg2 shifted={shifted} txt")
+    assert m["max_abs"] < 1e-3, m
+
+
+@pytest.mark.parametrize("shifted", [0, 1])
+def test_bench_path_cfg3_sampled_all_heads(torch_cuda, port, shifted):
+    """Config 3 (1080p x 45f, 96,480 tokens, 100 plain / 125 shifted windows)
+    in the benchmarked mode (fp16 in, S2_MODE_F16): all 20 heads of the
+    largest, the smallest and one random window, video rows of the full-layer
+    run, and the text partial sum of those windows through a window-subset
+    layer (the sharded path) against the oracle restricted to them."""
+    torch = torch_cuda
+    grid = synth.GRIDS["cfg3"]
+    T, H, W = grid
+    vid, txt, gam, fr = synth.layer_inputs(grid, heads=20, seed=51 + shifted)
+    vo, _ = run_gpu(torch, vid, txt, gam, fr, grid, 20, shifted, mode=s2b200.MODE_F16, in_dtype=torch.float16)
+    assert np.all(np.abs(vo).sum(axis=1) > 0), "a video row was not written"
+    wins = s2b200.make_windows(*grid, shifted)
+    sizes = (wins[:, 1] - wins[:, 0]) * (wins[:, 3] - wins[:, 2]) * (wins[:, 5] - wins[:, 4])
+    rng = np.random.default_rng(17 + shifted)
+    pick = sorted({int(np.argmax(sizes)), int(np.argmin(sizes)), int(rng.integers(len(wins)))})
+    mask = np.zeros(len(wins), np.uint8)
+    mask[pick] = 1
+    ro, rt, _ = port.window_attention(vid, txt, grid, 20, list(gam), fr, shifted, round_out=False,
+                                      window_mask=mask)
+    for w in pick:
+        t0, t1, h0, h1, w0, w1 = wins[w]
+        idx = ((np.arange(t0, t1)[:, None, None] * H + np.arange(h0, h1)[None, :, None]) * W
+               + np.arange(w0, w1)[None, None, :]).ravel()
+        parity.check(vo[idx], ro[idx], False, f"cfg3 shifted={shifted} window {w} ({sizes[w]} tokens)")
+    layer = make_layer(20, gam, fr, grid, shifted, mode=s2b200.MODE_F16)
+    layer.set_window_subset(np.array(pick, np.int32))
+    _, to_sub = layer.forward(torch.from_numpy(vid).to("cuda", torch.float16),
+                              torch.from_numpy(txt).to("cuda", torch.float16))
+    torch.cuda.synchronize()
+    assert layer.device_error() == 0
+    parity.check(to_sub.cpu().numpy(), rt, False, f"cfg3 shifted={shifted} text partial")
+
+
 def test_long_windows_override_cfg2(torch_cuda, port):
     """BASELINE's 6x15x20 windows: S = 1858 keys -> 15 key tiles per CTA."""
     _sampled(torch_cuda, port, "cfg2", 1, override=synth.OVERRIDES["cfg2"], n_win=2, heads_pick=(4,))

@@ -88,6 +88,23 @@ def test_config1_block_vs_reference(torch_cuda, ref):
     check_block(vo, to, evo, eto, vid, txt, "config 1")
 
 
+@pytest.mark.parametrize("index,shared,shifted", [(0, False, False), (11, True, True)])
+def test_config2_full_width_block_vs_reference(torch_cuda, ref, index, shared, shifted):
+    """The block the Euler-step bench runs 32 times, at full width and full
+    size: dim 2560, 20 heads, SwiGLU 6912, the 720p grid (21,600 video tokens,
+    58 text tokens). An unshared plain block (blocks 0-9) and a shared shifted
+    block (10-30), each against the reference's own
+    SeedVR2DiTBlock::forward (seedvr2_dit_block.cpp:1114-1267, oracle/_ref)."""
+    dim, heads, mlp, grid = 2560, 20, 6912, synth.GRIDS["cfg2"]
+    w = synth.block_weights(dim, heads, mlp, shared, seed=20 + index)
+    vid, txt, emb = synth.block_activations(grid, dim, seed=30 + index)
+    params = dict(block_index=index, shared=shared, last=False, shifted=shifted, dim=dim, heads=heads,
+                  head_dim=128, mlp_hidden=mlp, eps=1e-5)
+    evo, eto = ref.block_forward(params, w, vid, txt, emb, grid)
+    vo, to, _ = run_gpu(torch_cuda, params, w, vid, txt, emb, grid)
+    check_block(vo, to, evo, eto, vid, txt, f"config-2 block {index}")
+
+
 def test_host_forward_matches_device(torch_cuda):
     params, w, vid, txt, emb, shape, _, _ = refcases.block_case(refcases.BLOCK_CASES[3])
     vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
