@@ -289,8 +289,9 @@ S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
  * (deterministic: partial sums added in split order by a second kernel);
  * NULL = never split. A split result differs from the unsplit one within
  * fp32 rounding (another summation order). *extra_launches (may be NULL)
- * receives the kernels launched beyond the GEMM itself. err: device int32
- * error word (bounded waits), may be NULL. Stream-ordered. */
+ * receives the kernels launched beyond the GEMM itself. err (required):
+ * device int32 error word, set when a bounded wait inside the kernel gives
+ * up. Stream-ordered. */
 typedef enum s2_gemm_epilogue {
     S2_GEMM_SPLIT_F16 = 0,
     S2_GEMM_GATED_RESID_F32 = 2,
@@ -380,6 +381,15 @@ S2_API s2_status s2_dit_euler_step_host(s2_dit *model, void *stream, const float
 S2_API s2_status s2_dit_sample(s2_dit *model, void *stream, const float *noise, const float *condition, int T, int H,
                                int W, const float *positive_text, const float *negative_text, int Lt, int steps,
                                float cfg_scale, float cfg_rescale, float *out);
+
+/* The same loop with positive and negative texts of their own token counts
+ * (the reference's default embeddings are 58 and 64 tokens; each DiT
+ * forward takes any text length, dit.cpp:277-383). s2_dit_sample is this
+ * call with both lengths Lt. */
+S2_API s2_status s2_dit_sample_texts(s2_dit *model, void *stream, const float *noise, const float *condition, int T,
+                                     int H, int W, const float *positive_text, int positive_len,
+                                     const float *negative_text, int negative_len, int steps, float cfg_scale,
+                                     float cfg_rescale, float *out);
 
 /* Sampler pieces on DEVICE fp32 tensors of n elements (sampler.cpp):
  * timesteps of an n-step schedule (host; :181-187); classifier-free guidance

@@ -749,10 +749,20 @@ extern "C" s2_status s2_dit_sample(s2_dit *d, void *stream, const float *noise, 
                                    int H, int W, const float *positive_text, const float *negative_text, int Lt,
                                    int steps, float cfg_scale, float cfg_rescale, float *out)
 {
+    return s2_dit_sample_texts(d, stream, noise, condition, T, H, W, positive_text, Lt, negative_text, Lt, steps,
+                               cfg_scale, cfg_rescale, out);
+}
+
+extern "C" s2_status s2_dit_sample_texts(s2_dit *d, void *stream, const float *noise, const float *condition, int T,
+                                         int H, int W, const float *positive_text, int positive_len,
+                                         const float *negative_text, int negative_len, int steps, float cfg_scale,
+                                         float cfg_rescale, float *out)
+{
     s2::clear_error();
     const bool guide = cfg_scale != 1.0f;  // the engine runs the negative branch only then (engine.cpp:319)
-    if (!d || !noise || !condition || !positive_text || !out || T <= 0 || H <= 0 || W <= 0 || Lt <= 0 ||
-        steps <= 0 || (guide && !negative_text))
+    const int Lt = positive_len;
+    if (!d || !noise || !condition || !positive_text || !out || T <= 0 || H <= 0 || W <= 0 || positive_len <= 0 ||
+        steps <= 0 || (guide && (!negative_text || negative_len <= 0)))
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_sample: invalid arguments");
     if (d->vc != 2 * d->oc + 1)
         return s2::set_error(S2_UNSUPPORTED, "s2_dit_sample: video_channels %d != 2 * out_channels + 1", d->vc);
@@ -778,7 +788,7 @@ extern "C" s2_status s2_dit_sample(s2_dit *d, void *stream, const float *noise, 
         launches += d->last_launches + 1;
         float *factor = nullptr;
         if (guide) {
-            s = dit_forward_into(d, st, lat, T, H, W, negative_text, Lt, ts[i], nullptr, neg);
+            s = dit_forward_into(d, st, lat, T, H, W, negative_text, negative_len, ts[i], nullptr, neg);
             if (s != S2_OK) return s;
             launches += d->last_launches;
             if (rescale) {

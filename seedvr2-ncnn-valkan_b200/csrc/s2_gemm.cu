@@ -650,14 +650,15 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
 extern "C" s2_status s2_gemm(void *stream, const s2_gemm_desc *d, int *extra_launches)
 {
     s2::clear_error();
-    if (!d || !d->a || !d->b || d->M <= 0 || d->N <= 0 || d->K <= 0 || d->K % 64 != 0)
-        return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: NULL operand or bad shape (K must be a multiple of 64)");
+    if (!d || !d->a || !d->b || !d->err || d->M <= 0 || d->N <= 0 || d->K <= 0 || d->K % 64 != 0)
+        return s2::set_error(S2_INVALID_ARGUMENT,
+                             "s2_gemm: NULL operand or error word, or bad shape (K must be a multiple of 64)");
     if (d->epilogue != S2_GEMM_SPLIT_F16 && d->epilogue != S2_GEMM_GATED_RESID_F32 && d->epilogue != S2_GEMM_SWIGLU_F16)
         return s2::set_error(S2_UNSUPPORTED, "s2_gemm: unknown epilogue %d", d->epilogue);
-    if (d->epilogue == S2_GEMM_SPLIT_F16 && (d->split <= 0 || d->split % 8 != 0 || !d->out0 ||
+    if (d->epilogue == S2_GEMM_SPLIT_F16 && (d->split <= 0 || d->split % 32 != 0 || !d->out0 ||
                                              (d->N > d->split && !d->out1) || (d->N > 2 * d->split && !d->out2) ||
                                              d->N > 3 * d->split))
-        return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: split output needs split %% 8 == 0 and one buffer per part");
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: split output needs split %% 32 == 0 and one buffer per part");
     s2::GemmArgs g;
     g.M = d->M;
     g.N = d->N;

@@ -220,6 +220,10 @@ struct s2_attention_layer {
     s2_status build_plan(int Lt, cudaStream_t st)
     {
         if (plan_valid && plan_T == T && plan_H == H && plan_W == W && plan_Lt == Lt) return S2_OK;
+        // The tables below are overwritten by synchronous copies, which are not
+        // ordered after kernels still queued on a non-blocking stream: wait for
+        // the forwards that read the old plan (on whatever stream) first.
+        if (plan_valid) cudaDeviceSynchronize();
         plan_valid = false;
         slabs_valid = false;
         int count = 0;

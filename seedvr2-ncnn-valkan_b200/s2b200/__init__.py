@@ -165,6 +165,9 @@ _SIGS = {
     "s2_vae_attention_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_dit_sample": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp, _vp, ctypes.c_int, ctypes.c_int,
                                                                              ctypes.c_float, ctypes.c_float, _vp]),
+    "s2_dit_sample_texts": (ctypes.c_int, [_vp, _vp, _vp, _vp] + [ctypes.c_int] * 3
+                            + [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                               _vp]),
     "s2_sampler_timesteps": (ctypes.c_int, [ctypes.c_int, _f32p]),
     "s2_apply_cfg_workspace_bytes": (ctypes.c_size_t, []),
     "s2_apply_cfg": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_float, _vp, _vp]),
@@ -503,7 +506,10 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
 def gemm(epilogue, a, b, *, bias=None, gmul=None, resid=None, resid2=None, outs=(), y=None, y2=None, split=0,
          split_row=0, out_scale=1.0, workspace=None, err=None, stream=None) -> int:
     """s2_gemm: the block's InnerProduct on tcgen05 (a [M][K], b [N][K] fp16 CUDA
-    tensors). Returns the number of extra kernels launched (split-K finish)."""
+    tensors). Returns the number of extra kernels launched (split-K finish).
+    err: device int32 error word (a zeroed one is made when None)."""
+    if err is None:
+        err = _torch().zeros(1, dtype=_torch().int32, device=a.device)
     M, K = a.shape
     N = b.shape[0]
     o = list(outs) + [None] * (3 - len(outs))
@@ -611,10 +617,12 @@ class SeedVR2DiT:
         _, T, H, W = noise.shape
         if out is None:
             out = torch.empty_like(noise)
-        _check(lib().s2_dit_sample(self.handle, _stream_ptr(stream), _ptr(noise), _ptr(condition), T, H, W,
-                                   _ptr(positive_text), _ptr(negative_text), positive_text.shape[0], int(steps),
-                                   ctypes.c_float(cfg_scale), ctypes.c_float(cfg_rescale), _ptr(out)),
-               "s2_dit_sample")
+        neg_len = negative_text.shape[0] if negative_text is not None else 0
+        _check(lib().s2_dit_sample_texts(self.handle, _stream_ptr(stream), _ptr(noise), _ptr(condition), T, H, W,
+                                         _ptr(positive_text), positive_text.shape[0], _ptr(negative_text), neg_len,
+                                         int(steps), ctypes.c_float(cfg_scale), ctypes.c_float(cfg_rescale),
+                                         _ptr(out)),
+               "s2_dit_sample_texts")
         return out
 
     def set_comm(self, comm: "Comm | None"):

@@ -82,11 +82,14 @@ def test_make_condition(torch_cuda):
     assert np.array_equal(got.cpu().numpy(), oracle.SamplerPort(oracle.port().lib).make_condition(enc, noise, 0.1))
 
 
-@pytest.mark.parametrize("steps,cfg,rescale", [(1, 1.0, 0.0), (3, 1.0, 0.0), (2, 2.0, 0.0), (2, 3.0, 0.7)])
-def test_sample_vs_reference(torch_cuda, ref, steps, cfg, rescale):
+@pytest.mark.parametrize("steps,cfg,rescale,neg_len", [(1, 1.0, 0.0, 7), (3, 1.0, 0.0, 7), (2, 2.0, 0.0, 7),
+                                                       (2, 3.0, 0.7, 7), (2, 2.5, 0.5, 9)])
+def test_sample_vs_reference(torch_cuda, ref, steps, cfg, rescale, neg_len):
+    """neg_len != 7: the negative text has its own token count, as the
+    reference's default embeddings do (58 positive, 64 negative tokens)."""
     hp, wi, wo, bps, bws = build_case(4, 256, 2, 256, 256, four_block_flags)
     noise, cond, text = synth.dit_latents((2, 8, 10), 16, 7, 256)
-    neg_text = np.random.default_rng(5).standard_normal(text.shape).astype(np.float32)
+    neg_text = np.random.default_rng(5).standard_normal((neg_len, text.shape[1])).astype(np.float32)
     want = ref.sample(hp, wi, bps, bws, wo, noise, cond, text, neg_text if cfg != 1.0 else None, steps, cfg, rescale)
     m = make_model(4, 256, 2, 256, 256, wi, wo, bps, bws)
     dn, dc, dt, dnt = _dev(torch_cuda, noise, cond, text, neg_text)
