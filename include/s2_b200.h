@@ -504,6 +504,80 @@ S2_API s2_status s2_vae_attention_forward_host(s2_vae_attention *layer, void *st
 S2_API int s2_vae_attention_last_launches(const s2_vae_attention *layer);
 S2_API s2_status s2_vae_attention_device_error(s2_vae_attention *layer, int *code);
 
+/* ---- the VAE's other layers: GroupNorm, space-time shuffle, Conv3D ------- */
+
+/* All three work on ncnn 4-D blobs, fp32 [channels][cstep] whose channel
+ * plane holds frames x height x width values (x and y may have different
+ * csteps, each at least its plane); x and y must not alias. Device forwards
+ * are stream-ordered with no host synchronisation; the *_host variants copy
+ * packed host blobs [channels][plane] in and out and synchronise `stream`.
+ *
+ * DynamicFramewiseGroupNorm (src/layers/dynamic_framewise_group_norm.cpp):
+ * load_param :43-53 (channels from param key 10, a positive multiple of the
+ * 32 groups), load_model :55-61 (bias, then weight, [channels] each), forward
+ * :63-121 -- per frame and group of channels/32 channels, the mean and
+ * variance of its values (double sums), y = x * w / sqrt(var + 1e-6) +
+ * (b - mean * w / sqrt(var + 1e-6)). */
+typedef struct s2_vae_group_norm s2_vae_group_norm;
+S2_API s2_status s2_vae_group_norm_create(int device, int channels, s2_vae_group_norm **out);
+S2_API s2_status s2_vae_group_norm_destroy(s2_vae_group_norm *layer);
+S2_API s2_status s2_vae_group_norm_load(s2_vae_group_norm *layer, const float *bias, const float *weight);
+S2_API s2_status s2_vae_group_norm_forward(s2_vae_group_norm *layer, void *stream, const float *x, int frames,
+                                           int height, int width, long long cstep, float *y, long long y_cstep);
+S2_API s2_status s2_vae_group_norm_forward_host(s2_vae_group_norm *layer, void *stream, const float *x, int frames,
+                                                int height, int width, float *y);
+S2_API int s2_vae_group_norm_last_launches(const s2_vae_group_norm *layer);
+
+/* DynamicSpaceTimeShuffle (src/layers/dynamic_space_time_shuffle.cpp):
+ * load_param :41-55 (projected channels P from param key 10, in channels from
+ * key 11's [P, in]; P = in x 4 x temporal ratio), load_model :57-63 (bias [P],
+ * weight [P][in]), forward :65-130 -- a 1x1x1 projection whose channel
+ * ((oy * 2 + ox) * tr + ot) * in + c lands in output channel c at frame
+ * f * tr + ot (raw frame 1 dropped when tr > 1: T' = T * tr - 1), row
+ * 2 y + oy, column 2 x + ox. This build needs in channels % 32 == 0. */
+typedef struct s2_vae_space_time_shuffle s2_vae_space_time_shuffle;
+S2_API s2_status s2_vae_space_time_shuffle_create(int device, int in_channels, int projected_channels,
+                                                  s2_vae_space_time_shuffle **out);
+S2_API s2_status s2_vae_space_time_shuffle_destroy(s2_vae_space_time_shuffle *layer);
+S2_API s2_status s2_vae_space_time_shuffle_load(s2_vae_space_time_shuffle *layer, const float *bias,
+                                                const float *weight);
+S2_API s2_status s2_vae_space_time_shuffle_output_shape(const s2_vae_space_time_shuffle *layer, int frames, int height,
+                                                        int width, int *out_frames, int *out_height, int *out_width);
+S2_API s2_status s2_vae_space_time_shuffle_forward(s2_vae_space_time_shuffle *layer, void *stream, const float *x,
+                                                   int frames, int height, int width, long long cstep, float *y,
+                                                   long long y_cstep);
+S2_API s2_status s2_vae_space_time_shuffle_forward_host(s2_vae_space_time_shuffle *layer, void *stream,
+                                                        const float *x, int frames, int height, int width, float *y);
+S2_API int s2_vae_space_time_shuffle_last_launches(const s2_vae_space_time_shuffle *layer);
+S2_API s2_status s2_vae_space_time_shuffle_device_error(s2_vae_space_time_shuffle *layer, int *code);
+
+/* ncnn's Convolution3D as the VAE uses it (the layer the reference patches,
+ * patches/0001-feat-Convolution3D-Vulkan-pack1.patch): ParamDict fields of
+ * the layer -- num_output, kernel d/h/w, dilation, stride, pads (front, top,
+ * left, behind, bottom, right; all -233 = SAME_UPPER, all -234 = SAME_LOWER,
+ * resolved per input as :240-265), pad_value (0 in this build), bias_term;
+ * weights [out][in][kd][kh][kw] then bias [out]. out[p][z][i][j] = bias[p] +
+ * sum over q, kd, kh, kw of in[q][z sd + kd dd - front][i sh + kh dh -
+ * top][j sw + kw dw - left] * w[p][q][kd][kh][kw] (the patch's :17-25), as
+ * an implicit GEMM on tcgen05: fp16 operands, fp32 accumulation. This build
+ * needs stride_w <= 4. */
+typedef struct s2_vae_conv3d s2_vae_conv3d;
+S2_API s2_status s2_vae_conv3d_create(int device, int in_channels, int out_channels, int kernel_d, int kernel_h,
+                                      int kernel_w, int dilation_d, int dilation_h, int dilation_w, int stride_d,
+                                      int stride_h, int stride_w, int pad_front, int pad_top, int pad_left,
+                                      int pad_behind, int pad_bottom, int pad_right, float pad_value, int bias_term,
+                                      s2_vae_conv3d **out);
+S2_API s2_status s2_vae_conv3d_destroy(s2_vae_conv3d *layer);
+S2_API s2_status s2_vae_conv3d_load(s2_vae_conv3d *layer, const float *weight, const float *bias);
+S2_API s2_status s2_vae_conv3d_output_shape(const s2_vae_conv3d *layer, int frames, int height, int width,
+                                            int *out_frames, int *out_height, int *out_width);
+S2_API s2_status s2_vae_conv3d_forward(s2_vae_conv3d *layer, void *stream, const float *x, int frames, int height,
+                                       int width, long long cstep, float *y, long long y_cstep);
+S2_API s2_status s2_vae_conv3d_forward_host(s2_vae_conv3d *layer, void *stream, const float *x, int frames,
+                                            int height, int width, float *y);
+S2_API int s2_vae_conv3d_last_launches(const s2_vae_conv3d *layer);
+S2_API s2_status s2_vae_conv3d_device_error(s2_vae_conv3d *layer, int *code);
+
 /* ---- allocation-free variant -------------------------------------------- */
 
 /* Limits of the fixed scratch used by s2_dit_window_attention_noalloc

@@ -92,6 +92,58 @@ class Port(_Lib):
         L.s2o_vae_attention_tokens.argtypes = ([ctypes.c_int] * 4 + [_f32p] * 11 + [ctypes.c_int]
                                                + [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 2 + [_f32p])
 
+    def group_norm(self, x, bias, weight, threads=0):
+        """DynamicFramewiseGroupNorm on x [C, T, H, W]."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        y = np.zeros_like(x)
+        L = self.lib
+        L.s2o_group_norm.restype = ctypes.c_int
+        L.s2o_group_norm.argtypes = [ctypes.c_int] * 4 + [_f32p] * 3 + [ctypes.c_int, _f32p]
+        rc = L.s2o_group_norm(C, T, H, W, _ptr(_f32(bias)), _ptr(_f32(weight)), _ptr(x),
+                              int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"s2o_group_norm failed: {rc}")
+        return y
+
+    def space_time_shuffle(self, x, bias, weight, threads=0):
+        """DynamicSpaceTimeShuffle: x [Cin, T, H, W], weight [P, Cin] -> [Cin, T', 2H, 2W]."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        P = int(np.asarray(bias).size)
+        tr = P // C // 4
+        y = np.zeros((C, T * tr - 1 if tr > 1 else T, 2 * H, 2 * W), np.float32)
+        L = self.lib
+        L.s2o_space_time_shuffle.restype = ctypes.c_int
+        L.s2o_space_time_shuffle.argtypes = [ctypes.c_int] * 5 + [_f32p] * 3 + [ctypes.c_int, _f32p]
+        rc = L.s2o_space_time_shuffle(C, P, T, H, W, _ptr(_f32(bias)), _ptr(_f32(weight)), _ptr(x),
+                                      int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"s2o_space_time_shuffle failed: {rc}")
+        return y
+
+    def conv3d(self, x, weight, bias=None, stride=(1, 1, 1), dilation=(1, 1, 1), pad=(0, 0, 0, 0, 0, 0),
+               pad_value=0.0, threads=0):
+        """Convolution3D: x [Cin, T, H, W], weight [Cout, Cin, kd, kh, kw];
+        pad = (front, top, left, behind, bottom, right)."""
+        x = _f32(x)
+        weight = _f32(weight)
+        C, T, H, W = x.shape
+        Co, Ci, kd, kh, kw = weight.shape
+        assert Ci == C
+        L = self.lib
+        L.s2o_conv3d.restype = ctypes.c_int
+        L.s2o_conv3d.argtypes = ([ctypes.c_int] * 20 + [ctypes.c_float] + [_f32p] * 3 + [ctypes.c_int, _f32p]
+                                 + [_i32p] * 3)
+        od, oh, ow = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        args = [C, T, H, W, Co, kd, kh, kw, *stride, *dilation, *pad, ctypes.c_float(pad_value),
+                _ptr(None if bias is None else _f32(bias)), _ptr(weight), _ptr(x), int(threads or os.cpu_count() or 1)]
+        if L.s2o_conv3d(*args, None, ctypes.byref(od), ctypes.byref(oh), ctypes.byref(ow)) != 0:
+            raise ValueError("s2o_conv3d: bad arguments")
+        y = np.zeros((Co, od.value, oh.value, ow.value), np.float32)
+        L.s2o_conv3d(*args, _ptr(y), ctypes.byref(od), ctypes.byref(oh), ctypes.byref(ow))
+        return y
+
     def make_windows(self, T, H, W, shifted, override=(0, 0, 0)):
         n = self.lib.s2o_make_windows(T, H, W, int(shifted), *override, None, 0)
         out = np.zeros((max(n, 1), 6), dtype=np.int32)
@@ -328,6 +380,38 @@ class Ref(_Lib):
             latent = s.step_to(pred, latent, float(t), float(ts[i + 1])) if i + 1 < len(ts) else \
                 s.endpoint(pred, latent, float(t))
         return latent
+
+    def group_norm(self, x, bias, weight, threads=0):
+        """The reference's DynamicFramewiseGroupNorm on x [C, T, H, W]."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        y = np.zeros_like(x)
+        L = self.lib
+        L.ref_group_norm.restype = ctypes.c_int
+        L.ref_group_norm.argtypes = [ctypes.c_int] * 4 + [_f32p] * 3 + [ctypes.c_int, _f32p]
+        rc = L.ref_group_norm(C, T, H, W, _ptr(_f32(bias)), _ptr(_f32(weight)), _ptr(x),
+                              int(threads or os.cpu_count() or 1), _ptr(y))
+        if rc != 0:
+            raise ValueError(f"ref_group_norm failed: {rc}")
+        return y
+
+    def space_time_shuffle(self, x, bias, weight, threads=0):
+        """The reference's DynamicSpaceTimeShuffle: x [Cin, T, H, W], weight [P, Cin]."""
+        x = _f32(x)
+        C, T, H, W = x.shape
+        P = int(np.asarray(bias).size)
+        L = self.lib
+        L.ref_space_time_shuffle.restype = ctypes.c_int
+        L.ref_space_time_shuffle.argtypes = [ctypes.c_int] * 5 + [_f32p] * 3 + [ctypes.c_int, _f32p, _i32p]
+        of = ctypes.c_int(0)
+        tr = P // C // 4
+        y = np.zeros((C, T * tr - 1 if tr > 1 else T, 2 * H, 2 * W), np.float32)
+        rc = L.ref_space_time_shuffle(C, P, T, H, W, _ptr(_f32(bias)), _ptr(_f32(weight)), _ptr(x),
+                                      int(threads or os.cpu_count() or 1), _ptr(y), ctypes.byref(of))
+        if rc != 0:
+            raise ValueError(f"ref_space_time_shuffle failed: {rc}")
+        assert of.value == y.shape[1]
+        return y
 
     def vae_attention(self, x, weights_flat, threads=0):
         x = _f32(x)

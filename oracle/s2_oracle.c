@@ -484,3 +484,131 @@ void s2o_make_condition(const float *encoded, const float *noise, size_t n, floa
 {
     for (size_t i = 0; i < n; i++) output[i] = (1.0f - ratio) * encoded[i] + ratio * noise[i];
 }
+
+/* ---- VAE layers -------------------------------------------------------- */
+
+/* dynamic_framewise_group_norm.cpp:63-121: per (frame, group of C/32
+ * channels) double sums in channel-then-position order, mean and variance
+ * rounded to float as there, y = x * scale + offset without contraction. */
+int s2o_group_norm(int channels, int frames, int height, int width, const float *bias, const float *weight,
+                   const float *x, int num_threads, float *y)
+{
+    const int groups = 32;
+    if (channels <= 0 || channels % groups != 0 || frames <= 0 || height <= 0 || width <= 0) return -1;
+    const int cpg = channels / groups;
+    const size_t hw = (size_t)height * width, plane = hw * (size_t)frames;
+#pragma omp parallel for collapse(2) num_threads(num_threads > 0 ? num_threads : 1)
+    for (int f = 0; f < frames; f++)
+        for (int g = 0; g < groups; g++) {
+            double sum = 0.0, sq = 0.0;
+            for (int lc = 0; lc < cpg; lc++) {
+                const float *in = x + (size_t)(g * cpg + lc) * plane + (size_t)f * hw;
+                for (size_t i = 0; i < hw; i++) {
+                    const float v = in[i];
+                    sum += v;
+                    sq += (double)v * v;
+                }
+            }
+            const int count = cpg * (int)hw;
+            const float mean = (float)(sum / count);
+            const float var = (float)(sq / count - (double)mean * mean);
+            const float inv_std = 1.f / sqrtf((var > 0.f ? var : 0.f) + 1e-6f);
+            for (int lc = 0; lc < cpg; lc++) {
+                const int c = g * cpg + lc;
+                const float *in = x + (size_t)c * plane + (size_t)f * hw;
+                float *out = y + (size_t)c * plane + (size_t)f * hw;
+                const float scale = weight[c] * inv_std;
+                const float offset = bias[c] - mean * scale;
+                for (size_t i = 0; i < hw; i++) out[i] = in[i] * scale + offset;
+            }
+        }
+    return 0;
+}
+
+/* dynamic_space_time_shuffle.cpp:65-130: 1x1x1 projection accumulated in
+ * double from the bias, then projected channel
+ * ((oy * 2 + ox) * tr + ot) * Cin + c goes to output channel c at frame
+ * f * tr + ot (the duplicated raw frame 1 dropped when tr > 1), row
+ * 2 y + oy, column 2 x + ox. */
+int s2o_space_time_shuffle(int in_channels, int projected_channels, int frames, int height, int width,
+                           const float *bias, const float *weight, const float *x, int num_threads, float *y)
+{
+    const int sr = 2;
+    if (in_channels <= 0 || projected_channels % (in_channels * sr * sr) != 0) return -1;
+    const int tr = projected_channels / in_channels / (sr * sr);
+    if (tr <= 0) return -1;
+    const int out_frames = tr > 1 ? frames * tr - 1 : frames, ow = width * sr, oh = height * sr;
+    const size_t hw = (size_t)height * width, in_plane = hw * (size_t)frames;
+    const size_t out_plane = (size_t)ow * oh * (size_t)out_frames;
+#pragma omp parallel for num_threads(num_threads > 0 ? num_threads : 1)
+    for (int oc = 0; oc < in_channels; oc++)
+        for (int f = 0; f < frames; f++)
+            for (int yy = 0; yy < height; yy++)
+                for (int xx = 0; xx < width; xx++)
+                    for (int oy = 0; oy < sr; oy++)
+                        for (int ox = 0; ox < sr; ox++)
+                            for (int ot = 0; ot < tr; ot++) {
+                                const int p = ((oy * sr + ox) * tr + ot) * in_channels + oc;
+                                const int raw = f * tr + ot;
+                                if (tr > 1 && raw == 1) continue;
+                                const int of = tr > 1 && raw > 1 ? raw - 1 : raw;
+                                const float *wr = weight + (size_t)p * in_channels;
+                                double v = bias[p];
+                                for (int ic = 0; ic < in_channels; ic++)
+                                    v += (double)x[(size_t)ic * in_plane + (size_t)f * hw + (size_t)yy * width + xx] *
+                                         wr[ic];
+                                y[(size_t)oc * out_plane + (size_t)of * oh * ow + (size_t)(yy * sr + oy) * ow +
+                                  (size_t)(xx * sr + ox)] = (float)v;
+                            }
+    return 0;
+}
+
+/* Convolution3D (patch 0001 :17-25): out[p][z][i][j] = bias[p] + sum over
+ * input channels q, then taps (kd, kh, kw) in that order, of
+ * in[q][z*sd + kd*dd - pad_front][i*sh + kh*dh - pad_top][j*sw + kw*dw - pad_left]
+ * * weight[p][q][kd][kh][kw], out-of-range positions reading pad_value; fp32
+ * accumulation as the shader's afp sum. */
+int s2o_conv3d(int in_channels, int frames, int height, int width, int out_channels, int kd, int kh, int kw,
+               int sd, int sh, int sw, int dd, int dh, int dw, int pad_front, int pad_top, int pad_left,
+               int pad_behind, int pad_bottom, int pad_right, float pad_value, const float *bias,
+               const float *weight, const float *x, int num_threads, float *y, int *od, int *oh, int *ow)
+{
+    if (in_channels <= 0 || out_channels <= 0 || kd <= 0 || kh <= 0 || kw <= 0 || sd <= 0 || sh <= 0 || sw <= 0 ||
+        dd <= 0 || dh <= 0 || dw <= 0 || pad_front < 0 || pad_top < 0 || pad_left < 0 || pad_behind < 0 ||
+        pad_bottom < 0 || pad_right < 0)
+        return -1;
+    const int ed = dd * (kd - 1) + 1, eh = dh * (kh - 1) + 1, ew = dw * (kw - 1) + 1;
+    const int D = (frames + pad_front + pad_behind - ed) / sd + 1;
+    const int Hh = (height + pad_top + pad_bottom - eh) / sh + 1;
+    const int Ww = (width + pad_left + pad_right - ew) / sw + 1;
+    if (D <= 0 || Hh <= 0 || Ww <= 0) return -1;
+    if (od) *od = D;
+    if (oh) *oh = Hh;
+    if (ow) *ow = Ww;
+    if (!y) return 0;
+    const size_t in_plane = (size_t)frames * height * width, out_plane = (size_t)D * Hh * Ww;
+    const int maxk = kd * kh * kw;
+#pragma omp parallel for num_threads(num_threads > 0 ? num_threads : 1)
+    for (int p = 0; p < out_channels; p++)
+        for (int z = 0; z < D; z++)
+            for (int i = 0; i < Hh; i++)
+                for (int j = 0; j < Ww; j++) {
+                    float sum = bias ? bias[p] : 0.f;
+                    for (int q = 0; q < in_channels; q++) {
+                        const float *wq = weight + ((size_t)p * in_channels + q) * maxk;
+                        for (int a = 0; a < kd; a++)
+                            for (int b = 0; b < kh; b++)
+                                for (int c = 0; c < kw; c++) {
+                                    const int iz = z * sd + a * dd - pad_front;
+                                    const int ih = i * sh + b * dh - pad_top;
+                                    const int iw = j * sw + c * dw - pad_left;
+                                    float v = pad_value;
+                                    if (iz >= 0 && iz < frames && ih >= 0 && ih < height && iw >= 0 && iw < width)
+                                        v = x[(size_t)q * in_plane + ((size_t)iz * height + ih) * width + iw];
+                                    sum += v * wq[(a * kh + b) * kw + c];
+                                }
+                    }
+                    y[(size_t)p * out_plane + ((size_t)z * Hh + i) * Ww + j] = sum;
+                }
+    return 0;
+}

@@ -10,6 +10,15 @@
  *                            src/layers/dynamic_framewise_spatial_attention.cpp:79-210
  *   s2o_sampler_*         <- EulerSampler (timesteps, apply_cfg, step_to, endpoint)
  *                            src/model/sampler.cpp:19-62, 181-286
+ *   s2o_group_norm        <- DynamicFramewiseGroupNorm::forward
+ *                            src/layers/dynamic_framewise_group_norm.cpp:63-121
+ *   s2o_space_time_shuffle<- DynamicSpaceTimeShuffle::forward
+ *                            src/layers/dynamic_space_time_shuffle.cpp:65-130
+ *   s2o_conv3d            <- ncnn's Convolution3D as the reference patches it
+ *                            (patches/0001-feat-Convolution3D-Vulkan-pack1.patch:
+ *                            the shader's stated formula and loop order, :17-25,
+ *                            :87-127, SAME padding :240-265). ncnn itself is not
+ *                            vendored, so this one is a restatement only.
  *   s2o_condition_ratio / s2o_make_condition
  *                         <- transformed_condition_timestep / make_condition_latent
  *                            src/core/engine.cpp:79-121 (restated only: engine.cpp
@@ -90,6 +99,21 @@ void s2o_euler_step_to(const float *prediction, const float *current, size_t n, 
 void s2o_euler_endpoint(const float *prediction, const float *current, size_t n, float timestep, float *output);
 float s2o_condition_ratio(float noise_scale, int latent_frames, int latent_height, int latent_width);
 void s2o_make_condition(const float *encoded, const float *noise, size_t n, float ratio, float *output);
+
+/* VAE layers on [C][T][H][W] fp32 blobs (no cstep padding). */
+int s2o_group_norm(int channels, int frames, int height, int width, const float *bias, const float *weight,
+                   const float *x, int num_threads, float *y);
+/* y: [in_channels][T'][2H][2W], T' = T * tr - 1 when tr = projected / in / 4 > 1, else T. */
+int s2o_space_time_shuffle(int in_channels, int projected_channels, int frames, int height, int width,
+                           const float *bias, const float *weight, const float *x, int num_threads, float *y);
+/* Convolution3D: weight [out][in][kd][kh][kw], bias [out] or NULL; pads
+ * (front, top, left, behind, bottom, right) >= 0; out-of-range taps read
+ * pad_value. Returns the output extents in *od, *oh, *ow (y may be NULL to
+ * query them), or -1 on bad arguments. */
+int s2o_conv3d(int in_channels, int frames, int height, int width, int out_channels, int kd, int kh, int kw,
+               int sd, int sh, int sw, int dd, int dh, int dw, int pad_front, int pad_top, int pad_left,
+               int pad_behind, int pad_bottom, int pad_right, float pad_value, const float *bias,
+               const float *weight, const float *x, int num_threads, float *y, int *od, int *oh, int *ow);
 
 #ifdef __cplusplus
 }

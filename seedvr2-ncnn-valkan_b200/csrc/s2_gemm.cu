@@ -151,11 +151,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int tile = t / ks;
                 const int m0 = (tile / n_blocks) * kTileRows + static_cast<int>(rank) * kBM;
                 const int n0 = (tile % n_blocks) * kBN + static_cast<int>(rank) * T::kBRows;
+                // convolution: the tile's 128 rows are 4 runs of 32 output columns, each in
+                // one output row (owp is a multiple of 32); their input origins
+                int seg_w[4] = {0, 0, 0, 0}, seg_h[4] = {0, 0, 0, 0}, seg_d[4] = {0, 0, 0, 0};
+                if (!kPair && a.conv) {
+                    const s2::ConvGeom &g = a.geom;
+                    for (int sg = 0; sg < 4; ++sg) {
+                        const int pos = m0 + sg * 32, plane = g.oh * g.owp;
+                        const int z = pos / plane, rem = pos - z * plane, i = rem / g.owp, j0 = rem - i * g.owp;
+                        seg_w[sg] = j0 * g.sw - g.pl;
+                        seg_h[sg] = i * g.sh - g.pt;
+                        seg_d[sg] = z * g.sd - g.pf;
+                    }
+                }
                 for (int kc = kc_lo(t); kc < kc_hi(t); ++kc, ++p) {
                     const uint32_t s = p % kStages, u = p / kStages;
                     if (!(ok = mbar_wait(BAR(B_EMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_EMPTY))) break;
                     const uint32_t sa = base + s * kStageBytes;
-                    if constexpr (kPair) {
+                    if (!kPair && a.conv) {
+                        // tap (td, th, tw) and channel slice cs of this K slice
+                        const s2::ConvGeom &g = a.geom;
+                        const int tap = kc / g.cslices, cs = kc - tap * g.cslices;
+                        const int td = tap / (g.kh * g.kw), th = (tap / g.kw) % g.kh, tw = tap % g.kw;
+                        mbar_arrive_expect_tx(BAR(B_FULL + s), kStageBytes);
+#pragma unroll
+                        for (int sg = 0; sg < 4; ++sg)
+                            tma_load_4d(sa + sg * (kABytes / 4), &tmA, BAR(B_FULL + s), cs * kBK,
+                                        seg_w[sg] + tw * g.dw, seg_h[sg] + th * g.dh, seg_d[sg] + td * g.dd);
+                        tma_load_2d(sa + kABytes, &tmB, BAR(B_FULL + s), kc * kBK, n0);
+                    } else if constexpr (kPair) {
                         // both CTAs' slices are counted on rank 0's full barrier
                         if (rank == 0) mbar_arrive_expect_tx(BAR(B_FULL + s), 2 * kStageBytes);
                         const uint32_t fb = cluster_map(BAR(B_FULL + s), 0);
@@ -307,14 +331,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float res[32];
 #pragma unroll
                     for (int e = 0; e < 32; ++e)
-                        res[e] = (row_ok && n + e < a.n_valid) ? __ldg(a.resid + static_cast<size_t>(n + e) * a.ldt + row)
-                                                               : 0.f;
+                        res[e] = (a.resid && row_ok && n + e < a.n_valid)
+                                     ? __ldg(a.resid + static_cast<size_t>(n + e) * a.ldt + row)
+                                     : 0.f;
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int col = n + e;
                         if (row_ok && col < a.n_valid)
                             a.y[static_cast<size_t>(col) * a.ldt + row] =
                                 __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + res[e];
+                    }
+                } else if (a.epilogue == s2::GEMM_EPI_SHUFFLE_F32) {
+                    // the chunk's 32 columns share one (oy, ox, ot) offset (sh_cin % 32 == 0)
+                    const int q = n / a.sh_cin, c0 = n - q * a.sh_cin;
+                    const int ot = q % a.sh_tr, oxy = q / a.sh_tr, ox = oxy & 1, oy = oxy >> 1;
+                    const int hw = a.sh_h * a.sh_w;
+                    const int f = row / hw, yx = row - f * hw, yy = yx / a.sh_w, xx = yx - yy * a.sh_w;
+                    const int rawf = f * a.sh_tr + ot;
+                    const bool keep = row_ok && !(a.sh_tr > 1 && rawf == 1);
+                    const int of = (a.sh_tr > 1 && rawf > 1) ? rawf - 1 : rawf;
+                    const size_t pos = (static_cast<size_t>(of) * 2 * a.sh_h + 2 * yy + oy) * (2 * a.sh_w) + 2 * xx + ox;
+                    if (keep) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            a.y[static_cast<size_t>(c0 + e) * a.ldt + pos] =
+                                __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + n + e) : 0.f);
+                    }
+                } else if (a.epilogue == s2::GEMM_EPI_CONV_F32) {
+                    // output position of this row on the grid padded to owp columns
+                    const s2::ConvGeom &g = a.geom;
+                    const int plane = g.oh * g.owp;
+                    const int z = row / plane, rem = row - z * plane, i = rem / g.owp, j = rem - i * g.owp;
+                    if (row_ok && j < g.ow) {
+                        const size_t pos = (static_cast<size_t>(z) * g.oh + i) * g.ow + j;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (n + e < a.n_valid)
+                                a.y[static_cast<size_t>(n + e) * a.ldt + pos] =
+                                    __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + n + e) : 0.f);
                     }
                 } else if (a.epilogue == s2::GEMM_EPI_GATED_RESID_F32) {
                     // rows below the split (or all rows) leave by TMA store through the y map, which
@@ -477,6 +531,25 @@ bool make_map_2d(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t row
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The convolution input [D][H][W][cp] fp16 as a 4-D map (cp innermost): box
+// = 64 channels x (32 * sw) columns with element stride sw along W (32 output
+// columns' inputs), one row, one frame; 128B swizzle so that four boxes fill a
+// 128-row A stage exactly like one 2-D box. Out-of-range elements read zero.
+bool make_map_conv(CUtensorMap *map, const void *ptr, int cp, int W, int H, int D, int sw)
+{
+    auto encode = get_encode();
+    if (!encode) return false;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(cp), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                          static_cast<cuuint64_t>(D)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(cp) * 2, static_cast<cuuint64_t>(cp) * 2 * W,
+                             static_cast<cuuint64_t>(cp) * 2 * W * H};
+    cuuint32_t box[4] = {64, static_cast<cuuint32_t>(32 * sw), 1, 1};
+    cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(sw), 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map_2d_plain(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t rows, uint64_t row_bytes,
                        uint32_t box_inner, uint32_t box_rows)
 {
@@ -518,8 +591,18 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             if (!args.out[i] || (reinterpret_cast<uintptr_t>(args.out[i]) & 15u) != 0)
                 return set_error(S2_INVALID_ARGUMENT, "gemm: output %d missing or not 16-byte aligned", i);
     } else if (args.epilogue == GEMM_EPI_RESID_T_F32) {
-        if (!args.y || !args.resid || args.ldt < args.M || args.n_valid > args.N)
+        if (!args.y || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
+    } else if (args.epilogue == GEMM_EPI_SHUFFLE_F32) {
+        if (!args.y || args.sh_cin <= 0 || args.sh_cin % 32 != 0 || args.sh_tr <= 0 || args.sh_h <= 0 ||
+            args.sh_w <= 0 || args.N != 4 * args.sh_tr * args.sh_cin || args.M % (args.sh_h * args.sh_w) != 0)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad space-time shuffle output");
+    } else if (args.epilogue == GEMM_EPI_CONV_F32) {
+        const ConvGeom &g = args.geom;
+        if (!args.y || !args.conv || g.ow <= 0 || g.owp % 32 != 0 || g.owp < g.ow ||
+            args.M != g.od * g.oh * g.owp || args.n_valid > args.N ||
+            args.ldt < 1LL * g.od * g.oh * g.ow)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad convolution output");
     } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
         if (!args.y || args.N % 32 != 0 || (args.split_row > 0 && (!args.y2 || (args.resid && !args.resid2))) ||
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
@@ -553,15 +636,18 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     // 10-20 k rows (SwiGLU +7.6 %), but slower for short K (the VAE projections,
     // K = 512: -6 %) and a few thousand rows (-6 % on a 2.7 k-row QKV), so only
     // for M >= 4096 and K >= 1024. Needs N a multiple of 256.
-    bool pair = args.pair > 0 ||
-                (args.pair < 0 && bn == 256 && args.M >= 4096 && args.K >= 1024 && args.N % 256 == 0 && sms >= 2);
+    bool pair = !args.conv && (args.pair > 0 || (args.pair < 0 && bn == 256 && args.M >= 4096 && args.K >= 1024 &&
+                                                  args.N % 256 == 0 && sms >= 2));
     // Split-K for a few dozen rows (the text rows of a block): the tiles alone would
     // occupy a small part of the grid while each streams its whole weight slab; with
     // the K range split, up to 8 CTAs per tile stream it together (each split keeps
     // at least 4 K slices). Not for the channel-major epilogue (the VAE, many rows).
     int ks = 1;
     const long long tiles_k = mt * ((args.N + bn - 1) / bn);
-    if (args.partial && !pair && args.M <= kBM && args.epilogue != GEMM_EPI_RESID_T_F32 && tiles_k * 2 <= sms) {
+    if (args.partial && !pair && args.M <= kBM && !args.conv &&
+        (args.epilogue == GEMM_EPI_SPLIT_F16 || args.epilogue == GEMM_EPI_GATED_RESID_F32 ||
+         args.epilogue == GEMM_EPI_SWIGLU_F16) &&
+        tiles_k * 2 <= sms) {
         ks = static_cast<int>(std::min<long long>({8LL, sms / tiles_k, (args.K / kBK) / 4}));
         while (ks > 1 && static_cast<size_t>(ks) * args.M * args.N > args.partial_floats) --ks;
         if (ks < 2) ks = 1;
@@ -569,7 +655,19 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     if (pair && (bn != 256 || args.N % 256 != 0 || sms < 2))
         return set_error(S2_INVALID_ARGUMENT, "gemm: CTA pairs need 256-wide tiles and N %% 256 == 0 (N %d)", args.N);
     CUtensorMap ma, mb, mo[3];
-    if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM) ||
+    if (args.conv) {
+        // A: the convolution input [D][H][W][Cp] as a 4-D map, boxes of 64 channels x
+        // 32 output columns (element stride sw along W), 128B-swizzled like the 2-D A map
+        const ConvGeom &g = args.geom;
+        if (g.cslices <= 0 || args.K != g.cslices * kBK * g.kd * g.kh * g.kw || g.sw <= 0 || g.sw > 4 ||
+            ((reinterpret_cast<uintptr_t>(A)) & 15u) != 0)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad convolution geometry");
+        if (!make_map_conv(&ma, A, g.cslices * kBK, g.in_w, g.in_h, g.in_d, g.sw))
+            return set_error(S2_INFERENCE_FAILED, "gemm: convolution input tensor map failed");
+    } else if (!make_map_2d(&ma, A, args.K, args.M, static_cast<uint64_t>(args.K) * 2, kBK, kBM)) {
+        return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");
+    }
+    if (
         !make_map_2d(&mb, B, args.K, args.N, static_cast<uint64_t>(args.K) * 2, kBK,
                      static_cast<uint32_t>(pair ? bn / 2 : bn)))
         return set_error(S2_INFERENCE_FAILED, "gemm: cuTensorMapEncodeTiled failed");

@@ -29,7 +29,7 @@ enum GemmEpilogue : int {
     GEMM_EPI_SPLIT_F16 = 0,
     // fp32 channel-major output with residual: for n < n_valid,
     // y[n * ldt + row] = acc + bias[n] + resid[n * ldt + row] (1x1 conv back
-    // into an ncnn [C][cstep] blob).
+    // into an ncnn [C][cstep] blob; no residual when resid is null).
     GEMM_EPI_RESID_T_F32 = 1,
     // fp32 row-major output with the DiT block's gated residual
     // (apply_ada_output_and_residual, seedvr2_dit_block.cpp:807-825):
@@ -41,6 +41,31 @@ enum GemmEpilogue : int {
     // columns then the 128 matching "in" columns; out[0] is fp16
     // [row][N / 2], hidden column (n / 256) * 128 + j = silu(gate_j) * in_j.
     GEMM_EPI_SWIGLU_F16 = 3,
+    // Space-time shuffle (DynamicSpaceTimeShuffle, dynamic_space_time_shuffle.cpp:65-130):
+    // row = input token (f * sh_h + y) * sh_w + x, column p = ((oy * 2 + ox) * sh_tr + ot)
+    // * sh_cin + c; y[c * ldt + (t' * 2 sh_h + 2 y + oy) * 2 sh_w + 2 x + ox] = acc + bias[p]
+    // with t' = f * sh_tr + ot, less one past the dropped raw frame 1 when sh_tr > 1.
+    // Needs sh_cin % 32 == 0.
+    GEMM_EPI_SHUFFLE_F32 = 4,
+    // Convolution output: row = position (z * geom.oh + i) * geom.owp + j of the
+    // output grid padded to geom.owp columns; for j < geom.ow,
+    // y[n * ldt + (z * geom.oh + i) * geom.ow + j] = acc + bias[n] (n < n_valid).
+    GEMM_EPI_CONV_F32 = 5,
+};
+
+// Implicit-GEMM 3-D convolution: A is not a matrix but the im2col of a
+// token-major fp16 input [D][H][W][Cp] (Cp a multiple of 64) read through a
+// 4-D tensor map in boxes of 64 channels x 32 output columns; K slice kc is tap
+// kc / (Cp / 64) (taps in (kd, kh, kw) order) and channels 64 * (kc % (Cp / 64)).
+// Out-of-range taps read zeros (the TMA fill): zero padding.
+struct ConvGeom {
+    int od = 0, oh = 0, ow = 0, owp = 0;  // output extents; owp = ow rounded up to 32
+    int kd = 1, kh = 1, kw = 1;
+    int sd = 1, sh = 1, sw = 1;
+    int dd = 1, dh = 1, dw = 1;
+    int pf = 0, pt = 0, pl = 0;  // front / top / left padding
+    int cslices = 1;             // Cp / 64
+    int in_d = 0, in_h = 0, in_w = 0;  // input extents
 };
 
 struct GemmArgs {
@@ -72,10 +97,19 @@ struct GemmArgs {
     int ksplit = 0;
     int *extra_launches = nullptr;  // if set, incremented per kernel launched beyond the GEMM itself
     int32_t *err = nullptr;       // device error word (bounded waits)
+    int sh_cin = 0, sh_tr = 1, sh_h = 0, sh_w = 0;  // GEMM_EPI_SHUFFLE_F32 geometry
+    int conv = 0;                 // 1: A is the im2col of the convolution `geom`
+    ConvGeom geom;
 };
 
 // D[M][N] = A[M][K] B[N][K]^T on sm_100a: A and B fp16, K-major (row-major
 // with K contiguous, rows 16-byte aligned), fp32 accumulation in TMEM.
 s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs &args);
+
+// 3-D convolution as an implicit GEMM (args.conv = 1, args.geom set): A is the
+// token-major fp16 input [geom.in_d][geom.in_h][geom.in_w][Cp] (Cp = cslices *
+// 64, zero channels past the real ones), B the fp16 weights [N][taps * Cp]
+// (tap-major, K contiguous); args.M = od * oh * owp, args.K = taps * Cp,
+// args.epilogue = GEMM_EPI_CONV_F32. Same entry point: gemm_f16.
 
 }  // namespace s2

@@ -97,6 +97,19 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
         : "memory");
 }
 
+// 4-D tiled bulk tensor load global -> shared (c0 = innermost coordinate, which
+// must be 16-byte aligned; the outer coordinates may be negative or past the
+// extent, those elements are zero-filled). No multicast.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *tmap, uint32_t bar, int c0, int c1, int c2,
+                                            int c3)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 // 2-D tiled bulk tensor load global -> shared (c0 = innermost coordinate).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int c0, int c1)
 {

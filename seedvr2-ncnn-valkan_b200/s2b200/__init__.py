@@ -176,6 +176,32 @@ _SIGS = {
     "s2_condition_ratio": (ctypes.c_float, [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "s2_make_condition": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 4 + [ctypes.c_float, _vp]),
     "s2_gemm": (ctypes.c_int, [_vp, ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int)]),
+    "s2_vae_group_norm_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_vae_group_norm_destroy": (ctypes.c_int, [_vp]),
+    "s2_vae_group_norm_load": (ctypes.c_int, [_vp, _f32p, _f32p]),
+    "s2_vae_group_norm_forward": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3
+                                  + [ctypes.c_longlong, _vp, ctypes.c_longlong]),
+    "s2_vae_group_norm_forward_host": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp]),
+    "s2_vae_group_norm_last_launches": (ctypes.c_int, [_vp]),
+    "s2_vae_space_time_shuffle_create": (ctypes.c_int, [ctypes.c_int] * 3 + [ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_vae_space_time_shuffle_destroy": (ctypes.c_int, [_vp]),
+    "s2_vae_space_time_shuffle_load": (ctypes.c_int, [_vp, _f32p, _f32p]),
+    "s2_vae_space_time_shuffle_output_shape": (ctypes.c_int, [_vp] + [ctypes.c_int] * 3 + [_i32p] * 3),
+    "s2_vae_space_time_shuffle_forward": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3
+                                          + [ctypes.c_longlong, _vp, ctypes.c_longlong]),
+    "s2_vae_space_time_shuffle_forward_host": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp]),
+    "s2_vae_space_time_shuffle_last_launches": (ctypes.c_int, [_vp]),
+    "s2_vae_space_time_shuffle_device_error": (ctypes.c_int, [_vp, _i32p]),
+    "s2_vae_conv3d_create": (ctypes.c_int, [ctypes.c_int] * 18 + [ctypes.c_float, ctypes.c_int,
+                                                                  ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_vae_conv3d_destroy": (ctypes.c_int, [_vp]),
+    "s2_vae_conv3d_load": (ctypes.c_int, [_vp, _f32p, _f32p]),
+    "s2_vae_conv3d_output_shape": (ctypes.c_int, [_vp] + [ctypes.c_int] * 3 + [_i32p] * 3),
+    "s2_vae_conv3d_forward": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3
+                              + [ctypes.c_longlong, _vp, ctypes.c_longlong]),
+    "s2_vae_conv3d_forward_host": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp]),
+    "s2_vae_conv3d_last_launches": (ctypes.c_int, [_vp]),
+    "s2_vae_conv3d_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
@@ -911,3 +937,156 @@ class DynamicFramewiseSpatialAttention:
 
 def device_check(device: int = 0) -> int:
     return lib().s2_device_check(device)
+
+
+class _VaeLayer:
+    """Common plumbing of the VAE layers on ncnn 4-D blobs (fp32 [C, T, H, W])."""
+
+    _prefix = ""
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        self.handle = None
+        self._keep = ()
+
+    def _out_shape(self, T, H, W):
+        return T, H, W
+
+    def _out_channels(self):
+        raise NotImplementedError
+
+    def forward(self, x, y=None, stream=None):
+        """x: device fp32 [C, T, H, W] -> y [C_out, T', H', W'] (new tensor unless given)."""
+        torch = _torch()
+        C, T, H, W = x.shape
+        oT, oH, oW = self._out_shape(T, H, W)
+        if y is None:
+            y = torch.empty((self._out_channels(), oT, oH, oW), dtype=torch.float32, device=x.device)
+        _check(getattr(lib(), self._prefix + "_forward")(self.handle, _stream_ptr(stream), _ptr(x), T, H, W, T * H * W,
+                                                          _ptr(y), oT * oH * oW), self._prefix + "_forward")
+        return y
+
+    def forward_host(self, x: np.ndarray, stream=None) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        C, T, H, W = x.shape
+        oT, oH, oW = self._out_shape(T, H, W)
+        y = np.empty((self._out_channels(), oT, oH, oW), np.float32)
+        _check(getattr(lib(), self._prefix + "_forward_host")(
+            self.handle, _stream_ptr(stream) if stream is not None else None, ctypes.c_void_p(x.ctypes.data), T, H, W,
+            ctypes.c_void_p(y.ctypes.data)), self._prefix + "_forward_host")
+        return y
+
+    def last_launches(self) -> int:
+        return getattr(lib(), self._prefix + "_last_launches")(self.handle)
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            getattr(lib(), self._prefix + "_destroy")(self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DynamicFramewiseGroupNorm(_VaeLayer):
+    """The VAE's framewise GroupNorm (src/layers/dynamic_framewise_group_norm.cpp):
+    load_param(channels) (ParamDict key 10), load_model(bias, weight), forward."""
+
+    _prefix = "s2_vae_group_norm"
+
+    def load_param(self, channels: int):
+        h = ctypes.c_void_p()
+        _check(lib().s2_vae_group_norm_create(self.device, int(channels), ctypes.byref(h)), "s2_vae_group_norm_create")
+        self.close()
+        self.handle, self.channels = h, int(channels)
+        return S2_OK
+
+    def load_model(self, bias, weight):
+        b, w = (np.ascontiguousarray(a, np.float32).ravel() for a in (bias, weight))
+        _check(lib().s2_vae_group_norm_load(self.handle, b.ctypes.data_as(_f32p), w.ctypes.data_as(_f32p)),
+               "s2_vae_group_norm_load")
+        return S2_OK
+
+    def _out_channels(self):
+        return self.channels
+
+
+class DynamicSpaceTimeShuffle(_VaeLayer):
+    """The VAE decoder's space-time shuffle (src/layers/dynamic_space_time_shuffle.cpp):
+    load_param(in_channels, projected_channels) (ParamDict keys 11 and 10),
+    load_model(bias [P], weight [P, in]), forward -> [in, T', 2H, 2W]."""
+
+    _prefix = "s2_vae_space_time_shuffle"
+
+    def load_param(self, in_channels: int, projected_channels: int):
+        h = ctypes.c_void_p()
+        _check(lib().s2_vae_space_time_shuffle_create(self.device, int(in_channels), int(projected_channels),
+                                                      ctypes.byref(h)), "s2_vae_space_time_shuffle_create")
+        self.close()
+        self.handle, self.in_channels, self.projected = h, int(in_channels), int(projected_channels)
+        return S2_OK
+
+    def load_model(self, bias, weight):
+        b, w = (np.ascontiguousarray(a, np.float32).ravel() for a in (bias, weight))
+        _check(lib().s2_vae_space_time_shuffle_load(self.handle, b.ctypes.data_as(_f32p), w.ctypes.data_as(_f32p)),
+               "s2_vae_space_time_shuffle_load")
+        return S2_OK
+
+    def _out_shape(self, T, H, W):
+        o = [ctypes.c_int32(0) for _ in range(3)]
+        _check(lib().s2_vae_space_time_shuffle_output_shape(self.handle, T, H, W, *[ctypes.byref(v) for v in o]),
+               "s2_vae_space_time_shuffle_output_shape")
+        return tuple(v.value for v in o)
+
+    def _out_channels(self):
+        return self.in_channels
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_vae_space_time_shuffle_device_error(self.handle, ctypes.byref(code))
+        return code.value
+
+
+class Convolution3D(_VaeLayer):
+    """ncnn's Convolution3D as the VAE uses it (the layer the reference patches,
+    patches/0001-feat-Convolution3D-Vulkan-pack1.patch). load_param takes the
+    layer's ParamDict fields; load_model(weight [out, in, kd, kh, kw], bias)."""
+
+    _prefix = "s2_vae_conv3d"
+
+    def load_param(self, in_channels, num_output, kernel=(3, 3, 3), dilation=(1, 1, 1), stride=(1, 1, 1),
+                   pad=(0, 0, 0, 0, 0, 0), pad_value=0.0, bias_term=True):
+        """pad = (front, top, left, behind, bottom, right), or all -233 / -234 (SAME)."""
+        h = ctypes.c_void_p()
+        _check(lib().s2_vae_conv3d_create(self.device, int(in_channels), int(num_output), *map(int, kernel),
+                                          *map(int, dilation), *map(int, stride), *map(int, pad),
+                                          ctypes.c_float(pad_value), int(bool(bias_term)), ctypes.byref(h)),
+               "s2_vae_conv3d_create")
+        self.close()
+        self.handle, self.in_channels, self.num_output, self.bias_term = h, int(in_channels), int(num_output), bias_term
+        return S2_OK
+
+    def load_model(self, weight, bias=None):
+        w = np.ascontiguousarray(weight, np.float32).ravel()
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32).ravel()
+        _check(lib().s2_vae_conv3d_load(self.handle, w.ctypes.data_as(_f32p),
+                                        None if b is None else b.ctypes.data_as(_f32p)), "s2_vae_conv3d_load")
+        return S2_OK
+
+    def _out_shape(self, T, H, W):
+        o = [ctypes.c_int32(0) for _ in range(3)]
+        _check(lib().s2_vae_conv3d_output_shape(self.handle, T, H, W, *[ctypes.byref(v) for v in o]),
+               "s2_vae_conv3d_output_shape")
+        return tuple(v.value for v in o)
+
+    def _out_channels(self):
+        return self.num_output
+
+    def device_error(self) -> int:
+        code = ctypes.c_int32(0)
+        lib().s2_vae_conv3d_device_error(self.handle, ctypes.byref(code))
+        return code.value
+

@@ -102,3 +102,50 @@ def test_vae_token_subset_equals_full(port, i):
     for f in range(T):
         sel = np.arange(H * W)[::-1].copy()
         assert np.array_equal(port.vae_attention_tokens(x, w, f, sel), y[:, f].reshape(C, -1)[:, sel].T)
+
+
+# ---- the VAE's GroupNorm, space-time shuffle and Conv3D ----------------------
+
+@pytest.mark.parametrize("shape", [(32, 1, 4, 4), (64, 3, 10, 12), (96, 2, 5, 7)])
+def test_group_norm_restatement_matches_reference(port, ref, shape):
+    rng = np.random.default_rng(sum(shape))
+    x = (rng.standard_normal(shape) * 2 + 0.5).astype(np.float32)
+    b = rng.standard_normal(shape[0]).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(shape[0])).astype(np.float32)
+    assert np.array_equal(port.group_norm(x, b, w), ref.group_norm(x, b, w))
+
+
+@pytest.mark.parametrize("cin,tr,grid", [(32, 1, (1, 3, 5)), (64, 2, (3, 4, 6)), (32, 2, (1, 2, 2))])
+def test_space_time_shuffle_restatement_matches_reference(port, ref, cin, tr, grid):
+    rng = np.random.default_rng(cin + tr)
+    P = cin * 4 * tr
+    x = rng.standard_normal((cin,) + grid).astype(np.float32)
+    b = (0.02 * rng.standard_normal(P)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((P, cin))).astype(np.float32)
+    a, r = port.space_time_shuffle(x, b, w), ref.space_time_shuffle(x, b, w)
+    assert a.shape == (cin, grid[0] * tr - 1 if tr > 1 else grid[0], 2 * grid[1], 2 * grid[2])
+    assert np.array_equal(a, r)
+
+
+@pytest.mark.parametrize("case", [
+    dict(k=(3, 3, 3), s=(1, 1, 1), d=(1, 1, 1), p=(0, 1, 1, 0, 1, 1)),
+    dict(k=(3, 3, 3), s=(1, 2, 2), d=(1, 1, 1), p=(0, 1, 1, 0, 1, 1)),
+    dict(k=(1, 1, 1), s=(1, 1, 1), d=(1, 1, 1), p=(0, 0, 0, 0, 0, 0)),
+    dict(k=(3, 3, 3), s=(1, 1, 1), d=(1, 2, 2), p=(1, 2, 2, 1, 2, 2)),
+    dict(k=(2, 3, 1), s=(2, 1, 1), d=(1, 1, 1), p=(1, 0, 0, 0, 2, 0)),
+])
+def test_conv3d_restatement_matches_torch(port, case):
+    """The Convolution3D restatement (the formula of the reference's patch)
+    against PyTorch's conv3d on the same fp32 data, with explicit zero pads."""
+    import torch
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, 4, 9, 11)).astype(np.float32)
+    w = (0.2 * rng.standard_normal((6, 5) + case["k"])).astype(np.float32)
+    b = rng.standard_normal(6).astype(np.float32)
+    got = port.conv3d(x, w, b, stride=case["s"], dilation=case["d"], pad=case["p"])
+    pf, pt, pl, pb, pbo, pr = case["p"]
+    xp = np.pad(x, ((0, 0), (pf, pb), (pt, pbo), (pl, pr)))
+    want = torch.nn.functional.conv3d(torch.from_numpy(xp)[None].double(), torch.from_numpy(w).double(),
+                                      torch.from_numpy(b).double(), stride=case["s"], dilation=case["d"])[0].numpy()
+    assert got.shape == want.shape
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
