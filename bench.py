@@ -27,9 +27,18 @@ euler_step: the second half of the metric -- one full DiT Euler step
 vae_attention (N = 1): the VAE mid-block attention layer at config 4
             (C 512, 6 frames of 90x160) through s2_vae_attention_forward.
 
-Multi-GPU (torchrun): each rank processes its own clip's windows (weak
-scaling, no data-path collective). --shard instead splits ONE clip's windows
-across ranks (LPT by S_w^2) and all-reduces the text partial sums over NCCL.
+config3 (all N): BASELINE config 3, the 1080p x 45f ragged stress test
+            (12x67x120 = 96,480 tokens, 100 plain / 125 shifted windows):
+            one plain and one shifted attention layer per step through the
+            layer objects, sharded by window across the ranks at N > 1.
+vae_layers (N = 1): the VAE's GroupNorm, space-time shuffle and 3x3x3
+            Conv3D at the config-4 latent (512 channels, 6 x 90 x 160).
+
+Multi-GPU (torchrun): ONE clip's windows are split across the ranks (LPT by
+S_w^2, the north star's window sharding) and the text partial sums are
+all-reduced over NCCL after every layer: strong scaling of the headline
+stage, the config-3 stage and the Euler step. --weak instead gives each rank
+its own clip (weak scaling, no data-path collective).
 """
 from __future__ import annotations
 
@@ -276,7 +285,7 @@ def workload_config(args):
             "layers_per_step": 32, "grid": [6, 45, 80], "heads": 20, "head_dim": 128, "text_len": 58,
             "mode": args.mode, "io": "fp16 QKV in, fp16 out" if args.mode == "f16" else "fp16 QKV in, bf16 out",
             "l2": "no flush: every layer reads a distinct >L2 input (332 MB QKV, 356 MB packed Q/K/V)",
-            "sharding": "window-sharded single clip + NCCL text all-reduce" if args.shard else
+            "sharding": "window-sharded single clip + NCCL text all-reduce (strong)" if args.shard else
                         "one clip per rank (weak)"}
 
 
@@ -441,10 +450,13 @@ def run_ours(args, rank, world, local_rank):
                       step_flops_all, dist)
 
     extra = {}
+    if not args.no_cfg3:
+        extra["config3"] = run_cfg3(args, torch, s2b200, synth, dev, rank, world, dist)
     if not args.no_euler:
         extra["euler_step"] = run_euler(args, torch, s2b200, synth, dev, rank, world, dist)
     if world == 1 and not args.no_vae:
         extra["vae_attention"] = run_vae(args, torch, s2b200, synth, dev)
+        extra["vae_layers"] = run_vae_layers(args, torch, s2b200, synth, dev)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -622,6 +634,153 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
             "clocks": clk.summary(), **({"cpu_reference": cpu_ref} if cpu_ref else {})}
 
 
+def run_cfg3(args, torch, s2b200, synth, dev, rank, world, dist):
+    """the 1080p x 45f ragged shifted-window stress test, one
+    plain and one shifted attention layer per step (prologue, attention, text
+    mean through s2_attention_layer_forward), fp16 QKV in, fp16 out. At N > 1
+    each layer's windows are split across the ranks by LPT on S_w^2 and the
+    text partial sums are all-reduced (strong scaling); value = all ranks'
+    algorithmic FLOPs / max-over-ranks device time."""
+    grid = synth.GRIDS["cfg3"]
+    T, H, W = grid
+    heads, Lt, dim = 20, 58, 2560
+    mode = s2b200.MODE_F16 if args.mode == "f16" else s2b200.MODE_BF16_REF
+    vid, txt, gam, fr = synth.layer_inputs(grid, heads=heads, text_len=Lt, seed=77)
+    v = torch.from_numpy(vid).to(dev, torch.float16)
+    t = torch.from_numpy(txt).to(dev, torch.float16)
+    del vid
+    layers, flops = [], 0.0
+    for shifted in (0, 1):
+        wins = s2b200.make_windows(T, H, W, shifted)
+        lay = s2b200.SeedVR2DiTBlockAttention(device=dev.index, mode=mode)
+        lay.load_param(shifted=shifted, dim=dim, heads=heads)
+        lay.load_model(gam[0], gam[1], fr, gam[2], gam[3])
+        lay.set_runtime_shape(T, H, W)
+        ids = np.arange(len(wins))
+        if world > 1:
+            ids = s2b200.shard_windows(wins, Lt, world)[rank]
+            lay.set_window_subset(ids)
+        flops += synth.attention_flops(wins[ids], Lt, heads)
+        layers.append(lay)
+    vo = torch.zeros((T * H * W, dim), dtype=s2b200.mode_dtype(mode), device=dev)
+    to = torch.empty((Lt, dim), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for lay in layers:
+            lay.forward(v, t, vo, to, stream=stream)
+            if dist:
+                dist.all_reduce(to)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(1, args.cfg3_steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        for _ in range(2):
+            step()
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for lay in layers:
+        if lay.device_error() != 0:
+            raise RuntimeError("config-3 attention device error")
+    tot = torch.tensor([ms, flops], dtype=torch.float64, device=dev)
+    if dist:
+        ms_t = tot[:1].clone()
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        fl = tot[1:].clone()
+        dist.all_reduce(fl)
+        ms, flops = float(ms_t.item()), float(fl.item())
+    for lay in layers:
+        lay.close()
+    return {"workload": "config 3: 1080p x 45f, grid 12x67x120 = 96,480 tokens, 20 heads x 128, 58 text tokens, "
+                        "reference windows 3x15x27 (100 plain / 125 shifted); one plain + one shifted layer per step",
+            "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "tflop_per_step": flops / 1e12, "n_gpus": world,
+            "scaling": "strong (windows split across ranks, NCCL text all-reduce)" if world > 1 else "one GPU",
+            "gpu_launches_per_step": 6, "clocks": clk.summary()}
+
+
+def run_vae_layers(args, torch, s2b200, synth, dev):
+    """The VAE's GroupNorm, space-time shuffle (512 -> 4096 channels, temporal
+    ratio 2) and 3x3x3 Conv3D (512 -> 512, causal: two replicated leading
+    frames) at the config-4 latent, 512 x 6 x 90 x 160; device ms per forward,
+    achieved HBM bandwidth (GroupNorm: read x once, write y once) and tensor
+    throughput (2 x MACs)."""
+    C, T, H, W = synth.VAE_CFG4
+    rng = np.random.default_rng(3)
+    x = torch.randn((C, T, H, W), device=dev)
+    stream = torch.cuda.current_stream()
+    peaks, _ = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    steps = max(1, args.vae_steps)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    out = {}
+    gn = s2b200.DynamicFramewiseGroupNorm(device=dev.index)
+    gn.load_param(C)
+    gn.load_model(rng.standard_normal(C).astype(np.float32) * 0.1, 1 + 0.1 * rng.standard_normal(C).astype(np.float32))
+    y = torch.empty_like(x)
+    ms = timed(lambda: gn.forward(x, y, stream=stream))
+    algo = 2 * x.numel() * 4
+    out["group_norm"] = {"ms": ms, "gbs": algo / (ms * 1e-3) / 1e9, "hbm_frac": algo / (ms * 1e-3) / 1e9 / hbm,
+                         "algorithmic_bytes": algo, "launches": gn.last_launches()}
+    gn.close()
+    del y
+    P = C * 8
+    st = s2b200.DynamicSpaceTimeShuffle(device=dev.index)
+    st.load_param(C, P)
+    st.load_model(rng.standard_normal(P).astype(np.float32) * 0.02,
+                  (rng.standard_normal((P, C)) / np.sqrt(C)).astype(np.float32))
+    ys = torch.empty((C, 2 * T - 1, 2 * H, 2 * W), device=dev)
+    ms = timed(lambda: st.forward(x, ys, stream=stream))
+    fl = 2.0 * T * H * W * P * C
+    algo = x.numel() * 4 + ys.numel() * 4
+    out["space_time_shuffle"] = {"ms": ms, "tflops": fl / (ms * 1e-3) / 1e12, "gbs": algo / (ms * 1e-3) / 1e9,
+                                 "hbm_frac": algo / (ms * 1e-3) / 1e9 / hbm, "launches": st.last_launches(),
+                                 "shape": f"{C} x {T}x{H}x{W} -> {C} x {2 * T - 1}x{2 * H}x{2 * W}"}
+    if st.device_error() != 0:
+        raise RuntimeError("space-time shuffle device error")
+    st.close()
+    del ys
+    cv = s2b200.Convolution3D(device=dev.index)
+    cv.load_param(C, C, kernel=(3, 3, 3), pad=(0, 1, 1, 0, 1, 1))
+    cv.load_model((rng.standard_normal((C, C, 3, 3, 3)) / np.sqrt(27 * C)).astype(np.float32),
+                  rng.standard_normal(C).astype(np.float32) * 0.02)
+    xc = torch.randn((C, T + 2, H, W), device=dev)
+    yc = torch.empty((C, T, H, W), device=dev)
+    ms = timed(lambda: cv.forward(xc, yc, stream=stream))
+    fl = 2.0 * T * H * W * C * C * 27
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    out["conv3d"] = {"ms": ms, "tflops": fl / (ms * 1e-3) / 1e12, "frac_of_peak": fl / (ms * 1e-3) / 1e12 / peak,
+                     "tflop": fl / 1e12, "launches": cv.last_launches(),
+                     "shape": f"{C} -> {C}, 3x3x3, input {T + 2}x{H}x{W} (causal pad), output {T}x{H}x{W}"}
+    if cv.device_error() != 0:
+        raise RuntimeError("conv3d device error")
+    cv.close()
+    out["workload"] = "VAE layers at the config-4 latent: 512 channels x 6 frames x 90 x 160"
+    return out
+
+
 def run_vae(args, torch, s2b200, synth, dev):
     """VAE mid-block attention (config 4) on this GPU; returns a dict."""
     shape = synth.VAE_CFG4
@@ -686,7 +845,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["f16", "bf16"], default="f16")
     ap.add_argument("--override", action="store_true", help="BASELINE.json's 6x15x20 windows")
-    ap.add_argument("--shard", action="store_true", help="split one clip's windows across ranks")
+    ap.add_argument("--shard", action="store_true",
+                    help="split one clip's windows across ranks (the default when N > 1)")
+    ap.add_argument("--weak", action="store_true", help="N > 1: one clip per rank instead (weak scaling)")
+    ap.add_argument("--no-cfg3", action="store_true", help="skip the config-3 (1080p) stage")
+    ap.add_argument("--cfg3-steps", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -700,6 +863,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not args.weak:
+        args.shard = True
+    if args.weak:
+        args.shard = False
     if args.impl == "reference":
         run_reference_arm(args, rank)
         return
