@@ -342,20 +342,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + col) : 0.f) + res[e];
                     }
                 } else if (a.epilogue == s2::GEMM_EPI_SHUFFLE_F32) {
-                    // the chunk's 32 columns share one (oy, ox, ot) offset (sh_cin % 32 == 0)
-                    const int q = n / a.sh_cin, c0 = n - q * a.sh_cin;
-                    const int ot = q % a.sh_tr, oxy = q / a.sh_tr, ox = oxy & 1, oy = oxy >> 1;
+                    // columns in (oy, ot, c, ox) order, ox innermost: the chunk holds the (ox = 0, 1)
+                    // pairs of 16 channels with one (oy, ot), so each thread writes 16 float2 and a
+                    // warp's 32 tokens fill 256 contiguous bytes of each output row
+                    const int pair0 = n >> 1;
+                    const int q = pair0 / a.sh_cin, c0 = pair0 - q * a.sh_cin;
+                    const int oy = q / a.sh_tr, ot = q - oy * a.sh_tr;
                     const int hw = a.sh_h * a.sh_w;
                     const int f = row / hw, yx = row - f * hw, yy = yx / a.sh_w, xx = yx - yy * a.sh_w;
                     const int rawf = f * a.sh_tr + ot;
                     const bool keep = row_ok && !(a.sh_tr > 1 && rawf == 1);
                     const int of = (a.sh_tr > 1 && rawf > 1) ? rawf - 1 : rawf;
-                    const size_t pos = (static_cast<size_t>(of) * 2 * a.sh_h + 2 * yy + oy) * (2 * a.sh_w) + 2 * xx + ox;
+                    const size_t pos = (static_cast<size_t>(of) * 2 * a.sh_h + 2 * yy + oy) * (2 * a.sh_w) + 2 * xx;
                     if (keep) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            a.y[static_cast<size_t>(c0 + e) * a.ldt + pos] =
-                                __uint_as_float(r[e]) + (a.bias ? __ldg(a.bias + n + e) : 0.f);
+                        for (int k = 0; k < 16; ++k) {
+                            float2 v;
+                            v.x = __uint_as_float(r[2 * k]) + (a.bias ? __ldg(a.bias + n + 2 * k) : 0.f);
+                            v.y = __uint_as_float(r[2 * k + 1]) + (a.bias ? __ldg(a.bias + n + 2 * k + 1) : 0.f);
+                            *reinterpret_cast<float2 *>(a.y + static_cast<size_t>(c0 + k) * a.ldt + pos) = v;
+                        }
                     }
                 } else if (a.epilogue == s2::GEMM_EPI_CONV_F32) {
                     // output position of this row on the grid padded to owp columns
@@ -594,8 +600,9 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
         if (!args.y || args.ldt < args.M || args.n_valid > args.N)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad channel-major output");
     } else if (args.epilogue == GEMM_EPI_SHUFFLE_F32) {
-        if (!args.y || args.sh_cin <= 0 || args.sh_cin % 32 != 0 || args.sh_tr <= 0 || args.sh_h <= 0 ||
-            args.sh_w <= 0 || args.N != 4 * args.sh_tr * args.sh_cin || args.M % (args.sh_h * args.sh_w) != 0)
+        if (!args.y || args.sh_cin <= 0 || args.sh_cin % 16 != 0 || args.sh_tr <= 0 || args.sh_h <= 0 ||
+            args.sh_w <= 0 || args.N != 4 * args.sh_tr * args.sh_cin || args.M % (args.sh_h * args.sh_w) != 0 ||
+            args.ldt % 2 != 0 || (reinterpret_cast<uintptr_t>(args.y) & 7u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad space-time shuffle output");
     } else if (args.epilogue == GEMM_EPI_CONV_F32) {
         const ConvGeom &g = args.geom;

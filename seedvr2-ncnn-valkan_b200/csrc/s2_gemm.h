@@ -42,10 +42,11 @@ enum GemmEpilogue : int {
     // [row][N / 2], hidden column (n / 256) * 128 + j = silu(gate_j) * in_j.
     GEMM_EPI_SWIGLU_F16 = 3,
     // Space-time shuffle (DynamicSpaceTimeShuffle, dynamic_space_time_shuffle.cpp:65-130):
-    // row = input token (f * sh_h + y) * sh_w + x, column p = ((oy * 2 + ox) * sh_tr + ot)
-    // * sh_cin + c; y[c * ldt + (t' * 2 sh_h + 2 y + oy) * 2 sh_w + 2 x + ox] = acc + bias[p]
-    // with t' = f * sh_tr + ot, less one past the dropped raw frame 1 when sh_tr > 1.
-    // Needs sh_cin % 32 == 0.
+    // row = input token (f * sh_h + y) * sh_w + x, column n = ((oy * sh_tr + ot) * sh_cin
+    // + c) * 2 + ox (the projected channels permuted so that ox is innermost);
+    // y[c * ldt + (t' * 2 sh_h + 2 y + oy) * 2 sh_w + 2 x + ox] = acc + bias[n] with
+    // t' = f * sh_tr + ot, less one past the dropped raw frame 1 when sh_tr > 1.
+    // Needs sh_cin % 16 == 0, ldt even and y 8-byte aligned (float2 stores).
     GEMM_EPI_SHUFFLE_F32 = 4,
     // Convolution output: row = position (z * geom.oh + i) * geom.owp + j of the
     // output grid padded to geom.owp columns; for j < geom.ow,

@@ -129,6 +129,14 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int
                  "r"(src), "r"(c0), "r"(c1)
                  : "memory");
 }
+// Untiled bulk copy shared -> global of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned), tracked in this thread's bulk async group.
+__device__ __forceinline__ void bulk_store(void *gdst, uint32_t ssrc, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+                 "r"(ssrc), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N bulk groups of this thread still read their shared-memory source.
 template <int N>

@@ -380,8 +380,19 @@ extern "C" s2_status s2_vae_space_time_shuffle_load(s2_vae_space_time_shuffle *l
     s2::clear_error();
     if (!l || !bias || !weight) return s2::set_error(S2_INVALID_ARGUMENT, "s2_vae_space_time_shuffle_load: NULL argument");
     s2::DeviceGuard guard(l->device);
-    // load_model (:57-63): bias [P], then weight [P][Cin]
-    if (!upload_f32(l->bias, bias, l->proj) || !upload_f16(l->w16, weight, l->proj, l->cin, l->cpad, [](int j) { return j; }))
+    // load_model (:57-63): bias [P], then weight [P][Cin]. The projected channel
+    // p = ((oy * 2 + ox) * tr + ot) * Cin + c becomes GEMM column
+    // ((oy * tr + ot) * Cin + c) * 2 + ox, so that the epilogue writes (ox = 0, 1) pairs.
+    const int cin = l->cin, tr = l->tr, P = l->proj;
+    std::vector<float> wp(static_cast<size_t>(P) * cin), bp(P);
+    for (int p = 0; p < P; ++p) {
+        const int c = p % cin, t = p / cin, ot = t % tr, oxy = t / tr, ox = oxy & 1, oy = oxy >> 1;
+        const int n = ((oy * tr + ot) * cin + c) * 2 + ox;
+        bp[n] = bias[p];
+        std::copy(weight + static_cast<size_t>(p) * cin, weight + static_cast<size_t>(p + 1) * cin,
+                  wp.begin() + static_cast<size_t>(n) * cin);
+    }
+    if (!upload_f32(l->bias, bp.data(), P) || !upload_f16(l->w16, wp.data(), P, cin, l->cpad, [](int j) { return j; }))
         return s2::set_error(S2_OUT_OF_MEMORY, "s2_vae_space_time_shuffle_load: upload failed");
     l->loaded = true;
     return S2_OK;
@@ -408,8 +419,9 @@ extern "C" s2_status s2_vae_space_time_shuffle_forward(s2_vae_space_time_shuffle
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_vae_space_time_shuffle_forward: invalid arguments");
     const long long tokens = 1LL * frames * height * width;
     const int of = l->tr > 1 ? frames * l->tr - 1 : frames;
-    if (cstep < tokens || y_cstep < 4LL * of * height * width || tokens > (1LL << 30))
-        return s2::set_error(S2_INVALID_ARGUMENT, "s2_vae_space_time_shuffle_forward: bad cstep");
+    if (cstep < tokens || y_cstep < 4LL * of * height * width || tokens > (1LL << 30) || y_cstep % 2 != 0 ||
+        (reinterpret_cast<uintptr_t>(y) & 7u) != 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_vae_space_time_shuffle_forward: bad cstep or unaligned y");
     if (!l->loaded) return s2::set_error(S2_NOT_LOADED, "s2_vae_space_time_shuffle_forward: weights not loaded");
     s2::DeviceGuard guard(l->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
