@@ -320,6 +320,19 @@ S2_API s2_status s2_gemm(void *stream, const s2_gemm_desc *desc, int *extra_laun
 typedef struct s2_comm s2_comm;
 S2_API s2_status s2_comm_unique_id(char *id /* [S2_COMM_ID_BYTES] */);
 S2_API s2_status s2_comm_init(int device, int nranks, int rank, const char *id, s2_comm **out);
+/* The same with an explicit deadline (s2_comm_init uses $S2_COMM_TIMEOUT_MS,
+ * else 300 s): the ranks' rendezvous runs on a non-blocking NCCL communicator
+ * polled against the deadline, so a rank that never joins ends in
+ * ncclCommAbort and S2_INFERENCE_FAILED instead of blocking the host. Every
+ * later NCCL call's result and the communicator's asynchronous state are
+ * checked; after an abort the communicator refuses further work (destroy it). */
+S2_API s2_status s2_comm_init_timeout(int device, int nranks, int rank, const char *id, long long timeout_ms,
+                                      s2_comm **out);
+S2_API s2_status s2_comm_set_timeout(s2_comm *comm, long long timeout_ms);
+/* Waits on the host for `stream` (which holds this communicator's collectives)
+ * under the same watchdog: returns S2_OK when the stream's work finished, or
+ * aborts the communicator on an asynchronous NCCL error or at the deadline. */
+S2_API s2_status s2_comm_wait(s2_comm *comm, void *stream);
 S2_API s2_status s2_comm_destroy(s2_comm *comm);
 S2_API int s2_comm_size(const s2_comm *comm);
 S2_API int s2_comm_rank(const s2_comm *comm);
@@ -613,6 +626,21 @@ S2_API s2_status s2_dit_window_attention_noalloc(void *stream, s2_mode mode,
                                                  int heads, float eps, int shifted, int wt, int wh, int ww,
                                                  const float *gammas, const float *freqs21,
                                                  void *vid_out, float *txt_out, int32_t *err);
+
+/* ---- failure injection (tests only; no counterpart in the reference) ----- */
+
+/* The next n device allocations made by this library's layer objects fail as
+ * if the GPU were out of memory (their calls return S2_OUT_OF_MEMORY); 0 clears
+ * it. For exercising callers' out-of-memory paths. */
+S2_API s2_status s2_debug_fail_allocations(int n);
+/* One shot, for the next s2_window_attention launch in the process (layer
+ * forwards included): every bounded wait of that launch gives up after
+ * wait_ns (0 = the default 1 s), and with skip_k_tile >= 0 the load producer of
+ * its first CTA leaves out that K tile (counted from the CTA's first), so the
+ * tensor-core role's wait for it runs out. The launch then ends on its own with
+ * its error word set to 2 (the layer's device-error query returns
+ * S2_INFERENCE_FAILED) and frees its TMEM; launches after it are unaffected. */
+S2_API s2_status s2_debug_attention_fault(int skip_k_tile, unsigned long long wait_ns);
 
 /* ---- misc ---------------------------------------------------------------- */
 

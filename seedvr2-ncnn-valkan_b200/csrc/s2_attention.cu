@@ -118,6 +118,8 @@ struct AttnArgs {
     int text_len;
     int n_items;      // n_work * heads
     float scale_log2;
+    unsigned long long wait_ns;  // limit of every bounded wait
+    int skip_k;        // failure injection (tests): CTA 0's producer skips this K tile (-1: none)
 };
 
 // One (window, q-block, head) work item.
@@ -197,10 +199,10 @@ __device__ __forceinline__ uint32_t pack_out(float a, float b)
 }
 
 // Wait that ignores the abort flag (used only to drain in-flight async work).
-__device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *err)
+__device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity, int *err, uint64_t timeout_ns)
 {
     int dummy = 0;
-    return mbar_wait(bar, parity, &dummy, err, E_DRAIN);
+    return mbar_wait(bar, parity, &dummy, err, E_DRAIN, timeout_ns);
 }
 
 // Persistent: CTA b processes items b, b + gridDim.x, ... of the cost-ordered
@@ -248,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmV);
             uint32_t nq[kQT] = {0, 0};   // Q_i loads issued
             uint32_t kv = 0;             // K/V tiles issued (ring position)
+            uint32_t k_skipped = 0xffffffffu;  // ring position of a K load left out (failure injection)
             bool ok = true;
             ItemPrefetch pf_next = prefetch_item(a, blockIdx.x, load_work(a, blockIdx.x));
             int w_next = load_work(a, blockIdx.x + gridDim.x);
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pf_next = prefetch_item(a, t + gridDim.x, w_next);
                 w_next = load_work(a, t + 2 * gridDim.x);
                 for (int i = 0; i < it.n_q; ++i) {
-                    if (!(ok = mbar_wait(BAR(B_QEMPTY + i), (nq[i] & 1u) ^ 1u, abort, a.err, E_WAIT_Q))) break;
+                    if (!(ok = mbar_wait(BAR(B_QEMPTY + i), (nq[i] & 1u) ^ 1u, abort, a.err, E_WAIT_Q, a.wait_ns))) break;
                     const int row_q = it.seq0 + it.q0 + i * kBM;
                     mbar_arrive_expect_tx(BAR(B_QFULL + i), kTileBytes);
                     tma_load_3d(sQ + i * kTileBytes, &tmQ, BAR(B_QFULL + i), 0, row_q, it.head);
@@ -266,11 +269,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; ok && j < it.n_kv; ++j, ++kv) {
                     const uint32_t s = kv & 1u, u = kv >> 1;
                     const int row_kv = it.seq0 + j * kBN;
-                    if (!(ok = mbar_wait(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K))) break;
-                    mbar_arrive_expect_tx(BAR(B_KFULL + s), kTileBytes);
-                    tma_load_3d(sK + s * kTileBytes, &tmK, BAR(B_KFULL + s), 0, row_kv, it.head);
-                    tma_load_3d(sK + s * kTileBytes + kBoxBytes, &tmK, BAR(B_KFULL + s), 64, row_kv, it.head);
-                    if (!(ok = mbar_wait(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V))) {
+                    if (!(ok = mbar_wait(BAR(B_KEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_K, a.wait_ns))) break;
+                    if (blockIdx.x == 0 && static_cast<int>(kv) == a.skip_k) {
+                        k_skipped = kv;  // injected failure: this K tile never arrives
+                    } else {
+                        mbar_arrive_expect_tx(BAR(B_KFULL + s), kTileBytes);
+                        tma_load_3d(sK + s * kTileBytes, &tmK, BAR(B_KFULL + s), 0, row_kv, it.head);
+                        tma_load_3d(sK + s * kTileBytes + kBoxBytes, &tmK, BAR(B_KFULL + s), 64, row_kv, it.head);
+                    }
+                    if (!(ok = mbar_wait(BAR(B_VEMPTY + s), (u & 1u) ^ 1u, abort, a.err, E_WAIT_V, a.wait_ns))) {
                         ++kv;  // the K half of this tile is in flight
                         break;
                     }
@@ -282,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             // No load may still be landing in shared memory when the CTA exits:
             // wait for the last load issued into every buffer.
             for (int i = 0; i < kQT; ++i)
-                if (nq[i]) wait_drain(BAR(B_QFULL + i), (nq[i] - 1) & 1u, a.err);
+                if (nq[i]) wait_drain(BAR(B_QFULL + i), (nq[i] - 1) & 1u, a.err, a.wait_ns);
             for (uint32_t s = 0; s < kStages; ++s) {
                 if (kv > s) {
                     const uint32_t last = (kv - 1 - s) / kStages;  // use count - 1 of stage s
-                    wait_drain(BAR(B_KFULL + s), last & 1u, a.err);
-                    wait_drain(BAR(B_VFULL + s), last & 1u, a.err);
+                    if (s + last * kStages != k_skipped) wait_drain(BAR(B_KFULL + s), last & 1u, a.err, a.wait_ns);
+                    wait_drain(BAR(B_VFULL + s), last & 1u, a.err, a.wait_ns);
                 }
             }
         }
@@ -324,9 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 w_next = load_work(a, t + 2 * gridDim.x);
                 // S_i(0)
                 const uint32_t s0 = kv & 1u;
-                ok = mbar_wait(BAR(B_KFULL + s0), (kv >> 1) & 1u, abort, a.err, E_WAIT_K);
+                ok = mbar_wait(BAR(B_KFULL + s0), (kv >> 1) & 1u, abort, a.err, E_WAIT_K, a.wait_ns);
                 for (int i = 0; ok && i < it.n_q; ++i) {
-                    if (!(ok = mbar_wait(BAR(B_QFULL + i), nq[i] & 1u, abort, a.err, E_WAIT_Q))) break;
+                    if (!(ok = mbar_wait(BAR(B_QFULL + i), nq[i] & 1u, abort, a.err, E_WAIT_Q, a.wait_ns))) break;
                     tc_fence_after();
                     qk(i, s0);
                     mma_commit(BAR(B_SFULL + i));
@@ -337,21 +344,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; ok && j < it.n_kv; ++j) {
                     const uint32_t s = (kv + j) & 1u, sn = (kv + j + 1) & 1u;
                     const bool more = j + 1 < it.n_kv;
-                    ok = mbar_wait(BAR(B_VFULL + s), ((kv + j) >> 1) & 1u, abort, a.err, E_WAIT_V);
+                    ok = mbar_wait(BAR(B_VFULL + s), ((kv + j) >> 1) & 1u, abort, a.err, E_WAIT_V, a.wait_ns);
                     bool k_next = false;
                     for (int i = 0; ok && i < it.n_q; ++i) {
-                        if (!(ok = mbar_wait(BAR(B_PFULL + i), np[i] & 1u, abort, a.err, E_WAIT_P))) break;
+                        if (!(ok = mbar_wait(BAR(B_PFULL + i), np[i] & 1u, abort, a.err, E_WAIT_P, a.wait_ns))) break;
                         np[i]++;
                         // the previous item's epilogue must have read O_i before it is overwritten
                         if (j == 0 && !(ok = mbar_wait(BAR(B_OFREE + i), (nq[i] & 1u) ^ 1u, abort, a.err,
-                                                       E_WAIT_OFREE)))
+                                                       E_WAIT_OFREE, a.wait_ns)))
                             break;
                         tc_fence_after();
                         pv(i, s, j > 0 ? 1u : 0u);
                         if (more) {
                             if (!k_next) {
                                 if (!(ok = mbar_wait(BAR(B_KFULL + sn), ((kv + j + 1) >> 1) & 1u, abort, a.err,
-                                                     E_WAIT_K)))
+                                                     E_WAIT_K, a.wait_ns)))
                                     break;
                                 tc_fence_after();
                                 k_next = true;
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // All issued MMAs must retire before TMEM is released.
             mma_commit(BAR(B_DRAIN));
-            wait_drain(BAR(B_DRAIN), 0, a.err);
+            wait_drain(BAR(B_DRAIN), 0, a.err, a.wait_ns);
         }
       }
     } else {
@@ -397,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (g >= it.n_q) continue;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < it.n_kv; ++j) {
-                ok = mbar_wait(BAR(B_SFULL + g), ns & 1u, abort, a.err, E_WAIT_S);
+                ok = mbar_wait(BAR(B_SFULL + g), ns & 1u, abort, a.err, E_WAIT_S, a.wait_ns);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 ns++;
@@ -466,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(BAR(B_PFULL + g));
             }
             if (!ok) break;
-            ok = mbar_wait(BAR(B_ODONE + g), no & 1u, abort, a.err, E_WAIT_O);
+            ok = mbar_wait(BAR(B_ODONE + g), no & 1u, abort, a.err, E_WAIT_O, a.wait_ns);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             no++;
@@ -637,6 +644,7 @@ extern "C" s2_status s2_window_attention(void *stream, s2_mode mode, const void 
     args.text_len = text_len;
     args.n_items = static_cast<int>(n_items);
     args.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e) / sqrt(128)
+    s2::take_attention_fault(&args.skip_k, &args.wait_ns);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (mode) {
     case S2_MODE_F16: return launch<S2_MODE_F16>(st, mq, mk, mv, args, static_cast<int>(grid));

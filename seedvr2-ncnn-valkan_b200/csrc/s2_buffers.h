@@ -8,6 +8,10 @@
 
 namespace s2 {
 
+// Failure injection for tests (s2_debug_fail_allocations): true while the
+// counter of allocations to fail is positive (it is decremented).
+bool alloc_fault();
+
 struct DeviceBuffer {
     void *ptr = nullptr;
     size_t bytes = 0;
@@ -17,6 +21,7 @@ struct DeviceBuffer {
         if (ptr) cudaFree(ptr);
         ptr = nullptr;
         bytes = 0;
+        if (alloc_fault()) return false;
         if (cudaMalloc(&ptr, want) != cudaSuccess) {
             cudaGetLastError();
             return false;

@@ -11,12 +11,27 @@
 //   * a row exchange between the window ownerships of consecutive blocks
 //     (plain <-> shifted windows): one grouped ncclSend / ncclRecv per peer,
 //     the rank's own rows copied on the device.
+//
+// Failures: the ranks meet through a non-blocking communicator
+// (ncclConfig_t.blocking = 0) whose creation is polled with
+// ncclCommGetAsyncError against a deadline (s2_comm_init_timeout), so a rank
+// that never joins cannot block the host: at the deadline it is aborted and
+// S2_INFERENCE_FAILED returned. The collectives then run on a blocking
+// communicator split from it (the same enqueue semantics as before, which CUDA
+// graph capture of the sharded step relies on); every call's result and the
+// communicator's asynchronous state are checked, and s2_comm_wait waits for a
+// stream holding collectives under a watchdog that aborts the communicator on
+// an asynchronous error (a peer gone) or at the deadline. An aborted
+// communicator refuses further work.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "s2_buffers.h"
 #include "s2_comm.h"
@@ -34,6 +49,10 @@ struct Nccl {
     decltype(&ncclGroupStart) group_start = nullptr;
     decltype(&ncclGroupEnd) group_end = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
+    decltype(&ncclCommInitRankConfig) comm_init_rank_config = nullptr;
+    decltype(&ncclCommGetAsyncError) comm_async_error = nullptr;
+    decltype(&ncclCommAbort) comm_abort = nullptr;
+    decltype(&ncclCommSplit) comm_split = nullptr;
     bool ok = false;
 };
 
@@ -54,9 +73,14 @@ const Nccl &nccl()
         S2_SYM(group_start, "ncclGroupStart");
         S2_SYM(group_end, "ncclGroupEnd");
         S2_SYM(error_string, "ncclGetErrorString");
+        S2_SYM(comm_init_rank_config, "ncclCommInitRankConfig");
+        S2_SYM(comm_async_error, "ncclCommGetAsyncError");
+        S2_SYM(comm_abort, "ncclCommAbort");
+        S2_SYM(comm_split, "ncclCommSplit");
 #undef S2_SYM
         n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce && n.send && n.recv &&
-               n.group_start && n.group_end && n.error_string;
+               n.group_start && n.group_end && n.error_string && n.comm_init_rank_config && n.comm_async_error &&
+               n.comm_abort && n.comm_split;
     });
     return n;
 }
@@ -65,8 +89,60 @@ const Nccl &nccl()
 
 struct s2_comm {
     int device = 0, nranks = 1, rank = 0;
-    ncclComm_t comm = nullptr;
+    ncclComm_t comm = nullptr;   // blocking: the collectives
+    ncclComm_t meet = nullptr;   // non-blocking: the deadline-guarded rendezvous it was split from
+    long long timeout_ms = 300000;
+    bool aborted = false;
 };
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+// Default deadline of communicator creation and of every NCCL call:
+// $S2_COMM_TIMEOUT_MS, else 300 s.
+long long default_timeout_ms()
+{
+    const char *e = std::getenv("S2_COMM_TIMEOUT_MS");
+    const long long v = e ? std::atoll(e) : 0;
+    return v > 0 ? v : 300000;
+}
+
+// Aborts the communicator (its in-flight NCCL kernels stop, its bootstrap and
+// proxy threads end) and records why.
+s2_status abort_comm(s2_comm *c, const char *what, const char *why)
+{
+    if (!c->aborted) {
+        if (c->comm) nccl().comm_abort(c->comm);
+        if (c->meet) nccl().comm_abort(c->meet);
+        c->comm = c->meet = nullptr;
+    }
+    c->aborted = true;
+    return s2::set_error(S2_INFERENCE_FAILED, "%s: %s; communicator aborted (rank %d of %d)", what, why, c->rank,
+                         c->nranks);
+}
+
+// Polls communicator `nc`'s asynchronous state until its last call completed
+// (ncclSuccess), failed, or the deadline passed.
+s2_status settle_on(s2_comm *c, ncclComm_t nc, ncclResult_t r, const char *what)
+{
+    const Nccl &n = nccl();
+    if (r != ncclSuccess && r != ncclInProgress) return abort_comm(c, what, n.error_string(r));
+    const auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t q = n.comm_async_error(nc, &st);
+        if (q != ncclSuccess) return abort_comm(c, what, n.error_string(q));
+        if (st == ncclSuccess) return S2_OK;
+        if (st != ncclInProgress) return abort_comm(c, what, n.error_string(st));
+        if (Clock::now() > deadline) return abort_comm(c, what, "timed out");
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+s2_status settle(s2_comm *c, ncclResult_t r, const char *what) { return settle_on(c, c->comm, r, what); }
+
+}  // namespace
 
 static_assert(sizeof(ncclUniqueId) == S2_COMM_ID_BYTES, "NCCL unique id size");
 
@@ -83,10 +159,11 @@ extern "C" s2_status s2_comm_unique_id(char *id)
     return S2_OK;
 }
 
-extern "C" s2_status s2_comm_init(int device, int nranks, int rank, const char *id, s2_comm **out)
+extern "C" s2_status s2_comm_init_timeout(int device, int nranks, int rank, const char *id, long long timeout_ms,
+                                          s2_comm **out)
 {
     s2::clear_error();
-    if (!out || !id || nranks <= 0 || rank < 0 || rank >= nranks)
+    if (!out || !id || nranks <= 0 || rank < 0 || rank >= nranks || timeout_ms <= 0)
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_comm_init: invalid arguments");
     *out = nullptr;
     const Nccl &n = nccl();
@@ -98,13 +175,68 @@ extern "C" s2_status s2_comm_init(int device, int nranks, int rank, const char *
     c->device = device;
     c->nranks = nranks;
     c->rank = rank;
-    const ncclResult_t r = n.comm_init_rank(&c->comm, nranks, u, rank);
-    if (r != ncclSuccess) {
+    c->timeout_ms = timeout_ms;
+    // non-blocking: the call returns at once and the ranks' rendezvous is polled
+    // against the deadline, so a peer that never joins cannot block the host
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = n.comm_init_rank_config(&c->meet, nranks, u, rank, &cfg);
+    if (!c->meet) {
         delete c;
-        return s2::set_error(S2_INFERENCE_FAILED, "ncclCommInitRank: %s", n.error_string(r));
+        return s2::set_error(S2_INFERENCE_FAILED, "ncclCommInitRankConfig: %s", n.error_string(r));
+    }
+    s2_status s = settle_on(c, c->meet, r, "s2_comm_init (waiting for every rank to join)");
+    if (s == S2_OK) {
+        // every rank is there: split the blocking communicator of the collectives
+        ncclConfig_t bcfg = NCCL_CONFIG_INITIALIZER;
+        bcfg.blocking = 1;
+        const ncclResult_t rs = n.comm_split(c->meet, 0, rank, &c->comm, &bcfg);
+        s = settle_on(c, c->meet, rs, "s2_comm_init (split)");
+        if (s == S2_OK && !c->comm) s = abort_comm(c, "s2_comm_init (split)", "no communicator returned");
+        if (s == S2_OK) s = settle(c, ncclSuccess, "s2_comm_init (split)");
+    }
+    if (s != S2_OK) {
+        delete c;  // abort_comm released both communicators
+        return s;
     }
     *out = c;
     return S2_OK;
+}
+
+extern "C" s2_status s2_comm_init(int device, int nranks, int rank, const char *id, s2_comm **out)
+{
+    return s2_comm_init_timeout(device, nranks, rank, id, default_timeout_ms(), out);
+}
+
+extern "C" s2_status s2_comm_set_timeout(s2_comm *c, long long timeout_ms)
+{
+    if (!c || timeout_ms <= 0) return s2::set_error(S2_INVALID_ARGUMENT, "s2_comm_set_timeout: invalid arguments");
+    c->timeout_ms = timeout_ms;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_comm_wait(s2_comm *c, void *stream)
+{
+    s2::clear_error();
+    if (!c) return s2::set_error(S2_INVALID_ARGUMENT, "s2_comm_wait: communicator is NULL");
+    if (c->aborted) return s2::set_error(S2_INFERENCE_FAILED, "s2_comm_wait: communicator was aborted");
+    s2::DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const Nccl &n = nccl();
+    const auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return S2_OK;
+        if (q != cudaErrorNotReady)
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_comm_wait: stream failed: %s", cudaGetErrorString(q));
+        if (c->comm && c->nranks > 1) {
+            ncclResult_t as = ncclSuccess;
+            if (n.comm_async_error(c->comm, &as) != ncclSuccess || (as != ncclSuccess && as != ncclInProgress))
+                return abort_comm(c, "s2_comm_wait", n.error_string(as));
+        }
+        if (Clock::now() > deadline) return abort_comm(c, "s2_comm_wait", "stream did not finish in time");
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
 }
 
 extern "C" s2_status s2_comm_destroy(s2_comm *c)
@@ -112,6 +244,7 @@ extern "C" s2_status s2_comm_destroy(s2_comm *c)
     if (!c) return S2_OK;
     s2::DeviceGuard guard(c->device);
     if (c->comm) nccl().comm_destroy(c->comm);
+    if (c->meet) nccl().comm_abort(c->meet);  // idle since the split; no collective to finish
     delete c;
     return S2_OK;
 }
@@ -124,9 +257,9 @@ namespace s2 {
 s2_status comm_allreduce_f32(s2_comm *c, float *buf, size_t n, cudaStream_t st)
 {
     if (!c || c->nranks == 1 || n == 0) return S2_OK;
+    if (c->aborted) return set_error(S2_INFERENCE_FAILED, "ncclAllReduce: communicator was aborted");
     const Nccl &nc = nccl();
-    const ncclResult_t r = nc.all_reduce(buf, buf, n, ncclFloat, ncclSum, c->comm, st);
-    return r == ncclSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "ncclAllReduce: %s", nc.error_string(r));
+    return settle(c, nc.all_reduce(buf, buf, n, ncclFloat, ncclSum, c->comm, st), "ncclAllReduce");
 }
 
 s2_status comm_exchange(s2_comm *c, const void *send, const size_t *send_off, const size_t *send_bytes, void *recv,
@@ -141,6 +274,7 @@ s2_status comm_exchange(s2_comm *c, const void *send, const size_t *send_off, co
                         send_bytes[me], cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return set_error(S2_INFERENCE_FAILED, "exchange: own copy failed");
     if (!c || c->nranks == 1) return S2_OK;
+    if (c->aborted) return set_error(S2_INFERENCE_FAILED, "exchange: communicator was aborted");
     const Nccl &nc = nccl();
     ncclResult_t r = nc.group_start();
     for (int p = 0; p < c->nranks && r == ncclSuccess; ++p) {
@@ -151,8 +285,8 @@ s2_status comm_exchange(s2_comm *c, const void *send, const size_t *send_off, co
             r = nc.recv(static_cast<char *>(recv) + recv_off[p], recv_bytes[p], ncclChar, p, c->comm, st);
     }
     const ncclResult_t e = nc.group_end();
-    if (r == ncclSuccess) r = e;
-    return r == ncclSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "exchange: %s", nc.error_string(r));
+    if (r == ncclSuccess || r == ncclInProgress) r = e;
+    return settle(c, r, "exchange (grouped send/recv)");
 }
 
 }  // namespace s2

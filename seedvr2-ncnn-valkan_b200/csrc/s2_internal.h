@@ -16,6 +16,11 @@ void clear_error();
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// Failure injection for tests (s2_debug_attention_fault): hands the next
+// s2_window_attention launch its K tile to leave out (-1: none) and its wait
+// limit, then resets both (one shot).
+void take_attention_fault(int *skip_k, unsigned long long *wait_ns);
+
 // Attention core tiling shared by the planner and the kernel.
 constexpr int kTileM = 128;   // query rows per Q tile (one TMEM lane per row)
 constexpr int kQTiles = 2;    // Q tiles per CTA (one softmax warpgroup each)

@@ -1,6 +1,7 @@
 // Host-side planning for the windowed MM-attention path: window boxes,
 // varlen packing, CTA work list, error state.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -187,3 +188,42 @@ extern "C" s2_status s2_shard_windows(const s2_window *windows, int n, int text_
     }
     return S2_OK;
 }
+
+// ---- failure injection (tests) ------------------------------------------------
+
+namespace {
+std::atomic<int> g_fail_allocs{0};
+std::atomic<int> g_fault_skip_k{-1};
+std::atomic<unsigned long long> g_fault_wait_ns{0};
+}  // namespace
+
+namespace s2 {
+bool alloc_fault()
+{
+    int n = g_fail_allocs.load();
+    while (n > 0)
+        if (g_fail_allocs.compare_exchange_weak(n, n - 1)) return true;
+    return false;
+}
+
+void take_attention_fault(int *skip_k, unsigned long long *wait_ns)
+{
+    *skip_k = g_fault_skip_k.exchange(-1);
+    const unsigned long long w = g_fault_wait_ns.exchange(0);
+    *wait_ns = w ? w : 1000000000ull;  // the default limit: 1 s
+}
+}  // namespace s2
+
+extern "C" s2_status s2_debug_fail_allocations(int n)
+{
+    g_fail_allocs.store(n > 0 ? n : 0);
+    return S2_OK;
+}
+
+extern "C" s2_status s2_debug_attention_fault(int skip_k_tile, unsigned long long wait_ns)
+{
+    g_fault_skip_k.store(skip_k_tile >= 0 ? skip_k_tile : -1);
+    g_fault_wait_ns.store(wait_ns);
+    return S2_OK;
+}
+

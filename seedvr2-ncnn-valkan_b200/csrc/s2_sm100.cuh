@@ -62,7 +62,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 // pipeline ends the kernel with an error instead of hanging the GPU.
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s; a healthy wait is < 100 us
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code)
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code,
+                                          uint64_t timeout_ns = kWaitTimeoutNs)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
@@ -70,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort) return false;
-            if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+            if (global_timer_ns() - t0 > timeout_ns) {
                 *abort = 1;
                 if (err) atomicCAS(err, 0, code);
                 return false;

@@ -133,6 +133,10 @@ _SIGS = {
     "s2_comm_init": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
                                     ctypes.POINTER(ctypes.c_void_p)]),
     "s2_comm_destroy": (ctypes.c_int, [_vp]),
+    "s2_comm_init_timeout": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                            ctypes.c_longlong, ctypes.POINTER(ctypes.c_void_p)]),
+    "s2_comm_set_timeout": (ctypes.c_int, [_vp, ctypes.c_longlong]),
+    "s2_comm_wait": (ctypes.c_int, [_vp, _vp]),
     "s2_comm_size": (ctypes.c_int, [_vp]),
     "s2_comm_rank": (ctypes.c_int, [_vp]),
     "s2_attention_layer_set_local_rows": (ctypes.c_int, [_vp, ctypes.c_int]),
@@ -202,6 +206,8 @@ _SIGS = {
     "s2_vae_conv3d_forward_host": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 3 + [_vp]),
     "s2_vae_conv3d_last_launches": (ctypes.c_int, [_vp]),
     "s2_vae_conv3d_device_error": (ctypes.c_int, [_vp, _i32p]),
+    "s2_debug_fail_allocations": (ctypes.c_int, [ctypes.c_int]),
+    "s2_debug_attention_fault": (ctypes.c_int, [ctypes.c_int, ctypes.c_ulonglong]),
     "s2_last_error": (ctypes.c_char_p, []),
     "s2_device_check": (ctypes.c_int, [ctypes.c_int]),
     "s2_version": (ctypes.c_int, []),
