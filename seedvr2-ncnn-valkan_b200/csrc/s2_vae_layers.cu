@@ -446,6 +446,9 @@ extern "C" s2_status s2_vae_space_time_shuffle_forward(s2_vae_space_time_shuffle
     g.sh_tr = l->tr;
     g.sh_h = height;
     g.sh_w = width;
+    // K is short (the channels) and N long (4 x ratio x channels): with one CTA per 128 x 256
+    // tile every tile re-reads its 256 weight rows from L2; CTA pairs halve that traffic
+    g.pair = (tokens >= 4096 && l->proj % 256 == 0) ? 1 : 0;
     g.err = static_cast<int32_t *>(l->err.ptr);
     s = s2::gemm_f16(st, l->a16.ptr, l->w16.ptr, g);
     if (s != S2_OK) return s;
