@@ -267,6 +267,37 @@ S2_API s2_status s2_dit_block_forward_host(s2_dit_block *block, void *stream, co
                                            const float *txt, int Lt, const float *emb, const int32_t *vid_shape,
                                            float *vid_out, float *txt_out);
 S2_API int s2_dit_block_last_launches(const s2_dit_block *block);
+
+/* set_debug_tensors (seedvr2_dit_block.h:20-36, 58): the reference's 14
+ * capture points of one forward, written to DEVICE fp32 buffers the caller
+ * owns (NULL members are skipped; tensors = NULL switches capturing off), in
+ * the reference's [rows][channels] layouts:
+ *   qkv_vid [L][3 dim], qkv_txt [Lt][3 dim] -- the QKV projections (kept in
+ *     fp16 by this build: the captured values are those fp16 numbers);
+ *   norm_q_vid, norm_k_vid [L][dim], norm_q_txt, norm_k_txt [Lt][dim] -- per
+ *     head x * rsqrt(mean x^2 + eps) * gamma, before RoPE and rounding;
+ *   attention_q, attention_k, attention_v [rows][dim] -- the packed window
+ *     sequences (window by window, video (t, y, x) then text), bf16-rounded;
+ *   attention_output [rows][dim] -- each packed row's window output (video
+ *     rows as written to the attention output, text rows per window);
+ *   projected_vid [L][dim], projected_txt [Lt][dim] -- output projection +
+ *     bias, before the gate and residual;
+ *   output_vid [L][dim], output_txt [Lt][dim] -- the block outputs.
+ * rows = s2_dit_block_debug_rows (after set_runtime_shape). Capturing adds
+ * conversion kernels and two projection GEMMs to each forward. */
+typedef struct s2_block_debug {
+    float *qkv_vid, *qkv_txt;
+    float *norm_q_vid, *norm_q_txt, *norm_k_vid, *norm_k_txt;
+    float *attention_q, *attention_k, *attention_v, *attention_output;
+    float *projected_vid, *projected_txt;
+    float *output_vid, *output_txt;
+} s2_block_debug;
+S2_API s2_status s2_dit_block_set_debug_tensors(s2_dit_block *block, const s2_block_debug *tensors);
+/* The same for s2_dit_block_forward_host with HOST fp32 buffers (the
+ * reference's host Mats): the captures are staged on the device and copied
+ * out with the outputs. */
+S2_API s2_status s2_dit_block_set_debug_tensors_host(s2_dit_block *block, const s2_block_debug *tensors);
+S2_API s2_status s2_dit_block_debug_rows(s2_dit_block *block, int Lt, int *rows);
 S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
 
 /* ---- the block's projections (ncnn InnerProduct replacement) ------------- */

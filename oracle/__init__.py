@@ -306,6 +306,38 @@ class Ref(_Lib):
             raise ValueError(f"ref_block_forward failed: {rc}")
         return vo, to
 
+    def block_forward_debug(self, params, weights, vid, txt, emb, shape, threads=0):
+        """block_forward with the reference's debug capture (set_debug_tensors,
+        seedvr2_dit_block.h:20-36): returns (vid_out, txt_out, {name: array})
+        with the 14 capture points in SeedVR2DiTBlockDebugTensors order."""
+        p = params
+        weights, vid, txt, emb = _f32(weights), _f32(vid), _f32(txt), _f32(emb)
+        L, Lt, d = vid.shape[0], txt.shape[0], p["dim"]
+        T, H, W = shape
+        wins = self.make_windows(T, H, W, p["shifted"])
+        rows = int(sum((w[1] - w[0]) * (w[3] - w[2]) * (w[5] - w[4]) + Lt for w in wins))
+        shapes = [(L, 3 * d), (Lt, 3 * d), (L, d), (Lt, d), (L, d), (Lt, d), (rows, d), (rows, d), (rows, d),
+                  (rows, d), (L, d), (Lt, d), (L, d), (Lt, d)]
+        names = ["qkv_vid", "qkv_txt", "norm_q_vid", "norm_q_txt", "norm_k_vid", "norm_k_txt", "attention_q",
+                 "attention_k", "attention_v", "attention_output", "projected_vid", "projected_txt", "output_vid",
+                 "output_txt"]
+        caps = [np.zeros(sh, np.float32) for sh in shapes]
+        arr = (_f32p * 14)(*[_ptr(c) for c in caps])
+        vo = np.zeros((L, d), np.float32)
+        to = np.zeros((Lt, d), np.float32)
+        fn = self.lib.ref_block_forward_debug
+        fn.restype = ctypes.c_int
+        fn.argtypes = (self.lib.ref_block_forward.argtypes + [ctypes.POINTER(_f32p), _i32p])
+        n_rows = ctypes.c_int(0)
+        rc = fn(p["block_index"], int(p["shared"]), int(p["last"]), int(p["shifted"]), d, p["heads"], p["head_dim"],
+                p["mlp_hidden"], ctypes.c_float(p.get("eps", 1e-5)), _ptr(weights), weights.size, _ptr(vid), L,
+                _ptr(txt), Lt, _ptr(emb), T, H, W, int(threads or os.cpu_count() or 1), _ptr(vo), _ptr(to), arr,
+                ctypes.byref(n_rows))
+        if rc != 0:
+            raise ValueError(f"ref_block_forward_debug failed: {rc}")
+        assert n_rows.value == rows
+        return vo, to, dict(zip(names, caps))
+
     def dit_input(self, params, weights, latent33, text, timestep, threads=0):
         """SeedVR2DiTInput on latent [vc, T, H, W] (flattened here like
         SeedVR2DiT::forward, dit.cpp:70-86, 298) and text [Lt, tc].

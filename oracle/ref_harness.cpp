@@ -137,12 +137,37 @@ int ref_attention(const float* vid_qkv, int L, const float* txt_qkv, int Lt,
 // SeedVR2DiTBlock::load_param / load_model / forward (seedvr2_dit_block.cpp:
 // 643-688, 1114-1267): the whole block through the public layer API.
 // `weights` is the ModelBin stream in load_model order (all fp32).
+int ref_block_forward_debug(int block_index, int shared, int last, int shifted,
+                            int dim, int heads, int head_dim, int mlp_hidden, float eps,
+                            const float* weights, size_t n_weights,
+                            const float* vid, int L, const float* txt, int Lt, const float* emb,
+                            int frames, int height, int width, int num_threads,
+                            float* vid_out, float* txt_out, float** captures, int* capture_rows);
+
 int ref_block_forward(int block_index, int shared, int last, int shifted,
                       int dim, int heads, int head_dim, int mlp_hidden, float eps,
                       const float* weights, size_t n_weights,
                       const float* vid, int L, const float* txt, int Lt, const float* emb,
                       int frames, int height, int width, int num_threads,
                       float* vid_out, float* txt_out)
+{
+    return ref_block_forward_debug(block_index, shared, last, shifted, dim, heads, head_dim, mlp_hidden, eps,
+                                   weights, n_weights, vid, L, txt, Lt, emb, frames, height, width, num_threads,
+                                   vid_out, txt_out, nullptr, nullptr);
+}
+
+// The same with the layer's debug capture (set_debug_tensors,
+// seedvr2_dit_block.h:20-36, 58): captures[0..13] receive, when non-NULL,
+// qkv_vid, qkv_txt, norm_q_vid, norm_q_txt, norm_k_vid, norm_k_txt,
+// attention_q, attention_k, attention_v, attention_output, projected_vid,
+// projected_txt, output_vid, output_txt ([rows][channels] each, the
+// SeedVR2DiTBlockDebugTensors order); *capture_rows = packed attention rows.
+int ref_block_forward_debug(int block_index, int shared, int last, int shifted,
+                            int dim, int heads, int head_dim, int mlp_hidden, float eps,
+                            const float* weights, size_t n_weights,
+                            const float* vid, int L, const float* txt, int Lt, const float* emb,
+                            int frames, int height, int width, int num_threads,
+                            float* vid_out, float* txt_out, float** captures, int* capture_rows)
 {
     SeedVR2DiTBlock layer;
     ncnn::ParamDict pd;
@@ -173,11 +198,21 @@ int ref_block_forward(int block_index, int shared, int last, int shifted,
     ((int*)shape.data)[2] = width;
     bottom[3] = shape;
     layer.set_runtime_shape(frames, height, width);
+    SeedVR2DiTBlockDebugTensors dbg;
+    if (captures) layer.set_debug_tensors(&dbg);
     const int ret = layer.forward(bottom, top, opt);
     layer.destroy_pipeline(opt);
     if (ret != 0) return ret;
     copy_out(top[0], vid_out);
     copy_out(top[1], txt_out);
+    if (captures) {
+        const ncnn::Mat* m[14] = {&dbg.qkv_vid, &dbg.qkv_txt, &dbg.norm_q_vid, &dbg.norm_q_txt, &dbg.norm_k_vid,
+                                  &dbg.norm_k_txt, &dbg.attention_q, &dbg.attention_k, &dbg.attention_v,
+                                  &dbg.attention_output, &dbg.projected_vid, &dbg.projected_txt, &dbg.output_vid,
+                                  &dbg.output_txt};
+        for (int i = 0; i < 14; i++) copy_out(*m[i], captures[i]);
+        if (capture_rows) *capture_rows = dbg.attention_q.h;
+    }
     return 0;
 }
 

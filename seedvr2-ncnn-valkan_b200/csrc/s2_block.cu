@@ -188,6 +188,12 @@ struct s2_dit_block {
     s2::DeviceBuffer hv, ht, he, hov, hot;  // forward_host staging
     int last_launches = 0;
     cudaStream_t last_stream = nullptr;
+    bool debug_on = false;  // set_debug_tensors (device buffers)
+    s2_block_debug debug{};
+    bool debug_host_on = false;  // set_debug_tensors_host (host buffers, forward_host)
+    static_assert(sizeof(s2_block_debug) == 14 * sizeof(float *), "s2_block_debug is 14 pointers");
+    s2_block_debug debug_host{};
+    s2::DeviceBuffer debug_stage;
     const Branch &tb() const { return shared ? vid : txt; }
 };
 
@@ -234,7 +240,7 @@ extern "C" s2_status s2_dit_block_destroy(s2_dit_block *b)
         s2::DeviceGuard guard(b->device);
         b->vid.release();
         b->txt.release();
-        for (s2::DeviceBuffer *x : {&b->mods, &b->err, &b->hv, &b->ht, &b->he, &b->hov, &b->hot})
+        for (s2::DeviceBuffer *x : {&b->mods, &b->err, &b->hv, &b->ht, &b->he, &b->hov, &b->hot, &b->debug_stage})
             x->release();
     }
     s2_attention_layer_destroy(b->attn);
@@ -470,6 +476,18 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         return s;
     }
     launches += s2_attention_layer_last_launches(b->attn);
+    if (b->debug_on) {
+        const s2_block_debug &g = b->debug;
+        const long long nq = static_cast<long long>(L) * 3 * d, nt = static_cast<long long>(Lt) * 3 * d;
+        if ((g.qkv_vid && (s = s2::to_f32(st, S2_MODE_F16, qkv_vid, nq, g.qkv_vid)) != S2_OK) ||
+            (g.qkv_txt && Lt > 0 && (s = s2::to_f32(st, S2_MODE_F16, qkv_txt, nt, g.qkv_txt)) != S2_OK) ||
+            (s = s2::attention_debug_capture(b->attn, st, qkv_vid, S2_F16, L, qkv_txt, Lt, att_vid, g.attention_q,
+                                             g.attention_k, g.attention_v, g.attention_output, g.norm_q_vid,
+                                             g.norm_k_vid, g.norm_q_txt, g.norm_k_txt)) != S2_OK) {
+            b->last_launches = launches;
+            return s;
+        }
+    }
     if (reduce && reduce->fn && Lt > 0 &&
         (s = reduce->fn(reduce->ctx, static_cast<float *>(sc.att_txt32.ptr), static_cast<size_t>(Lt) * d, st)) != S2_OK) {
         b->last_launches = launches;
@@ -482,6 +500,28 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         if (cudaGetLastError() != cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: convert launch failed");
         ++launches;
+    }
+    // debug capture: the output projection + bias alone (the reference's vid_projected /
+    // txt_projected, seedvr2_dit_block.cpp:1176-1191); the forward fuses it with the gate
+    if (b->debug_on) {
+        const s2_block_debug &g = b->debug;
+        s2::GemmArgs q;
+        q.K = d;
+        q.N = d;
+        q.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+        q.err = err;
+        if (g.projected_vid) {
+            q.M = L;
+            q.bias = static_cast<const float *>(V.proj_b.ptr);
+            q.y = g.projected_vid;
+            S2_TRY(s2::gemm_f16(st, att_vid, V.proj.ptr, q));
+        }
+        if (g.projected_txt && Lt > 0) {
+            q.M = Lt;
+            q.bias = static_cast<const float *>(T.proj_b.ptr);
+            q.y = g.projected_txt;
+            S2_TRY(s2::gemm_f16(st, att_txt16, T.proj.ptr, q));
+        }
     }
     // output projection + gated residual
     const bool merged_rest = merged && !b->last;
@@ -576,8 +616,46 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         b->last_launches = launches;
         return s;
     }
+    if (b->debug_on) {
+        const s2_block_debug &g = b->debug;
+        if ((g.output_vid && cudaMemcpyAsync(g.output_vid, vid_out, static_cast<size_t>(L) * dz * 4,
+                                             cudaMemcpyDeviceToDevice, st) != cudaSuccess) ||
+            (g.output_txt && Lt > 0 &&
+             cudaMemcpyAsync(g.output_txt, txt_out, static_cast<size_t>(Lt) * dz * 4, cudaMemcpyDeviceToDevice, st) !=
+                 cudaSuccess))
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: debug copy failed");
+    }
 #undef S2_TRY
     b->last_launches = launches + extra;
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_set_debug_tensors(s2_dit_block *b, const s2_block_debug *tensors)
+{
+    s2::clear_error();
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_set_debug_tensors: block is NULL");
+    b->debug_on = tensors != nullptr;
+    b->debug = tensors ? *tensors : s2_block_debug{};
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_set_debug_tensors_host(s2_dit_block *b, const s2_block_debug *tensors)
+{
+    s2::clear_error();
+    if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_set_debug_tensors_host: block is NULL");
+    b->debug_host_on = tensors != nullptr;
+    b->debug_host = tensors ? *tensors : s2_block_debug{};
+    return S2_OK;
+}
+
+extern "C" s2_status s2_dit_block_debug_rows(s2_dit_block *b, int Lt, int *rows)
+{
+    s2::clear_error();
+    if (!b || !rows || Lt < 0) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_debug_rows: invalid arguments");
+    int n_video = 0;
+    const s2_status s = s2_attention_layer_local_rows(b->attn, Lt, &n_video);  // builds the plan for Lt
+    if (s != S2_OK) return s;
+    *rows = s2::attention_debug_rows(b->attn);
     return S2_OK;
 }
 
@@ -603,10 +681,47 @@ extern "C" s2_status s2_dit_block_forward_host(s2_dit_block *b, void *stream, co
                        cudaSuccess) ||
         cudaMemcpyAsync(b->he.ptr, emb, 6 * d * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
         return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward_host: upload failed");
+    // host debug captures: staged in one device buffer, copied out after the forward
+    float *const *hosts = reinterpret_cast<float *const *>(&b->debug_host);
+    size_t counts[14] = {};
+    const bool host_debug = b->debug_host_on;
+    if (host_debug) {
+        int rows = 0;
+        if ((s = s2_dit_block_debug_rows(b, Lt, &rows)) != S2_OK) return s;
+        const size_t Lz = static_cast<size_t>(L), Tz = static_cast<size_t>(Lt), Rz = static_cast<size_t>(rows);
+        const size_t n[14] = {Lz * 3 * d, Tz * 3 * d, Lz * d, Tz * d, Lz * d, Tz * d, Rz * d, Rz * d, Rz * d, Rz * d,
+                              Lz * d, Tz * d, Lz * d, Tz * d};
+        size_t total = 0;
+        for (int i = 0; i < 14; ++i) {
+            counts[i] = hosts[i] ? n[i] : 0;
+            total += (counts[i] + 63) / 64 * 64;
+        }
+        if (!b->debug_stage.ensure(std::max<size_t>(total, 64) * 4))
+            return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_block_forward_host: debug staging allocation failed");
+        float **dev = reinterpret_cast<float **>(&b->debug);
+        float *at = static_cast<float *>(b->debug_stage.ptr);
+        for (int i = 0; i < 14; ++i) {
+            dev[i] = counts[i] ? at : nullptr;
+            at += (counts[i] + 63) / 64 * 64;
+        }
+        b->debug_on = true;
+    }
     s = s2_dit_block_forward(b, stream, static_cast<const float *>(b->hv.ptr), L, static_cast<const float *>(b->ht.ptr), Lt,
                              static_cast<const float *>(b->he.ptr), static_cast<float *>(b->hov.ptr),
                              static_cast<float *>(b->hot.ptr));
-    if (s != S2_OK) return s;
+    if (host_debug) {
+        b->debug_on = false;
+        if (s == S2_OK)
+            for (int i = 0; i < 14 && s == S2_OK; ++i)
+                if (counts[i] && cudaMemcpyAsync(hosts[i], reinterpret_cast<float **>(&b->debug)[i], counts[i] * 4,
+                                                 cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    s = s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward_host: debug download failed");
+        b->debug = s2_block_debug{};
+    }
+    if (s != S2_OK) {
+        cudaStreamSynchronize(st);  // no copy may still touch the caller's buffers
+        return s;
+    }
     if (cudaMemcpyAsync(vid_out, b->hov.ptr, vb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         (Lt > 0 && cudaMemcpyAsync(txt_out, b->hot.ptr, static_cast<size_t>(Lt) * d * 4, cudaMemcpyDeviceToHost, st) !=
                        cudaSuccess) ||

@@ -7,6 +7,8 @@
 // is three stream-ordered launches (prologue, attention, text mean) with no
 // host synchronisation. Workspaces (packed Q/K/V, per-window text slabs) grow
 // on demand and are reused across calls.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -686,7 +688,115 @@ extern "C" s2_status s2_attention_layer_device_error(s2_attention_layer *l, int 
     return S2_OK;
 }
 
+// ---- debug capture (the block's set_debug_tensors) -----------------------------
+
+namespace {
+
+__device__ __forceinline__ float load_f(const void *p, size_t i, int dtype)
+{
+    if (dtype == S2_F32) return static_cast<const float *>(p)[i];
+    if (dtype == S2_F16) return __half2float(static_cast<const __half *>(p)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+}
+
+// packed [heads][n_rows][128] fp16 -> [n_rows][heads * 128] fp32
+__global__ void packed_rows_kernel(const __half *__restrict__ p, int heads, int n_rows, float *__restrict__ out)
+{
+    const long long n = 1LL * n_rows * heads * S2_HEAD_DIM;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+        const int row = static_cast<int>(i / (heads * S2_HEAD_DIM)), c = static_cast<int>(i % (heads * S2_HEAD_DIM));
+        const int h = c / S2_HEAD_DIM, d = c % S2_HEAD_DIM;
+        out[i] = __half2float(p[(static_cast<size_t>(h) * n_rows + row) * S2_HEAD_DIM + d]);
+    }
+}
+
+// the per-window output of every packed row: video rows from vid_out, text rows
+// from their window's text slab (the values the text mean sums)
+__global__ void window_outputs_kernel(const s2_row *__restrict__ rows, const int32_t *__restrict__ cu, int n_windows,
+                                      int n_rows, int text_len, int dim, const void *vid_out, const void *txt_partial,
+                                      int dtype, float *__restrict__ out)
+{
+    const long long n = 1LL * n_rows * dim;
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+        const int r = static_cast<int>(i / dim), c = static_cast<int>(i % dim);
+        const int src = rows[r].src;
+        if (src >= 0) {
+            out[i] = load_f(vid_out, static_cast<size_t>(src) * dim + c, dtype);
+        } else {
+            int lo = 0, hi = n_windows - 1;  // last window with cu[w] <= r
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (cu[mid] <= r) lo = mid; else hi = mid - 1;
+            }
+            out[i] = load_f(txt_partial, (static_cast<size_t>(lo) * text_len + (-src - 1)) * dim + c, dtype);
+        }
+    }
+}
+
+// x * (1 / sqrt(mean(x^2) + eps)) * gamma per (row, head) of the q and k parts of
+// [n][3 dim] rows, before RoPE and rounding (the reference's normalized values,
+// seedvr2_dit_block.cpp:942-952: double sum, float scale, no contraction)
+__global__ void norm_capture_kernel(const void *qkv, int dtype, int n, int heads, float eps, const float *__restrict__ gq,
+                                    const float *__restrict__ gk, float *__restrict__ out_q, float *__restrict__ out_k)
+{
+    const int dim = heads * S2_HEAD_DIM;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < 2 * n * heads; t += gridDim.x * blockDim.x) {
+        const int part = t / (n * heads), rh = t % (n * heads), row = rh / heads, h = rh % heads;
+        float *out = part == 0 ? out_q : out_k;
+        if (!out) continue;
+        const float *g = part == 0 ? gq : gk;
+        const size_t base = static_cast<size_t>(row) * 3 * dim + static_cast<size_t>(part) * dim + h * S2_HEAD_DIM;
+        double ss = 0.0;
+        for (int d = 0; d < S2_HEAD_DIM; ++d) {
+            const float x = load_f(qkv, base + d, dtype);
+            ss += static_cast<double>(x) * x;
+        }
+        const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(static_cast<float>(ss / S2_HEAD_DIM), eps)));
+        for (int d = 0; d < S2_HEAD_DIM; ++d)
+            out[static_cast<size_t>(row) * dim + h * S2_HEAD_DIM + d] =
+                __fmul_rn(__fmul_rn(load_f(qkv, base + d, dtype), inv), g[d]);
+    }
+}
+
+int grid_for_n(long long n) { return static_cast<int>(std::min<long long>((n + 255) / 256, 4096)); }
+
+}  // namespace
+
 namespace s2 {
+
+int attention_debug_rows(const s2_attention_layer *l) { return l && l->plan_valid ? l->n_rows : 0; }
+
+s2_status attention_debug_capture(s2_attention_layer *l, cudaStream_t st, const void *vid_qkv, s2_dtype in_dtype,
+                                  int L, const void *txt_qkv, int Lt, const void *vid_out, float *att_q, float *att_k,
+                                  float *att_v, float *att_o, float *nq_vid, float *nk_vid, float *nq_txt,
+                                  float *nk_txt)
+{
+    if (!l || !l->plan_valid) return set_error(S2_NOT_LOADED, "debug capture: the layer has not run");
+    DeviceGuard g(l->device);
+    const int dim = l->heads * S2_HEAD_DIM;
+    const long long n = 1LL * l->n_rows * dim;
+    const AttnScratch &sc = *l->sc;
+    const __half *packed[3] = {static_cast<const __half *>(sc.q.ptr), static_cast<const __half *>(sc.k.ptr),
+                               static_cast<const __half *>(sc.v.ptr)};
+    float *outs[3] = {att_q, att_k, att_v};
+    for (int i = 0; i < 3; ++i)
+        if (outs[i]) packed_rows_kernel<<<grid_for_n(n), 256, 0, st>>>(packed[i], l->heads, l->n_rows, outs[i]);
+    const int out_dtype = l->mode == S2_MODE_BF16_REF ? S2_BF16 : S2_F16;
+    if (att_o)
+        window_outputs_kernel<<<grid_for_n(n), 256, 0, st>>>(static_cast<const s2_row *>(l->d_rows.ptr),
+                                                              static_cast<const int32_t *>(l->d_cu.ptr), l->n_local,
+                                                              l->n_rows, Lt, dim, vid_out, sc.txt_partial.ptr,
+                                                              out_dtype, att_o);
+    const float *gm = l->gammas();  // [4][128]: q_vid, k_vid, q_txt, k_txt
+    if (nq_vid || nk_vid)
+        norm_capture_kernel<<<grid_for_n(2LL * L * l->heads), 256, 0, st>>>(vid_qkv, in_dtype, L, l->heads, l->eps, gm,
+                                                                          gm + 128, nq_vid, nk_vid);
+    if (Lt > 0 && (nq_txt || nk_txt))
+        norm_capture_kernel<<<grid_for_n(2LL * Lt * l->heads), 256, 0, st>>>(txt_qkv, in_dtype, Lt, l->heads, l->eps,
+                                                                           gm + 256, gm + 384, nq_txt, nk_txt);
+    return cudaGetLastError() == cudaSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "debug capture: launch failed");
+}
+
 void share_attention_scratch(s2_attention_layer *dst, const s2_attention_layer *src)
 {
     if (dst && src && dst != src) dst->sc = src->sc;

@@ -27,6 +27,16 @@ s2_status dit_block_forward_ex(s2_dit_block *b, void *stream, const float *vid, 
                                const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce);
 s2_attention_layer *dit_block_attention(s2_dit_block *b);
 
+// Debug capture of the attention stage the layer just ran (the block's
+// set_debug_tensors): packed Q/K/V and the per-window outputs as [rows][dim]
+// fp32, the pre-RoPE normalised q/k of the video and text rows; NULL outputs
+// are skipped. attention_debug_rows: the packed row count of the current plan.
+int attention_debug_rows(const s2_attention_layer *l);
+s2_status attention_debug_capture(s2_attention_layer *l, cudaStream_t st, const void *vid_qkv, s2_dtype in_dtype,
+                                  int L, const void *txt_qkv, int Lt, const void *vid_out, float *att_q, float *att_k,
+                                  float *att_v, float *att_o, float *nq_vid, float *nk_vid, float *nq_txt,
+                                  float *nk_txt);
+
 // y = fp16( (x * inv_rms(x) [* gamma]) * mul + add0 + add1 ) per row
 // (s2_block.cu); gamma and mul may be null (no gamma / no modulation).
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,
@@ -34,6 +44,8 @@ s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps,
 // out [8][dim] modulation vectors of one branch (see modulation_kernel).
 s2_status modulation_vectors(cudaStream_t st, const float *emb, const float *mod6, int dim, float *out);
 s2_status f32_to_f16(cudaStream_t st, const float *x, long long n, void *y_f16);
+// fp32 copy of n 16-bit values: bf16 for S2_MODE_BF16_REF, fp16 otherwise (s2_prologue.cu).
+s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst);
 
 // Sampler pieces (s2_sampler.cu). Guidance rescale factor of (pos, neg) into
 // device memory inside `workspace` (cfg_workspace_bytes(), 16-byte aligned);

@@ -174,6 +174,16 @@ inline int reference_code(s2_status s)
 
 // ---- SeedVR2DiTBlock ------------------------------------------------------------
 
+// The reference's debug capture (seedvr2_dit_block.h:20-36): [rows][channels]
+// fp32 Mats of one forward, filled when set with set_debug_tensors.
+struct SeedVR2DiTBlockDebugTensors {
+    Mat qkv_vid, qkv_txt;
+    Mat norm_q_vid, norm_q_txt, norm_k_vid, norm_k_txt;
+    Mat attention_q, attention_k, attention_v, attention_output;
+    Mat projected_vid, projected_txt;
+    Mat output_vid, output_txt;
+};
+
 class SeedVR2DiTBlock
 {
 public:
@@ -246,9 +256,36 @@ public:
             return fail(-1, "invalid input shapes");
         top[0].create(dim, vid.h);
         top[1].create(dim, txt.h);
-        return track(s2_dit_block_forward_host(block_, opt.stream, vid, vid.h, txt, txt.h, emb,
-                                               static_cast<const int32_t *>(shape), top[0], top[1]));
+        if (debug_) {
+            // set_debug_tensors: size the capture Mats for this forward and hand them to the library
+            const int32_t *sh = static_cast<const int32_t *>(shape);
+            int rows = 0;
+            s2_status s = s2_dit_block_set_runtime_shape(block_, sh[0], sh[1], sh[2]);
+            if (s == S2_OK) s = s2_dit_block_debug_rows(block_, txt.h, &rows);
+            if (s != S2_OK) return track(s);
+            SeedVR2DiTBlockDebugTensors &t = *debug_;
+            const int L = vid.h, Lt = txt.h;
+            Mat *m[14] = {&t.qkv_vid, &t.qkv_txt, &t.norm_q_vid, &t.norm_q_txt, &t.norm_k_vid, &t.norm_k_txt,
+                          &t.attention_q, &t.attention_k, &t.attention_v, &t.attention_output, &t.projected_vid,
+                          &t.projected_txt, &t.output_vid, &t.output_txt};
+            const int h[14] = {L, Lt, L, Lt, L, Lt, rows, rows, rows, rows, L, Lt, L, Lt};
+            s2_block_debug dbg;
+            float **p = reinterpret_cast<float **>(&dbg);
+            for (int i = 0; i < 14; ++i) {
+                m[i]->create(i < 2 ? 3 * dim : dim, h[i]);
+                p[i] = static_cast<float *>(*m[i]);
+            }
+            s2_dit_block_set_debug_tensors_host(block_, &dbg);
+        }
+        const int rc = track(s2_dit_block_forward_host(block_, opt.stream, vid, vid.h, txt, txt.h, emb,
+                                                       static_cast<const int32_t *>(shape), top[0], top[1]));
+        if (debug_) s2_dit_block_set_debug_tensors_host(block_, nullptr);
+        return rc;
     }
+
+    // Only for stage-by-stage numerical comparison; the tensors must outlive the
+    // forwards that fill them (seedvr2_dit_block.h:58).
+    void set_debug_tensors(SeedVR2DiTBlockDebugTensors *tensors) { debug_ = tensors; }
 
     // The same on device buffers (fp32, row-major), stream-ordered.
     int forward_device(const float *vid, int L, const float *txt, int Lt, const float *emb, float *vid_out,
@@ -268,6 +305,7 @@ public:
 private:
     int device_;
     s2_dit_block *block_ = nullptr;
+    SeedVR2DiTBlockDebugTensors *debug_ = nullptr;
     mutable std::string error_;
 
     int track(s2_status s) const

@@ -64,6 +64,16 @@ class GemmDesc(ctypes.Structure):
 GEMM_SPLIT_F16, GEMM_GATED_RESID_F32, GEMM_SWIGLU_F16 = 0, 2, 3
 
 
+DEBUG_TENSORS = ("qkv_vid", "qkv_txt", "norm_q_vid", "norm_q_txt", "norm_k_vid", "norm_k_txt", "attention_q",
+                 "attention_k", "attention_v", "attention_output", "projected_vid", "projected_txt", "output_vid",
+                 "output_txt")
+
+
+class BlockDebug(ctypes.Structure):
+    """s2_block_debug: device fp32 buffers of the block's 14 capture points."""
+    _fields_ = [(n, ctypes.c_void_p) for n in DEBUG_TENSORS]
+
+
 class Window(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("t0", "t1", "h0", "h1", "w0", "w1")]
 
@@ -155,6 +165,8 @@ _SIGS = {
     "s2_dit_block_forward_host": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _i32p, _vp,
                                                  _vp]),
     "s2_dit_block_last_launches": (ctypes.c_int, [_vp]),
+    "s2_dit_block_set_debug_tensors": (ctypes.c_int, [_vp, ctypes.POINTER(BlockDebug)]),
+    "s2_dit_block_debug_rows": (ctypes.c_int, [_vp, ctypes.c_int, _i32p]),
     "s2_dit_block_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_spatial_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_int, _vp, _vp]),
@@ -751,6 +763,32 @@ class SeedVR2DiTBlock:
                                                ctypes.c_void_p(vo.ctypes.data), ctypes.c_void_p(to.ctypes.data)),
                "s2_dit_block_forward_host")
         return vo, to
+
+    def debug_rows(self, text_len: int) -> int:
+        n = ctypes.c_int32(0)
+        _check(lib().s2_dit_block_debug_rows(self.handle, int(text_len), ctypes.byref(n)), "s2_dit_block_debug_rows")
+        return n.value
+
+    def set_debug_tensors(self, L: int, text_len: int, names=DEBUG_TENSORS):
+        """set_debug_tensors (seedvr2_dit_block.h:58): allocate device fp32
+        buffers for the named capture points and return them as a dict; the
+        next forwards fill them. None switches capturing off."""
+        if names is None:
+            _check(lib().s2_dit_block_set_debug_tensors(self.handle, None), "s2_dit_block_set_debug_tensors")
+            self._debug = None
+            return None
+        torch = _torch()
+        d, rows = self.dim, self.debug_rows(text_len)
+        shapes = {"qkv_vid": (L, 3 * d), "qkv_txt": (text_len, 3 * d), "norm_q_vid": (L, d), "norm_k_vid": (L, d),
+                  "norm_q_txt": (text_len, d), "norm_k_txt": (text_len, d), "attention_q": (rows, d),
+                  "attention_k": (rows, d), "attention_v": (rows, d), "attention_output": (rows, d),
+                  "projected_vid": (L, d), "projected_txt": (text_len, d), "output_vid": (L, d),
+                  "output_txt": (text_len, d)}
+        bufs = {n: torch.zeros(shapes[n], dtype=torch.float32, device=f"cuda:{self.device}") for n in names}
+        dbg = BlockDebug(**{n: t.data_ptr() for n, t in bufs.items()})
+        _check(lib().s2_dit_block_set_debug_tensors(self.handle, ctypes.byref(dbg)), "s2_dit_block_set_debug_tensors")
+        self._debug = bufs
+        return bufs
 
     def last_launches(self) -> int:
         return lib().s2_dit_block_last_launches(self.handle)

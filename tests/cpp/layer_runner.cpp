@@ -13,7 +13,8 @@
 // with make_input() :83-95 and weights :50-68 in load_model order.
 //
 // Thresholds are the reference runners' own: max|diff| < 1e-3 for the block, < 1e-4
-// for the VAE attention layer.
+// for the VAE attention layer. Two more cases compare the 14 debug capture points
+// (set_debug_tensors) with the reference's own captures of the same forward.
 //
 // usage: layer_runner <path to libs2ref.so>
 #include <dlfcn.h>
@@ -31,6 +32,8 @@ namespace
 using RefBlock = int (*)(int, int, int, int, int, int, int, int, float, const float *, size_t, const float *, int,
                          const float *, int, const float *, int, int, int, int, float *, float *);
 using RefVae = int (*)(int, int, int, int, const float *, size_t, const float *, int, float *);
+using RefBlockDebug = int (*)(int, int, int, int, int, int, int, int, float, const float *, size_t, const float *, int,
+                              const float *, int, const float *, int, int, int, int, float *, float *, float **, int *);
 
 struct BlockCase {
     int dim, heads, head_dim, mlp, T, H, W, text_len;
@@ -85,7 +88,13 @@ double max_abs(const float *a, const float *b, size_t n)
     return worst;
 }
 
-int run_block(const BlockCase &tc, RefBlock ref, double &diff)
+// With `refd` set, both sides capture the reference's 14 debug tensors
+// (set_debug_tensors, seedvr2_dit_block.h:20-36) and *debug_worst receives the
+// largest per-capture max|diff| relative to its allowance: 2e-3 of the
+// capture's scale (this build keeps the QKV projections in fp16), or one bf16
+// ulp of it for the bf16-rounded attention captures; <= 1 passes.
+int run_block(const BlockCase &tc, RefBlock ref, double &diff, RefBlockDebug refd = nullptr,
+              double *debug_worst = nullptr)
 {
     std::vector<float> weights;
     push_branch(weights, tc, 0);
@@ -98,10 +107,32 @@ int run_block(const BlockCase &tc, RefBlock ref, double &diff)
     fill_rows(emb, tc.dim * 6, 1, 200);
 
     std::vector<float> rv(vid.size()), rt(txt.size());
-    if (ref(0, tc.shared, tc.last, tc.shifted, tc.dim, tc.heads, tc.head_dim, tc.mlp, 1e-5f, weights.data(),
-            weights.size(), vid.data(), L, txt.data(), tc.text_len, emb.data(), tc.T, tc.H, tc.W, 4, rv.data(),
-            rt.data()) != 0)
+    s2b200::SeedVR2DiTBlockDebugTensors mine;
+    std::vector<std::vector<float>> theirs(14);
+    if (refd) {
+        // capture sizes: packed rows = sum over windows of (L_w + text_len)
+        int n_win = 0, rows = 0;
+        s2_make_windows(tc.T, tc.H, tc.W, tc.shifted ? 1 : 0, 0, 0, 0, nullptr, 0, &n_win);
+        std::vector<s2_window> wins(n_win);
+        s2_make_windows(tc.T, tc.H, tc.W, tc.shifted ? 1 : 0, 0, 0, 0, wins.data(), n_win, &n_win);
+        for (const s2_window &w : wins) rows += (w.t1 - w.t0) * (w.h1 - w.h0) * (w.w1 - w.w0) + tc.text_len;
+        const int h[14] = {L, tc.text_len, L, tc.text_len, L, tc.text_len, rows, rows, rows, rows,
+                           L, tc.text_len, L, tc.text_len};
+        float *ptrs[14];
+        for (int k = 0; k < 14; ++k) {
+            theirs[k].assign(static_cast<size_t>(h[k]) * (k < 2 ? 3 * tc.dim : tc.dim), 0.f);
+            ptrs[k] = theirs[k].data();
+        }
+        int got_rows = 0;
+        if (refd(0, tc.shared, tc.last, tc.shifted, tc.dim, tc.heads, tc.head_dim, tc.mlp, 1e-5f, weights.data(),
+                 weights.size(), vid.data(), L, txt.data(), tc.text_len, emb.data(), tc.T, tc.H, tc.W, 4, rv.data(),
+                 rt.data(), ptrs, &got_rows) != 0 || got_rows != rows)
+            return -2;
+    } else if (ref(0, tc.shared, tc.last, tc.shifted, tc.dim, tc.heads, tc.head_dim, tc.mlp, 1e-5f, weights.data(),
+                   weights.size(), vid.data(), L, txt.data(), tc.text_len, emb.data(), tc.T, tc.H, tc.W, 4, rv.data(),
+                   rt.data()) != 0) {
         return -2;
+    }
 
     s2b200::SeedVR2DiTBlock layer;
     s2b200::ParamDict pd;
@@ -120,6 +151,7 @@ int run_block(const BlockCase &tc, RefBlock ref, double &diff)
         return -1;
     }
     layer.set_runtime_shape(tc.T, tc.H, tc.W);
+    if (refd) layer.set_debug_tensors(&mine);
     std::vector<s2b200::Mat> bottom(4), top(2);
     bottom[0].create(tc.dim, L);
     bottom[1].create(tc.dim, tc.text_len);
@@ -136,6 +168,26 @@ int run_block(const BlockCase &tc, RefBlock ref, double &diff)
         return -1;
     }
     diff = std::fmax(max_abs(top[0], rv.data(), rv.size()), max_abs(top[1], rt.data(), rt.size()));
+    if (refd && debug_worst) {
+        const s2b200::Mat *m[14] = {&mine.qkv_vid, &mine.qkv_txt, &mine.norm_q_vid, &mine.norm_q_txt, &mine.norm_k_vid,
+                                    &mine.norm_k_txt, &mine.attention_q, &mine.attention_k, &mine.attention_v,
+                                    &mine.attention_output, &mine.projected_vid, &mine.projected_txt,
+                                    &mine.output_vid, &mine.output_txt};
+        *debug_worst = 0.0;
+        for (int k = 0; k < 14; ++k) {
+            const std::vector<float> &r = theirs[k];
+            if (r.empty()) continue;
+            if (m[k]->empty() || static_cast<size_t>(m[k]->w) * m[k]->h != r.size()) {
+                *debug_worst = 1e9;
+                continue;
+            }
+            double amax = 0.0;
+            for (float v : r) amax = std::fmax(amax, std::fabs(v));
+            const double allow = (k >= 6 && k <= 9) ? std::fmax(2e-3 * std::fmax(1.0, amax), amax / 128.0)
+                                                    : 2e-3 * std::fmax(1.0, amax);
+            *debug_worst = std::fmax(*debug_worst, max_abs(*m[k], r.data(), r.size()) / allow);
+        }
+    }
     return 0;
 }
 
@@ -231,7 +283,8 @@ int main(int argc, char **argv)
     }
     auto ref_block = reinterpret_cast<RefBlock>(dlsym(lib, "ref_block_forward"));
     auto ref_vae = reinterpret_cast<RefVae>(dlsym(lib, "ref_vae_attention"));
-    if (!ref_block || !ref_vae) {
+    auto ref_block_debug = reinterpret_cast<RefBlockDebug>(dlsym(lib, "ref_block_forward_debug"));
+    if (!ref_block || !ref_vae || !ref_block_debug) {
         std::fprintf(stderr, "reference symbols missing\n");
         return 2;
     }
@@ -258,6 +311,14 @@ int main(int argc, char **argv)
         const int r = run_block(tc, ref_block, diff);
         const bool ok = r == 0 && diff < 1e-3;
         std::printf("[block %d] %s : max|diff| = %.6g %s\n", i++, tc.name, r == 0 ? diff : -1.0, ok ? "PASS" : "FAIL");
+        ok ? ++pass : ++fail;
+    }
+    for (int c : {1, 3}) {  // set_debug_tensors on a shifted and an unshifted case
+        double diff = 0.0, worst = 0.0;
+        const int r = run_block(blocks[c], ref_block, diff, ref_block_debug, &worst);
+        const bool ok = r == 0 && diff < 1e-3 && worst <= 1.0;
+        std::printf("[debug %d] 14 capture points vs the reference's : worst diff / allowance = %.4g %s\n", c,
+                    r == 0 ? worst : -1.0, ok ? "PASS" : "FAIL");
         ok ? ++pass : ++fail;
     }
     i = 0;

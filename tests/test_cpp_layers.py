@@ -47,4 +47,4 @@ def test_layer_runner_on_gpu(tmp_path):
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("[")]
-    assert len(lines) == 9 and all(ln.endswith("PASS") for ln in lines), r.stdout
+    assert len(lines) == 11 and all(ln.endswith("PASS") for ln in lines), r.stdout

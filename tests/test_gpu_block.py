@@ -105,6 +105,46 @@ def test_config2_full_width_block_vs_reference(torch_cuda, ref, index, shared, s
     check_block(vo, to, evo, eto, vid, txt, f"config-2 block {index}")
 
 
+@pytest.mark.parametrize("shared,last,shifted", [(False, False, True), (True, True, False)])
+def test_debug_tensors_vs_reference(torch_cuda, ref, shared, last, shifted):
+    """set_debug_tensors: all 14 capture points against the reference's own
+    captures of the same forward (seedvr2_dit_block.h:20-36). The QKV
+    projections are fp16 here (the reference keeps fp32), so captures before
+    the bf16 rounding are gated at 2e-3 of their scale; the bf16-rounded q/k/v
+    and window outputs at max(2e-3, one bf16 ulp) per element; every capture
+    at cosine >= 0.9999."""
+    torch = torch_cuda
+    dim, heads, mlp, grid = 256, 2, 256, (2, 8, 12)
+    w = synth.block_weights(dim, heads, mlp, shared, seed=70 + shared)
+    vid, txt, emb = synth.block_activations(grid, dim, seed=71)
+    params = dict(block_index=12 if shared else 3, shared=shared, last=last, shifted=shifted, dim=dim, heads=heads,
+                  head_dim=128, mlp_hidden=mlp, eps=1e-5)
+    evo, eto, caps = ref.block_forward_debug(params, w, vid, txt, emb, grid)
+    b = s2b200.SeedVR2DiTBlock()
+    assert b.load_param(**params) == 0
+    b.load_model(w)
+    b.set_runtime_shape(*grid)
+    bufs = b.set_debug_tensors(vid.shape[0], txt.shape[0])
+    vo, to = b.forward(torch.from_numpy(vid).cuda(), torch.from_numpy(txt).cuda(), torch.from_numpy(emb).cuda())
+    torch.cuda.synchronize()
+    assert b.device_error() == 0
+    for name, want in caps.items():
+        got = bufs[name].cpu().numpy()
+        assert got.shape == want.shape, (name, got.shape, want.shape)
+        if name.startswith("attention_"):
+            parity.check(got, want, True, name)
+        else:
+            m = parity.metrics(got, want)
+            scale = max(1.0, float(np.abs(want).max()))
+            assert m["max_abs"] <= parity.MAX_ABS * scale and m["cosine"] >= parity.COSINE, (name, m)
+    # capturing does not change the outputs
+    b.set_debug_tensors(0, 0, names=None)
+    vo2, to2 = b.forward(torch.from_numpy(vid).cuda(), torch.from_numpy(txt).cuda(), torch.from_numpy(emb).cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(vo, vo2) and torch.equal(to, to2)
+    assert np.array_equal(bufs["output_vid"].cpu().numpy(), vo.cpu().numpy())
+
+
 def test_host_forward_matches_device(torch_cuda):
     params, w, vid, txt, emb, shape, _, _ = refcases.block_case(refcases.BLOCK_CASES[3])
     vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
