@@ -166,6 +166,7 @@ _SIGS = {
                                                  _vp]),
     "s2_dit_block_last_launches": (ctypes.c_int, [_vp]),
     "s2_dit_block_set_debug_tensors": (ctypes.c_int, [_vp, ctypes.POINTER(BlockDebug)]),
+    "s2_dit_block_set_debug_tensors_host": (ctypes.c_int, [_vp, ctypes.POINTER(BlockDebug)]),
     "s2_dit_block_debug_rows": (ctypes.c_int, [_vp, ctypes.c_int, _i32p]),
     "s2_dit_block_device_error": (ctypes.c_int, [_vp, _i32p]),
     "s2_spatial_attention": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
