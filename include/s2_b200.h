@@ -112,6 +112,32 @@ S2_API s2_status s2_build_varlen(int frames, int height, int width,
  * text_len). Every window has one owner, so every video token has one. */
 S2_API s2_status s2_shard_windows(const s2_window *windows, int n, int text_len, int n_ranks, int32_t *owner);
 
+/* The sharded DiT step's ownership of BOTH window kinds of a grid, chosen
+ * together so that few rows change owner at the plain <-> shifted layer
+ * boundaries: the plain windows (owner_plain, s2_make_windows order) in
+ * contiguous runs of their order with the smallest largest run cost (S_w^2); each
+ * shifted window (owner_shifted), costliest first, to the rank holding most of
+ * its rows whose load stays within 2 % of the mean (else the least loaded).
+ * Per-kind s2_shard_windows ownership is returned instead when it moves fewer
+ * rows at no worse balance (small grids whose tilings split along frames). */
+S2_API s2_status s2_shard_windows_joint(int frames, int height, int width, int wt, int wh, int ww, int text_len,
+                                        int n_ranks, int32_t *owner_plain, int32_t *owner_shifted);
+/* Rank `rank`'s view of that ownership for window kind `kind` (0 plain, 1
+ * shifted) and the row exchange to the other kind, as the sharded step runs
+ * it: the windows it owns (window_ids, *n_windows); its local rows
+ * (local_tokens: the patched-grid token of each, window by window, (t, y, x)
+ * inside a window; *n_local); send_rows: its local rows to send, destination
+ * by destination (send_counts[n_ranks]), each in the destination's local order
+ * of the other kind; recv_rows: where the rows received from each source
+ * (recv_counts[n_ranks]) go in its local order of the other kind; its own
+ * rows are among both (a local copy). *moved_rows: tokens of the grid whose
+ * owner changes. Arrays may be NULL; their sizes are at most frames*height*width
+ * (windows: the kind's window count). */
+S2_API s2_status s2_shard_exchange(int frames, int height, int width, int wt, int wh, int ww, int text_len,
+                                   int n_ranks, int rank, int kind, int32_t *window_ids, int *n_windows,
+                                   int32_t *local_tokens, int *n_local, int32_t *send_counts, int32_t *send_rows,
+                                   int32_t *recv_counts, int32_t *recv_rows, long long *moved_rows);
+
 /* ---- device kernels (explicit buffers) ---------------------------------- */
 
 /* Fused prologue: per (packed row, head) RMSNorm over 128 dims (eps) times

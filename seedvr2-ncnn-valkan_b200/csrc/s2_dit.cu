@@ -407,69 +407,45 @@ extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int las
     return S2_OK;
 }
 
-// Window ownership of both window kinds, every rank's local row order, and the
-// row-exchange maps between them; sets every block's window subset.
+// Window ownership of both window kinds (s2_shard_windows_joint), every rank's
+// local row order, and the row-exchange maps between them (s2::shard_exchange_maps,
+// the host function the CPU-rank tests check); sets every block's window subset.
 static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
 {
     auto &sh = d->sh;
     if (sh.valid && sh.T == T && sh.Hp == Hp && sh.Wp == Wp && sh.Lt == Lt) return S2_OK;
     sh.valid = false;
-    const int N = s2_comm_size(d->comm), me = s2_comm_rank(d->comm), L = T * Hp * Wp;
-    std::vector<std::vector<std::vector<int32_t>>> tok(2, std::vector<std::vector<int32_t>>(N));
-    std::vector<std::vector<int32_t>> own_rank(2, std::vector<int32_t>(L, -1)), own_idx(2, std::vector<int32_t>(L, -1));
+    const int N = s2_comm_size(d->comm), me = s2_comm_rank(d->comm);
+    s2::ShardMaps m;
+    s2_status s = s2::shard_exchange_maps(T, Hp, Wp, d->wt, d->wh, d->ww, Lt, N, me, m);
+    if (s != S2_OK) return s;
     for (int k = 0; k < 2; ++k) {
-        int n = 0;
-        s2_status s = s2_make_windows(T, Hp, Wp, k, d->wt, d->wh, d->ww, nullptr, 0, &n);
-        if (s != S2_OK) return s;
-        std::vector<s2_window> w(n);
-        s2_make_windows(T, Hp, Wp, k, d->wt, d->wh, d->ww, w.data(), n, &n);
-        std::vector<int32_t> owner(n);
-        if ((s = s2_shard_windows(w.data(), n, Lt, N, owner.data())) != S2_OK) return s;
-        sh.ids[k].clear();
-        for (int i = 0; i < n; ++i) {
-            if (owner[i] == me) sh.ids[k].push_back(i);
-            auto &list = tok[k][owner[i]];
-            for (int t = w[i].t0; t < w[i].t1; ++t)
-                for (int y = w[i].h0; y < w[i].h1; ++y)
-                    for (int x = w[i].w0; x < w[i].w1; ++x) {
-                        const int p = (t * Hp + y) * Wp + x;
-                        own_rank[k][p] = owner[i];
-                        own_idx[k][p] = static_cast<int32_t>(list.size());
-                        list.push_back(p);
-                    }
-        }
-        for (int p = 0; p < L; ++p)
-            if (own_rank[k][p] < 0) return s2::set_error(S2_INFERENCE_FAILED, "shard: token %d has no window", p);
-        sh.n_local[k] = static_cast<int>(tok[k][me].size());
-        if (!sh.tok[k].ensure(std::max<size_t>(tok[k][me].size(), 1) * 4) ||
-            cudaMemcpy(sh.tok[k].ptr, tok[k][me].data(), tok[k][me].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        sh.ids[k] = m.ids[k];
+        sh.n_local[k] = static_cast<int>(m.tok[k].size());
+        if (!sh.tok[k].ensure(std::max<size_t>(m.tok[k].size(), 1) * 4) ||
+            cudaMemcpy(sh.tok[k].ptr, m.tok[k].data(), m.tok[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
     }
     const size_t row_bytes = static_cast<size_t>(d->dim) * 4;
     for (int k = 0; k < 2; ++k) {
-        const int k2 = 1 - k;
-        std::vector<int32_t> src, dst;
         sh.send_off[k].assign(N, 0);
         sh.send_bytes[k].assign(N, 0);
         sh.recv_off[k].assign(N, 0);
         sh.recv_bytes[k].assign(N, 0);
-        for (int p2 = 0; p2 < N; ++p2) {  // rows I send to p2, in p2's local order of kind k2
-            sh.send_off[k][p2] = src.size() * row_bytes;
-            for (int p : tok[k2][p2])
-                if (own_rank[k][p] == me) src.push_back(own_idx[k][p]);
-            sh.send_bytes[k][p2] = src.size() * row_bytes - sh.send_off[k][p2];
+        size_t so = 0, ro = 0;
+        for (int p = 0; p < N; ++p) {
+            sh.send_off[k][p] = so * row_bytes;
+            sh.send_bytes[k][p] = static_cast<size_t>(m.send_count[k][p]) * row_bytes;
+            so += m.send_count[k][p];
+            sh.recv_off[k][p] = ro * row_bytes;
+            sh.recv_bytes[k][p] = static_cast<size_t>(m.recv_count[k][p]) * row_bytes;
+            ro += m.recv_count[k][p];
         }
-        for (int p1 = 0; p1 < N; ++p1) {  // rows I receive from p1, in my local order of kind k2
-            sh.recv_off[k][p1] = dst.size() * row_bytes;
-            for (size_t i = 0; i < tok[k2][me].size(); ++i)
-                if (own_rank[k][tok[k2][me][i]] == p1) dst.push_back(static_cast<int32_t>(i));
-            sh.recv_bytes[k][p1] = dst.size() * row_bytes - sh.recv_off[k][p1];
-        }
-        sh.send_rows[k] = static_cast<int>(src.size());
-        if (!sh.send_src[k].ensure(std::max<size_t>(src.size(), 1) * 4) ||
-            !sh.recv_dst[k].ensure(std::max<size_t>(dst.size(), 1) * 4) ||
-            cudaMemcpy(sh.send_src[k].ptr, src.data(), src.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemcpy(sh.recv_dst[k].ptr, dst.data(), dst.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        sh.send_rows[k] = static_cast<int>(m.src[k].size());
+        if (!sh.send_src[k].ensure(std::max<size_t>(m.src[k].size(), 1) * 4) ||
+            !sh.recv_dst[k].ensure(std::max<size_t>(m.dst[k].size(), 1) * 4) ||
+            cudaMemcpy(sh.send_src[k].ptr, m.src[k].data(), m.src[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(sh.recv_dst[k].ptr, m.dst[k].data(), m.dst[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
     }
     for (int i = 0; i < d->n_blocks; ++i) {

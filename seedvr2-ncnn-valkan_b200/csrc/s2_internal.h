@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "s2_b200.h"
 
@@ -15,6 +16,22 @@ s2_status set_error(s2_status st, const char *fmt, ...);
 void clear_error();
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// The sharded step's window ownership (s2_shard_windows_joint) of both window
+// kinds and rank `rank`'s view of it: the windows it owns (ids), its local token
+// order (tok: patched-grid token per local row), and the row exchange from kind
+// k to kind 1 - k -- src[k]: local rows of kind k to send, destination rank by
+// destination rank (send_count), each in the destination's local order of kind
+// 1 - k; dst[k]: where the received rows go in this rank's local order of kind
+// 1 - k, source rank by source rank (recv_count). moved_rows[k]: tokens whose
+// owner changes from kind k to kind 1 - k (all ranks).
+struct ShardMaps {
+    std::vector<int32_t> ids[2], tok[2], src[2], dst[2];
+    std::vector<int32_t> send_count[2], recv_count[2];
+    long long moved_rows[2] = {0, 0};
+};
+s2_status shard_exchange_maps(int T, int H, int W, int wt, int wh, int ww, int text_len, int n_ranks, int rank,
+                              ShardMaps &maps);
 
 // Failure injection for tests (s2_debug_attention_fault): hands the next
 // s2_window_attention launch its K tile to leave out (-1: none) and its wait

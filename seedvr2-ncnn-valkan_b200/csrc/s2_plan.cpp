@@ -189,6 +189,231 @@ extern "C" s2_status s2_shard_windows(const s2_window *windows, int n, int text_
     return S2_OK;
 }
 
+// ---- joint ownership and row-exchange maps of the sharded step ---------------
+
+namespace {
+
+s2_status windows_of(int T, int H, int W, int kind, int wt, int wh, int ww, std::vector<s2_window> &w)
+{
+    int n = 0;
+    s2_status s = s2_make_windows(T, H, W, kind, wt, wh, ww, nullptr, 0, &n);
+    if (s != S2_OK) return s;
+    w.resize(n);
+    return s2_make_windows(T, H, W, kind, wt, wh, ww, w.data(), n, &n);
+}
+
+double window_cost(const s2_window &w, int text_len)
+{
+    const double s = static_cast<double>(w.t1 - w.t0) * (w.h1 - w.h0) * (w.w1 - w.w0) + text_len;
+    return s * s;
+}
+
+}  // namespace
+
+extern "C" s2_status s2_shard_windows_joint(int frames, int height, int width, int wt, int wh, int ww, int text_len,
+                                            int n_ranks, int32_t *owner_plain, int32_t *owner_shifted)
+{
+    s2::clear_error();
+    if (!owner_plain || !owner_shifted || n_ranks <= 0 || text_len < 0)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_shard_windows_joint: invalid arguments");
+    std::vector<s2_window> w0, w1;
+    s2_status s = windows_of(frames, height, width, 0, wt, wh, ww, w0);
+    if (s == S2_OK) s = windows_of(frames, height, width, 1, wt, wh, ww, w1);
+    if (s != S2_OK) return s;
+    // plain windows: contiguous runs of the window order (width-major, then height, then
+    // time: neighbouring windows share a column band), the runs chosen to minimise the
+    // largest run cost (bisection on that cap; greedy packing decides feasibility)
+    std::vector<double> c0(w0.size());
+    double total = 0.0, biggest = 0.0;
+    for (size_t i = 0; i < w0.size(); ++i) {
+        c0[i] = window_cost(w0[i], text_len);
+        total += c0[i];
+        biggest = std::max(biggest, c0[i]);
+    }
+    auto runs = [&](double cap, int32_t *own) {
+        int r = 0;
+        double acc = 0.0;
+        for (size_t i = 0; i < c0.size(); ++i) {
+            if (acc > 0.0 && acc + c0[i] > cap) {
+                ++r;
+                acc = 0.0;
+            }
+            acc += c0[i];
+            if (own) own[i] = std::min(r, n_ranks - 1);
+        }
+        return r + 1;
+    };
+    double lo = std::max(biggest, total / n_ranks), hi = total;
+    for (int it = 0; it < 64 && hi - lo > 1e-9 * total; ++it) {
+        const double mid = 0.5 * (lo + hi);
+        (runs(mid, nullptr) <= n_ranks ? hi : lo) = mid;
+    }
+    runs(hi, owner_plain);
+    // the owner of every token under the plain ownership
+    const long long L = 1LL * frames * height * width;
+    std::vector<int32_t> tok_owner(static_cast<size_t>(L), 0);
+    for (size_t i = 0; i < w0.size(); ++i)
+        for (int t = w0[i].t0; t < w0[i].t1; ++t)
+            for (int y = w0[i].h0; y < w0[i].h1; ++y)
+                for (int x = w0[i].w0; x < w0[i].w1; ++x)
+                    tok_owner[(static_cast<size_t>(t) * height + y) * width + x] = owner_plain[i];
+    // shifted windows, costliest first: to the rank holding most of its rows whose load
+    // stays within 2 % of the mean; otherwise to the least loaded rank
+    double total1 = 0.0;
+    for (const s2_window &w : w1) total1 += window_cost(w, text_len);
+    const double cap = 1.02 * total1 / n_ranks;
+    std::vector<int> order(w1.size());
+    for (size_t i = 0; i < w1.size(); ++i) order[i] = static_cast<int>(i);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return window_cost(w1[a], text_len) > window_cost(w1[b], text_len); });
+    std::vector<double> load(n_ranks, 0.0);
+    std::vector<long long> overlap(n_ranks);
+    for (int i : order) {
+        std::fill(overlap.begin(), overlap.end(), 0);
+        for (int t = w1[i].t0; t < w1[i].t1; ++t)
+            for (int y = w1[i].h0; y < w1[i].h1; ++y)
+                for (int x = w1[i].w0; x < w1[i].w1; ++x) ++overlap[tok_owner[(static_cast<size_t>(t) * height + y) * width + x]];
+        const double c = window_cost(w1[i], text_len);
+        int best = -1;
+        for (int r = 0; r < n_ranks; ++r)
+            if (load[r] + c <= cap && (best < 0 || overlap[r] > overlap[best])) best = r;
+        if (best < 0) {
+            best = 0;
+            for (int r = 1; r < n_ranks; ++r)
+                if (load[r] < load[best]) best = r;
+        }
+        owner_shifted[i] = best;
+        load[best] += c;
+    }
+    // Per-kind LPT (s2_shard_windows) is kept instead when it happens to move fewer rows
+    // at no worse balance (small grids whose two tilings split along the same frames).
+    std::vector<int32_t> lpt0(w0.size()), lpt1(w1.size());
+    if (s2_shard_windows(w0.data(), static_cast<int>(w0.size()), text_len, n_ranks, lpt0.data()) == S2_OK &&
+        s2_shard_windows(w1.data(), static_cast<int>(w1.size()), text_len, n_ranks, lpt1.data()) == S2_OK) {
+        auto score = [&](const int32_t *o0, const int32_t *o1, long long &moved, double &worst) {
+            std::vector<int32_t> own(static_cast<size_t>(L));
+            for (size_t i = 0; i < w0.size(); ++i)
+                for (int t = w0[i].t0; t < w0[i].t1; ++t)
+                    for (int y = w0[i].h0; y < w0[i].h1; ++y)
+                        for (int x = w0[i].w0; x < w0[i].w1; ++x)
+                            own[(static_cast<size_t>(t) * height + y) * width + x] = o0[i];
+            moved = 0;
+            for (size_t i = 0; i < w1.size(); ++i)
+                for (int t = w1[i].t0; t < w1[i].t1; ++t)
+                    for (int y = w1[i].h0; y < w1[i].h1; ++y)
+                        for (int x = w1[i].w0; x < w1[i].w1; ++x)
+                            moved += own[(static_cast<size_t>(t) * height + y) * width + x] != o1[i];
+            worst = 0.0;
+            for (int k = 0; k < 2; ++k) {
+                const std::vector<s2_window> &w = k ? w1 : w0;
+                const int32_t *o = k ? o1 : o0;
+                std::vector<double> ld(n_ranks, 0.0);
+                double sum = 0.0;
+                for (size_t i = 0; i < w.size(); ++i) {
+                    ld[o[i]] += window_cost(w[i], text_len);
+                    sum += window_cost(w[i], text_len);
+                }
+                worst = std::max(worst, *std::max_element(ld.begin(), ld.end()) / (sum / n_ranks));
+            }
+        };
+        long long mj = 0, ml = 0;
+        double bj = 0.0, bl = 0.0;
+        score(owner_plain, owner_shifted, mj, bj);
+        score(lpt0.data(), lpt1.data(), ml, bl);
+        if (ml < mj && bl <= bj) {
+            std::copy(lpt0.begin(), lpt0.end(), owner_plain);
+            std::copy(lpt1.begin(), lpt1.end(), owner_shifted);
+        }
+    }
+    return S2_OK;
+}
+
+namespace s2 {
+
+s2_status shard_exchange_maps(int T, int H, int W, int wt, int wh, int ww, int text_len, int n_ranks, int rank,
+                              ShardMaps &m)
+{
+    std::vector<s2_window> w[2];
+    for (int k = 0; k < 2; ++k) {
+        const s2_status s = windows_of(T, H, W, k, wt, wh, ww, w[k]);
+        if (s != S2_OK) return s;
+    }
+    std::vector<int32_t> owner[2] = {std::vector<int32_t>(w[0].size()), std::vector<int32_t>(w[1].size())};
+    s2_status s = s2_shard_windows_joint(T, H, W, wt, wh, ww, text_len, n_ranks, owner[0].data(), owner[1].data());
+    if (s != S2_OK) return s;
+    const long long L = 1LL * T * H * W;
+    std::vector<std::vector<std::vector<int32_t>>> tok(2, std::vector<std::vector<int32_t>>(n_ranks));
+    std::vector<std::vector<int32_t>> own_rank(2, std::vector<int32_t>(L, -1)), own_idx(2, std::vector<int32_t>(L, -1));
+    for (int k = 0; k < 2; ++k) {
+        m.ids[k].clear();
+        for (size_t i = 0; i < w[k].size(); ++i) {
+            const int o = owner[k][i];
+            if (o == rank) m.ids[k].push_back(static_cast<int32_t>(i));
+            auto &list = tok[k][o];
+            for (int t = w[k][i].t0; t < w[k][i].t1; ++t)
+                for (int y = w[k][i].h0; y < w[k][i].h1; ++y)
+                    for (int x = w[k][i].w0; x < w[k][i].w1; ++x) {
+                        const int p = (t * H + y) * W + x;
+                        own_rank[k][p] = o;
+                        own_idx[k][p] = static_cast<int32_t>(list.size());
+                        list.push_back(p);
+                    }
+        }
+        for (long long p = 0; p < L; ++p)
+            if (own_rank[k][p] < 0) return set_error(S2_INFERENCE_FAILED, "shard: token %lld has no window", p);
+        m.tok[k] = tok[k][rank];
+    }
+    m.moved_rows[0] = m.moved_rows[1] = 0;
+    for (int k = 0; k < 2; ++k) {
+        const int k2 = 1 - k;
+        m.src[k].clear();
+        m.dst[k].clear();
+        m.send_count[k].assign(n_ranks, 0);
+        m.recv_count[k].assign(n_ranks, 0);
+        for (int p2 = 0; p2 < n_ranks; ++p2) {  // rows I send to p2, in p2's local order of kind k2
+            for (int p : tok[k2][p2])
+                if (own_rank[k][p] == rank) {
+                    m.src[k].push_back(own_idx[k][p]);
+                    ++m.send_count[k][p2];
+                }
+        }
+        for (int p1 = 0; p1 < n_ranks; ++p1)  // rows I receive from p1, in my local order of kind k2
+            for (size_t i = 0; i < tok[k2][rank].size(); ++i)
+                if (own_rank[k][tok[k2][rank][i]] == p1) {
+                    m.dst[k].push_back(static_cast<int32_t>(i));
+                    ++m.recv_count[k][p1];
+                }
+        for (long long p = 0; p < L; ++p)
+            if (own_rank[k][p] != own_rank[k2][p]) ++m.moved_rows[k];
+    }
+    return S2_OK;
+}
+
+}  // namespace s2
+
+extern "C" s2_status s2_shard_exchange(int frames, int height, int width, int wt, int wh, int ww, int text_len,
+                                       int n_ranks, int rank, int kind, int32_t *window_ids, int *n_windows,
+                                       int32_t *local_tokens, int *n_local, int32_t *send_counts, int32_t *send_rows,
+                                       int32_t *recv_counts, int32_t *recv_rows, long long *moved_rows)
+{
+    s2::clear_error();
+    if (n_ranks <= 0 || rank < 0 || rank >= n_ranks || (kind != 0 && kind != 1) || !n_windows || !n_local)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_shard_exchange: invalid arguments");
+    s2::ShardMaps m;
+    const s2_status s = s2::shard_exchange_maps(frames, height, width, wt, wh, ww, text_len, n_ranks, rank, m);
+    if (s != S2_OK) return s;
+    *n_windows = static_cast<int>(m.ids[kind].size());
+    *n_local = static_cast<int>(m.tok[kind].size());
+    if (window_ids) std::copy(m.ids[kind].begin(), m.ids[kind].end(), window_ids);
+    if (local_tokens) std::copy(m.tok[kind].begin(), m.tok[kind].end(), local_tokens);
+    if (send_counts) std::copy(m.send_count[kind].begin(), m.send_count[kind].end(), send_counts);
+    if (recv_counts) std::copy(m.recv_count[kind].begin(), m.recv_count[kind].end(), recv_counts);
+    if (send_rows) std::copy(m.src[kind].begin(), m.src[kind].end(), send_rows);
+    if (recv_rows) std::copy(m.dst[kind].begin(), m.dst[kind].end(), recv_rows);
+    if (moved_rows) *moved_rows = m.moved_rows[kind];
+    return S2_OK;
+}
+
 // ---- failure injection (tests) ------------------------------------------------
 
 namespace {

@@ -94,6 +94,9 @@ _SIGS = {
                                                            _i32p, ctypes.POINTER(Row), _i32p]),
     "s2_plan_work": (ctypes.c_int, [_i32p, ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
     "s2_shard_windows": (ctypes.c_int, [ctypes.POINTER(Window), ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p]),
+    "s2_shard_windows_joint": (ctypes.c_int, [ctypes.c_int] * 8 + [_i32p, _i32p]),
+    "s2_shard_exchange": (ctypes.c_int, [ctypes.c_int] * 10 + [_i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p,
+                                                              _i32p, ctypes.POINTER(ctypes.c_longlong)]),
     "s2_rope_table_bytes": (ctypes.c_size_t, [ctypes.c_int]),
     "s2_rope_table": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
     "s2_qk_norm_rope": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, _vp,
@@ -373,6 +376,24 @@ def shard_windows(windows: np.ndarray, text_len: int, n_ranks: int) -> list[np.n
         owner[i] = r
         load[r] += costs[i]
     return [np.nonzero(owner == r)[0].astype(np.int32) for r in range(n_ranks)]
+
+
+def shard_exchange(grid, text_len: int, n_ranks: int, rank: int, kind: int, override=(0, 0, 0)) -> dict:
+    """s2_shard_exchange: rank `rank`'s windows, local rows and row-exchange maps
+    from window kind `kind` to the other kind (host planning, no GPU)."""
+    T, H, W = grid
+    L = T * H * W
+    ids, tok = np.zeros(L, np.int32), np.zeros(L, np.int32)
+    sc, rc = np.zeros(n_ranks, np.int32), np.zeros(n_ranks, np.int32)
+    sr, rr = np.zeros(L, np.int32), np.zeros(L, np.int32)
+    nw, nl, moved = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_longlong(0)
+    p = lambda a: a.ctypes.data_as(_i32p)  # noqa: E731
+    _check(lib().s2_shard_exchange(T, H, W, *override, text_len, n_ranks, rank, kind, p(ids), ctypes.byref(nw),
+                                   p(tok), ctypes.byref(nl), p(sc), p(sr), p(rc), p(rr), ctypes.byref(moved)),
+           "s2_shard_exchange")
+    return {"window_ids": ids[:nw.value].copy(), "local_tokens": tok[:nl.value].copy(), "send_counts": sc,
+            "send_rows": sr[:int(sc.sum())].copy(), "recv_counts": rc, "recv_rows": rr[:int(rc.sum())].copy(),
+            "moved_rows": moved.value}
 
 
 def shard_owners(windows: np.ndarray, text_len: int, n_ranks: int) -> np.ndarray:

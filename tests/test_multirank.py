@@ -89,3 +89,79 @@ def test_library_sharding_matches_python_lpt(grid, shifted, n):
     parts = s2b200.shard_windows(wins, 58, n)
     for r in range(n):
         assert np.nonzero(owner == r)[0].tolist() == parts[r].tolist()
+
+
+# ---- the sharded DiT step's row exchange (plain <-> shifted ownership) -------------
+
+def _exchange_rank_main(rank, world, port, grid, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    ok = True
+    try:
+        for kind in (0, 1):
+            m = s2b200.shard_exchange(grid, 58, world, rank, kind)
+            nxt = s2b200.shard_exchange(grid, 58, world, rank, 1 - kind)
+            # every local row carries its token id; exchange them exactly as the step exchanges hidden rows
+            x = torch.from_numpy(m["local_tokens"].astype(np.float64))
+            send = x[torch.from_numpy(m["send_rows"]).long()]
+            recv = torch.empty(int(m["recv_counts"].sum()), dtype=torch.float64)
+            dist.all_to_all_single(recv, send, output_split_sizes=m["recv_counts"].tolist(),
+                                   input_split_sizes=m["send_counts"].tolist())
+            y = torch.full((len(nxt["local_tokens"]),), -1.0, dtype=torch.float64)
+            y[torch.from_numpy(m["recv_rows"]).long()] = recv
+            ok &= bool(torch.equal(y, torch.from_numpy(nxt["local_tokens"].astype(np.float64))))
+        np.save(os.path.join(out_dir, f"ok_{rank}.npy"), np.array([ok]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_exchange_maps_on_gloo_ranks(tmp_path, world):
+    """The maps of the sharded Euler step (s2_shard_exchange, the host function
+    the GPU path uploads): each gloo rank holds its local rows of one window
+    kind (values = token ids), exchanges them with all_to_all_single as the step
+    does with hidden rows, and must end with exactly its local rows of the other
+    kind in their order -- both directions, 720p grid."""
+    grid = (6, 45, 80)
+    mp.start_processes(_exchange_rank_main, args=(world, _free_port(), grid, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        assert bool(np.load(tmp_path / f"ok_{r}.npy")[0]), f"rank {r}"
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("grid", [(6, 45, 80), (12, 67, 120), (2, 16, 30)])
+def test_shard_local_rows_follow_the_single_rank_order(grid, world):
+    """Every rank's local rows are the single-rank packed order (s2_build_varlen:
+    window by window, (t, y, x) inside a window) restricted to its windows; the
+    ranks' rows partition the grid; the joint ownership keeps every layer kind's
+    load within the stated bounds and moves fewer rows than per-kind LPT."""
+    T, H, W = grid
+    L = T * H * W
+    for kind in (0, 1):
+        wins = s2b200.make_windows(T, H, W, kind)
+        cu, rows = s2b200.build_varlen(T, H, W, wins, 0)
+        seen = np.zeros(L, np.int64)
+        for r in range(world):
+            m = s2b200.shard_exchange(grid, 58, world, r, kind)
+            want = np.concatenate([rows[cu[i]:cu[i + 1], 0] for i in m["window_ids"]]) if len(m["window_ids"]) \
+                else np.zeros(0, np.int32)
+            assert np.array_equal(m["local_tokens"], want), (kind, r)
+            seen[m["local_tokens"]] += 1
+        assert np.all(seen == 1), "the ranks' rows must partition the grid"
+    if world > 1:
+        moved = s2b200.shard_exchange(grid, 58, world, 0, 0)["moved_rows"]
+        lpt = [s2b200.shard_owners(s2b200.make_windows(T, H, W, k), 58, world) for k in (0, 1)]
+        tok = [np.zeros(L, np.int64) for _ in range(2)]
+        for k in (0, 1):
+            for i, w in enumerate(s2b200.make_windows(T, H, W, k)):
+                t = np.arange(w[0], w[1])[:, None, None]
+                y = np.arange(w[2], w[3])[None, :, None]
+                x = np.arange(w[4], w[5])[None, None, :]
+                tok[k][((t * H + y) * W + x).ravel()] = lpt[k][i]
+        assert moved <= int((tok[0] != tok[1]).sum()), (moved, int((tok[0] != tok[1]).sum()))
+        # the shifted layers' load stays within the 2 % cap whenever a rank can take each window
+        w1 = s2b200.make_windows(T, H, W, 1)
+        cost = (((w1[:, 1] - w1[:, 0]) * (w1[:, 3] - w1[:, 2]) * (w1[:, 5] - w1[:, 4])) + 58.0) ** 2
+        load = np.array([cost[s2b200.shard_exchange(grid, 58, world, r, 1)["window_ids"]].sum() for r in range(world)])
+        assert load.max() <= max(1.02 * cost.sum() / world, cost.max()) * 1.0001
