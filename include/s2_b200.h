@@ -695,8 +695,9 @@ S2_API s2_status s2_debug_fail_allocations(int n);
  * wait_ns (0 = the default 1 s), and with skip_k_tile >= 0 the load producer of
  * its first CTA leaves out that K tile (counted from the CTA's first), so the
  * tensor-core role's wait for it runs out. The launch then ends on its own with
- * its error word set (2 or 3: the K wait, or the producer's wait for the V slot
- * that role never released, whichever gives up first), the layer's
+ * its error word set (2, 3 or 5: the K wait, the producer's wait for a slot
+ * that role never released, or a softmax wait for the S tile that was never
+ * computed, whichever gives up first), the layer's
  * device-error query returns S2_INFERENCE_FAILED, its TMEM is freed, and
  * launches after it are unaffected. */
 S2_API s2_status s2_debug_attention_fault(int skip_k_tile, unsigned long long wait_ns);
