@@ -408,8 +408,12 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     const int gemm_rows_min = Lt > 0 ? std::min(L, Lt) : L;
     const bool need_splitk = gemm_rows_min <= 128 && std::max(d, h) >= 512;
     const size_t splitk_cap = need_splitk ? BlockScratch::splitk_floats(b->device) : 0;
-    if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) || !sc.qkv_vid.ensure(Lz * 3 * d * 2) ||
-        !sc.qkv_txt.ensure(Tz * 3 * d * 2) || !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
+    // The attention prologue (QK-RMSNorm, MM-RoPE, bf16 rounding, window packing) runs in
+    // the Q|K|V projection's epilogue on the fp32 accumulator. The projection itself is
+    // materialised (fp32, by a second GEMM) only for the debug captures.
+    if (!sc.a_vid.ensure(Lz * d * 2) || !sc.a_txt.ensure(Tz * d * 2) ||
+        (b->debug_on && (!sc.qkv_vid.ensure(Lz * 3 * d * 4) || !sc.qkv_txt.ensure(Tz * 3 * d * 4))) ||
+        !sc.att_vid.ensure(Lz * d * 2) || !sc.att_txt32.ensure(Tz * d * 4) ||
         !sc.att_txt16.ensure(Tz * d * 2) || !sc.h_vid.ensure(Lz * d * 4) || !sc.h_txt.ensure(Tz * d * 4) ||
         !sc.hid_vid.ensure(Lz * h * 2) || !sc.hid_txt.ensure(Tz * h * 2) || !b->err.ensure(4) ||
         (need_splitk && !sc.splitk.ensure(splitk_cap * sizeof(float))) ||
@@ -433,8 +437,6 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     const size_t dz = static_cast<size_t>(d);
     __half *a_vid = static_cast<__half *>(sc.a_vid.ptr);
     __half *a_txt = merged ? a_vid + static_cast<size_t>(L) * dz : static_cast<__half *>(sc.a_txt.ptr);
-    __half *qkv_vid = static_cast<__half *>(sc.qkv_vid.ptr);
-    __half *qkv_txt = merged ? qkv_vid + static_cast<size_t>(L) * 3 * dz : static_cast<__half *>(sc.qkv_txt.ptr);
     __half *att_vid = static_cast<__half *>(sc.att_vid.ptr);
     __half *att_txt16 = merged ? att_vid + static_cast<size_t>(L) * dz : static_cast<__half *>(sc.att_txt16.ptr);
     float *h_vid = static_cast<float *>(sc.h_vid.ptr);
@@ -450,38 +452,62 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
     S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid));
     if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, a_txt));
-    // QKV projections (no bias)
+    // QKV projections (no bias) into the attention core's packed operands; the map
+    // covers the L video rows, then the Lt text rows (the merged GEMM's rows L.., or
+    // the text GEMM's rows)
     float *splitk = need_splitk ? static_cast<float *>(sc.splitk.ptr) : nullptr;
     int extra = 0;  // split-K finish kernels
     s2::GemmArgs g;
     g.K = d;
     g.N = 3 * d;
-    g.split = 3 * d;
     g.err = err;
-    g.partial = splitk;
-    g.partial_floats = splitk_cap;
     g.extra_launches = &extra;
     g.M = merged ? L + Lt : L;
-    g.out[0] = qkv_vid;
+    g.epilogue = s2::GEMM_EPI_QKV_PACK;
+    S2_TRY(s2::attention_pack_target(b->attn, st, L, Lt, &g));
+    --launches;  // set-up only
     S2_TRY(s2::gemm_f16(st, a_vid, V.qkv.ptr, g));
     if (Lt > 0 && !merged) {
         g.M = Lt;
-        g.out[0] = qkv_txt;
+        g.pk.map += L;
         S2_TRY(s2::gemm_f16(st, a_txt, T.qkv.ptr, g));
     }
-    // windowed MM attention (prologue, attention, text mean)
-    if ((s = s2_attention_layer_forward(b->attn, stream, qkv_vid, S2_F16, L, qkv_txt, Lt, att_vid,
-                                        static_cast<float *>(sc.att_txt32.ptr))) != S2_OK) {
+    // windowed MM attention (attention core, text mean)
+    if ((s = s2::attention_forward_packed(b->attn, st, L, Lt, att_vid, static_cast<float *>(sc.att_txt32.ptr))) !=
+        S2_OK) {
         b->last_launches = launches;
         return s;
     }
     launches += s2_attention_layer_last_launches(b->attn);
     if (b->debug_on) {
+        // the projection alone in fp32 (the reference's qkv_vid / qkv_txt captures), from
+        // which the pre-RoPE normalised q/k captures are taken
         const s2_block_debug &g = b->debug;
-        const long long nq = static_cast<long long>(L) * 3 * d, nt = static_cast<long long>(Lt) * 3 * d;
-        if ((g.qkv_vid && (s = s2::to_f32(st, S2_MODE_F16, qkv_vid, nq, g.qkv_vid)) != S2_OK) ||
-            (g.qkv_txt && Lt > 0 && (s = s2::to_f32(st, S2_MODE_F16, qkv_txt, nt, g.qkv_txt)) != S2_OK) ||
-            (s = s2::attention_debug_capture(b->attn, st, qkv_vid, S2_F16, L, qkv_txt, Lt, att_vid, g.attention_q,
+        float *q32v = static_cast<float *>(sc.qkv_vid.ptr), *q32t = static_cast<float *>(sc.qkv_txt.ptr);
+        s2::GemmArgs q;
+        q.K = d;
+        q.N = 3 * d;
+        q.epilogue = s2::GEMM_EPI_GATED_RESID_F32;
+        q.err = err;
+        q.M = merged ? L + Lt : L;
+        q.y = q32v;
+        if (merged) {
+            q.split_row = L;
+            q.y2 = q32t;
+        }
+        S2_TRY(s2::gemm_f16(st, a_vid, V.qkv.ptr, q));
+        if (Lt > 0 && !merged) {
+            q.M = Lt;
+            q.y = q32t;
+            S2_TRY(s2::gemm_f16(st, a_txt, T.qkv.ptr, q));
+        }
+        const size_t nq = static_cast<size_t>(L) * 3 * d * 4, nt = static_cast<size_t>(Lt) * 3 * d * 4;
+        if ((g.qkv_vid && cudaMemcpyAsync(g.qkv_vid, q32v, nq, cudaMemcpyDeviceToDevice, st) != cudaSuccess) ||
+            (g.qkv_txt && Lt > 0 && cudaMemcpyAsync(g.qkv_txt, q32t, nt, cudaMemcpyDeviceToDevice, st) != cudaSuccess)) {
+            b->last_launches = launches;
+            return s2::set_error(S2_INFERENCE_FAILED, "s2_dit_block_forward: debug copy failed");
+        }
+        if ((s = s2::attention_debug_capture(b->attn, st, q32v, S2_F32, L, q32t, Lt, att_vid, g.attention_q,
                                              g.attention_k, g.attention_v, g.attention_output, g.norm_q_vid,
                                              g.norm_k_vid, g.norm_q_txt, g.norm_k_txt)) != S2_OK) {
             b->last_launches = launches;

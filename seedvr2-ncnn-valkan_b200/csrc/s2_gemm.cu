@@ -16,6 +16,7 @@
 // Every wait is bounded (s2dev::mbar_wait): on timeout the CTA records an
 // error code in args.err, drains its in-flight copies and MMAs and exits.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -84,6 +85,15 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
 {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Round two values to bf16 (RNE), then store those values as fp16 (exact in
+// fp16's normal range): the attention core's operand format.
+__device__ __forceinline__ uint32_t pack_bf16_h2(float a, float b)
+{
+    const __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(&r);
+    return pack_h2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
 }
 
 template <int BN, bool kPair>
@@ -295,7 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < a.M;
             const bool split_k = ks > 1;
-            for (int c = 0; c < kBN / 32 && (split_k || a.epilogue != s2::GEMM_EPI_SWIGLU_F16); ++c) {
+            for (int c = 0; c < kBN / 32 && (split_k || (a.epilogue != s2::GEMM_EPI_SWIGLU_F16 &&
+                                                          a.epilogue != s2::GEMM_EPI_QKV_PACK)); ++c) {
                 const int n = n0 + c * 32;
                 if (n >= a.N) break;
                 uint32_t r[32];
@@ -432,6 +443,103 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            pack_h2(f[6], f[7]));
                     }
                     store_chunk(&tmO0, v4, n0 / 2 + c * 32, m0 + quad * 32);
+                }
+            }
+            if (a.epilogue == s2::GEMM_EPI_QKV_PACK && ok) {
+                // Per 128-column head block: Q/K rows are RMS-normalised over the head (two
+                // passes over TMEM: the fp64 square sum, then the scaled values), V rows only
+                // rounded. The warp stages its 32 rows x 256 B (16-byte chunk k of row r at
+                // k ^ (r % 8): conflict-free) and stores them as whole 256-byte packed rows.
+                const s2::PackArgs &pk = a.pk;
+                // map entries: packed row >= 0 (video), -1 - l (text row l), -0x7fffffff (a video
+                // row the layer's window subset does not hold: nothing stored)
+                const int4 mp = row_ok ? __ldg(pk.map + row) : make_int4(-0x7fffffff, 0, 0, 0);
+                const bool text = row_ok && mp.x < 0 && mp.x != -0x7fffffff;
+                const float *gam = pk.gammas + (text ? 2 : 0) * 128;
+                uint4 *stage = reinterpret_cast<uint4 *>(stg0_g);
+                for (int hc = 0; hc < kBN / 128; ++hc) {
+                    const int col0 = n0 + hc * 128;
+                    if (col0 >= a.N) break;
+                    const int sec = col0 / pk.dim, head = (col0 - sec * pk.dim) >> 7;
+                    const uint32_t tcol = tmem + lane_off + b * kBN + hc * 128;
+                    float inv = 1.f;
+                    if (sec < 2) {
+                        // Square sum in fp32 over four interleaved chains. The reference sums in
+                        // fp64; here the fp32 sum is within ~2e-6 (relative) of it, below the
+                        // ~1e-6-level difference between this accumulator and the reference's
+                        // CPU projection it normalises, and the fp64 pipe of this part made the
+                        // fp64 sum cost +20 % of the whole GEMM (760 vs 633 us per 720p block).
+                        float sq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t r[32];
+                            tmem_ld32(tcol + c * 32, r);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                const float x = __uint_as_float(r[e]);
+                                sq[e & 3] = __fmaf_rn(x, x, sq[e & 3]);
+                            }
+                        }
+                        const float ss = __fadd_rn(__fadd_rn(sq[0], sq[1]), __fadd_rn(sq[2], sq[3]));
+                        inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.f / 128.f), pk.eps)));
+                    }
+                    __syncwarp();  // the previous head block's stores have read the staging rows
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t r[32];
+                        tmem_ld32(tcol + c * 32, r);
+                        tmem_wait_ld();
+                        float x[32];
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(r[e]);
+                        if (sec < 2) {
+                            const float *gm = gam + sec * 128 + c * 32;
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], inv), __ldg(gm + e));
+                            // pairs (2 gp, 2 gp + 1), gp = axis * 21 + pair over dims 0..125
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int gp = c * 16 + i;
+                                if (gp < 63) {
+                                    const int axis = gp / 21, pr = gp - axis * 21;
+                                    const int pos = axis == 0 ? mp.y : (axis == 1 ? mp.z : mp.w);
+                                    const float2 cs = __ldg(pk.rope + pr * pk.max_pos + pos);
+                                    const float f0 = x[2 * i], f1 = x[2 * i + 1];
+                                    x[2 * i] = __fsub_rn(__fmul_rn(f0, cs.x), __fmul_rn(f1, cs.y));
+                                    x[2 * i + 1] = __fadd_rn(__fmul_rn(f1, cs.x), __fmul_rn(f0, cs.y));
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            stage[lane * 16 + ((4 * c + v) ^ (lane & 7))] =
+                                make_uint4(pack_bf16_h2(x[8 * v], x[8 * v + 1]), pack_bf16_h2(x[8 * v + 2], x[8 * v + 3]),
+                                           pack_bf16_h2(x[8 * v + 4], x[8 * v + 5]),
+                                           pack_bf16_h2(x[8 * v + 6], x[8 * v + 7]));
+                    }
+                    __syncwarp();
+                    uint4 *outb = static_cast<uint4 *>(sec == 0 ? pk.q : (sec == 1 ? pk.k : pk.v)) +
+                                  static_cast<size_t>(head) * pk.n_rows * 16;
+                    const int dst_me = mp.x;
+                    // video rows: two whole rows per store instruction
+#pragma unroll 4
+                    for (int k2 = 0; k2 < 16; ++k2) {
+                        const int rr = 2 * k2 + (lane >> 4), chunk = lane & 15;
+                        const int d = __shfl_sync(0xffffffffu, dst_me, rr);
+                        const uint4 v4 = stage[rr * 16 + (chunk ^ (rr & 7))];
+                        if (d >= 0) outb[static_cast<size_t>(d) * 16 + chunk] = v4;
+                    }
+                    // text rows: the same values into every window's copy of the row
+                    uint32_t tmask = __ballot_sync(0xffffffffu, text);
+                    while (tmask) {
+                        const int rr = __ffs(tmask) - 1;
+                        tmask &= tmask - 1;
+                        const int l = -1 - __shfl_sync(0xffffffffu, dst_me, rr);
+                        const uint4 v4 = stage[rr * 16 + ((lane & 15) ^ (rr & 7))];
+                        for (int w = lane >> 4; w < pk.n_windows; w += 2)
+                            outb[static_cast<size_t>(__ldg(pk.text_dst + w) + l) * 16 + (lane & 15)] = v4;
+                    }
                 }
             }
             tc_fence_before();
@@ -617,6 +725,13 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {
         if (!args.out[0] || args.N % 256 != 0 || (reinterpret_cast<uintptr_t>(args.out[0]) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad SwiGLU output (N %d must be a multiple of 256)", args.N);
+    } else if (args.epilogue == GEMM_EPI_QKV_PACK) {
+        const PackArgs &pk = args.pk;
+        if (pk.dim <= 0 || pk.dim % 128 != 0 || args.N != 3 * pk.dim || !pk.map || !pk.q || !pk.k || !pk.v ||
+            !pk.gammas || !pk.rope || pk.n_rows <= 0 || (pk.n_windows > 0 && !pk.text_dst) ||
+            ((reinterpret_cast<uintptr_t>(pk.q) | reinterpret_cast<uintptr_t>(pk.k) | reinterpret_cast<uintptr_t>(pk.v)) &
+             15u) != 0)
+            return set_error(S2_INVALID_ARGUMENT, "gemm: bad packed Q/K/V output");
     } else {
         return set_error(S2_UNSUPPORTED, "gemm: unknown epilogue %d", args.epilogue);
     }

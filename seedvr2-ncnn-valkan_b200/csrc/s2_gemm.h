@@ -52,6 +52,31 @@ enum GemmEpilogue : int {
     // output grid padded to geom.owp columns; for j < geom.ow,
     // y[n * ldt + (z * geom.oh + i) * geom.ow + j] = acc + bias[n] (n < n_valid).
     GEMM_EPI_CONV_F32 = 5,
+    // The DiT block's fused Q|K|V projection with the attention prologue applied
+    // to the fp32 accumulator (normalize_and_rotate, seedvr2_dit_block.cpp:942-974):
+    // per row and head of the Q and K column blocks, RMS normalisation over the
+    // 128 head dims (squares summed in fp32, four chains), times the branch
+    // gamma, 3-axis RoPE on dims 0..125; V unchanged; every value rounded to
+    // bf16 (RNE) and stored as fp16 into the window-packed, head-major operands
+    // of the attention core at the row's packed row (text rows: into every
+    // window's text rows). See PackArgs. N = 3 * dim, dim a multiple of 128.
+    GEMM_EPI_QKV_PACK = 6,
+};
+
+// GEMM_EPI_QKV_PACK targets.
+struct PackArgs {
+    // per GEMM row: {packed row, pt, ph, pw}, {-1 - l, l, l, l} for text row l, or
+    // {-0x7fffffff, ...} for a row that has no packed row (nothing is stored)
+    const int4 *map = nullptr;
+    const int32_t *text_dst = nullptr;  // per window: packed row of its text row 0
+    int n_windows = 0;
+    void *q = nullptr, *k = nullptr, *v = nullptr;  // fp16 [dim / 128][n_rows][128]
+    int n_rows = 0;
+    int dim = 0;                        // heads * 128
+    const float *gammas = nullptr;      // [q video, k video, q text, k text][128]
+    const float2 *rope = nullptr;       // (cos, sin) pair-major: [21][max_pos]
+    int max_pos = 0;
+    float eps = 0.f;
 };
 
 // Implicit-GEMM 3-D convolution: A is not a matrix but the im2col of a
@@ -101,6 +126,7 @@ struct GemmArgs {
     int sh_cin = 0, sh_tr = 1, sh_h = 0, sh_w = 0;  // GEMM_EPI_SHUFFLE_F32 geometry
     int conv = 0;                 // 1: A is the im2col of the convolution `geom`
     ConvGeom geom;
+    PackArgs pk;                  // GEMM_EPI_QKV_PACK
 };
 
 // D[M][N] = A[M][K] B[N][K]^T on sm_100a: A and B fp16, K-major (row-major

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "s2_buffers.h"
+#include "s2_gemm.h"
 #include "s2_internal.h"
 #include "s2_ops.h"
 
@@ -62,6 +63,9 @@ struct s2_attention_layer {
     int n_total_windows = 0, n_local = 0, n_rows = 0, n_work = 0, max_pos = 0;
     std::vector<int32_t> h_cu;
     DeviceBuffer d_cu, d_rows, d_work, d_rope;
+    // fused-prologue targets: per video row (then per text row) its packed row and
+    // RoPE positions, and per window the packed row of its first text row
+    DeviceBuffer d_pack_map, d_text_dst, d_rope_pairs;
 
     DeviceBuffer d_weights;  // gammas [4][128] + freqs [21]
     std::shared_ptr<AttnScratch> sc = std::make_shared<AttnScratch>();
@@ -95,7 +99,7 @@ struct s2_attention_layer {
     ~s2_attention_layer()
     {
         DeviceGuard g(device);
-        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_weights, &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt, &d_slab_work})
+        for (DeviceBuffer *b : {&d_cu, &d_rows, &d_work, &d_rope, &d_pack_map, &d_text_dst, &d_rope_pairs, &d_weights, &d_err, &d_in_vid, &d_in_txt, &d_out_vid, &d_out_vid32, &d_out_txt, &d_slab_work})
             b->release();
         for (cudaEvent_t e : ev_in) cudaEventDestroy(e);
         for (cudaEvent_t e : ev_cmp) cudaEventDestroy(e);
@@ -270,9 +274,25 @@ struct s2_attention_layer {
         n_rows = rows;
         n_work = nw;
         max_pos = mp;
+        // inverse of the packed row table for the fused prologue: video row -> its packed
+        // row and positions; text row l -> {-1 - l, l, l, l} (the same in every window)
+        std::vector<int4> h_map(static_cast<size_t>(n_video) + std::max(Lt, 0), make_int4(-0x7fffffff, 0, 0, 0));
+        for (int p = 0; p < rows; ++p)
+            if (h_rows[p].src >= 0 && h_rows[p].src < n_video)
+                h_map[h_rows[p].src] = make_int4(p, h_rows[p].pt, h_rows[p].ph, h_rows[p].pw);
+        for (int t = 0; t < Lt; ++t) h_map[static_cast<size_t>(n_video) + t] = make_int4(-1 - t, t, t, t);
+        std::vector<int32_t> h_tdst(std::max(n_local, 1), 0);
+        for (int w = 0; w < n_local; ++w) h_tdst[w] = h_cu[w + 1] - Lt;
         if (!d_cu.ensure(h_cu.size() * sizeof(int32_t)) || !d_rows.ensure(h_rows.size() * sizeof(s2_row)) ||
-            !d_work.ensure(h_work.size() * sizeof(int32_t)) || !d_rope.ensure(s2_rope_table_bytes(max_pos)))
+            !d_work.ensure(h_work.size() * sizeof(int32_t)) || !d_rope.ensure(s2_rope_table_bytes(max_pos)) ||
+            !d_pack_map.ensure(h_map.size() * sizeof(int4)) || !d_text_dst.ensure(h_tdst.size() * sizeof(int32_t)) ||
+            !d_rope_pairs.ensure(s2_rope_table_bytes(max_pos)))
             return s2::set_error(S2_OUT_OF_MEMORY, "attention plan: device allocation failed");
+        if (cudaMemcpy(d_pack_map.ptr, h_map.data(), h_map.size() * sizeof(int4), cudaMemcpyHostToDevice) !=
+                cudaSuccess ||
+            cudaMemcpy(d_text_dst.ptr, h_tdst.data(), h_tdst.size() * sizeof(int32_t), cudaMemcpyHostToDevice) !=
+                cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "attention plan: upload failed");
         // Stream-ordered uploads from host vectors need the host side to stay
         // alive until the copy completes: copy synchronously (plans change
         // rarely -- once per runtime shape).
@@ -283,6 +303,8 @@ struct s2_attention_layer {
                 cudaSuccess)
             return s2::set_error(S2_INFERENCE_FAILED, "attention plan: upload failed");
         rc = s2_rope_table(st, freqs(), max_pos, d_rope.ptr);
+        if (rc != S2_OK) return rc;
+        rc = s2::rope_table_pairs(st, freqs(), max_pos, d_rope_pairs.ptr);
         if (rc != S2_OK) return rc;
         plan_T = T;
         plan_H = H;
@@ -405,6 +427,42 @@ extern "C" s2_status s2_attention_layer_local_rows(s2_attention_layer *l, int Lt
 
 extern "C" int s2_attention_layer_last_launches(const s2_attention_layer *l) { return l ? l->last_launches : 0; }
 
+// Packed Q/K/V and text-slab workspace for the current plan, and the error word.
+static s2_status ensure_workspace(s2_attention_layer *l, int Lt)
+{
+    const int dim = l->heads * S2_HEAD_DIM;
+    const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;
+    const size_t txt_bytes = static_cast<size_t>(std::max(l->n_local, 1)) * std::max(Lt, 1) * dim * 2;
+    AttnScratch &sc = *l->sc;
+    if (!sc.q.ensure(qkv_bytes) || !sc.k.ensure(qkv_bytes) || !sc.v.ensure(qkv_bytes) || !sc.txt_partial.ensure(txt_bytes))
+        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: workspace allocation failed");
+    if (!l->d_err.ptr && (!l->d_err.ensure(sizeof(int32_t)) || cudaMemset(l->d_err.ptr, 0, sizeof(int32_t)) != cudaSuccess))
+        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: error word allocation failed");
+    return S2_OK;
+}
+
+// The attention core over the packed operands of the current plan, then the text
+// mean of the per-window text outputs; sets last_launches.
+static s2_status attention_and_text(s2_attention_layer *l, cudaStream_t st, int Lt, void *vid_out, float *txt_out)
+{
+    const int dim = l->heads * S2_HEAD_DIM;
+    AttnScratch &sc = *l->sc;
+    s2_status rc = s2_window_attention(st, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
+                                       static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
+                                       static_cast<const s2_row *>(l->d_rows.ptr),
+                                       static_cast<const int32_t *>(l->d_work.ptr), l->n_work, vid_out,
+                                       sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
+    if (rc != S2_OK) return rc;
+    l->last_launches = 1;
+    if (Lt > 0) {
+        rc = s2_text_window_sum(st, l->mode, sc.txt_partial.ptr, l->n_local, Lt, dim,
+                                1.f / static_cast<float>(l->n_total_windows), 0, txt_out);
+        if (rc != S2_OK) return rc;
+        l->last_launches = 2;
+    }
+    return S2_OK;
+}
+
 extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *stream, const void *vid_qkv,
                                                 s2_dtype in_dtype, int L, const void *txt_qkv, int Lt,
                                                 void *vid_out, float *txt_out)
@@ -423,31 +481,59 @@ extern "C" s2_status s2_attention_layer_forward(s2_attention_layer *l, void *str
         return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: vid rows %d != %d (%s)", L, l->n_video,
                              l->local_rows ? "the subset's video tokens" : "T*H*W");
     if (rc != S2_OK) return rc;
-    const int dim = l->heads * S2_HEAD_DIM;
-    const size_t qkv_bytes = static_cast<size_t>(l->n_rows) * dim * 2;
-    const size_t txt_bytes = static_cast<size_t>(std::max(l->n_local, 1)) * std::max(Lt, 1) * dim * 2;
+    if ((rc = ensure_workspace(l, Lt)) != S2_OK) return rc;
     AttnScratch &sc = *l->sc;
-    if (!sc.q.ensure(qkv_bytes) || !sc.k.ensure(qkv_bytes) || !sc.v.ensure(qkv_bytes) || !sc.txt_partial.ensure(txt_bytes))
-        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: workspace allocation failed");
-    if (!l->d_err.ptr && (!l->d_err.ensure(sizeof(int32_t)) || cudaMemset(l->d_err.ptr, 0, sizeof(int32_t)) != cudaSuccess))
-        return s2::set_error(S2_OUT_OF_MEMORY, "attention layer: error word allocation failed");
     rc = s2_qk_norm_rope(stream, vid_qkv, txt_qkv, in_dtype, l->heads, l->eps, l->gammas(), l->d_rope.ptr,
                          static_cast<const s2_row *>(l->d_rows.ptr), l->n_rows, l->mode, sc.q.ptr, sc.k.ptr,
                          sc.v.ptr);
     if (rc != S2_OK) return rc;
-    rc = s2_window_attention(stream, l->mode, sc.q.ptr, sc.k.ptr, sc.v.ptr, l->heads, l->n_rows,
-                             static_cast<const int32_t *>(l->d_cu.ptr), l->n_local, Lt,
-                             static_cast<const s2_row *>(l->d_rows.ptr), static_cast<const int32_t *>(l->d_work.ptr),
-                             l->n_work, vid_out, sc.txt_partial.ptr, static_cast<int32_t *>(l->d_err.ptr));
+    rc = attention_and_text(l, st, Lt, vid_out, txt_out);
+    if (rc == S2_OK) ++l->last_launches;
+    return rc;
+}
+
+s2_status s2::attention_pack_target(s2_attention_layer *l, cudaStream_t st, int L, int Lt, s2::GemmArgs *g)
+{
+    if (!l || !g) return s2::set_error(S2_INVALID_ARGUMENT, "attention pack target: NULL argument");
+    if (!l->loaded) return s2::set_error(S2_NOT_LOADED, "attention layer: weights not loaded");
+    if (!l->shape_valid) return s2::set_error(S2_NOT_LOADED, "attention layer: runtime shape not set");
+    if (Lt < 0) return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: negative text length");
+    DeviceGuard dg(l->device);
+    l->last_stream = st;
+    s2_status rc = l->build_plan(Lt, st);
     if (rc != S2_OK) return rc;
-    l->last_launches = 2;
-    if (Lt > 0) {
-        rc = s2_text_window_sum(stream, l->mode, sc.txt_partial.ptr, l->n_local, Lt, dim,
-                                1.f / static_cast<float>(l->n_total_windows), 0, txt_out);
-        if (rc != S2_OK) return rc;
-        l->last_launches = 3;
-    }
+    if (L != l->n_video)
+        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: vid rows %d != %d (%s)", L, l->n_video,
+                             l->local_rows ? "the subset's video tokens" : "T*H*W");
+    if ((rc = ensure_workspace(l, Lt)) != S2_OK) return rc;
+    AttnScratch &sc = *l->sc;
+    s2::PackArgs &pk = g->pk;
+    pk.map = static_cast<const int4 *>(l->d_pack_map.ptr);
+    pk.text_dst = static_cast<const int32_t *>(l->d_text_dst.ptr);
+    pk.n_windows = Lt > 0 ? l->n_local : 0;
+    pk.q = sc.q.ptr;
+    pk.k = sc.k.ptr;
+    pk.v = sc.v.ptr;
+    pk.n_rows = l->n_rows;
+    pk.dim = l->heads * S2_HEAD_DIM;
+    pk.gammas = l->gammas();
+    pk.rope = static_cast<const float2 *>(l->d_rope_pairs.ptr);
+    pk.max_pos = l->max_pos;
+    pk.eps = l->eps;
     return S2_OK;
+}
+
+s2_status s2::attention_forward_packed(s2_attention_layer *l, cudaStream_t st, int L, int Lt, void *vid_out,
+                                       float *txt_out)
+{
+    if (!l) return s2::set_error(S2_INVALID_ARGUMENT, "layer is NULL");
+    l->last_launches = 0;
+    if (!l->plan_valid || l->plan_Lt != Lt || L != l->n_video || !l->sc->q.ptr)
+        return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: packed forward without a matching pack target");
+    if (!vid_out || (Lt > 0 && !txt_out)) return s2::set_error(S2_INVALID_ARGUMENT, "attention layer: NULL buffer");
+    DeviceGuard dg(l->device);
+    l->last_stream = st;
+    return attention_and_text(l, st, Lt, vid_out, txt_out);
 }
 
 // The host-buffer forward as a three-stream pipeline over the frame slabs:

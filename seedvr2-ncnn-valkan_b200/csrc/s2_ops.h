@@ -37,6 +37,19 @@ s2_status attention_debug_capture(s2_attention_layer *l, cudaStream_t st, const 
                                   float *att_v, float *att_o, float *nq_vid, float *nk_vid, float *nq_txt,
                                   float *nk_txt);
 
+// Attention prologue fused into the block's Q|K|V projection: the layer's
+// current plan as the targets of GEMM_EPI_QKV_PACK (the packed Q/K/V workspace,
+// the row map of the layer's L video rows followed by its Lt text rows, the
+// per-window text rows, gammas, RoPE table, eps), plan and workspace set up for
+// (L, Lt); then attention_forward_packed runs the attention core and the text
+// mean on the packed operands the projection wrote.
+struct GemmArgs;
+// (cos, sin) of pos * freqs[pair] as [pair][max_pos] (s2_prologue.cu)
+s2_status rope_table_pairs(cudaStream_t st, const float *freqs21, int max_pos, void *table);
+s2_status attention_pack_target(s2_attention_layer *l, cudaStream_t st, int L, int Lt, GemmArgs *g);
+s2_status attention_forward_packed(s2_attention_layer *l, cudaStream_t st, int L, int Lt, void *vid_out,
+                                   float *txt_out);
+
 // y = fp16( (x * inv_rms(x) [* gamma]) * mul + add0 + add1 ) per row
 // (s2_block.cu); gamma and mul may be null (no gamma / no modulation).
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma,

@@ -38,6 +38,19 @@ __global__ void rope_table_kernel(const float *__restrict__ freqs, int max_pos, 
     table[i] = make_float2(c, s);
 }
 
+// The same values pair-major: table[pair * max_pos + pos] (a warp whose rows have
+// different positions reads one pair's entries from one or two cache lines).
+__global__ void rope_table_pairs_kernel(const float *__restrict__ freqs, int max_pos, float2 *__restrict__ table)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= max_pos * kPairs) return;
+    const int pair = i / max_pos, pos = i - pair * max_pos;
+    const float angle = __fmul_rn(static_cast<float>(pos), freqs[pair]);
+    float s, c;
+    sincosf(angle, &s, &c);
+    table[i] = make_float2(c, s);
+}
+
 template <typename T>
 struct Load8;
 
@@ -349,6 +362,15 @@ extern "C" s2_status s2_text_window_sum(void *stream, s2_mode mode, const void *
 }
 
 namespace s2 {
+s2_status rope_table_pairs(cudaStream_t st, const float *freqs21, int max_pos, void *table)
+{
+    if (!freqs21 || max_pos <= 0 || !table) return set_error(S2_INVALID_ARGUMENT, "rope table: invalid arguments");
+    const int n = max_pos * kPairs;
+    rope_table_pairs_kernel<<<(n + 255) / 256, 256, 0, st>>>(freqs21, max_pos, static_cast<float2 *>(table));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? S2_OK : set_error(S2_INFERENCE_FAILED, "rope table: launch failed: %s", cudaGetErrorString(e));
+}
+
 // 16-bit (mode dtype) -> fp32, used by the host-buffer forward.
 s2_status to_f32(cudaStream_t st, s2_mode mode, const void *src, long long n, float *dst)
 {
