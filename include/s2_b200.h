@@ -114,10 +114,13 @@ S2_API s2_status s2_shard_windows(const s2_window *windows, int n, int text_len,
 
 /* The sharded DiT step's ownership of BOTH window kinds of a grid, chosen
  * together so that few rows change owner at the plain <-> shifted layer
- * boundaries: the plain windows (owner_plain, s2_make_windows order) in
- * contiguous runs of their order with the smallest largest run cost (S_w^2); each
- * shifted window (owner_shifted), costliest first, to the rank holding most of
- * its rows whose load stays within 2 % of the mean (else the least loaded).
+ * boundaries. A window's cost is a block's work on it: its video rows L_w (the
+ * projections, MLP and norms, which dominate) + 1e-4 * S_w^2 (its attention,
+ * S_w = L_w + text_len), in units of one row's per-row work. The plain windows
+ * (owner_plain, s2_make_windows order) go in contiguous runs of their order with
+ * the smallest largest run cost; each shifted window (owner_shifted), costliest
+ * first, to the rank holding most of its rows whose load stays within 2 % of
+ * the mean (else the least loaded).
  * Per-kind s2_shard_windows ownership is returned instead when it moves fewer
  * rows at no worse balance (small grids whose tilings split along frames). */
 S2_API s2_status s2_shard_windows_joint(int frames, int height, int width, int wt, int wh, int ww, int text_len,
@@ -137,6 +140,14 @@ S2_API s2_status s2_shard_exchange(int frames, int height, int width, int wt, in
                                    int n_ranks, int rank, int kind, int32_t *window_ids, int *n_windows,
                                    int32_t *local_tokens, int *n_local, int32_t *send_counts, int32_t *send_rows,
                                    int32_t *recv_counts, int32_t *recv_rows, long long *moved_rows);
+/* Where each of rank `rank`'s kind-`kind` local rows goes at the boundary to
+ * the other kind, as the sharded step's exchange kernel writes it: the rank
+ * holding the row's token under the other kind (dest_rank) and the row's index
+ * in that rank's local order of the other kind (dest_row). *n_local = the
+ * rank's kind-`kind` local row count; arrays may be NULL. */
+S2_API s2_status s2_shard_row_destinations(int frames, int height, int width, int wt, int wh, int ww,
+                                           int text_len, int n_ranks, int rank, int kind, int32_t *dest_rank,
+                                           int32_t *dest_row, int *n_local);
 
 /* ---- device kernels (explicit buffers) ---------------------------------- */
 

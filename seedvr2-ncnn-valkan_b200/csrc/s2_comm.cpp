@@ -4,13 +4,13 @@
 // that copy, any other loads the system one, and a process that never creates
 // a communicator never loads NCCL at all.
 //
-// The step needs two collectives (no counterpart in the reference, which runs
-// on one device):
+// The step needs (no counterpart in the reference, which runs on one device):
 //   * an fp32 sum all-reduce of each block's per-rank text attention mean
 //     [58][2560] (and of the disjoint per-rank parts of the output latent);
-//   * a row exchange between the window ownerships of consecutive blocks
-//     (plain <-> shifted windows): one grouped ncclSend / ncclRecv per peer,
-//     the rank's own rows copied on the device.
+//   * every rank's buffers of the row exchange between the window ownerships
+//     of consecutive blocks mapped into every other rank (comm_share: CUDA IPC
+//     handles all-gathered over NCCL); the exchange itself is a kernel of the
+//     DiT that stores rows into peer memory.
 //
 // Failures: the ranks meet through a non-blocking communicator
 // (ncclConfig_t.blocking = 0) whose creation is polled with
@@ -32,6 +32,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "s2_buffers.h"
 #include "s2_comm.h"
@@ -44,10 +45,7 @@ struct Nccl {
     decltype(&ncclCommInitRank) comm_init_rank = nullptr;
     decltype(&ncclCommDestroy) comm_destroy = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
-    decltype(&ncclSend) send = nullptr;
-    decltype(&ncclRecv) recv = nullptr;
-    decltype(&ncclGroupStart) group_start = nullptr;
-    decltype(&ncclGroupEnd) group_end = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
     decltype(&ncclCommInitRankConfig) comm_init_rank_config = nullptr;
     decltype(&ncclCommGetAsyncError) comm_async_error = nullptr;
@@ -68,19 +66,15 @@ const Nccl &nccl()
         S2_SYM(comm_init_rank, "ncclCommInitRank");
         S2_SYM(comm_destroy, "ncclCommDestroy");
         S2_SYM(all_reduce, "ncclAllReduce");
-        S2_SYM(send, "ncclSend");
-        S2_SYM(recv, "ncclRecv");
-        S2_SYM(group_start, "ncclGroupStart");
-        S2_SYM(group_end, "ncclGroupEnd");
+        S2_SYM(all_gather, "ncclAllGather");
         S2_SYM(error_string, "ncclGetErrorString");
         S2_SYM(comm_init_rank_config, "ncclCommInitRankConfig");
         S2_SYM(comm_async_error, "ncclCommGetAsyncError");
         S2_SYM(comm_abort, "ncclCommAbort");
         S2_SYM(comm_split, "ncclCommSplit");
 #undef S2_SYM
-        n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce && n.send && n.recv &&
-               n.group_start && n.group_end && n.error_string && n.comm_init_rank_config && n.comm_async_error &&
-               n.comm_abort && n.comm_split;
+        n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce && n.all_gather &&
+               n.error_string && n.comm_init_rank_config && n.comm_async_error && n.comm_abort && n.comm_split;
     });
     return n;
 }
@@ -262,31 +256,54 @@ s2_status comm_allreduce_f32(s2_comm *c, float *buf, size_t n, cudaStream_t st)
     return settle(c, nc.all_reduce(buf, buf, n, ncclFloat, ncclSum, c->comm, st), "ncclAllReduce");
 }
 
-s2_status comm_exchange(s2_comm *c, const void *send, const size_t *send_off, const size_t *send_bytes, void *recv,
-                        const size_t *recv_off, const size_t *recv_bytes, cudaStream_t st)
+s2_status comm_share(s2_comm *c, void *local, void **peers, cudaStream_t st)
 {
-    const int me = c ? c->rank : 0;
-    // own part: a device copy
-    if (send_bytes[me] != recv_bytes[me])
-        return set_error(S2_INVALID_ARGUMENT, "exchange: own segment %zu != %zu bytes", send_bytes[me], recv_bytes[me]);
-    if (send_bytes[me] &&
-        cudaMemcpyAsync(static_cast<char *>(recv) + recv_off[me], static_cast<const char *>(send) + send_off[me],
-                        send_bytes[me], cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-        return set_error(S2_INFERENCE_FAILED, "exchange: own copy failed");
-    if (!c || c->nranks == 1) return S2_OK;
-    if (c->aborted) return set_error(S2_INFERENCE_FAILED, "exchange: communicator was aborted");
-    const Nccl &nc = nccl();
-    ncclResult_t r = nc.group_start();
-    for (int p = 0; p < c->nranks && r == ncclSuccess; ++p) {
+    const int n = c ? c->nranks : 1, me = c ? c->rank : 0;
+    for (int p = 0; p < n; ++p) peers[p] = p == me ? local : nullptr;
+    if (n == 1) return S2_OK;
+    if (c->aborted) return set_error(S2_INFERENCE_FAILED, "share: communicator was aborted");
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+        return set_error(S2_UNSUPPORTED, "share: not during stream capture");
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, local) != cudaSuccess)
+        return set_error(S2_INFERENCE_FAILED, "share: cudaIpcGetMemHandle failed (not a cudaMalloc base pointer?)");
+    std::vector<cudaIpcMemHandle_t> all(n);
+    struct Tmp {  // the all-gather buffer, released on every path
+        DeviceBuffer b;
+        ~Tmp() { b.release(); }
+    } dev;
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    if (!dev.b.ensure(n * hb)) return set_error(S2_OUT_OF_MEMORY, "share: handle buffer");
+    char *d = static_cast<char *>(dev.b.ptr);
+    if (cudaMemcpy(d + me * hb, &h, hb, cudaMemcpyHostToDevice) != cudaSuccess)
+        return set_error(S2_INFERENCE_FAILED, "share: handle upload failed");
+    s2_status s = settle(c, nccl().all_gather(d + me * hb, d, hb, ncclChar, c->comm, st), "share (ncclAllGather)");
+    if (s != S2_OK) return s;
+    if (cudaMemcpyAsync(all.data(), d, n * hb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return set_error(S2_INFERENCE_FAILED, "share: handle download failed");
+    for (int p = 0; p < n; ++p) {
         if (p == me) continue;
-        if (send_bytes[p])
-            r = nc.send(static_cast<const char *>(send) + send_off[p], send_bytes[p], ncclChar, p, c->comm, st);
-        if (r == ncclSuccess && recv_bytes[p])
-            r = nc.recv(static_cast<char *>(recv) + recv_off[p], recv_bytes[p], ncclChar, p, c->comm, st);
+        if (cudaIpcOpenMemHandle(&peers[p], all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            for (int q = 0; q < p; ++q)
+                if (q != me && peers[q]) cudaIpcCloseMemHandle(peers[q]);
+            for (int q = 0; q < n; ++q) peers[q] = q == me ? local : nullptr;
+            return set_error(S2_INFERENCE_FAILED,
+                             "share: cudaIpcOpenMemHandle of rank %d failed (ranks must be processes with peer access)", p);
+        }
     }
-    const ncclResult_t e = nc.group_end();
-    if (r == ncclSuccess || r == ncclInProgress) r = e;
-    return settle(c, r, "exchange (grouped send/recv)");
+    return S2_OK;
+}
+
+void comm_unshare(s2_comm *c, void **peers)
+{
+    const int n = c ? c->nranks : 1, me = c ? c->rank : 0;
+    for (int p = 0; p < n; ++p) {
+        if (p != me && peers[p]) cudaIpcCloseMemHandle(peers[p]);
+        peers[p] = nullptr;
+    }
 }
 
 }  // namespace s2

@@ -12,10 +12,13 @@ namespace s2 {
 // In-place fp32 sum over all ranks (no-op for a single rank or a null comm).
 s2_status comm_allreduce_f32(s2_comm *c, float *buf, size_t n, cudaStream_t st);
 
-// Every rank sends send[send_off[p] .. + send_bytes[p]) to rank p and receives
-// recv_bytes[p] bytes from rank p at recv + recv_off[p]; the rank's own
-// segment is a device copy. All ranks call it with matching sizes.
-s2_status comm_exchange(s2_comm *c, const void *send, const size_t *send_off, const size_t *send_bytes, void *recv,
-                        const size_t *recv_off, const size_t *recv_bytes, cudaStream_t st);
+// Maps every rank's `local` allocation (a cudaMalloc base pointer; all ranks
+// pass their buffer of the same role) into this process through CUDA IPC
+// handles all-gathered over NCCL: peers[p] = rank p's allocation, peers[rank] =
+// local (peers has comm size entries). Host-synchronising set-up call, not for
+// stream capture; ranks must be processes on GPUs with peer access.
+// comm_unshare closes the peers' mappings (before those allocations change).
+s2_status comm_share(s2_comm *c, void *local, void **peers, cudaStream_t st);
+void comm_unshare(s2_comm *c, void **peers);
 
 }  // namespace s2

@@ -173,26 +173,99 @@ __global__ void unpatchify_local_kernel(const float *__restrict__ proj, int oc, 
     }
 }
 
-// dst[i] = src[map[i]] (rows of dim floats)
-__global__ void gather_rows_kernel(const float4 *__restrict__ src, const int32_t *__restrict__ map, int n, int dim4,
-                                   float4 *__restrict__ dst)
+// ---- row exchange over peer memory (sharded step) -------------------------------
+// At a plain <-> shifted boundary every rank writes each of its hidden rows
+// straight into the buffer that becomes the next block's input on the rank
+// that owns the row's token under the next window kind (its own, or a peer's
+// mapped through CUDA IPC): plain stores, over NVLink for peers. No collective
+// library call, no pack or scatter pass. Ordering, per boundary and epoch e
+// (a device counter every rank advances in step):
+//   ready: a rank announces e once its previous block has finished reading the
+//          destination buffer (stream order), so peers may overwrite it;
+//   rows:  each CTA waits for every rank's ready, copies its rows, fences at
+//          system scope; the last CTA announces done e to every rank;
+//   wait:  the next block starts after every rank's done e.
+// Every wait is bounded; on expiry the DiT's error word gets a code and the
+// kernel returns (a peer that died makes the step fail, not hang).
+constexpr int kMaxRanks = 8;
+enum : int { XF_READY = 0, XF_DONE = kMaxRanks, XF_EPOCH = 2 * kMaxRanks, XF_COUNT = XF_EPOCH + 1, XF_WORDS = 32 };
+enum : int { E_XFER_READY = 48, E_XFER_DONE = 49 };
+constexpr unsigned long long kXferTimeoutNs = 10000000000ull;  // 10 s
+
+struct XferPeers {
+    float4 *dst[kMaxRanks];     // every rank's destination rows (this rank's own among them)
+    int32_t *flags[kMaxRanks];  // every rank's flag words
+};
+
+__device__ __forceinline__ unsigned long long xf_now()
 {
-    const long long total = 1LL * n * dim4;
-    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
-        const long long r = i / dim4;
-        dst[i] = src[1LL * map[r] * dim4 + (i - r * dim4)];
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void st_release_sys(int32_t *p, int v)
+{
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int32_t *p)
+{
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// every rank's word flags[slot + rank] has reached epoch e (bounded)
+__device__ bool xf_wait_all(const int32_t *flags, int slot, int n, int e)
+{
+    const unsigned long long t0 = xf_now();
+    for (int p = 0; p < n; ++p)
+        while (ld_acquire_sys(flags + slot + p) < e) {
+            if (xf_now() - t0 > kXferTimeoutNs) return false;
+            __nanosleep(200);
+        }
+    return true;
+}
+
+__global__ void xfer_ready_kernel(XferPeers pp, int32_t *flags, int me, int n)
+{
+    if (threadIdx.x != 0) return;
+    const int e = flags[XF_EPOCH] + 1;
+    flags[XF_EPOCH] = e;
+    for (int p = 0; p < n; ++p) st_release_sys(pp.flags[p] + XF_READY + me, e);
+}
+
+// row r -> rank map[r].x, row map[r].y (a warp per row)
+__global__ void __launch_bounds__(256) xfer_rows_kernel(const float4 *__restrict__ src, const int2 *__restrict__ map,
+                                                        int n_rows, int dim4, XferPeers pp, int32_t *flags, int me,
+                                                        int n, int32_t *err)
+{
+    __shared__ int ready;
+    const int e = flags[XF_EPOCH];
+    if (threadIdx.x == 0) {
+        ready = xf_wait_all(flags, XF_READY, n, e);
+        if (!ready) atomicCAS(err, 0, E_XFER_READY);
+    }
+    __syncthreads();
+    if (ready) {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = blockIdx.x * 8 + warp; r < n_rows; r += gridDim.x * 8) {
+            const int2 d = __ldg(map + r);
+            const float4 *s = src + static_cast<size_t>(r) * dim4;
+            float4 *o = pp.dst[d.x] + static_cast<size_t>(d.y) * dim4;
+            for (int c = lane; c < dim4; c += 32) o[c] = __ldg(s + c);
+        }
+    }
+    __threadfence_system();  // this thread's stores, at system scope, before the CTA counts as done
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(flags + XF_COUNT, 1) == static_cast<int>(gridDim.x) - 1) {
+        flags[XF_COUNT] = 0;
+        __threadfence_system();
+        for (int p = 0; p < n; ++p) st_release_sys(pp.flags[p] + XF_DONE + me, e);
     }
 }
 
-// dst[map[i]] = src[i]
-__global__ void scatter_rows_kernel(const float4 *__restrict__ src, const int32_t *__restrict__ map, int n, int dim4,
-                                    float4 *__restrict__ dst)
+__global__ void xfer_wait_kernel(const int32_t *flags, int n, int32_t *err)
 {
-    const long long total = 1LL * n * dim4;
-    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
-        const long long r = i / dim4;
-        dst[1LL * map[r] * dim4 + (i - r * dim4)] = src[i];
-    }
+    if (threadIdx.x == 0 && !xf_wait_all(flags, XF_DONE, n, flags[XF_EPOCH])) atomicCAS(err, 0, E_XFER_DONE);
 }
 
 unsigned grid_for(long long n) { return static_cast<unsigned>(std::min<long long>((n + 255) / 256, 4096)); }
@@ -240,12 +313,25 @@ struct s2_dit {
         int T = 0, Hp = 0, Wp = 0, Lt = -1;
         int n_local[2] = {0, 0};
         std::vector<int32_t> ids[2];
-        s2::DeviceBuffer tok[2];                  // local row -> patched-grid token, per window kind
-        s2::DeviceBuffer send_src[2], recv_dst[2];  // exchange from kind k to kind 1 - k
-        std::vector<size_t> send_off[2], send_bytes[2], recv_off[2], recv_bytes[2];
-        int send_rows[2] = {0, 0};
+        s2::DeviceBuffer tok[2];   // local row -> patched-grid token, per window kind
+        s2::DeviceBuffer dest[2];  // local row of kind k -> (rank, row) under kind 1 - k (int2)
     } sh;
-    s2::DeviceBuffer xsend, xrecv;
+    // peer mappings of the exchange's destination buffers (vid_a, vid_b) and flag words
+    struct Xfer {
+        int n = 0, me = 0;
+        void *mine[3] = {nullptr, nullptr, nullptr};  // the local allocations the mappings were made for
+        void *peer[3][kMaxRanks] = {};                // [vid_a, vid_b, flags][rank]
+        s2::DeviceBuffer flags;
+        void unshare()
+        {
+            for (int b = 0; b < 3; ++b) {
+                for (int p = 0; p < n; ++p)
+                    if (p != me && peer[b][p]) cudaIpcCloseMemHandle(peer[b][p]);
+                for (int p = 0; p < kMaxRanks; ++p) peer[b][p] = nullptr;
+                mine[b] = nullptr;
+            }
+        }
+    } xf;
     // Euler-step graph: the call it was captured for and its launch count
     struct StepKey {
         int T = 0, H = 0, W = 0, Lt = 0;
@@ -311,13 +397,13 @@ extern "C" s2_status s2_dit_destroy(s2_dit *d)
     for (s2_dit_block *b : d->blocks) s2_dit_block_destroy(b);
     s2::DeviceGuard guard(d->device);
     d->drop_graph();
+    d->xf.unshare();
     if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
     for (s2::DeviceBuffer *b : {&d->w_vid, &d->b_vid, &d->w_txt, &d->b_txt, &d->w_t1, &d->b_t1, &d->w_t2, &d->b_t2,
                                 &d->w_t3, &d->b_t3, &d->o_norm, &d->o_mod6, &d->w_out, &d->b_out, &d->omods,
                                 &d->latent, &d->patches, &d->txt16, &d->vid_a, &d->vid_b, &d->txt_a, &d->txt_b,
-                                &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise, &d->xsend, &d->xrecv,
-                                &d->sh.tok[0], &d->sh.tok[1], &d->sh.send_src[0], &d->sh.send_src[1],
-                                &d->sh.recv_dst[0], &d->sh.recv_dst[1],
+                                &d->sinus, &d->th1, &d->th2, &d->emb, &d->o16, &d->proj, &d->err, &d->h_noise,
+                                &d->sh.tok[0], &d->sh.tok[1], &d->sh.dest[0], &d->sh.dest[1], &d->xf.flags,
                                 &d->h_cond, &d->h_text, &d->h_x0})
         b->release();
     delete d;
@@ -426,26 +512,11 @@ static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
             cudaMemcpy(sh.tok[k].ptr, m.tok[k].data(), m.tok[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
     }
-    const size_t row_bytes = static_cast<size_t>(d->dim) * 4;
     for (int k = 0; k < 2; ++k) {
-        sh.send_off[k].assign(N, 0);
-        sh.send_bytes[k].assign(N, 0);
-        sh.recv_off[k].assign(N, 0);
-        sh.recv_bytes[k].assign(N, 0);
-        size_t so = 0, ro = 0;
-        for (int p = 0; p < N; ++p) {
-            sh.send_off[k][p] = so * row_bytes;
-            sh.send_bytes[k][p] = static_cast<size_t>(m.send_count[k][p]) * row_bytes;
-            so += m.send_count[k][p];
-            sh.recv_off[k][p] = ro * row_bytes;
-            sh.recv_bytes[k][p] = static_cast<size_t>(m.recv_count[k][p]) * row_bytes;
-            ro += m.recv_count[k][p];
-        }
-        sh.send_rows[k] = static_cast<int>(m.src[k].size());
-        if (!sh.send_src[k].ensure(std::max<size_t>(m.src[k].size(), 1) * 4) ||
-            !sh.recv_dst[k].ensure(std::max<size_t>(m.dst[k].size(), 1) * 4) ||
-            cudaMemcpy(sh.send_src[k].ptr, m.src[k].data(), m.src[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemcpy(sh.recv_dst[k].ptr, m.dst[k].data(), m.dst[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        std::vector<int2> dest(m.tok[k].size());
+        for (size_t i = 0; i < dest.size(); ++i) dest[i] = make_int2(m.dest_rank[k][i], m.dest_row[k][i]);
+        if (!sh.dest[k].ensure(std::max<size_t>(dest.size(), 1) * sizeof(int2)) ||
+            cudaMemcpy(sh.dest[k].ptr, dest.data(), dest.size() * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
     }
     for (int i = 0; i < d->n_blocks; ++i) {
@@ -456,6 +527,38 @@ static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
     }
     sh.T = T, sh.Hp = Hp, sh.Wp = Wp, sh.Lt = Lt;
     sh.valid = true;
+    return S2_OK;
+}
+
+// Peer mappings of the exchange's destinations (vid_a, vid_b) and flag words,
+// (re)made whenever one of those allocations changed: every rank's allocations
+// change in the same call (same sizes), so every rank makes the same
+// collective calls. Host-synchronising; not during stream capture.
+static s2_status xfer_setup(s2_dit *d, cudaStream_t st)
+{
+    auto &x = d->xf;
+    const int n = s2_comm_size(d->comm), me = s2_comm_rank(d->comm);
+    if (n > kMaxRanks)
+        return s2::set_error(S2_UNSUPPORTED, "sharded step: at most %d ranks (got %d)", kMaxRanks, n);
+    if (!x.flags.ptr) {
+        if (!x.flags.ensure(XF_WORDS * sizeof(int32_t)))
+            return s2::set_error(S2_OUT_OF_MEMORY, "sharded step: flag words");
+        if (cudaMemset(x.flags.ptr, 0, XF_WORDS * sizeof(int32_t)) != cudaSuccess)
+            return s2::set_error(S2_INFERENCE_FAILED, "sharded step: flag words memset failed");
+    }
+    void *cur[3] = {d->vid_a.ptr, d->vid_b.ptr, x.flags.ptr};
+    if (x.n == n && x.me == me && cur[0] == x.mine[0] && cur[1] == x.mine[1] && cur[2] == x.mine[2]) return S2_OK;
+    x.unshare();
+    x.n = n;
+    x.me = me;
+    for (int b = 0; b < 3; ++b) {
+        const s2_status s = s2::comm_share(d->comm, cur[b], x.peer[b], st);
+        if (s != S2_OK) {
+            x.unshare();
+            return s;
+        }
+        x.mine[b] = cur[b];
+    }
     return S2_OK;
 }
 
@@ -512,9 +615,8 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     int rows0 = rows;
     if (sharded) {
         S2_TRY(build_shard(d, T, Hp, Wp, Lt));
+        S2_TRY(xfer_setup(d, st));
         rows0 = d->sh.n_local[d->shifted[0]];
-        if (!d->xsend.ensure(Rz * D * 4) || !d->xrecv.ensure(Rz * D * 4))
-            return s2::set_error(S2_OUT_OF_MEMORY, "s2_dit_forward: exchange buffers");
     } else if (d->sh.valid) {
         for (s2_dit_block *b : d->blocks) {  // back to whole-clip blocks
             S2_TRY(s2_dit_block_set_window_subset(b, nullptr, 0));
@@ -575,21 +677,30 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     int kind = d->shifted[0], n_rows = rows0;
     for (int i = 0; i < d->n_blocks; ++i) {
         if (sharded && d->shifted[i] != kind) {
-            // re-partition the hidden rows from this kind's window ownership to the next one's
-            auto &sh = d->sh;
-            const int dim4 = D / 4;
-            gather_rows_kernel<<<grid_for(1LL * sh.send_rows[kind] * dim4), 256, 0, st>>>(
-                reinterpret_cast<const float4 *>(vid_cur), static_cast<const int32_t *>(sh.send_src[kind].ptr),
-                sh.send_rows[kind], dim4, static_cast<float4 *>(d->xsend.ptr));
-            S2_TRY(check("exchange pack"));
-            S2_TRY(s2::comm_exchange(d->comm, d->xsend.ptr, sh.send_off[kind].data(), sh.send_bytes[kind].data(),
-                                     d->xrecv.ptr, sh.recv_off[kind].data(), sh.recv_bytes[kind].data(), st));
+            // re-partition the hidden rows from this kind's window ownership to the next one's:
+            // every row goes straight into the next block's input buffer of its new owner
+            // (vid_nxt here and on every rank, whose last reader was the previous block)
+            auto &x = d->xf;
+            const int bi = vid_nxt == static_cast<float *>(d->vid_a.ptr) ? 0 : 1;
+            XferPeers pp;
+            for (int p = 0; p < kMaxRanks; ++p) {
+                pp.dst[p] = static_cast<float4 *>(p < x.n ? x.peer[bi][p] : nullptr);
+                pp.flags[p] = static_cast<int32_t *>(p < x.n ? x.peer[2][p] : nullptr);
+            }
+            int32_t *flags = static_cast<int32_t *>(x.flags.ptr);
+            xfer_ready_kernel<<<1, 32, 0, st>>>(pp, flags, x.me, x.n);
+            S2_TRY(check("exchange ready"));
+            const int n_old = n_rows;
+            const unsigned xg = static_cast<unsigned>(std::max(1, std::min((n_old + 7) / 8, 4 * 148)));
+            xfer_rows_kernel<<<xg, 256, 0, st>>>(reinterpret_cast<const float4 *>(vid_cur),
+                                                  static_cast<const int2 *>(d->sh.dest[kind].ptr), n_old, D / 4, pp,
+                                                  flags, x.me, x.n, err);
+            S2_TRY(check("exchange rows"));
+            xfer_wait_kernel<<<1, 32, 0, st>>>(flags, x.n, err);
+            S2_TRY(check("exchange wait"));
             kind = d->shifted[i];
-            n_rows = sh.n_local[kind];
-            scatter_rows_kernel<<<grid_for(1LL * n_rows * dim4), 256, 0, st>>>(
-                static_cast<const float4 *>(d->xrecv.ptr), static_cast<const int32_t *>(sh.recv_dst[1 - kind].ptr),
-                n_rows, dim4, reinterpret_cast<float4 *>(vid_cur));
-            S2_TRY(check("exchange unpack"));
+            n_rows = d->sh.n_local[kind];
+            std::swap(vid_cur, vid_nxt);
         }
         S2_TRY(s2_dit_block_set_runtime_shape(d->blocks[i], T, Hp, Wp));
         S2_TRY(s2::dit_block_forward_ex(d->blocks[i], stream, vid_cur, n_rows, txt_cur, Lt, emb, vid_nxt, txt_nxt,
@@ -788,9 +899,10 @@ extern "C" s2_status s2_dit_sample_texts(s2_dit *d, void *stream, const float *n
 extern "C" s2_status s2_dit_set_comm(s2_dit *d, s2_comm *comm)
 {
     if (!d) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_set_comm: model is NULL");
+    s2::DeviceGuard guard(d->device);
+    d->xf.unshare();
     d->comm = comm;
     d->sh.valid = false;
-    s2::DeviceGuard guard(d->device);
     d->drop_graph();
     d->key_valid = false;
     if (!comm || s2_comm_size(comm) == 1)

@@ -24,9 +24,11 @@ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 // destination rank (send_count), each in the destination's local order of kind
 // 1 - k; dst[k]: where the received rows go in this rank's local order of kind
 // 1 - k, source rank by source rank (recv_count). moved_rows[k]: tokens whose
-// owner changes from kind k to kind 1 - k (all ranks).
+// owner changes from kind k to kind 1 - k (all ranks). dest_rank[k][i] /
+// dest_row[k][i]: the rank that holds this rank's kind-k local row i under
+// kind 1 - k, and the row's index in that rank's kind-(1 - k) local order.
 struct ShardMaps {
-    std::vector<int32_t> ids[2], tok[2], src[2], dst[2];
+    std::vector<int32_t> ids[2], tok[2], src[2], dst[2], dest_rank[2], dest_row[2];
     std::vector<int32_t> send_count[2], recv_count[2];
     long long moved_rows[2] = {0, 0};
 };

@@ -202,10 +202,16 @@ s2_status windows_of(int T, int H, int W, int kind, int wt, int wh, int ww, std:
     return s2_make_windows(T, H, W, kind, wt, wh, ww, w.data(), n, &n);
 }
 
+// A window's share of a sharded DiT block's time, in units of one video row's
+// per-row work (the projections, MLP and norms: ~128 ns per row per block at
+// 720p) plus its attention (~11 ps per S_w^2 with S_w = video rows + text rows):
+// the projections dominate, so ownership balances rows first.
+constexpr double kAttnPerRow = 1e-4;
 double window_cost(const s2_window &w, int text_len)
 {
-    const double s = static_cast<double>(w.t1 - w.t0) * (w.h1 - w.h0) * (w.w1 - w.w0) + text_len;
-    return s * s;
+    const double l = static_cast<double>(w.t1 - w.t0) * (w.h1 - w.h0) * (w.w1 - w.w0);
+    const double s = l + text_len;
+    return l + kAttnPerRow * s * s;
 }
 
 }  // namespace
@@ -385,6 +391,13 @@ s2_status shard_exchange_maps(int T, int H, int W, int wt, int wh, int ww, int t
                 }
         for (long long p = 0; p < L; ++p)
             if (own_rank[k][p] != own_rank[k2][p]) ++m.moved_rows[k];
+        m.dest_rank[k].resize(m.tok[k].size());
+        m.dest_row[k].resize(m.tok[k].size());
+        for (size_t i = 0; i < m.tok[k].size(); ++i) {
+            const int p = m.tok[k][i];
+            m.dest_rank[k][i] = own_rank[k2][p];
+            m.dest_row[k][i] = own_idx[k2][p];
+        }
     }
     return S2_OK;
 }
@@ -411,6 +424,22 @@ extern "C" s2_status s2_shard_exchange(int frames, int height, int width, int wt
     if (send_rows) std::copy(m.src[kind].begin(), m.src[kind].end(), send_rows);
     if (recv_rows) std::copy(m.dst[kind].begin(), m.dst[kind].end(), recv_rows);
     if (moved_rows) *moved_rows = m.moved_rows[kind];
+    return S2_OK;
+}
+
+extern "C" s2_status s2_shard_row_destinations(int frames, int height, int width, int wt, int wh, int ww,
+                                              int text_len, int n_ranks, int rank, int kind, int32_t *dest_rank,
+                                              int32_t *dest_row, int *n_local)
+{
+    s2::clear_error();
+    if (n_ranks <= 0 || rank < 0 || rank >= n_ranks || (kind != 0 && kind != 1) || !n_local)
+        return s2::set_error(S2_INVALID_ARGUMENT, "s2_shard_row_destinations: invalid arguments");
+    s2::ShardMaps m;
+    const s2_status s = s2::shard_exchange_maps(frames, height, width, wt, wh, ww, text_len, n_ranks, rank, m);
+    if (s != S2_OK) return s;
+    *n_local = static_cast<int>(m.tok[kind].size());
+    if (dest_rank) std::copy(m.dest_rank[kind].begin(), m.dest_rank[kind].end(), dest_rank);
+    if (dest_row) std::copy(m.dest_row[kind].begin(), m.dest_row[kind].end(), dest_row);
     return S2_OK;
 }
 

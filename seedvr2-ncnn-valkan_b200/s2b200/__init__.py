@@ -97,6 +97,7 @@ _SIGS = {
     "s2_shard_windows_joint": (ctypes.c_int, [ctypes.c_int] * 8 + [_i32p, _i32p]),
     "s2_shard_exchange": (ctypes.c_int, [ctypes.c_int] * 10 + [_i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p,
                                                               _i32p, ctypes.POINTER(ctypes.c_longlong)]),
+    "s2_shard_row_destinations": (ctypes.c_int, [ctypes.c_int] * 10 + [_i32p, _i32p, ctypes.POINTER(ctypes.c_int)]),
     "s2_rope_table_bytes": (ctypes.c_size_t, [ctypes.c_int]),
     "s2_rope_table": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
     "s2_qk_norm_rope": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp, _vp, _vp,
@@ -394,6 +395,19 @@ def shard_exchange(grid, text_len: int, n_ranks: int, rank: int, kind: int, over
     return {"window_ids": ids[:nw.value].copy(), "local_tokens": tok[:nl.value].copy(), "send_counts": sc,
             "send_rows": sr[:int(sc.sum())].copy(), "recv_counts": rc, "recv_rows": rr[:int(rc.sum())].copy(),
             "moved_rows": moved.value}
+
+
+def shard_row_destinations(grid, text_len: int, n_ranks: int, rank: int, kind: int, override=(0, 0, 0)):
+    """s2_shard_row_destinations: (dest_rank, dest_row) of each of rank `rank`'s
+    kind-`kind` local rows under the other kind (host planning, no GPU)."""
+    T, H, W = grid
+    L = T * H * W
+    dr, dw = np.zeros(L, np.int32), np.zeros(L, np.int32)
+    nl = ctypes.c_int(0)
+    p = lambda a: a.ctypes.data_as(_i32p)  # noqa: E731
+    _check(lib().s2_shard_row_destinations(T, H, W, *override, text_len, n_ranks, rank, kind, p(dr), p(dw),
+                                           ctypes.byref(nl)), "s2_shard_row_destinations")
+    return dr[:nl.value].copy(), dw[:nl.value].copy()
 
 
 def shard_owners(windows: np.ndarray, text_len: int, n_ranks: int) -> np.ndarray:

@@ -160,8 +160,34 @@ def test_shard_local_rows_follow_the_single_rank_order(grid, world):
                 x = np.arange(w[4], w[5])[None, None, :]
                 tok[k][((t * H + y) * W + x).ravel()] = lpt[k][i]
         assert moved <= int((tok[0] != tok[1]).sum()), (moved, int((tok[0] != tok[1]).sum()))
-        # the shifted layers' load stays within the 2 % cap whenever a rank can take each window
+        # the shifted layers' load (video rows + 1e-4 * S_w^2: a block's work) stays within the
+        # 2 % cap whenever a rank can take each window
         w1 = s2b200.make_windows(T, H, W, 1)
-        cost = (((w1[:, 1] - w1[:, 0]) * (w1[:, 3] - w1[:, 2]) * (w1[:, 5] - w1[:, 4])) + 58.0) ** 2
+        rows1 = ((w1[:, 1] - w1[:, 0]) * (w1[:, 3] - w1[:, 2]) * (w1[:, 5] - w1[:, 4])).astype(np.float64)
+        cost = rows1 + 1e-4 * (rows1 + 58.0) ** 2
         load = np.array([cost[s2b200.shard_exchange(grid, 58, world, r, 1)["window_ids"]].sum() for r in range(world)])
         assert load.max() <= max(1.02 * cost.sum() / world, cost.max()) * 1.0001
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("grid", [(6, 45, 80), (2, 16, 30)])
+def test_row_destinations_cover_every_rank_once(grid, world):
+    """The peer-store exchange's per-row destinations (s2_shard_row_destinations):
+    every rank's kind-k row goes to the rank holding its token under the other
+    kind, at that token's place in that rank's local order, and together the
+    ranks fill every destination row exactly once; the rows that leave their
+    rank are the grid's moved rows."""
+    for kind in (0, 1):
+        other = [s2b200.shard_exchange(grid, 58, world, r, 1 - kind)["local_tokens"] for r in range(world)]
+        filled = [np.zeros(len(o), np.int64) for o in other]
+        moved = 0
+        for r in range(world):
+            tok = s2b200.shard_exchange(grid, 58, world, r, kind)["local_tokens"]
+            dr, dw = s2b200.shard_row_destinations(grid, 58, world, r, kind)
+            assert len(dr) == len(tok)
+            for i in range(len(tok)):
+                assert other[dr[i]][dw[i]] == tok[i], (kind, r, i)
+                filled[dr[i]][dw[i]] += 1
+            moved += int((dr != r).sum())
+        assert all(np.all(f == 1) for f in filled), kind
+        assert moved == s2b200.shard_exchange(grid, 58, world, 0, kind)["moved_rows"]
