@@ -384,7 +384,8 @@ extern "C" s2_status s2_dit_block_set_local_rows(s2_dit_block *b, int enable)
 }
 
 s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt, int Lt,
-                                   const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce)
+                                   const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce,
+                                   const RowScatter *scatter)
 {
     s2::clear_error();
     if (!b) return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: block is NULL");
@@ -393,6 +394,8 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: invalid arguments");
     if (vid == vid_out || (Lt > 0 && txt == txt_out))
         return s2::set_error(S2_INVALID_ARGUMENT, "s2_dit_block_forward: in-place forward is not supported");
+    if (scatter && (b->debug_on || b->debug_host_on || !scatter->dest))
+        return s2::set_error(S2_UNSUPPORTED, "s2_dit_block_forward: row scatter without debug captures only");
     s2::DeviceGuard guard(b->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int d = b->dim, h = b->hidden;
@@ -594,7 +597,7 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     }
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
     auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y,
-                   int split, float *y2) -> s2_status {
+                   int split, float *y2, const s2::RowScatter *sc_rows) -> s2_status {
         s2_status r = rms_ada3(st, hx, rows, d, b->eps, mb + 3 * dz, a16);
         if (r != S2_OK) return r;
         ++launches;
@@ -621,6 +624,11 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         o.extra_launches = &extra;
         o.resid = hx;
         o.y = y;
+        if (sc_rows) {
+            o.y = nullptr;
+            o.row_dest = sc_rows->dest;
+            for (int q = 0; q < 8; ++q) o.dest_base[q] = sc_rows->base[q];
+        }
         if (split > 0) {
             o.split_row = split;
             o.resid2 = hx + static_cast<size_t>(split) * dz;
@@ -632,13 +640,13 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         return S2_OK;
     };
     if ((s = mlp(mv, V, h_vid, merged_rest ? L + Lt : L, a_vid, static_cast<__half *>(sc.hid_vid.ptr), vid_out,
-                 merged_rest ? L : 0, txt_out)) != S2_OK) {
+                 merged_rest ? L : 0, txt_out, scatter)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
     if (Lt > 0 && !b->last && !merged_rest &&
         (s = mlp(mt, T, h_txt, Lt, static_cast<__half *>(sc.a_txt.ptr), static_cast<__half *>(sc.hid_txt.ptr), txt_out,
-                 0, nullptr)) != S2_OK) {
+                 0, nullptr, nullptr)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }

@@ -9,8 +9,8 @@
 //     [58][2560] (and of the disjoint per-rank parts of the output latent);
 //   * every rank's buffers of the row exchange between the window ownerships
 //     of consecutive blocks mapped into every other rank (comm_share: CUDA IPC
-//     handles all-gathered over NCCL); the exchange itself is a kernel of the
-//     DiT that stores rows into peer memory.
+//     handles all-gathered over NCCL); the exchange itself is the epilogue of
+//     the DiT block's last GEMM, which stores rows into peer memory.
 //
 // Failures: the ranks meet through a non-blocking communicator
 // (ncclConfig_t.blocking = 0) whose creation is polled with

@@ -174,27 +174,29 @@ __global__ void unpatchify_local_kernel(const float *__restrict__ proj, int oc, 
 }
 
 // ---- row exchange over peer memory (sharded step) -------------------------------
-// At a plain <-> shifted boundary every rank writes each of its hidden rows
-// straight into the buffer that becomes the next block's input on the rank
-// that owns the row's token under the next window kind (its own, or a peer's
-// mapped through CUDA IPC): plain stores, over NVLink for peers. No collective
-// library call, no pack or scatter pass. Ordering, per boundary and epoch e
-// (a device counter every rank advances in step):
-//   ready: a rank announces e once its previous block has finished reading the
-//          destination buffer (stream order), so peers may overwrite it;
-//   rows:  each CTA waits for every rank's ready, copies its rows, fences at
-//          system scope; the last CTA announces done e to every rank;
-//   wait:  the next block starts after every rank's done e.
-// Every wait is bounded; on expiry the DiT's error word gets a code and the
+// At a plain <-> shifted boundary the last GEMM of the block before it (the MLP
+// output projection with its gated residual) stores every output row straight
+// into the next block's input buffer on the rank that owns the row's token
+// under the next window kind -- its own buffer, or a peer's mapped through CUDA
+// IPC (plain stores over NVLink): the exchange has no pass or collective call
+// of its own. Ordering, with the same buffer role (vid_nxt) on every rank:
+//   * the destination is free: it is each rank's input of the previous block,
+//     last read by that block's output projection; the writer's text
+//     all-reduce in the current block, before its MLP, completes only once
+//     every rank has reached that all-reduce, i.e. finished the previous block;
+//   * the rows have landed before the next block reads them: each epilogue
+//     thread fences its stores at system scope; after the GEMM every rank
+//     announces epoch e (a device counter all ranks advance in step) to every
+//     rank, and waits until every rank announced e.
+// The wait is bounded; on expiry the DiT's error word gets a code and the
 // kernel returns (a peer that died makes the step fail, not hang).
 constexpr int kMaxRanks = 8;
-enum : int { XF_READY = 0, XF_DONE = kMaxRanks, XF_EPOCH = 2 * kMaxRanks, XF_COUNT = XF_EPOCH + 1, XF_WORDS = 32 };
-enum : int { E_XFER_READY = 48, E_XFER_DONE = 49 };
+enum : int { XF_DONE = 0, XF_EPOCH = kMaxRanks, XF_WORDS = 16 };
+enum : int { E_XFER_DONE = 49 };
 constexpr unsigned long long kXferTimeoutNs = 10000000000ull;  // 10 s
 
-struct XferPeers {
-    float4 *dst[kMaxRanks];     // every rank's destination rows (this rank's own among them)
-    int32_t *flags[kMaxRanks];  // every rank's flag words
+struct XferFlags {
+    int32_t *flags[kMaxRanks];  // every rank's flag words (this rank's own among them)
 };
 
 __device__ __forceinline__ unsigned long long xf_now()
@@ -213,59 +215,31 @@ __device__ __forceinline__ int ld_acquire_sys(const int32_t *p)
     asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-// every rank's word flags[slot + rank] has reached epoch e (bounded)
-__device__ bool xf_wait_all(const int32_t *flags, int slot, int n, int e)
-{
-    const unsigned long long t0 = xf_now();
-    for (int p = 0; p < n; ++p)
-        while (ld_acquire_sys(flags + slot + p) < e) {
-            if (xf_now() - t0 > kXferTimeoutNs) return false;
-            __nanosleep(200);
-        }
-    return true;
-}
 
-__global__ void xfer_ready_kernel(XferPeers pp, int32_t *flags, int me, int n)
+// this rank's rows of the exchange are stored: announce the next epoch to every rank
+__global__ void xfer_done_kernel(XferFlags ff, int32_t *flags, int me, int n)
 {
     if (threadIdx.x != 0) return;
     const int e = flags[XF_EPOCH] + 1;
     flags[XF_EPOCH] = e;
-    for (int p = 0; p < n; ++p) st_release_sys(pp.flags[p] + XF_READY + me, e);
+    __threadfence_system();
+    for (int p = 0; p < n; ++p) st_release_sys(ff.flags[p] + XF_DONE + me, e);
 }
 
-// row r -> rank map[r].x, row map[r].y (a warp per row)
-__global__ void __launch_bounds__(256) xfer_rows_kernel(const float4 *__restrict__ src, const int2 *__restrict__ map,
-                                                        int n_rows, int dim4, XferPeers pp, int32_t *flags, int me,
-                                                        int n, int32_t *err)
-{
-    __shared__ int ready;
-    const int e = flags[XF_EPOCH];
-    if (threadIdx.x == 0) {
-        ready = xf_wait_all(flags, XF_READY, n, e);
-        if (!ready) atomicCAS(err, 0, E_XFER_READY);
-    }
-    __syncthreads();
-    if (ready) {
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int r = blockIdx.x * 8 + warp; r < n_rows; r += gridDim.x * 8) {
-            const int2 d = __ldg(map + r);
-            const float4 *s = src + static_cast<size_t>(r) * dim4;
-            float4 *o = pp.dst[d.x] + static_cast<size_t>(d.y) * dim4;
-            for (int c = lane; c < dim4; c += 32) o[c] = __ldg(s + c);
-        }
-    }
-    __threadfence_system();  // this thread's stores, at system scope, before the CTA counts as done
-    __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(flags + XF_COUNT, 1) == static_cast<int>(gridDim.x) - 1) {
-        flags[XF_COUNT] = 0;
-        __threadfence_system();
-        for (int p = 0; p < n; ++p) st_release_sys(pp.flags[p] + XF_DONE + me, e);
-    }
-}
-
+// every rank announced this epoch (bounded)
 __global__ void xfer_wait_kernel(const int32_t *flags, int n, int32_t *err)
 {
-    if (threadIdx.x == 0 && !xf_wait_all(flags, XF_DONE, n, flags[XF_EPOCH])) atomicCAS(err, 0, E_XFER_DONE);
+    if (threadIdx.x != 0) return;
+    const int e = flags[XF_EPOCH];
+    const unsigned long long t0 = xf_now();
+    for (int p = 0; p < n; ++p)
+        while (ld_acquire_sys(flags + XF_DONE + p) < e) {
+            if (xf_now() - t0 > kXferTimeoutNs) {
+                atomicCAS(err, 0, E_XFER_DONE);
+                return;
+            }
+            __nanosleep(200);
+        }
 }
 
 unsigned grid_for(long long n) { return static_cast<unsigned>(std::min<long long>((n + 255) / 256, 4096)); }
@@ -676,36 +650,32 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     const float *emb = static_cast<const float *>(d->emb.ptr);
     int kind = d->shifted[0], n_rows = rows0;
     for (int i = 0; i < d->n_blocks; ++i) {
-        if (sharded && d->shifted[i] != kind) {
-            // re-partition the hidden rows from this kind's window ownership to the next one's:
-            // every row goes straight into the next block's input buffer of its new owner
-            // (vid_nxt here and on every rank, whose last reader was the previous block)
-            auto &x = d->xf;
+        // a block followed by the other window kind writes its video rows straight into the
+        // next block's input (vid_nxt, on this rank and the peers) in the next kind's ownership
+        const bool exchange = sharded && i + 1 < d->n_blocks && d->shifted[i + 1] != kind;
+        s2::RowScatter rs;
+        if (exchange) {
+            const auto &x = d->xf;
             const int bi = vid_nxt == static_cast<float *>(d->vid_a.ptr) ? 0 : 1;
-            XferPeers pp;
-            for (int p = 0; p < kMaxRanks; ++p) {
-                pp.dst[p] = static_cast<float4 *>(p < x.n ? x.peer[bi][p] : nullptr);
-                pp.flags[p] = static_cast<int32_t *>(p < x.n ? x.peer[2][p] : nullptr);
-            }
-            int32_t *flags = static_cast<int32_t *>(x.flags.ptr);
-            xfer_ready_kernel<<<1, 32, 0, st>>>(pp, flags, x.me, x.n);
-            S2_TRY(check("exchange ready"));
-            const int n_old = n_rows;
-            const unsigned xg = static_cast<unsigned>(std::max(1, std::min((n_old + 7) / 8, 4 * 148)));
-            xfer_rows_kernel<<<xg, 256, 0, st>>>(reinterpret_cast<const float4 *>(vid_cur),
-                                                  static_cast<const int2 *>(d->sh.dest[kind].ptr), n_old, D / 4, pp,
-                                                  flags, x.me, x.n, err);
-            S2_TRY(check("exchange rows"));
-            xfer_wait_kernel<<<1, 32, 0, st>>>(flags, x.n, err);
-            S2_TRY(check("exchange wait"));
-            kind = d->shifted[i];
-            n_rows = d->sh.n_local[kind];
-            std::swap(vid_cur, vid_nxt);
+            rs.dest = static_cast<const int2 *>(d->sh.dest[kind].ptr);
+            for (int p = 0; p < x.n; ++p) rs.base[p] = static_cast<float *>(x.peer[bi][p]);
         }
         S2_TRY(s2_dit_block_set_runtime_shape(d->blocks[i], T, Hp, Wp));
         S2_TRY(s2::dit_block_forward_ex(d->blocks[i], stream, vid_cur, n_rows, txt_cur, Lt, emb, vid_nxt, txt_nxt,
-                                        sharded ? &reduce : nullptr));
+                                        sharded ? &reduce : nullptr, exchange ? &rs : nullptr));
         launches += s2_dit_block_last_launches(d->blocks[i]);
+        if (exchange) {
+            const auto &x = d->xf;
+            XferFlags ff;
+            for (int p = 0; p < kMaxRanks; ++p) ff.flags[p] = static_cast<int32_t *>(p < x.n ? x.peer[2][p] : nullptr);
+            int32_t *flags = static_cast<int32_t *>(x.flags.ptr);
+            xfer_done_kernel<<<1, 32, 0, st>>>(ff, flags, x.me, x.n);
+            S2_TRY(check("exchange announce"));
+            xfer_wait_kernel<<<1, 32, 0, st>>>(flags, x.n, err);
+            S2_TRY(check("exchange wait"));
+            kind = d->shifted[i + 1];
+            n_rows = d->sh.n_local[kind];
+        }
         std::swap(vid_cur, vid_nxt);
         std::swap(txt_cur, txt_nxt);
     }

@@ -420,7 +420,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     const int y_rows = a.split_row > 0 ? a.split_row : a.M;
-                    if (m0 + quad * 32 < y_rows) store_chunk32(&tmO0, outv, n, m0 + quad * 32);
+                    if (a.row_dest) {
+                        // every row to its own destination: the warp stages its 32 rows' 128-byte
+                        // segments (16-byte chunk k of row r at k ^ (r % 8)) and stores them four
+                        // rows per instruction
+                        float *my_dst = nullptr;
+                        if (row_ok && row < y_rows) {
+                            const int2 dd = __ldg(a.row_dest + row);
+                            float *bp = a.dest_base[0];
+#pragma unroll
+                            for (int q = 1; q < 8; ++q)
+                                if (dd.x == q) bp = a.dest_base[q];
+                            my_dst = bp + static_cast<size_t>(dd.y) * a.N + n;
+                        }
+                        float4 *stg = reinterpret_cast<float4 *>(stg0_g);
+                        __syncwarp();
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) stg[lane * 8 + (k ^ (lane & 7))] = outv[k];
+                        __syncwarp();
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int rr = 4 * k + (lane >> 3), cc = lane & 7;
+                            const unsigned long long pa =
+                                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_dst), rr);
+                            const float4 v = stg[rr * 8 + (cc ^ (rr & 7))];
+                            if (pa) reinterpret_cast<float4 *>(pa)[cc] = v;
+                        }
+                    } else if (m0 + quad * 32 < y_rows) {
+                        store_chunk32(&tmO0, outv, n, m0 + quad * 32);
+                    }
                 }
             }
             if (kBN == 256 && a.epilogue == s2::GEMM_EPI_SWIGLU_F16 && !split_k && ok) {
@@ -542,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            if (a.row_dest) __threadfence_system();  // row stores into peers' memory, before the kernel ends
             tc_fence_before();
             if constexpr (kPair) {
                 if (rank == 0)
@@ -719,7 +748,8 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             args.ldt < 1LL * g.od * g.oh * g.ow)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad convolution output");
     } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
-        if (!args.y || args.N % 32 != 0 || (args.split_row > 0 && (!args.y2 || (args.resid && !args.resid2))) ||
+        if ((!args.y && !args.row_dest) || args.N % 32 != 0 ||
+            (args.split_row > 0 && (!args.y2 || (args.resid && !args.resid2))) ||
             ((reinterpret_cast<uintptr_t>(args.y) | reinterpret_cast<uintptr_t>(args.resid)) & 15u) != 0)
             return set_error(S2_INVALID_ARGUMENT, "gemm: bad gated-residual output");
     } else if (args.epilogue == GEMM_EPI_SWIGLU_F16) {
@@ -766,7 +796,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     // at least 4 K slices). Not for the channel-major epilogue (the VAE, many rows).
     int ks = 1;
     const long long tiles_k = mt * ((args.N + bn - 1) / bn);
-    if (args.partial && !pair && args.M <= kBM && !args.conv &&
+    if (args.partial && !pair && args.M <= kBM && !args.conv && !args.row_dest &&
         (args.epilogue == GEMM_EPI_SPLIT_F16 || args.epilogue == GEMM_EPI_GATED_RESID_F32 ||
          args.epilogue == GEMM_EPI_SWIGLU_F16) &&
         tiles_k * 2 <= sms) {
@@ -804,7 +834,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             if (!make_map_2d_plain(&mo[i], ptr, cols, args.M, cols * 2, 32, 32))
                 return set_error(S2_INFERENCE_FAILED, "gemm: output tensor map failed");
         }
-    } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32) {
+    } else if (args.epilogue == GEMM_EPI_GATED_RESID_F32 && !args.row_dest) {
         const uint64_t rows = args.split_row > 0 ? static_cast<uint64_t>(args.split_row) : static_cast<uint64_t>(args.M);
         if (!make_map_2d_plain_f32(&mo[0], args.y, args.N, rows, static_cast<uint64_t>(args.N) * 4, 32, 32))
             return set_error(S2_INFERENCE_FAILED, "gemm: output tensor map failed");

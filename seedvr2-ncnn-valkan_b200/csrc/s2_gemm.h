@@ -127,6 +127,12 @@ struct GemmArgs {
     int conv = 0;                 // 1: A is the im2col of the convolution `geom`
     ConvGeom geom;
     PackArgs pk;                  // GEMM_EPI_QKV_PACK
+    // GEMM_EPI_GATED_RESID_F32 row scatter: with row_dest set, row r (< split_row, or
+    // < M) goes to dest_base[row_dest[r].x] + row_dest[r].y * N instead of y -- any
+    // rank's buffer mapped into this process (peer stores over NVLink), each thread
+    // fencing its stores at system scope before the kernel ends. No split-K.
+    const int2 *row_dest = nullptr;
+    float *dest_base[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
 // D[M][N] = A[M][K] B[N][K]^T on sm_100a: A and B fp16, K-major (row-major

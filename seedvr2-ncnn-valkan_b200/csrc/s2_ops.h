@@ -22,9 +22,20 @@ struct TextReduce {
     void *ctx = nullptr;
 };
 
-// s2_dit_block_forward with an optional text reduction.
+// Where a sharded step's block writes its video output rows instead of vid_out:
+// row r to base[dest[r].x] + dest[r].y * dim (the next block's input on the row's
+// next owner; bases of other ranks are peer mappings). The stores are plain, so
+// the caller orders them with the destination's readers.
+struct RowScatter {
+    const int2 *dest = nullptr;
+    float *base[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+};
+
+// s2_dit_block_forward with an optional text reduction and an optional scatter of
+// the video output rows (not with debug captures).
 s2_status dit_block_forward_ex(s2_dit_block *b, void *stream, const float *vid, int L, const float *txt, int Lt,
-                               const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce);
+                               const float *emb, float *vid_out, float *txt_out, const TextReduce *reduce,
+                               const RowScatter *scatter = nullptr);
 s2_attention_layer *dit_block_attention(s2_dit_block *b);
 
 // Debug capture of the attention stage the layer just ran (the block's
