@@ -480,6 +480,11 @@ static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
     s2_status s = s2::shard_exchange_maps(T, Hp, Wp, d->wt, d->wh, d->ww, Lt, N, me, m);
     if (s != S2_OK) return s;
     for (int k = 0; k < 2; ++k) {
+        if (m.tok[k].empty())
+            return s2::set_error(S2_UNSUPPORTED,
+                                 "sharded step: rank %d owns no %s window of the %dx%dx%d grid (too few windows for %d "
+                                 "ranks; use fewer ranks or smaller windows)",
+                                 me, k ? "shifted" : "plain", T, Hp, Wp, N);
         sh.ids[k] = m.ids[k];
         sh.n_local[k] = static_cast<int>(m.tok[k].size());
         if (!sh.tok[k].ensure(std::max<size_t>(m.tok[k].size(), 1) * 4) ||

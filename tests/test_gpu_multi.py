@@ -1,8 +1,9 @@
-"""The sharded DiT Euler step on 2 GPUs (one process per GPU, the library's
-NCCL communicator): each rank keeps only its windows' video rows, all-reduces
-every block's text attention mean and exchanges rows between the plain and
-shifted window ownerships. The result must match the same step on one GPU and
-the reference. Skipped where the box has fewer than 2 GPUs.
+"""The sharded DiT Euler step on 2 and 4 GPUs (one process per GPU, the
+library's NCCL communicator): each rank keeps only its windows' video rows,
+all-reduces every block's text attention mean, and at every plain <-> shifted
+boundary the block's last GEMM stores each row into its next owner's input
+buffer (peer memory over NVLink). The result must match the same step on one
+GPU (and, on 2 GPUs, the reference). Skipped where the box has too few GPUs.
 """
 from __future__ import annotations
 
@@ -32,10 +33,10 @@ def _case():
     return flags, wi, wo, bws, noise, cond, text
 
 
-def _model(device, flags, wi, wo, bws):
+def _model(device, flags, wi, wo, bws, windows=(0, 0, 0)):
     c = CASE
     m = s2b200.SeedVR2DiT(device=device, n_blocks=c["n_blocks"], dim=c["dim"], heads=c["heads"],
-                          mlp_hidden=c["mlp"], text_channels=c["tc"])
+                          mlp_hidden=c["mlp"], text_channels=c["tc"], window_override=windows)
     m.load_input(wi)
     m.load_output(wo)
     for i, f in enumerate(flags):
@@ -43,7 +44,7 @@ def _model(device, flags, wi, wo, bws):
     return m
 
 
-def _rank(rank, world, port, out_dir):
+def _rank(rank, world, port, out_dir, windows=(0, 0, 0)):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -51,7 +52,7 @@ def _rank(rank, world, port, out_dir):
     torch.cuda.set_device(rank)
     comm = s2b200.Comm.create(rank, rank, world)
     flags, wi, wo, bws, noise, cond, text = _case()
-    m = _model(rank, flags, wi, wo, bws)
+    m = _model(rank, flags, wi, wo, bws, windows)
     m.set_comm(comm)
     args = [torch.from_numpy(a).cuda(rank) for a in (noise, cond, text)]
     x0 = m.euler_step(*args)        # eager
@@ -88,3 +89,24 @@ def test_sharded_euler_step_two_gpus(tmp_path, ref):
     assert m["max_abs"] <= 1e-4, m                           # only the text sums change order
     p = parity.metrics(noise - outs[0], noise - ex0)
     assert p["nrmse"] <= 0.02 and p["cosine"] >= 0.9998, p
+
+
+def test_sharded_euler_step_four_gpus(tmp_path):
+    """Four ranks, each writing rows to three peers at every boundary: explicit 1x3x4
+    windows on the 2x6x10 token grid (12 plain windows), so every rank owns windows
+    of both kinds; checked against the same model on one GPU."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    windows = (1, 3, 4)
+    port = 29500 + (os.getpid() + 500) % 1000
+    mp.start_processes(_rank, args=(4, port, str(tmp_path), windows), nprocs=4, join=True, start_method="spawn")
+    flags, wi, wo, bws, noise, cond, text = _case()
+    single = _model(0, flags, wi, wo, bws, windows).euler_step_host(noise, cond, text)
+    outs = [np.load(tmp_path / f"x0_{r}.npy") for r in range(4)]
+    for r in range(1, 4):
+        assert np.array_equal(outs[0], outs[r]), r
+    assert np.array_equal(outs[0], np.load(tmp_path / "x0b_0.npy"))
+    m = parity.metrics(outs[0], single)
+    assert m["max_abs"] <= 1e-4, m
