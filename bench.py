@@ -285,7 +285,8 @@ def workload_config(args):
             "layers_per_step": 32, "grid": [6, 45, 80], "heads": 20, "head_dim": 128, "text_len": 58,
             "mode": args.mode, "io": "fp16 QKV in, fp16 out" if args.mode == "f16" else "fp16 QKV in, bf16 out",
             "l2": "no flush: every layer reads a distinct >L2 input (332 MB QKV, 356 MB packed Q/K/V)",
-            "sharding": "window-sharded single clip + NCCL text all-reduce (strong)" if args.shard else
+            "sharding": "window-sharded single clip + per-layer NCCL text all-reduce, overlapped with the next "
+                        "layer (strong)" if args.shard else
                         "one clip per rank (weak)"}
 
 
@@ -347,7 +348,11 @@ def run_ours(args, rank, world, local_rank):
     ws = [torch.empty((heads, n_rows_max, 128), dtype=torch.float16, device=dev) for _ in range(3)]
     vid_out = torch.zeros((T * H * W, dim), dtype=out_dtype, device=dev)
     txt_part = torch.empty((max(p["n_local"] for p in plans), Lt, dim), dtype=out_dtype, device=dev)
-    txt_out = torch.empty((Lt, dim), dtype=torch.float32, device=dev)
+    # one text output per layer of a step: a sharded layer's all-reduce of its text mean runs
+    # asynchronously (NCCL's stream) while the next, independent layer computes; a step ends
+    # once all of its all-reduces completed (inside the timed region)
+    txt_outs = [torch.empty((Lt, dim), dtype=torch.float32, device=dev) for _ in range(32)]
+    pending = []
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     lib = s2b200.lib()
     sp = s2b200._stream_ptr(stream)
@@ -374,13 +379,17 @@ def run_ours(args, rank, world, local_rank):
         if ev:
             ev[2].record(stream)
         rc = lib.s2_text_window_sum(sp, mode, vp(txt_part), p["n_local"], Lt, dim, 1.0 / p["n_total"], 0,
-                                    vp(txt_out))
+                                    vp(txt_outs[i]))
         if rc:
             raise RuntimeError(s2b200.last_error())
         if ev:
             ev[3].record(stream)
         if args.shard and world > 1:
-            dist.all_reduce(txt_out)
+            pending.append(dist.all_reduce(txt_outs[i], async_op=True))
+
+    def end_step():
+        while pending:
+            pending.pop().wait()  # the current stream waits for the collective
 
     layers_per_step = 32
     t_w = time.time()
@@ -388,6 +397,7 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(args.warmup):
             for i in range(layers_per_step):
                 layer(i)
+            end_step()
     torch.cuda.synchronize()
     n_pre = preroll_steps((time.time() - t_w) * 1e3 / max(1, args.warmup), dist, dev)
     if int(err.item()) != 0:
@@ -403,10 +413,12 @@ def run_ours(args, rank, world, local_rank):
         for _ in range(n_pre):
             for i in range(layers_per_step):
                 layer(i)
+            end_step()
         start.record(stream)
         for s in range(args.steps):
             for i in range(layers_per_step):
                 layer(i, evs[s * layers_per_step + i])
+            end_step()
         end.record(stream)
         torch.cuda.synchronize()
     if dist:
@@ -625,8 +637,9 @@ def run_euler(args, torch, s2b200, synth, dev, rank, world, dist):
             "gemm_tflop_per_step": gemm / 1e12, "attention_tflop_per_step": att / 1e12,
             "tflops_overall": (gemm + att) / (ms * 1e-3) / 1e12, "gpu_launches_per_step": launches,
             "cuda_graph": True, "n_gpus": world,
-            "sharding": "one step split by window across the GPUs (NCCL text all-reduce + row exchange at every "
-                        "plain/shifted boundary), strong scaling" if world > 1 else "one GPU",
+            "sharding": "one step split by window across the GPUs (NCCL text all-reduce per block; the row "
+                        "exchange at every plain/shifted boundary stored by the MLP output GEMM into the next "
+                        "owner's buffer over NVLink), strong scaling" if world > 1 else "one GPU",
             "finite": ok, "weights_load_s": load_s,
             "e2e": {"ms_per_step": e2e_ms, "unit": "ms", "steps": e2e_steps,
                     "h2d_bytes_per_step": int(hn.nbytes + hc.nbytes + ht.nbytes),
@@ -663,14 +676,19 @@ def run_cfg3(args, torch, s2b200, synth, dev, rank, world, dist):
         flops += synth.attention_flops(wins[ids], Lt, heads)
         layers.append(lay)
     vo = torch.zeros((T * H * W, dim), dtype=s2b200.mode_dtype(mode), device=dev)
-    to = torch.empty((Lt, dim), dtype=torch.float32, device=dev)
+    tos = [torch.empty((Lt, dim), dtype=torch.float32, device=dev) for _ in layers]
     stream = torch.cuda.current_stream()
 
     def step():
-        for lay in layers:
+        # each layer's text all-reduce overlaps the next, independent layer; the step ends
+        # once both completed
+        pending = []
+        for lay, to in zip(layers, tos):
             lay.forward(v, t, vo, to, stream=stream)
             if dist:
-                dist.all_reduce(to)
+                pending.append(dist.all_reduce(to, async_op=True))
+        for h in pending:
+            h.wait()
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -705,7 +723,8 @@ def run_cfg3(args, torch, s2b200, synth, dev, rank, world, dist):
                         "reference windows 3x15x27 (100 plain / 125 shifted); one plain + one shifted layer per step",
             "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms, "steps": steps,
             "tflop_per_step": flops / 1e12, "n_gpus": world,
-            "scaling": "strong (windows split across ranks, NCCL text all-reduce)" if world > 1 else "one GPU",
+            "scaling": "strong (windows split across ranks, NCCL text all-reduce overlapped with the next layer)"
+            if world > 1 else "one GPU",
             "gpu_launches_per_step": 6, "clocks": clk.summary()}
 
 
