@@ -37,13 +37,26 @@ namespace {
 //        add0 = emb[6c + s], add1 = shift[c] precomputed (:784-805)
 // mul == nullptr skips the modulation (the last block's text input); gamma is
 // the output head's RMSNorm weight (seedvr2_dit_output.cpp:383).
-__global__ void __launch_bounds__(256) rms_ada_kernel(const float *__restrict__ x, int rows, int dim, float eps,
-                                                      const float *__restrict__ gamma, const float *__restrict__ mul,
-                                                      const float *__restrict__ add0, const float *__restrict__ add1,
-                                                      __half *__restrict__ y)
+// A run of rows with its own input, modulation vectors and output: one launch
+// normalises the video rows and the text rows of a block (each with its branch's
+// vectors), where the text rows alone would be a launch of a few dozen warps.
+struct RmsSeg {
+    const float *x = nullptr;
+    const float *gamma = nullptr, *mul = nullptr, *add0 = nullptr, *add1 = nullptr;
+    __half *y = nullptr;
+    int rows = 0;
+};
+
+__global__ void __launch_bounds__(256) rms_ada_kernel(const RmsSeg s0, const RmsSeg s1, int dim, float eps)
 {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= rows) return;
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (w >= s0.rows + s1.rows) return;
+    const bool second = w >= s0.rows;
+    const int warp = second ? w - s0.rows : w;
+    const float *x = second ? s1.x : s0.x;
+    const float *gamma = second ? s1.gamma : s0.gamma, *mul = second ? s1.mul : s0.mul;
+    const float *add0 = second ? s1.add0 : s0.add0, *add1 = second ? s1.add1 : s0.add1;
+    __half *y = second ? s1.y : s0.y;
     const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(warp) * dim);
     double ss = 0.0;
     for (int i = lane; i < dim / 4; i += 32) {
@@ -324,10 +337,34 @@ extern "C" s2_status s2_dit_block_set_window_subset(s2_dit_block *b, const int32
 
 namespace {
 
-s2_status rms_ada3(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *mod3, __half *y)
+RmsSeg seg3(const float *x, int rows, int dim, const float *mod3, __half *y)
 {
-    return s2::rms_ada(st, x, rows, dim, eps, nullptr, mod3, mod3 ? mod3 + dim : nullptr,
-                       mod3 ? mod3 + 2 * dim : nullptr, y);
+    RmsSeg g;
+    g.x = x;
+    g.rows = rows;
+    g.mul = mod3;
+    g.add0 = mod3 ? mod3 + dim : nullptr;
+    g.add1 = mod3 ? mod3 + 2 * dim : nullptr;
+    g.y = y;
+    return g;
+}
+
+s2_status rms_launch(cudaStream_t st, const RmsSeg &a, const RmsSeg &b, int dim, float eps)
+{
+    const int rows = a.rows + b.rows;
+    if (rows <= 0) return S2_OK;
+    if (dim % 4 != 0) return s2::set_error(S2_INVALID_ARGUMENT, "rms_ada: dim %d not a multiple of 4", dim);
+    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a, b, dim, eps);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "rms_ada launch: %s", cudaGetErrorString(e));
+}
+
+// RMSNorm + adaLN (slot given by mod3) of `rows` rows, and of a second run of rows
+// with its own vectors in the same launch
+s2_status rms_ada3(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *mod3, __half *y,
+                   const float *x2 = nullptr, int rows2 = 0, const float *mod3_2 = nullptr, __half *y2 = nullptr)
+{
+    return rms_launch(st, seg3(x, rows, dim, mod3, y), seg3(x2, rows2, dim, mod3_2, y2), dim, eps);
 }
 
 }  // namespace
@@ -337,11 +374,15 @@ namespace s2 {
 s2_status rms_ada(cudaStream_t st, const float *x, int rows, int dim, float eps, const float *gamma, const float *mul,
                   const float *add0, const float *add1, void *y)
 {
-    if (rows <= 0) return S2_OK;
-    if (dim % 4 != 0) return set_error(S2_INVALID_ARGUMENT, "rms_ada: dim %d not a multiple of 4", dim);
-    rms_ada_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, dim, eps, gamma, mul, add0, add1, static_cast<__half *>(y));
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? S2_OK : s2::set_error(S2_INFERENCE_FAILED, "rms_ada launch: %s", cudaGetErrorString(e));
+    RmsSeg a;
+    a.x = x;
+    a.rows = rows;
+    a.gamma = gamma;
+    a.mul = mul;
+    a.add0 = add0;
+    a.add1 = add1;
+    a.y = static_cast<__half *>(y);
+    return rms_launch(st, a, RmsSeg{}, dim, eps);
 }
 
 s2_status modulation_vectors(cudaStream_t st, const float *emb, const float *mod6, int dim, float *out)
@@ -453,8 +494,7 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         S2_TRY(s2::modulation_vectors(st, emb, T.m(0, d), d, mt));
     }
     // attention input: RMSNorm + adaLN (slot 0); the last block's text is only normalised
-    S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid));
-    if (Lt > 0) S2_TRY(rms_ada3(st, txt, Lt, d, b->eps, b->last ? nullptr : mt, a_txt));
+    S2_TRY(rms_ada3(st, vid, L, d, b->eps, mv, a_vid, txt, Lt, b->last ? nullptr : mt, a_txt));
     // QKV projections (no bias) into the attention core's packed operands; the map
     // covers the L video rows, then the Lt text rows (the merged GEMM's rows L.., or
     // the text GEMM's rows)
@@ -473,6 +513,8 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     if (Lt > 0 && !merged) {
         g.M = Lt;
         g.pk.map += L;
+        g.partial = splitk;  // a few dozen rows: split K, the finish kernel applies the prologue
+        g.partial_floats = splitk_cap;
         S2_TRY(s2::gemm_f16(st, a_txt, T.qkv.ptr, g));
     }
     // windowed MM attention (attention core, text mean)
@@ -596,11 +638,19 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         S2_TRY(s2::gemm_f16(st, att_txt16, T.proj.ptr, q));
     }
     // MLP: RMSNorm + adaLN (slot 3), SwiGLU GEMM, output GEMM + gated residual
+    // a text branch with its own MLP (unshared weights, not the last block) has its MLP input
+    // normalised in the video rows' launch
+    const bool text_mlp = Lt > 0 && !b->last && !merged_rest;
     auto mlp = [&](const float *mb, const Branch &br, const float *hx, int rows, __half *a16, __half *hid, float *y,
-                   int split, float *y2, const s2::RowScatter *sc_rows) -> s2_status {
-        s2_status r = rms_ada3(st, hx, rows, d, b->eps, mb + 3 * dz, a16);
-        if (r != S2_OK) return r;
-        ++launches;
+                   int split, float *y2, const s2::RowScatter *sc_rows, bool normed) -> s2_status {
+        s2_status r;
+        if (!normed) {
+            r = text_mlp ? rms_ada3(st, hx, rows, d, b->eps, mb + 3 * dz, a16, h_txt, Lt, mt + 3 * dz,
+                                    static_cast<__half *>(sc.a_txt.ptr))
+                         : rms_ada3(st, hx, rows, d, b->eps, mb + 3 * dz, a16);
+            if (r != S2_OK) return r;
+            ++launches;
+        }
         s2::GemmArgs u;
         u.M = rows;
         u.N = 2 * h;
@@ -640,13 +690,13 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
         return S2_OK;
     };
     if ((s = mlp(mv, V, h_vid, merged_rest ? L + Lt : L, a_vid, static_cast<__half *>(sc.hid_vid.ptr), vid_out,
-                 merged_rest ? L : 0, txt_out, scatter)) != S2_OK) {
+                 merged_rest ? L : 0, txt_out, scatter, false)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }
-    if (Lt > 0 && !b->last && !merged_rest &&
+    if (text_mlp &&
         (s = mlp(mt, T, h_txt, Lt, static_cast<__half *>(sc.a_txt.ptr), static_cast<__half *>(sc.hid_txt.ptr), txt_out,
-                 0, nullptr, nullptr)) != S2_OK) {
+                 0, nullptr, nullptr, true)) != S2_OK) {
         b->last_launches = launches;
         return s;
     }

@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     store_chunk(&tmO0, v4, n0 / 2 + c * 32, m0 + quad * 32);
                 }
             }
-            if (a.epilogue == s2::GEMM_EPI_QKV_PACK && ok) {
+            if (a.epilogue == s2::GEMM_EPI_QKV_PACK && !split_k && ok) {
                 // Per 128-column head block: Q/K rows are RMS-normalised over the head (two
                 // passes over TMEM: the fp64 square sum, then the scaled values), V rows only
                 // rounded. The warp stages its 32 rows x 256 B (16-byte chunk k of row r at
@@ -598,6 +598,63 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_dealloc(tmem, kTmemCols);
     }
 #undef BAR
+}
+
+// Split-K finish of GEMM_EPI_QKV_PACK (the text rows' projection): one warp per
+// (row, 128-column head block), each lane four consecutive dims; the splits are
+// added in order, then the same prologue as the fused epilogue (fp32 square sum,
+// here reduced across the warp; inv-RMS x gamma; RoPE pairs; bf16 rounding) and
+// the packed stores (text rows into every window).
+__global__ void __launch_bounds__(256) splitk_pack_kernel(const s2::GemmArgs a, int ks)
+{
+    const int gw = static_cast<int>((blockIdx.x * 256LL + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int nhb = a.N / 128;
+    if (gw >= a.M * nhb) return;
+    const int row = gw / nhb, col0 = (gw - row * nhb) * 128;
+    const s2::PackArgs &pk = a.pk;
+    const int4 mp = __ldg(pk.map + row);
+    if (mp.x == -0x7fffffff) return;  // a row without a packed row
+    const bool text = mp.x < 0;
+    const int sec = col0 / pk.dim, head = (col0 - sec * pk.dim) >> 7;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < ks; ++sp) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(a.partial + (static_cast<size_t>(sp) * a.M + row) * a.N +
+                                                                col0) + lane);
+        x[0] = __fadd_rn(x[0], v.x);
+        x[1] = __fadd_rn(x[1], v.y);
+        x[2] = __fadd_rn(x[2], v.z);
+        x[3] = __fadd_rn(x[3], v.w);
+    }
+    if (sec < 2) {
+        float ss = __fmaf_rn(x[3], x[3], __fmaf_rn(x[2], x[2], __fmaf_rn(x[1], x[1], __fmul_rn(x[0], x[0]))));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.f / 128.f), pk.eps)));
+        const float *gm = pk.gammas + (text ? 2 : 0) * 128 + sec * 128 + 4 * lane;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], inv), __ldg(gm + e));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int gp = 2 * lane + i;
+            if (gp < 63) {
+                const int axis = gp / 21, pr = gp - axis * 21;
+                const int pos = axis == 0 ? mp.y : (axis == 1 ? mp.z : mp.w);
+                const float2 cs = __ldg(pk.rope + pr * pk.max_pos + pos);
+                const float f0 = x[2 * i], f1 = x[2 * i + 1];
+                x[2 * i] = __fsub_rn(__fmul_rn(f0, cs.x), __fmul_rn(f1, cs.y));
+                x[2 * i + 1] = __fadd_rn(__fmul_rn(f1, cs.x), __fmul_rn(f0, cs.y));
+            }
+        }
+    }
+    const uint2 v2 = make_uint2(pack_bf16_h2(x[0], x[1]), pack_bf16_h2(x[2], x[3]));
+    uint2 *outb = static_cast<uint2 *>(sec == 0 ? pk.q : (sec == 1 ? pk.k : pk.v)) +
+                  static_cast<size_t>(head) * pk.n_rows * 32;
+    if (!text) {
+        outb[static_cast<size_t>(mp.x) * 32 + lane] = v2;
+    } else {
+        const int l = -1 - mp.x;
+        for (int w = 0; w < pk.n_windows; ++w) outb[static_cast<size_t>(__ldg(pk.text_dst + w) + l) * 32 + lane] = v2;
+    }
 }
 
 // Split-K finish: out = epilogue(sum over splits of partial[split][row][n]), the
@@ -798,7 +855,7 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
     const long long tiles_k = mt * ((args.N + bn - 1) / bn);
     if (args.partial && !pair && args.M <= kBM && !args.conv && !args.row_dest &&
         (args.epilogue == GEMM_EPI_SPLIT_F16 || args.epilogue == GEMM_EPI_GATED_RESID_F32 ||
-         args.epilogue == GEMM_EPI_SWIGLU_F16) &&
+         args.epilogue == GEMM_EPI_SWIGLU_F16 || args.epilogue == GEMM_EPI_QKV_PACK) &&
         tiles_k * 2 <= sms) {
         ks = static_cast<int>(std::min<long long>({8LL, sms / tiles_k, (args.K / kBK) / 4}));
         while (ks > 1 && static_cast<size_t>(ks) * args.M * args.N > args.partial_floats) --ks;
@@ -883,7 +940,11 @@ s2_status gemm_f16(cudaStream_t st, const void *A, const void *B, const GemmArgs
             gemm_kernel<256, false><<<grid, kThreads, Tile<256>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], ka);
         else
             gemm_kernel<128, false><<<grid, kThreads, Tile<128>::kSmemBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], ka);
-        if (ks > 1) {
+        if (ks > 1 && args.epilogue == GEMM_EPI_QKV_PACK) {
+            const long long warps = 1LL * args.M * (args.N / 128);
+            splitk_pack_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(ka, ks);
+            if (args.extra_launches) ++*args.extra_launches;
+        } else if (ks > 1) {
             const long long outs = 1LL * args.M * (args.epilogue == GEMM_EPI_SWIGLU_F16 ? args.N / 2 : args.N);
             const int fgrid = static_cast<int>(std::min<long long>((outs + 255) / 256, 4LL * sms));
             splitk_finish_kernel<<<fgrid, 256, 0, st>>>(ka, ks);

@@ -54,13 +54,14 @@ def test_runner_cases_vs_reference(torch_cuda, golden, i):
     vo, to, b = run_gpu(torch_cuda, params, w, vid, txt, emb, shape)
     g = golden("block_runner_cases.npz")
     check_block(vo, to, g[f"c{i}_vid_out"], g[f"c{i}_txt_out"], vid, txt, f"runner case {i}")
-    # modulation vectors (1 + 1 when the text branch has its own, used weights), 2 norms, QKV with the
-    # attention prologue in its epilogue (text rows inside the video GEMM when the weights are shared),
-    # attention core + text mean, text convert, projections (merged unless last), MLP norm + 2 GEMMs
-    # (+ the text's own unless shared or last)
+    # modulation vectors (1 + 1 when the text branch has its own, used weights), one norm launch for
+    # the video and text rows, QKV with the attention prologue in its epilogue (text rows inside the
+    # video GEMM when the weights are shared), attention core + text mean, text convert, projections
+    # (merged unless last), MLP norm (the text rows' too) + 2 GEMMs (+ the text's own 2 GEMMs unless
+    # shared or last)
     shared, last = params["shared"], params["last"]
-    expected = (1 + (not shared and not last) + 2 + (1 if shared else 2) + 2 + 1
-                + (1 if shared and not last else 2) + 3 + (3 if not shared and not last else 0))
+    expected = (1 + (not shared and not last) + 1 + (1 if shared else 2) + 2 + 1
+                + (1 if shared and not last else 2) + 3 + (2 if not shared and not last else 0))
     assert b.last_launches() == expected
 
 
