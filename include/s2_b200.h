@@ -359,7 +359,11 @@ S2_API s2_status s2_dit_block_device_error(s2_dit_block *block, int *code);
  * fp32 rounding (another summation order). *extra_launches (may be NULL)
  * receives the kernels launched beyond the GEMM itself. err (required):
  * device int32 error word, set when a bounded wait inside the kernel gives
- * up. Stream-ordered. */
+ * up. row_dest (S2_GEMM_GATED_RESID_F32 only, may be NULL): device int32
+ * pairs {0, r'} per row r below split_row (or M): row r is written to y at
+ * row r' instead of row r (the row scatter the sharded Euler step uses with
+ * other ranks' buffers, here within y; every destination row written once;
+ * no split-K). Stream-ordered. */
 typedef enum s2_gemm_epilogue {
     S2_GEMM_SPLIT_F16 = 0,
     S2_GEMM_GATED_RESID_F32 = 2,
@@ -376,6 +380,7 @@ typedef struct s2_gemm_desc {
     float *workspace;
     size_t workspace_floats;
     int32_t *err;
+    const int32_t *row_dest;
 } s2_gemm_desc;
 S2_API s2_status s2_gemm(void *stream, const s2_gemm_desc *desc, int *extra_launches);
 

@@ -990,6 +990,13 @@ extern "C" s2_status s2_gemm(void *stream, const s2_gemm_desc *d, int *extra_lau
     g.partial = d->workspace;
     g.partial_floats = d->workspace ? d->workspace_floats : 0;
     g.err = d->err;
+    if (d->row_dest) {
+        if (d->epilogue != S2_GEMM_GATED_RESID_F32 || !d->y)
+            return s2::set_error(S2_INVALID_ARGUMENT, "s2_gemm: row_dest needs the gated-residual epilogue and y");
+        g.row_dest = reinterpret_cast<const int2 *>(d->row_dest);
+        g.dest_base[0] = d->y;
+        g.y = nullptr;
+    }
     int extra = 0;
     g.extra_launches = &extra;
     const s2_status s = s2::gemm_f16(static_cast<cudaStream_t>(stream), d->a, d->b, g);

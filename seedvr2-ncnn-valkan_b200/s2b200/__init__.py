@@ -58,7 +58,8 @@ class GemmDesc(ctypes.Structure):
                 + [(n, ctypes.c_void_p) for n in ("a", "b", "bias", "gmul", "resid", "resid2", "out0", "out1", "out2",
                                                   "y", "y2")]
                 + [("split", ctypes.c_int), ("split_row", ctypes.c_int), ("out_scale", ctypes.c_float),
-                   ("workspace", ctypes.c_void_p), ("workspace_floats", ctypes.c_size_t), ("err", ctypes.c_void_p)])
+                   ("workspace", ctypes.c_void_p), ("workspace_floats", ctypes.c_size_t), ("err", ctypes.c_void_p),
+                   ("row_dest", ctypes.c_void_p)])
 
 
 GEMM_SPLIT_F16, GEMM_GATED_RESID_F32, GEMM_SWIGLU_F16 = 0, 2, 3
@@ -584,10 +585,11 @@ def text_window_sum(txt_partial, n_windows, text_len, dim, scale, txt_out, accum
 
 
 def gemm(epilogue, a, b, *, bias=None, gmul=None, resid=None, resid2=None, outs=(), y=None, y2=None, split=0,
-         split_row=0, out_scale=1.0, workspace=None, err=None, stream=None) -> int:
+         split_row=0, out_scale=1.0, workspace=None, err=None, stream=None, row_dest=None) -> int:
     """s2_gemm: the block's InnerProduct on tcgen05 (a [M][K], b [N][K] fp16 CUDA
     tensors). Returns the number of extra kernels launched (split-K finish).
-    err: device int32 error word (a zeroed one is made when None)."""
+    err: device int32 error word (a zeroed one is made when None). row_dest:
+    device int32 [rows][2] of {0, destination row of y} (gated residual only)."""
     if err is None:
         err = _torch().zeros(1, dtype=_torch().int32, device=a.device)
     M, K = a.shape
@@ -601,7 +603,7 @@ def gemm(epilogue, a, b, *, bias=None, gmul=None, resid=None, resid2=None, outs=
                  resid=_ptr(resid), resid2=_ptr(resid2), out0=_ptr(o[0]), out1=_ptr(o[1]), out2=_ptr(o[2]),
                  y=_ptr(y), y2=_ptr(y2), split=int(split), split_row=int(split_row), out_scale=float(out_scale),
                  workspace=_ptr(workspace), workspace_floats=0 if workspace is None else workspace.numel(),
-                 err=_ptr(err))
+                 err=_ptr(err), row_dest=_ptr(row_dest))
     extra = ctypes.c_int(0)
     _check(lib().s2_gemm(_stream_ptr(stream), ctypes.byref(d), ctypes.byref(extra)), "s2_gemm")
     return extra.value

@@ -110,6 +110,36 @@ def test_splitk_gated_residual(torch_cuda, split_row, K):
     torch.testing.assert_close(res["plain"][0], ref, atol=5e-4, rtol=1e-4)
 
 
+@pytest.mark.parametrize("M,K,split_row", [(300, 2560, 0), (4160, 2560, 0), (4160, 6912, 4102)])
+def test_gated_residual_row_scatter(torch_cuda, M, K, split_row):
+    """The row scatter of the gated-residual epilogue (each row of the block's MLP
+    output stored at its next owner's row; here a permutation within y): every row
+    equals the plain epilogue's row bit for bit at its destination, rows past the
+    split still go to y2. M = 4160 runs the CTA-pair GEMM, 300 the single-CTA one."""
+    torch = torch_cuda
+    d = 2560
+    a, b, g = _operands(torch, M, d, K, 11 + M)
+    bias = (torch.randn(d, generator=g) * 0.02).cuda()
+    gmul = (torch.randn(d, generator=g) * 0.02 + 1.0).cuda()
+    resid = torch.randn(M, d, generator=g).cuda()
+    rows = split_row or M
+    perm = torch.randperm(rows, generator=g)
+    dest = torch.stack([torch.zeros(rows, dtype=torch.int32), perm.to(torch.int32)], 1).contiguous().cuda()
+    kw = dict(split_row=split_row, resid2=resid[split_row:]) if split_row else {}
+    y_plain = torch.full((rows, d), float("nan"), device="cuda")
+    y_sc = torch.full((rows, d), float("nan"), device="cuda")
+    y2_plain = torch.full((max(M - rows, 1), d), float("nan"), device="cuda")
+    y2_sc = torch.full((max(M - rows, 1), d), float("nan"), device="cuda")
+    s2b200.gemm(s2b200.GEMM_GATED_RESID_F32, a, b, bias=bias, gmul=gmul, resid=resid, y=y_plain,
+                y2=y2_plain if split_row else None, **kw)
+    s2b200.gemm(s2b200.GEMM_GATED_RESID_F32, a, b, bias=bias, gmul=gmul, resid=resid, y=y_sc,
+                y2=y2_sc if split_row else None, row_dest=dest, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(y_sc[perm.cuda()], y_plain)
+    if split_row:
+        assert torch.equal(y2_sc, y2_plain)
+
+
 def test_splitk_gated_residual_last_block_rule(torch_cuda):
     """The last block's text rule: no gate, output scale 2: y = 2 (acc + b + resid)."""
     torch = torch_cuda
