@@ -451,7 +451,8 @@ def run_ours(args, rank, world, local_rank):
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     traffic = profile_traffic("window_attention_cfg2.md")
-    pro_bytes = synth.prologue_bytes(T * H * W, Lt, (plans[0]["n_rows"] + plans[1]["n_rows"]) / 2, heads, 2)
+    pro_bytes = synth.prologue_bytes(T * H * W, Lt, heads, 2)
+    pro_moved = synth.prologue_bytes_moved(T * H * W, Lt, (plans[0]["n_rows"] + plans[1]["n_rows"]) / 2, heads, 2)
     pro_gbs = pro_bytes / (float(np.mean(t_pro)) * 1e-3) / 1e9
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
 
@@ -485,7 +486,8 @@ def run_ours(args, rank, world, local_rank):
                              "ms_per_launch": {"plain": att_plain, "shifted": att_shift}},
                 "kernels": {"prologue_ms": float(np.mean(t_pro)), "attention_ms": att_ms,
                             "text_sum_ms": float(np.mean(t_txt)), "prologue_gbs": pro_gbs,
-                            "prologue_hbm_frac": pro_gbs / hbm_peak},
+                            "prologue_hbm_frac": pro_gbs / hbm_peak,
+                            "prologue_moved_gbs": pro_moved / (float(np.mean(t_pro)) * 1e-3) / 1e9},
                 "clocks": clk.summary()}
         if e2e:
             line["e2e"] = e2e

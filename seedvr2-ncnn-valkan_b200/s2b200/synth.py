@@ -51,9 +51,17 @@ def attention_flops(windows: np.ndarray, text_len: int, heads: int) -> float:
     return float(np.sum(4.0 * s.astype(np.float64) ** 2 * HEAD_DIM * heads))
 
 
-def prologue_bytes(L: int, text_len: int, n_rows: int, heads: int, in_bytes: int) -> float:
+def prologue_bytes(L: int, text_len: int, heads: int, in_bytes: int) -> float:
     """Algorithmic HBM bytes of the prologue: read each QKV row once (video and
-    text), write the packed q/k/v rows in 16-bit."""
+    text), write each row's packed q/k/v once in 16-bit (text rows once, not per
+    window)."""
+    dim = heads * HEAD_DIM
+    return float((L + text_len) * 3 * dim * in_bytes + (L + text_len) * 3 * dim * 2)
+
+
+def prologue_bytes_moved(L: int, text_len: int, n_rows: int, heads: int, in_bytes: int) -> float:
+    """Bytes the prologue moves: the algorithmic read, and the packed rows it
+    writes, the text rows once per window (n_rows packed rows)."""
     dim = heads * HEAD_DIM
     return float((L + text_len) * 3 * dim * in_bytes + n_rows * 3 * dim * 2)
 
