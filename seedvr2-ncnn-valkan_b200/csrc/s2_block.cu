@@ -507,8 +507,10 @@ s2_status s2::dit_block_forward_ex(s2_dit_block *b, void *stream, const float *v
     g.extra_launches = &extra;
     g.M = merged ? L + Lt : L;
     g.epilogue = s2::GEMM_EPI_QKV_PACK;
-    S2_TRY(s2::attention_pack_target(b->attn, st, L, Lt, &g));
-    --launches;  // set-up only
+    if ((s = s2::attention_pack_target(b->attn, st, L, Lt, &g)) != S2_OK) {  // set-up only, no launch
+        b->last_launches = launches;
+        return s;
+    }
     S2_TRY(s2::gemm_f16(st, a_vid, V.qkv.ptr, g));
     if (Lt > 0 && !merged) {
         g.M = Lt;
