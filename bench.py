@@ -13,8 +13,7 @@ e2e       = same metric through the layer's host-buffer C-ABI call
             (s2_attention_layer_forward_host): pinned host QKV in, host
             outputs back, copies inside the timed region.
 roofline  = the attention kernel alone: FLOPs per launch / mean launch time
-            (events around each launch, in up to 3 further steps after the
-            timed ones).
+            (events around each launch inside the timed region).
 cpu_baseline / --impl reference: the reference's own CPU attention()
             (oracle/_ref, built from the reference sources) on a bounded
             sample of the same workload, on this host's cores.
@@ -404,6 +403,8 @@ def run_ours(args, rank, world, local_rank):
     if int(err.item()) != 0:
         raise RuntimeError(f"attention kernel device error {int(err.item())}")
 
+    n_ev = layers_per_step * args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
@@ -416,23 +417,13 @@ def run_ours(args, rank, world, local_rank):
         start.record(stream)
         for s in range(args.steps):
             for i in range(layers_per_step):
-                layer(i)
+                layer(i, evs[s * layers_per_step + i])
             end_step()
         end.record(stream)
         torch.cuda.synchronize()
     if dist:
         dist.barrier()
     ms = start.elapsed_time(end)
-    # per-kernel times from further steps with events between the kernels, kept out of the
-    # timed steps so that those run their kernels back to back as a real step does (each
-    # kernel's set-up may overlap the previous kernel's tail: programmatic launch)
-    n_brk = min(args.steps, 3)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(layers_per_step * n_brk)]
-    for s in range(n_brk):
-        for i in range(layers_per_step):
-            layer(i, evs[s * layers_per_step + i])
-        end_step()
-    torch.cuda.synchronize()
     if int(err.item()) != 0:
         raise RuntimeError(f"attention kernel device error {int(err.item())}")
     t_pro = np.array([e[0].elapsed_time(e[1]) for e in evs])
