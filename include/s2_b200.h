@@ -501,7 +501,10 @@ S2_API s2_status s2_make_condition(void *stream, const float *encoded, const flo
 /* From the second call with the same shapes, buffers and timestep,
  * s2_dit_euler_step replays the step as one CUDA graph (captured on an
  * internal stream); enable = 0 keeps every call eager. On by default; a call
- * on a stream that is itself being captured always runs eagerly. */
+ * on a stream that is itself being captured always runs eagerly. A call of
+ * s2_dit_forward or s2_dit_sample(_texts) on the model drops the graph (it may
+ * grow the workspaces the graph points at): the next Euler step runs eagerly
+ * and captures again. */
 S2_API s2_status s2_dit_set_graph(s2_dit *model, int enable);
 
 /* Shard the DiT step over the communicator's ranks (NULL = one GPU). Every
@@ -511,7 +514,9 @@ S2_API s2_status s2_dit_set_graph(s2_dit *model, int enable);
  * ownerships of consecutive blocks, and all ranks end with the full output
  * (disjoint per-rank parts summed). All ranks call forward / euler_step with
  * the same inputs, in the same order (the graph of a sharded step holds the
- * NCCL calls: destroy the model before the communicator). */
+ * NCCL calls: destroy the model before the communicator). At the first call
+ * for a grid the ranks gather each other's grid and window sizes and all
+ * return S2_INVALID_ARGUMENT when they differ. */
 S2_API s2_status s2_dit_set_comm(s2_dit *model, s2_comm *comm);
 S2_API int s2_dit_last_launches(const s2_dit *model);
 S2_API s2_status s2_dit_device_error(s2_dit *model, int *code);

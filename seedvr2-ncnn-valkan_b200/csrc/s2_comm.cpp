@@ -256,33 +256,45 @@ s2_status comm_allreduce_f32(s2_comm *c, float *buf, size_t n, cudaStream_t st)
     return settle(c, nc.all_reduce(buf, buf, n, ncclFloat, ncclSum, c->comm, st), "ncclAllReduce");
 }
 
+s2_status comm_allgather_host(s2_comm *c, const void *local, size_t bytes, void *all, cudaStream_t st)
+{
+    const int n = c ? c->nranks : 1, me = c ? c->rank : 0;
+    if (n == 1) {
+        std::memcpy(all, local, bytes);
+        return S2_OK;
+    }
+    if (c->aborted) return set_error(S2_INFERENCE_FAILED, "all-gather: communicator was aborted");
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+        return set_error(S2_UNSUPPORTED, "all-gather: not during stream capture");
+    struct Tmp {  // the device buffer of the all-gather, released on every path
+        DeviceBuffer b;
+        ~Tmp() { b.release(); }
+    } dev;
+    if (!dev.b.ensure(n * bytes)) return set_error(S2_OUT_OF_MEMORY, "all-gather: device buffer");
+    char *d = static_cast<char *>(dev.b.ptr);
+    if (cudaMemcpy(d + me * bytes, local, bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+        return set_error(S2_INFERENCE_FAILED, "all-gather: upload failed");
+    s2_status s = settle(c, nccl().all_gather(d + me * bytes, d, bytes, ncclChar, c->comm, st), "ncclAllGather");
+    if (s != S2_OK) return s;
+    if (cudaMemcpyAsync(all, d, n * bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return set_error(S2_INFERENCE_FAILED, "all-gather: download failed");
+    // bounded: a rank that never joins ends in an aborted communicator, not a blocked host
+    return s2_comm_wait(c, st);
+}
+
 s2_status comm_share(s2_comm *c, void *local, void **peers, cudaStream_t st)
 {
     const int n = c ? c->nranks : 1, me = c ? c->rank : 0;
     for (int p = 0; p < n; ++p) peers[p] = p == me ? local : nullptr;
     if (n == 1) return S2_OK;
     if (c->aborted) return set_error(S2_INFERENCE_FAILED, "share: communicator was aborted");
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
-        return set_error(S2_UNSUPPORTED, "share: not during stream capture");
     cudaIpcMemHandle_t h;
     if (cudaIpcGetMemHandle(&h, local) != cudaSuccess)
         return set_error(S2_INFERENCE_FAILED, "share: cudaIpcGetMemHandle failed (not a cudaMalloc base pointer?)");
     std::vector<cudaIpcMemHandle_t> all(n);
-    struct Tmp {  // the all-gather buffer, released on every path
-        DeviceBuffer b;
-        ~Tmp() { b.release(); }
-    } dev;
-    const size_t hb = sizeof(cudaIpcMemHandle_t);
-    if (!dev.b.ensure(n * hb)) return set_error(S2_OUT_OF_MEMORY, "share: handle buffer");
-    char *d = static_cast<char *>(dev.b.ptr);
-    if (cudaMemcpy(d + me * hb, &h, hb, cudaMemcpyHostToDevice) != cudaSuccess)
-        return set_error(S2_INFERENCE_FAILED, "share: handle upload failed");
-    s2_status s = settle(c, nccl().all_gather(d + me * hb, d, hb, ncclChar, c->comm, st), "share (ncclAllGather)");
+    const s2_status s = comm_allgather_host(c, &h, sizeof(h), all.data(), st);
     if (s != S2_OK) return s;
-    if (cudaMemcpyAsync(all.data(), d, n * hb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
-        return set_error(S2_INFERENCE_FAILED, "share: handle download failed");
     for (int p = 0; p < n; ++p) {
         if (p == me) continue;
         if (cudaIpcOpenMemHandle(&peers[p], all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {

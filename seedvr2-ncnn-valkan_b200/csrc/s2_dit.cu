@@ -328,6 +328,14 @@ struct s2_dit {
         if (exec) cudaGraphExecDestroy(exec);
         exec = nullptr;
     }
+    // A forward outside the Euler-step graph may grow (reallocate) the buffers
+    // the graph's kernels point at, or remake the peer mappings of a sharded
+    // step: the next Euler step then runs eagerly and captures again.
+    void forget_step_graph()
+    {
+        drop_graph();
+        key_valid = false;
+    }
 };
 
 extern "C" s2_status s2_dit_create(int device, int n_blocks, int dim, int heads, int head_dim, int mlp_hidden,
@@ -470,12 +478,29 @@ extern "C" s2_status s2_dit_load_block(s2_dit *d, int index, int shared, int las
 // Window ownership of both window kinds (s2_shard_windows_joint), every rank's
 // local row order, and the row-exchange maps between them (s2::shard_exchange_maps,
 // the host function the CPU-rank tests check); sets every block's window subset.
-static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
+static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt, cudaStream_t st, bool *rebuilt)
 {
     auto &sh = d->sh;
+    *rebuilt = false;
     if (sh.valid && sh.T == T && sh.Hp == Hp && sh.Wp == Wp && sh.Lt == Lt) return S2_OK;
     sh.valid = false;
     const int N = s2_comm_size(d->comm), me = s2_comm_rank(d->comm);
+    {
+        // every rank derives every rank's maps from the grid, so all must run the same one:
+        // a rank with other shapes would store rows where no peer expects them
+        const int32_t mine[7] = {T, Hp, Wp, Lt, d->wt, d->wh, d->ww};
+        std::vector<int32_t> all(7 * static_cast<size_t>(N));
+        const s2_status g = s2::comm_allgather_host(d->comm, mine, sizeof(mine), all.data(), st);
+        if (g != S2_OK) return g;
+        for (int r = 0; r < N; ++r)
+            if (!std::equal(mine, mine + 7, all.begin() + 7 * r))
+                return s2::set_error(S2_INVALID_ARGUMENT,
+                                     "sharded step: rank %d runs a %dx%dx%d token grid with %d text tokens and windows "
+                                     "%dx%dx%d, rank %d a %dx%dx%d grid with %d and %dx%dx%d (all ranks must run the "
+                                     "same step)",
+                                     r, all[7 * r], all[7 * r + 1], all[7 * r + 2], all[7 * r + 3], all[7 * r + 4],
+                                     all[7 * r + 5], all[7 * r + 6], me, T, Hp, Wp, Lt, d->wt, d->wh, d->ww);
+    }
     s2::ShardMaps m;
     s2_status s = s2::shard_exchange_maps(T, Hp, Wp, d->wt, d->wh, d->ww, Lt, N, me, m);
     if (s != S2_OK) return s;
@@ -506,14 +531,17 @@ static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt)
     }
     sh.T = T, sh.Hp = Hp, sh.Wp = Wp, sh.Lt = Lt;
     sh.valid = true;
+    *rebuilt = true;
     return S2_OK;
 }
 
 // Peer mappings of the exchange's destinations (vid_a, vid_b) and flag words,
-// (re)made whenever one of those allocations changed: every rank's allocations
-// change in the same call (same sizes), so every rank makes the same
-// collective calls. Host-synchronising; not during stream capture.
-static s2_status xfer_setup(s2_dit *d, cudaStream_t st)
+// made again whenever the shard maps were rebuilt (`rebuilt`: a new grid, which
+// every rank meets in the same call, checked by build_shard), so every rank
+// makes the same collective calls. The allocations only grow with the grid, so
+// they cannot move without a rebuild; if they did, the call fails rather than
+// share on one rank alone. Host-synchronising; not during stream capture.
+static s2_status xfer_setup(s2_dit *d, cudaStream_t st, bool rebuilt)
 {
     auto &x = d->xf;
     const int n = s2_comm_size(d->comm), me = s2_comm_rank(d->comm);
@@ -526,7 +554,14 @@ static s2_status xfer_setup(s2_dit *d, cudaStream_t st)
             return s2::set_error(S2_INFERENCE_FAILED, "sharded step: flag words memset failed");
     }
     void *cur[3] = {d->vid_a.ptr, d->vid_b.ptr, x.flags.ptr};
-    if (x.n == n && x.me == me && cur[0] == x.mine[0] && cur[1] == x.mine[1] && cur[2] == x.mine[2]) return S2_OK;
+    const bool same = x.n == n && x.me == me && cur[0] == x.mine[0] && cur[1] == x.mine[1] && cur[2] == x.mine[2];
+    if (!rebuilt) {
+        if (same) return S2_OK;
+        d->sh.valid = false;  // the next call rebuilds the maps and shares again
+        return s2::set_error(S2_INFERENCE_FAILED,
+                             "sharded step: exchange buffers are not mapped for the current grid (an earlier set-up "
+                             "failed or they moved without a new grid)");
+    }
     x.unshare();
     x.n = n;
     x.me = me;
@@ -534,6 +569,7 @@ static s2_status xfer_setup(s2_dit *d, cudaStream_t st)
         const s2_status s = s2::comm_share(d->comm, cur[b], x.peer[b], st);
         if (s != S2_OK) {
             x.unshare();
+            d->sh.valid = false;
             return s;
         }
         x.mine[b] = cur[b];
@@ -593,8 +629,9 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
     const bool sharded = d->comm && s2_comm_size(d->comm) > 1;
     int rows0 = rows;
     if (sharded) {
-        S2_TRY(build_shard(d, T, Hp, Wp, Lt));
-        S2_TRY(xfer_setup(d, st));
+        bool rebuilt = false;
+        S2_TRY(build_shard(d, T, Hp, Wp, Lt, st, &rebuilt));
+        S2_TRY(xfer_setup(d, st, rebuilt));
         rows0 = d->sh.n_local[d->shifted[0]];
     } else if (d->sh.valid) {
         for (s2_dit_block *b : d->blocks) {  // back to whole-clip blocks
@@ -726,6 +763,10 @@ static s2_status dit_forward_into(s2_dit *d, void *stream, const float *latent, 
 extern "C" s2_status s2_dit_forward(s2_dit *d, void *stream, const float *latent, int T, int H, int W,
                                     const float *text, int Lt, float timestep, float *prediction)
 {
+    if (d) {
+        s2::DeviceGuard guard(d->device);
+        d->forget_step_graph();
+    }
     return dit_forward_into(d, stream, latent, T, H, W, text, Lt, timestep, nullptr, prediction);
 }
 
@@ -832,6 +873,7 @@ extern "C" s2_status s2_dit_sample_texts(s2_dit *d, void *stream, const float *n
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long plane = 1LL * T * H * W, n = plane * d->oc;
     const bool rescale = guide && cfg_rescale != 0.0f;
+    d->forget_step_graph();
     if (!d->latent.ensure(static_cast<size_t>(plane) * d->vc * 4) || !d->pred_pos.ensure(static_cast<size_t>(n) * 4) ||
         (guide && !d->pred_neg.ensure(static_cast<size_t>(n) * 4)) ||
         (rescale && !d->cfg_ws.ensure(s2::cfg_workspace_bytes())))

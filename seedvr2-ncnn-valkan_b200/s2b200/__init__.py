@@ -881,6 +881,10 @@ class Comm:
         dist.broadcast(t, 0, group=pg)
         return cls(device, rank, world, bytes(t.cpu().tolist()))
 
+    def set_timeout(self, ms: int):
+        """Deadline of this communicator's host-side waits (s2_comm_set_timeout)."""
+        _check(lib().s2_comm_set_timeout(self.handle, int(ms)), "s2_comm_set_timeout")
+
     def close(self):
         if self.handle is not None and self.handle.value:
             lib().s2_comm_destroy(self.handle)

@@ -159,6 +159,37 @@ def test_graph_replay_matches_eager(torch_cuda):
     assert m.last_launches() == eager.last_launches()
 
 
+def test_graph_dropped_by_forward_on_larger_grid(torch_cuda):
+    """A captured Euler-step graph points at the step's workspaces; a plain
+    forward (and a sampling loop) on a larger grid grows them, so the next Euler
+    step for the first grid must run again (eager, then a new capture) and give
+    the eager model's result."""
+    torch = torch_cuda
+    hp, wi, wo, bps, bws = build_case(4, 256, 2, 256, 256, four_block_flags)
+    noise, cond, text = synth.dit_latents((2, 8, 12), 16, 9, 256)
+    n, c, t = (torch.from_numpy(a).cuda() for a in (noise, cond, text))
+    m = make_model(4, 256, 2, 256, 256, wi, wo, bps, bws)
+    x0 = torch.empty_like(n)
+    for _ in range(3):  # eager, captured, replayed
+        m.euler_step(n, c, t, 1000.0, x0)
+    big_n, big_c, big_t = (torch.from_numpy(a).cuda() for a in synth.dit_latents((3, 16, 20), 16, 9, 256))
+    big_lat = torch.cat([big_n, big_c, torch.ones_like(big_n[:1])], 0)
+    m.forward(big_lat, big_t, 1000.0)
+    m.sample(big_n, big_c, big_t, steps=1)
+    outs = []
+    for _ in range(3):
+        x0.zero_()
+        m.euler_step(n, c, t, 1000.0, x0)
+        torch.cuda.synchronize()
+        outs.append(x0.cpu().numpy().copy())
+    assert m.device_error() == 0
+    eager = make_model(4, 256, 2, 256, 256, wi, wo, bps, bws)
+    eager.set_graph(False)
+    ref_out = eager.euler_step(n, c, t, 1000.0).cpu().numpy()
+    for o in outs:
+        assert np.array_equal(o, ref_out)
+
+
 def test_load_exported_model_dir(torch_cuda, tmp_path):
     """A model directory in the reference's exported layout (fp16-tagged
     InnerProduct weights) loads through s2_dit_load_dir and gives exactly the

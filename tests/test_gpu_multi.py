@@ -68,6 +68,49 @@ def _rank(rank, world, port, out_dir, windows=(0, 0, 0)):
     dist.destroy_process_group()
 
 
+def _rank_mismatch(rank, world, port, out_dir):
+    """Each rank steps a grid of its own width: every rank must refuse the step."""
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    comm = s2b200.Comm.create(rank, rank, world)
+    comm.set_timeout(60000)
+    flags, wi, wo, bws, _, _, text = _case()
+    m = _model(rank, flags, wi, wo, bws)
+    m.set_comm(comm)
+    T, H, W = CASE["lat"]
+    noise, cond, _ = synth.dit_latents((T, H, W + 4 * rank), 16, CASE["Lt"], CASE["tc"])
+    status, msg = 0, ""
+    try:
+        m.euler_step(*(torch.from_numpy(a).cuda(rank) for a in (noise, cond, text)))
+    except s2b200.S2Error as e:
+        status, msg = e.status, str(e)
+    with open(os.path.join(out_dir, f"mismatch_{rank}.txt"), "w") as f:
+        f.write(f"{status}\n{msg}\n")
+    m.close()
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_step_refuses_different_grids(tmp_path):
+    """Ranks called with different grids would derive different exchange maps:
+    the shard set-up gathers every rank's grid and all ranks return
+    S2_INVALID_ARGUMENT instead of storing rows where no peer expects them."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = 29500 + (os.getpid() + 250) % 1000
+    mp.start_processes(_rank_mismatch, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        status, msg = (tmp_path / f"mismatch_{r}.txt").read_text().split("\n", 1)
+        assert int(status) == s2b200.S2_INVALID_ARGUMENT, (r, status, msg)
+        assert "all ranks must run the same step" in msg, msg
+
+
 def test_sharded_euler_step_two_gpus(tmp_path, ref):
     import torch
     import torch.multiprocessing as mp
