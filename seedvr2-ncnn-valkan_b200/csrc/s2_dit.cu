@@ -516,9 +516,17 @@ static s2_status build_shard(s2_dit *d, int T, int Hp, int Wp, int Lt, cudaStrea
             cudaMemcpy(sh.tok[k].ptr, m.tok[k].data(), m.tok[k].size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
     }
+    const long long rows = 1LL * T * Hp * Wp;  // every rank's hidden-state buffers hold this many rows
     for (int k = 0; k < 2; ++k) {
         std::vector<int2> dest(m.tok[k].size());
-        for (size_t i = 0; i < dest.size(); ++i) dest[i] = make_int2(m.dest_rank[k][i], m.dest_row[k][i]);
+        for (size_t i = 0; i < dest.size(); ++i) {
+            // the MLP output GEMM stores row i at (rank, row) in peer memory: keep every store
+            // inside the destination's buffer whatever the maps say
+            if (m.dest_rank[k][i] < 0 || m.dest_rank[k][i] >= N || m.dest_row[k][i] < 0 || m.dest_row[k][i] >= rows)
+                return s2::set_error(S2_INFERENCE_FAILED, "shard: row %zu has destination (%d, %d) outside %d ranks x %lld rows",
+                                     i, m.dest_rank[k][i], m.dest_row[k][i], N, rows);
+            dest[i] = make_int2(m.dest_rank[k][i], m.dest_row[k][i]);
+        }
         if (!sh.dest[k].ensure(std::max<size_t>(dest.size(), 1) * sizeof(int2)) ||
             cudaMemcpy(sh.dest[k].ptr, dest.data(), dest.size() * sizeof(int2), cudaMemcpyHostToDevice) != cudaSuccess)
             return s2::set_error(S2_OUT_OF_MEMORY, "shard: map upload failed");
