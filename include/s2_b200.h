@@ -15,11 +15,12 @@
  *    `void* stream` (NULL = legacy default stream) and never synchronise the
  *    host, except the *_host variants, which copy host buffers in and out.
  *  - Device pointers are caller-owned. Layer objects own only their weights,
- *    cached window plans and workspaces. Those workspaces grow (are
- *    reallocated) when an object first meets a larger shape, so a caller that
- *    captures an object's forward into its own CUDA graph keeps the graph only
- *    while it calls that object with shapes no larger than the captured ones
- *    (or captures again). The DiT's own Euler-step graph handles this itself.
+ *    cached window plans and workspaces. A call with another shape rebuilds
+ *    the cached plans (in place, or reallocated when larger) and may grow the
+ *    workspaces, so a caller that captures an object's forward into its own
+ *    CUDA graph may replay it only while every call on that object uses the
+ *    captured shapes; after any other call it captures again. The DiT's own
+ *    Euler-step graph handles this itself.
  *  - head_dim is 128 (the reference's MM-RoPE covers dims 0..125 and assumes
  *    128, seedvr2_dit_block.cpp:956-971).
  */
